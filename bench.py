@@ -1,0 +1,375 @@
+"""Benchmark: rel-pos MHA encoder frames/s on B200.
+
+One step = one RelPositionMultiHeadAttention forward (fused Q|K|V GEMM,
+linear_pos GEMM, fused rel-pos attention, linear_out GEMM) over a batch of
+16 utterances of T=750 frames (d_model 1024, 8 heads of 128, bf16), lengths
+uniform in [375, 750] with the key padding mask.  Frames counted are valid
+frames (sum of lengths).  Multi-GPU: one process per GPU, each with its own
+16-utterance batch (weak scaling, no collective on the data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the CPU restatement of the reference algorithm
+(oracle/, ORC_REFERENCE_ALGO mode: query blocks, materialised (q+v)P^T,
+rel_shift by pad/reshape, masked softmax) on the host cores; the reference
+itself (Rust over MLX/Metal, macOS only) cannot run on this machine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "rel-pos MHA encoder frames/s at 1/2/4/8 B200; % of tensor/HBM roofline"
+B, T, D, H = 16, 750, 1024, 8
+LEN_LO, LEN_HI = 375, 750
+WORKLOAD = ("BASELINE config 1: offline batched full-context rel-pos MHA layer, bf16, "
+            "B=16 T=750 d_model=1024 8x128 heads, lengths U[375,750] with key padding mask")
+L2_FLUSH_BYTES = 256 << 20
+
+
+def workload(seed: int):
+    rng = np.random.default_rng(seed)
+    f = lambda *s: (rng.standard_normal(s) * 0.02).astype(np.float32)
+    w = {"wq": f(D, D), "bq": f(D), "wk": f(D, D), "bk": f(D), "wv": f(D, D), "bv": f(D),
+         "wo": f(D, D), "bo": f(D), "wp": f(D, D), "pos_bias_u": f(H, D // H),
+         "pos_bias_v": f(H, D // H)}
+    x = rng.standard_normal((B, T, D)).astype(np.float32)
+    lengths = rng.integers(LEN_LO, LEN_HI + 1, B).astype(np.int32)
+    return w, x, lengths
+
+
+def algorithmic_flops(lengths):
+    """Per forward, counting useful work only: projections 2*K*N per valid
+    frame (Q,K,V,out), linear_pos over the 2T-1 positions, attention
+    3 products (ac, bd, PV) x 2*dh per visible (query, key) pair of valid
+    queries."""
+    dh = D // H
+    valid = int(np.sum(lengths))
+    proj = 4 * 2 * valid * D * D
+    pos = 2 * (2 * T - 1) * D * D
+    attn = 3 * 2 * dh * H * int(np.sum(lengths.astype(np.int64) ** 2))
+    return proj, pos, attn
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def oracle_sample(w, x, lengths, n_utts, threads):
+    """Time the CPU restatement on the first n_utts utterances; returns
+    (valid frames, seconds)."""
+    from oracle import oracle as orc
+    orc.set_threads(threads)
+    pe = orc.get_encoding(D, 5000, T)
+    xs, ls = x[:n_utts], lengths[:n_utts]
+    t0 = time.perf_counter()
+    orc.mha_forward(xs, w, pe, H, lengths=ls, mode=orc.ORC_REFERENCE_ALGO, bf16=True)
+    return int(ls.sum()), time.perf_counter() - t0
+
+
+class ClockSampler:
+    """nvidia-smi clocks during the timed region (one GPU)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [s.strip() for s in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def run_reference(args):
+    """The reference arm: CPU restatement of the reference algorithm."""
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    w, x, lengths = workload(1234)
+    threads = os.cpu_count() or 1
+    n_utts = 2
+    for _ in range(args.warmup):
+        oracle_sample(w, x, lengths, n_utts, threads)
+    times, frames = [], 0
+    for _ in range(args.steps):
+        fr, dt = oracle_sample(w, x, lengths, n_utts, threads)
+        times.append(dt)
+        frames = fr
+    total = sum(times)
+    value = frames * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "frames/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (f32 math, bf16 rounding)",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "sample_utterances": n_utts},
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "port",
+                         "sample": f"{n_utts} of the 16 utterances per step (valid frames "
+                                   f"{frames}), CPU restatement of the reference algorithm "
+                                   f"(ORC_REFERENCE_ALGO), host CPU: {cpu_model()}"},
+        "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference (Rust + MLX Metal/Accelerate, macOS only) cannot be built or "
+                "run here; this arm times its algorithm restated in C (oracle/)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    w, x, lengths = workload(1234 + rank)
+    attn = nrp.RelPositionMultiHeadAttention(D, H, True, ctx=ctx)
+    attn.set_linear(nrp.LINEAR_Q, nrp.LinearLayer.standard(w["wq"], w["bq"]))
+    attn.set_linear(nrp.LINEAR_K, nrp.LinearLayer.standard(w["wk"], w["bk"]))
+    attn.set_linear(nrp.LINEAR_V, nrp.LinearLayer.standard(w["wv"], w["bv"]))
+    attn.set_linear(nrp.LINEAR_OUT, nrp.LinearLayer.standard(w["wo"], w["bo"]))
+    attn.set_linear(nrp.LINEAR_POS, nrp.LinearLayer.standard(w["wp"], None))
+    attn.set_pos_bias(w["pos_bias_u"], w["pos_bias_v"])
+    attn.set_dtype(nrp.BF16)
+    pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
+    pe.set_dtype(nrp.BF16)
+    pos = pe.get_encoding(T)
+    dev = torch.device("cuda", local)
+    xd = torch.from_numpy(x).to(dev, torch.bfloat16)
+    out = torch.empty_like(xd)
+    mask = nrp.key_padding_mask(lengths, T)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(o=out, xin=xd):
+        attn.forward(xin, pos, None, mask, out=o)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    ctx.check()
+
+    # ---- device-timed region: inputs resident in HBM, L2 flushed between steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            step()
+            ends[k].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ctx.check()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    frames = int(lengths.sum())
+    value = world * frames * args.steps / (total_ms / 1e3)
+
+    # ---- per-kernel device times (CUDA events around each launch), same steps
+    ctx.profile(True)
+    ctx.profile_reset()
+    for k in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    launches = sum(n for n, _ in prof.values())
+
+    # ---- end to end through the public API with host buffers
+    x_host = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    len_host = torch.from_numpy(lengths.copy()).pin_memory()
+    x_dev2 = torch.empty_like(xd)
+    e_s = torch.cuda.Event(enable_timing=True)
+    e_e = torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        x_dev2.copy_(x_host, non_blocking=True)
+        mask.lengths.copy_(len_host, non_blocking=True)
+        step(out, x_dev2)
+        out_host.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e_s.record(stream)
+    for _ in range(args.steps):
+        x_dev2.copy_(x_host, non_blocking=True)
+        mask.lengths.copy_(len_host, non_blocking=True)
+        step(out, x_dev2)
+        out_host.copy_(out, non_blocking=True)
+    e_e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e_s.elapsed_time(e_e)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
+    h2d = x_host.numel() * 2 + len_host.numel() * 4
+    d2h = out_host.numel() * 2
+
+    # ---- roofline of the dominant kernel
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    tflops_peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "measured (bf16_tflops_sustained, MEASURED_PEAKS.json)"
+    if not tflops_peak:
+        tflops_peak, peak_src = 1400.0, "fallback 1.4 PFLOP/s sustained"
+    proj, pos_f, attn_f = algorithmic_flops(lengths)
+    per_kind_flops = {"gemm_bf16": proj + pos_f, "attn_sm100": attn_f}
+    kern = {}
+    for name, (n, ms) in prof.items():
+        kern[name] = {"launches": n, "ms_total": ms, "share": ms / max(sum(m for _, m in prof.values()), 1e-9)}
+    dominant = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
+    roof = None
+    if dominant in per_kind_flops:
+        n, ms = prof[dominant]
+        flop_per_launch = per_kind_flops[dominant] * args.steps / n
+        achieved = flop_per_launch / (ms / n / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": tflops_peak,
+                "unit": "TFLOP/s", "frac": achieved / tflops_peak, "traffic": None,
+                "peak_source": peak_src,
+                "algorithmic_flop_per_launch": flop_per_launch}
+    attn_roof = None
+    if "attn_sm100" in prof:
+        n, ms = prof["attn_sm100"]
+        a = attn_f * args.steps / n / (ms / n / 1e3) / 1e12
+        attn_roof = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s"}
+    gemm_roof = None
+    if "gemm_bf16" in prof:
+        n, ms = prof["gemm_bf16"]
+        g = (proj + pos_f) * args.steps / (ms / 1e3) / 1e12
+        gemm_roof = {"achieved": g, "frac": g / tflops_peak, "unit": "TFLOP/s"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        oracle_sample(w, x, lengths, 1, threads)  # warm-up
+        runs = [oracle_sample(w, x, lengths, 2, threads) for _ in range(3)]
+        fr = runs[0][0]
+        med = statistics.median(r[1] for r in runs)
+        cpu = {"value": fr / med, "unit": "frames/s", "cores": threads, "kind": "port",
+               "sample": f"2 of 16 utterances ({fr} valid frames), median of 3 after a warm-up; "
+                         f"CPU restatement of the reference algorithm (ORC_REFERENCE_ALGO, bf16 "
+                         f"rounding), host CPU: {cpu_model()}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "seq_len": T, "d_model": D,
+                       "heads": H, "valid_frames_per_gpu": frames,
+                       "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                       "parallelism": f"utterance-parallel replicas x{world}"},
+            "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "roofline_kernels": {"attn_sm100": attn_roof, "gemm_bf16": gemm_roof},
+            "kernels": kern,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,248 @@
+/*
+ * nemo_relpos.h -- C ABI of libnemo_relpos.so, a B200 (sm_100a)
+ * implementation of the FastConformer encoder's relative-position
+ * multi-head self-attention of animaslabs/mlx-nemo-rs (crate mlx-voice).
+ *
+ * The ABI replaces the reference's `internals` attention-module API and its
+ * streaming-cache structs; each declaration names the reference item
+ * (file:line, paths relative to the reference project root) it stands in
+ * for.  Conventions:
+ *   - every function returns an int status: NRP_OK (0) or a negative
+ *     NRP_ERR_* code; nrp_last_error() gives this thread's last message;
+ *   - tensors are row-major; "device" pointers are caller-owned CUDA memory
+ *     on the context's device; "host" pointers are read during the call;
+ *   - device work is queued on the caller's cudaStream_t (passed as void*,
+ *     NULL = legacy default stream) with no hidden device synchronisation;
+ *   - a handle is used by one host thread at a time (the reference's
+ *     `&mut self` methods); one device per context.
+ */
+#ifndef NEMO_RELPOS_H
+#define NEMO_RELPOS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NRP_ABI_VERSION 1
+
+/* Status codes (the reference's core::error::Error kinds, src/core/error.rs:7-60). */
+#define NRP_OK 0
+#define NRP_ERR_INVALID -1     /* bad argument or shape (Error::Model / ShapeMismatch) */
+#define NRP_ERR_CUDA -2        /* CUDA runtime/driver error (Error::Mlx's role) */
+#define NRP_ERR_UNSUPPORTED -3 /* configuration not implemented (Error::NotImplemented) */
+#define NRP_ERR_NOMEM -4       /* device allocation failed */
+#define NRP_ERR_DEVICE -5      /* a kernel reported a bounded wait that expired */
+
+typedef enum { NRP_DTYPE_F32 = 0, NRP_DTYPE_BF16 = 1 } nrp_dtype;
+
+/* Which projection of RelPositionMultiHeadAttention (attention.rs:333-342). */
+typedef enum {
+  NRP_LINEAR_Q = 0,
+  NRP_LINEAR_K = 1,
+  NRP_LINEAR_V = 2,
+  NRP_LINEAR_OUT = 3,
+  NRP_LINEAR_POS = 4
+} nrp_linear_id;
+
+/* AttentionContext (attention.rs:210-216): left/right frames, chunked = the
+ * "chunked_limited" style. */
+typedef struct {
+  int32_t left;
+  int32_t right;
+  int32_t chunked;
+} nrp_att_context;
+
+/* StreamingConfig (src/asr/streaming/core.rs:27-67). */
+typedef struct {
+  int32_t chunk_size[2];
+  int32_t shift_size[2];
+  int32_t cache_drop_size;
+  int32_t last_channel_cache_size;
+  int32_t last_time_cache_size;
+  int32_t valid_out_len;
+  int32_t pre_encode_cache_size[2];
+  int32_t drop_extra_pre_encoded;
+  int32_t lookahead_frames;
+  int32_t mode_idx;
+  int32_t left_context;
+  int32_t right_context;
+} nrp_streaming_config;
+
+typedef struct nrp_context nrp_context;
+typedef struct nrp_attn nrp_attn;
+typedef struct nrp_cache nrp_cache;
+
+/* ------------------------------------------------------------- library */
+int nrp_abi_version(void);
+/* Message of this thread's last failed call ("" if none). */
+const char* nrp_last_error(void);
+
+/* ------------------------------------------- host-side logic (no device) */
+
+/* RelPositionalEncoding::get_encoding (attention.rs:131-177) of a table
+ * built by RelPositionalEncoding::new(d_model, max_len, _)
+ * (attention.rs:35-51, create_pe 59-103): writes [2*seq_len-1, d_model] f32
+ * for positions (seq_len-1)..-(seq_len-1).  seq_len == 0 is an error
+ * (132-136); seq_len > max_len rebuilds the table at seq_len (137-145). */
+int nrp_pe_encoding_host(int d_model, int max_len, int seq_len, float* out);
+
+/* RelPositionalEncoding::xscale (attention.rs:36-40, 186-188). */
+float nrp_pe_xscale(int d_model, int xscaling);
+
+/* AttentionContext::new (attention.rs:220-227): writes *out and returns 1
+ * ("Some"), or returns 0 ("None") when left < 0 and right < 0.  style is
+ * "regular" or "chunked_limited". */
+int nrp_att_context_new(int left, int right, const char* style, nrp_att_context* out);
+
+/* AttentionContext::block_mask (attention.rs:232-272) as visibility bytes
+ * vis[(i-start)*seq_len + j] (1 = visible). */
+int nrp_block_mask_host(const nrp_att_context* context, int start, int end, int seq_len,
+                        uint8_t* vis);
+
+/* key_padding_mask (attention.rs:280-294): returns 0 ("None") when no frame
+ * is padding, else 1 and, when mask != NULL, writes the additive mask
+ * [batch, seq_len] (0 or -inf; each row keeps max(len,1) keys). */
+int nrp_key_padding_mask_host(const int32_t* lengths, int batch, int seq_len, float* mask);
+
+/* create_attention_mask (src/asr/modules/encoders/conformer.rs:97-221):
+ * vis [tensor_seq_len, max_audio_length] for the query rows of the current
+ * chunk.  context == NULL means no att_context_size. */
+int nrp_streaming_mask_host(const nrp_att_context* context, int max_audio_length, int cache_len,
+                            int filled_cache_len, int tensor_seq_len, int valid_seq_len,
+                            uint8_t* vis);
+
+/* compute_streaming_config (src/asr/streaming/core.rs:247-362) for one
+ * mode's (left, right) context. */
+int nrp_streaming_config_compute(int left, int right, int chunked, int n_layers,
+                                 int subsampling_factor, int conv_kernel_size, int causal_conv,
+                                 int mode_idx, int max_context, nrp_streaming_config* out);
+
+/* ------------------------------------------------------------- context */
+/* One CUDA device; owns the device error word kernels report into. */
+int nrp_context_create(int device, nrp_context** out);
+int nrp_context_destroy(nrp_context* ctx);
+/* Synchronises `stream`, then reads and clears the device error word:
+ * NRP_ERR_DEVICE if a kernel gave up on a bounded wait since the last check. */
+int nrp_context_check(nrp_context* ctx, void* stream);
+
+/* get_encoding on the device in the given dtype (f32 table cast like
+ * RelPositionalEncoding::set_dtype, attention.rs:180-183): dev_out
+ * [2*seq_len-1, d_model]. */
+int nrp_pe_encoding(nrp_context* ctx, int d_model, int max_len, int seq_len, int dtype,
+                    void* dev_out, void* stream);
+
+/* ------------------------------------------------------ attention module */
+/* RelPositionMultiHeadAttention::new (attention.rs:367-406): zero
+ * parameters, dtype f32.  head_dim = d_model / n_heads. */
+int nrp_attn_create(nrp_context* ctx, int d_model, int n_heads, int use_bias, nrp_attn** out);
+int nrp_attn_destroy(nrp_attn* attn);
+
+/* RelPositionMultiHeadAttention::set_dtype (attention.rs:409-423) with
+ * LinearLayer::cast (src/core/quantization.rs:92-114): weights, biases,
+ * quantisation scales/biases and pos_bias_u/v are rounded to dtype; clears
+ * the cached streaming positions. */
+int nrp_attn_set_dtype(nrp_attn* attn, int dtype);
+
+/* The pub field cache_drop_size (attention.rs:349-350), set by
+ * ConformerEncoder::setup_streaming (conformer.rs:812-817). */
+int nrp_attn_set_cache_drop_size(nrp_attn* attn, int cache_drop_size);
+
+/* load_weights for one projection, Standard arm (attention.rs:863-880 via
+ * Weights::fetch_linear, src/core/loading.rs:151-158, and load_linear_layer,
+ * quantization.rs:327-345): weight host f32 [d_model, d_model] ([out, in]),
+ * bias host f32 [d_model] or NULL (linear_pos has none). */
+int nrp_attn_load_linear(nrp_attn* attn, int which, const float* weight, const float* bias);
+
+/* Quantized arm (load_linear_layer, quantization.rs:299-326; MLX layout
+ * doc 4-8): wq host u32 [d_model, d_model*bits/32], scales/biases host f32
+ * [d_model, d_model/group_size] (the file's F16 values widened), bias host
+ * f32 [d_model] or NULL.  Supported: bits 8, group_size 64. */
+int nrp_attn_load_linear_quantized(nrp_attn* attn, int which, int bits, int group_size,
+                                   const uint32_t* wq, const float* scales, const float* biases,
+                                   const float* bias);
+
+/* pos_bias_u / pos_bias_v (attention.rs:882-890): host f32 [n_heads, head_dim]. */
+int nrp_attn_load_pos_bias(nrp_attn* attn, const float* pos_bias_u, const float* pos_bias_v);
+
+/* RelPositionMultiHeadAttention::forward (attention.rs:446-573):
+ * x device [batch, seq_len, d_model] in the module dtype; pos_emb device
+ * [2*seq_len-1, d_model] (module dtype); lengths device int32 [batch] or
+ * NULL -- the key_padding_mask of attention.rs:280-294 (keys >= max(len,1)
+ * hidden; pass NULL when no frame is padding); context NULL for full
+ * attention; out device [batch, seq_len, d_model].  Query rows past a
+ * sequence's length are unspecified (conformer.rs:1590-1593); this
+ * implementation writes finite values there.  bf16 needs head_dim 128. */
+int nrp_attn_forward(nrp_attn* attn, void* stream, const void* x, int batch, int seq_len,
+                     const void* pos_emb, const int32_t* lengths,
+                     const nrp_att_context* context, void* out);
+
+/* ---------------------------------------------------- streaming caches */
+/* One layer's share of EncoderCache (src/asr/streaming/core.rs:117-127):
+ * the attention-input cache last_channel[layer] ([batch, cache_len,
+ * d_model], f32, zero-initialised) kept as a ring, plus device K/V rings of
+ * its projections so cached frames are not re-projected every chunk. */
+int nrp_cache_create(nrp_attn* attn, int batch, int cache_len, nrp_cache** out);
+int nrp_cache_destroy(nrp_cache* cache);
+/* Zero the cache (EncoderCache::new state). */
+int nrp_cache_reset(nrp_cache* cache, void* stream);
+/* Copy in / out the cache in EncoderCache.last_channel order (oldest frame
+ * first): device f32 [batch, cache_len, d_model].  Import re-projects K/V
+ * with the module's current weights. */
+int nrp_cache_import_h(nrp_cache* cache, const float* h, void* stream);
+int nrp_cache_export_h(nrp_cache* cache, float* h, void* stream);
+
+/* RelPositionMultiHeadAttention::forward_with_cache (attention.rs:606-816)
+ * as ConformerEncoder::forward_streaming drives it per layer
+ * (conformer.rs:883-1000): x device [batch, seq_len, d_model]; pos_emb
+ * device [2*(cache_len+seq_len)-1, d_model] (projected once per length and
+ * reused, 749-761); filled = the first stream's fill level (clamped to
+ * [0, cache_len]), valid = its valid frame count; context NULL = no
+ * att_context_size.  The attention mask is create_attention_mask's
+ * (conformer.rs:97-221); rows with no visible key give 0 (781-790).  The
+ * cache then slides by seq_len - cache_drop_size frames (661-684, 983-1000). */
+int nrp_attn_forward_with_cache(nrp_attn* attn, void* stream, const void* x, int batch,
+                                int seq_len, const void* pos_emb, nrp_cache* cache, int filled,
+                                int valid, const nrp_att_context* context, void* out);
+
+/* --------------------------------------------------- linear primitives */
+/* LinearLayer::forward, Standard arm (quantization.rs:128-135) on device
+ * buffers: y[M,N] = x[M,K] . w[N,K]^T (+ bias[N]), dtype f32 or bf16 for
+ * every operand.  bf16 needs K % 64 == 0 and N % 32 == 0. */
+int nrp_linear(nrp_context* ctx, void* stream, int dtype, const void* x, int M, int K,
+               const void* w, int N, const void* bias, void* y);
+
+/* LinearLayer::forward, Quantized arm (quantization.rs:137-160):
+ * y[M,N] = x[M,K] . dequant(wq, scales, biases)^T (+ bias), MLX affine
+ * 8-bit, group 64; x, scales, biases, bias, y bf16 on the device; wq device
+ * u32 [N, K/4].  M <= 16 runs the HBM-bound GEMV, larger M the tcgen05
+ * GEMM with in-register dequantisation. */
+int nrp_qlinear(nrp_context* ctx, void* stream, const void* x, int M, int K, const uint32_t* wq,
+                const void* scales, const void* biases, int N, int group_size, int bits,
+                const void* bias, void* y);
+
+/* ------------------------------------------------------------ profiling */
+/* Per-kernel device time from CUDA events the library records on the
+ * launching stream around each launch while enabled (the reference has no
+ * profiler integration; its timing is end to end, examples/eval.rs:158-215). */
+typedef enum {
+  NRP_KERNEL_GEMM_BF16 = 0,   /* tcgen05 projection GEMM */
+  NRP_KERNEL_GEMM_Q8 = 1,     /* tcgen05 GEMM, 8-bit weights dequantised in smem */
+  NRP_KERNEL_QGEMV = 2,       /* small-M 8-bit GEMV */
+  NRP_KERNEL_GEMM_F32 = 3,    /* f32 CUDA-core GEMM */
+  NRP_KERNEL_ATTN_SM100 = 4,  /* fused offline rel-pos attention, tcgen05 */
+  NRP_KERNEL_ATTN_SIMT = 5,   /* f32 offline attention, CUDA cores */
+  NRP_KERNEL_ATTN_STREAM = 6, /* streaming attention against the ring cache */
+  NRP_KERNEL_RING_APPEND = 7, /* streaming cache slide */
+  NRP_KERNEL_KINDS = 8
+} nrp_kernel_kind;
+int nrp_profile_enable(nrp_context* ctx, int enable);
+int nrp_profile_reset(nrp_context* ctx);
+/* Synchronises on the recorded events; writes launches and total ms of `kind`. */
+int nrp_profile_read(nrp_context* ctx, int kind, int64_t* launches, double* total_ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

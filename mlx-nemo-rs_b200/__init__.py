@@ -1,0 +1,609 @@
+"""B200 rel-pos MHA for FastConformer -- Python mirror of the reference API.
+
+A thin ctypes layer over libnemo_relpos.so (include/nemo_relpos.h) whose
+names, argument meanings and errors follow the `internals` API of
+animaslabs/mlx-nemo-rs that the library replaces:
+
+    src/asr/modules/encoders/attention.rs  RelPositionalEncoding,
+        AttentionContext, key_padding_mask, RelPositionMultiHeadAttention
+    src/core/quantization.rs               QuantizationConfig, LinearLayer
+    src/asr/streaming/core.rs              EncoderCache, StreamingConfig,
+        compute_streaming_config, StreamingModeInfo
+
+Tensors are torch CUDA tensors (torch is the device-memory and stream
+plumbing; every computation runs in the library's kernels).  There is no
+CPU fallback: without the built library or a B200 the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnemo_relpos.so")
+
+NRP_OK = 0
+NRP_ERR_INVALID = -1
+NRP_ERR_CUDA = -2
+NRP_ERR_UNSUPPORTED = -3
+NRP_ERR_NOMEM = -4
+NRP_ERR_DEVICE = -5
+
+F32 = 0
+BF16 = 1
+LINEAR_Q, LINEAR_K, LINEAR_V, LINEAR_OUT, LINEAR_POS = range(5)
+_LINEAR_NAMES = ("linear_q", "linear_k", "linear_v", "linear_out", "linear_pos")
+
+MAX_SCORE_ELEMENTS = 1 << 26  # attention.rs:198 (no blocking is needed here)
+
+
+class NrpError(RuntimeError):
+    """Error from the library; `code` is the NRP_ERR_* status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class _AttCtx(C.Structure):
+    _fields_ = [("left", C.c_int32), ("right", C.c_int32), ("chunked", C.c_int32)]
+
+
+class _StreamCfg(C.Structure):
+    _fields_ = [("chunk_size", C.c_int32 * 2), ("shift_size", C.c_int32 * 2),
+                ("cache_drop_size", C.c_int32), ("last_channel_cache_size", C.c_int32),
+                ("last_time_cache_size", C.c_int32), ("valid_out_len", C.c_int32),
+                ("pre_encode_cache_size", C.c_int32 * 2), ("drop_extra_pre_encoded", C.c_int32),
+                ("lookahead_frames", C.c_int32), ("mode_idx", C.c_int32),
+                ("left_context", C.c_int32), ("right_context", C.c_int32)]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded C library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise NrpError(NRP_ERR_UNSUPPORTED,
+                           f"{LIB_PATH} is missing: run python mlx-nemo-rs_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        vp, i, f = C.c_void_p, C.c_int, C.c_float
+        sig = {
+            "nrp_abi_version": ([], i),
+            "nrp_last_error": ([], C.c_char_p),
+            "nrp_pe_encoding_host": ([i, i, i, vp], i),
+            "nrp_pe_xscale": ([i, i], f),
+            "nrp_att_context_new": ([i, i, C.c_char_p, vp], i),
+            "nrp_block_mask_host": ([vp, i, i, i, vp], i),
+            "nrp_key_padding_mask_host": ([vp, i, i, vp], i),
+            "nrp_streaming_mask_host": ([vp, i, i, i, i, i, vp], i),
+            "nrp_streaming_config_compute": ([i] * 9 + [vp], i),
+            "nrp_context_create": ([i, vp], i),
+            "nrp_context_destroy": ([vp], i),
+            "nrp_context_check": ([vp, vp], i),
+            "nrp_pe_encoding": ([vp, i, i, i, i, vp, vp], i),
+            "nrp_attn_create": ([vp, i, i, i, vp], i),
+            "nrp_attn_destroy": ([vp], i),
+            "nrp_attn_set_dtype": ([vp, i], i),
+            "nrp_attn_set_cache_drop_size": ([vp, i], i),
+            "nrp_attn_load_linear": ([vp, i, vp, vp], i),
+            "nrp_attn_load_linear_quantized": ([vp, i, i, i, vp, vp, vp, vp], i),
+            "nrp_attn_load_pos_bias": ([vp, vp, vp], i),
+            "nrp_attn_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
+            "nrp_cache_create": ([vp, i, i, vp], i),
+            "nrp_cache_destroy": ([vp], i),
+            "nrp_cache_reset": ([vp, vp], i),
+            "nrp_cache_import_h": ([vp, vp, vp], i),
+            "nrp_cache_export_h": ([vp, vp, vp], i),
+            "nrp_attn_forward_with_cache": ([vp, vp, vp, i, i, vp, vp, i, i, vp, vp], i),
+            "nrp_linear": ([vp, vp, i, vp, i, i, vp, i, vp, vp], i),
+            "nrp_qlinear": ([vp, vp, vp, i, i, vp, vp, vp, i, i, i, vp, vp], i),
+            "nrp_profile_enable": ([vp, i], i),
+            "nrp_profile_reset": ([vp], i),
+            "nrp_profile_read": ([vp, i, vp, vp], i),
+        }
+        for name, (args, res) in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc < 0:
+        raise NrpError(rc, lib().nrp_last_error().decode())
+    return rc
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _np_f32(a) -> np.ndarray:
+    if hasattr(a, "detach"):
+        a = a.detach().float().cpu().numpy()
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _torch_dtype(dtype: int):
+    import torch
+    return torch.bfloat16 if dtype == BF16 else torch.float32
+
+
+# ----------------------------------------------------------------- context
+class Context:
+    """One CUDA device (nrp_context)."""
+
+    _default: Dict[int, "Context"] = {}
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().nrp_context_create(device, C.byref(h)))
+        self.handle = h
+        self.device = device
+
+    @classmethod
+    def default(cls, device: int = 0) -> "Context":
+        if device not in cls._default:
+            cls._default[device] = Context(device)
+        return cls._default[device]
+
+    def check(self, stream=None):
+        """Synchronise and raise NrpError(NRP_ERR_DEVICE) if a kernel gave up
+        on a bounded wait."""
+        _check(lib().nrp_context_check(self.handle, stream if stream is not None else _stream()))
+
+    KERNELS = ("gemm_bf16", "gemm_q8", "qgemv", "gemm_f32", "attn_sm100", "attn_simt",
+               "attn_stream", "ring_append")
+
+    def profile(self, enable: bool = True):
+        _check(lib().nrp_profile_enable(self.handle, int(enable)))
+
+    def profile_reset(self):
+        _check(lib().nrp_profile_reset(self.handle))
+
+    def profile_read(self) -> Dict[str, Tuple[int, float]]:
+        """{kernel: (launches, total ms)} for kernels that ran."""
+        res = {}
+        for k, name in enumerate(self.KERNELS):
+            n = C.c_int64()
+            ms = C.c_double()
+            _check(lib().nrp_profile_read(self.handle, k, C.byref(n), C.byref(ms)))
+            if n.value:
+                res[name] = (n.value, ms.value)
+        return res
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().nrp_context_destroy(self.handle)
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------- positional encoding
+class RelPositionalEncoding:
+    """attention.rs:19-194.  get_encoding returns a device tensor
+    [1, 2*seq_len-1, d_model] in the table's dtype."""
+
+    def __init__(self, d_model: int, max_len: int, xscaling: bool, device: int = 0):
+        self._d_model = d_model
+        self.max_len = max_len
+        self._xscale = float(lib().nrp_pe_xscale(d_model, int(bool(xscaling))))
+        self.dtype = F32
+        self.device = device
+
+    def xscale(self) -> float:
+        return self._xscale
+
+    def d_model(self) -> int:
+        return self._d_model
+
+    def set_dtype(self, dtype: int):
+        self.dtype = dtype
+
+    def get_encoding_host(self, seq_len: int) -> np.ndarray:
+        out = np.empty((2 * max(seq_len, 1) - 1, self._d_model), np.float32)
+        _check(lib().nrp_pe_encoding_host(self._d_model, self.max_len, seq_len,
+                                          out.ctypes.data))
+        return out[None]
+
+    def get_encoding(self, seq_len: int):
+        import torch
+        if seq_len <= 0:
+            _check(lib().nrp_pe_encoding_host(self._d_model, self.max_len, seq_len, None))
+        out = torch.empty((1, 2 * seq_len - 1, self._d_model), dtype=_torch_dtype(self.dtype),
+                          device=f"cuda:{self.device}")
+        _check(lib().nrp_pe_encoding(Context.default(self.device).handle, self._d_model,
+                                     self.max_len, seq_len, self.dtype, out.data_ptr(),
+                                     _stream()))
+        return out
+
+
+# ------------------------------------------------------------------ masks
+@dataclass(frozen=True)
+class AttentionContext:
+    """attention.rs:210-273."""
+    left: int
+    right: int
+    chunked: bool
+
+    @staticmethod
+    def new(size: Tuple[int, int], style: str) -> Optional["AttentionContext"]:
+        c = _AttCtx()
+        some = _check(lib().nrp_att_context_new(int(size[0]), int(size[1]), style.encode(),
+                                                C.byref(c)))
+        return AttentionContext(c.left, c.right, bool(c.chunked)) if some else None
+
+    def _c(self) -> _AttCtx:
+        return _AttCtx(self.left, self.right, int(self.chunked))
+
+    def block_mask(self, start: int, end: int, seq_len: int) -> np.ndarray:
+        vis = np.empty((end - start, seq_len), np.uint8)
+        c = self._c()
+        _check(lib().nrp_block_mask_host(C.byref(c), start, end, seq_len, vis.ctypes.data))
+        return vis.astype(bool)
+
+
+class KeyPaddingMask:
+    """key_padding_mask's value (attention.rs:280-294), kept as the device
+    lengths the kernels read; `additive()` is the reference's [B,1,1,T] form."""
+
+    def __init__(self, lengths, seq_len: int):
+        import torch
+        self.seq_len = seq_len
+        self.lengths = torch.as_tensor(np.asarray(lengths, np.int32)).cuda()
+        self._host = np.asarray(lengths, np.int32)
+
+    def additive(self) -> np.ndarray:
+        m = np.empty((len(self._host), self.seq_len), np.float32)
+        _check(lib().nrp_key_padding_mask_host(self._host.ctypes.data, len(self._host),
+                                               self.seq_len, m.ctypes.data))
+        return m[:, None, None, :]
+
+
+def key_padding_mask(lengths, seq_len: int) -> Optional[KeyPaddingMask]:
+    h = np.ascontiguousarray(lengths, np.int32)
+    some = _check(lib().nrp_key_padding_mask_host(h.ctypes.data, len(h), seq_len, None))
+    return KeyPaddingMask(h, seq_len) if some else None
+
+
+def create_attention_mask(att_context_size, att_context_style, max_audio_length, cache_len,
+                          filled_cache_len, tensor_seq_len, valid_seq_len) -> np.ndarray:
+    """conformer.rs:97-221 (visibility, [tensor_seq_len, max_audio_length])."""
+    vis = np.empty((tensor_seq_len, max_audio_length), np.uint8)
+    ctx = None
+    if att_context_size is not None:
+        ctx = _AttCtx(att_context_size[0], att_context_size[1],
+                      int(att_context_style == "chunked_limited"))
+    _check(lib().nrp_streaming_mask_host(C.byref(ctx) if ctx is not None else None,
+                                         max_audio_length, cache_len, filled_cache_len,
+                                         tensor_seq_len, valid_seq_len, vis.ctypes.data))
+    return vis.astype(bool)
+
+
+# ------------------------------------------------------------ quantization
+@dataclass
+class QuantizationConfig:
+    """quantization.rs:20-32."""
+    bits: int = 8
+    group_size: int = 64
+
+
+class LinearLayer:
+    """quantization.rs:36-163: Standard {weight, bias} or Quantized {weight
+    (u32 packed), scales, biases, bias, bits, group_size}; host arrays."""
+
+    def __init__(self, weight, bias=None, scales=None, biases=None, bits=8, group_size=64):
+        self.weight = weight
+        self.bias = bias
+        self.scales = scales
+        self.biases = biases
+        self.bits = bits
+        self.group_size = group_size
+
+    @staticmethod
+    def standard(weight, bias=None) -> "LinearLayer":
+        return LinearLayer(weight, bias)
+
+    @staticmethod
+    def quantized(weight, scales, biases, bias, bits, group_size) -> "LinearLayer":
+        return LinearLayer(weight, bias, scales, biases, bits, group_size)
+
+    def is_quantized(self) -> bool:
+        return self.scales is not None
+
+
+def load_linear_layer(weights: Dict[str, object], prefix: str,
+                      quant: Optional[QuantizationConfig]) -> Optional[LinearLayer]:
+    """quantization.rs:289-349: `.scales` + `.biases` mean quantized,
+    default (8, 64); 3-D pointwise weights [O,1,I] are squeezed."""
+    w = weights.get(f"{prefix}.weight")
+    s = weights.get(f"{prefix}.scales")
+    b = weights.get(f"{prefix}.biases")
+    bias = weights.get(f"{prefix}.bias")
+    if w is not None and s is not None and b is not None:
+        bits, gs = (quant.bits, quant.group_size) if quant else (8, 64)
+        return LinearLayer.quantized(w, s, b, bias, bits, gs)
+    if w is not None:
+        w = np.asarray(w.detach().cpu() if hasattr(w, "detach") else w)
+        if w.ndim == 3 and w.shape[1] == 1:
+            w = w[:, 0, :]
+        return LinearLayer.standard(w, bias)
+    return None
+
+
+# ------------------------------------------------------- the attention
+class RelPositionMultiHeadAttention:
+    """attention.rs:328-894 on the B200 kernels."""
+
+    def __init__(self, d_model: int, n_heads: int, use_bias: bool = True,
+                 ctx: Optional[Context] = None):
+        self.ctx = ctx or Context.default()
+        h = C.c_void_p()
+        _check(lib().nrp_attn_create(self.ctx.handle, d_model, n_heads, int(bool(use_bias)),
+                                     C.byref(h)))
+        self.handle = h
+        self.d_model = d_model
+        self._n_heads = n_heads
+        self.dtype = F32
+        self._cache_drop_size = 0
+        self.att_context_size: Optional[Tuple[int, int]] = None
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().nrp_attn_destroy(self.handle)
+        except Exception:
+            pass
+
+    def head_dim(self) -> int:
+        return self.d_model // self._n_heads
+
+    def n_heads(self) -> int:
+        return self._n_heads
+
+    @property
+    def cache_drop_size(self) -> int:
+        return self._cache_drop_size
+
+    @cache_drop_size.setter
+    def cache_drop_size(self, n: int):
+        _check(lib().nrp_attn_set_cache_drop_size(self.handle, int(n)))
+        self._cache_drop_size = int(n)
+
+    def set_dtype(self, dtype: int):
+        _check(lib().nrp_attn_set_dtype(self.handle, dtype))
+        self.dtype = dtype
+
+    def set_linear(self, which: int, layer: LinearLayer):
+        if layer.is_quantized():
+            wq = np.ascontiguousarray(np.asarray(layer.weight), np.uint32)
+            s = _np_f32(layer.scales)
+            b = _np_f32(layer.biases)
+            bias = _np_f32(layer.bias) if layer.bias is not None else None
+            _check(lib().nrp_attn_load_linear_quantized(
+                self.handle, which, layer.bits, layer.group_size, wq.ctypes.data,
+                s.ctypes.data, b.ctypes.data, bias.ctypes.data if bias is not None else None))
+        else:
+            w = _np_f32(layer.weight)
+            bias = _np_f32(layer.bias) if layer.bias is not None else None
+            _check(lib().nrp_attn_load_linear(self.handle, which, w.ctypes.data,
+                                              bias.ctypes.data if bias is not None else None))
+
+    def set_pos_bias(self, u, v):
+        u = _np_f32(u)
+        v = _np_f32(v)
+        _check(lib().nrp_attn_load_pos_bias(self.handle, u.ctypes.data, v.ctypes.data))
+
+    def load_weights(self, weights: Dict[str, object], prefix: str,
+                     quant: Optional[QuantizationConfig] = None):
+        """attention.rs:863-893."""
+        for which, name in enumerate(_LINEAR_NAMES):
+            layer = load_linear_layer(weights, f"{prefix}.{name}", quant)
+            if layer is not None:
+                self.set_linear(which, layer)
+        u = weights.get(f"{prefix}.pos_bias_u")
+        v = weights.get(f"{prefix}.pos_bias_v")
+        if u is not None or v is not None:
+            n = self.d_model
+            cur_u = _np_f32(u) if u is not None else np.zeros(n, np.float32)
+            cur_v = _np_f32(v) if v is not None else np.zeros(n, np.float32)
+            self.set_pos_bias(cur_u, cur_v)
+
+    def forward(self, x, pos_emb, context: Optional[AttentionContext] = None,
+                key_mask: Optional[KeyPaddingMask] = None, out=None):
+        """attention.rs:446-454.  x [B,T,D], pos_emb [1 or none, 2T-1, D]."""
+        import torch
+        B, T, D = x.shape
+        pe = pos_emb.reshape(-1, D)
+        if out is None:
+            out = torch.empty_like(x)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_attn_forward(
+            self.handle, _stream(), x.data_ptr(), B, T, pe.data_ptr(),
+            key_mask.lengths.data_ptr() if key_mask is not None else None,
+            C.byref(c) if c is not None else None, out.data_ptr()))
+        return out
+
+    def forward_with_cache(self, x, pos_emb, cache: "AttentionCache", cache_filled_len: int,
+                           valid_len: Optional[int] = None,
+                           context: Optional[AttentionContext] = None, out=None):
+        """attention.rs:606-816 as driven per layer by
+        ConformerEncoder::forward_streaming (conformer.rs:883-1000).
+        Returns the output; `cache` slides in place."""
+        import torch
+        B, T, D = x.shape
+        pe = pos_emb.reshape(-1, D)
+        if out is None:
+            out = torch.empty_like(x)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_attn_forward_with_cache(
+            self.handle, _stream(), x.data_ptr(), B, T, pe.data_ptr(), cache.handle,
+            int(cache_filled_len), T if valid_len is None else int(valid_len),
+            C.byref(c) if c is not None else None, out.data_ptr()))
+        return out
+
+
+class AttentionCache:
+    """One layer's EncoderCache.last_channel (streaming/core.rs:117-127) as a
+    device ring with derived K/V rings."""
+
+    def __init__(self, attn: RelPositionMultiHeadAttention, batch: int, cache_len: int):
+        h = C.c_void_p()
+        _check(lib().nrp_cache_create(attn.handle, batch, cache_len, C.byref(h)))
+        self.handle = h
+        self.attn = attn
+        self.batch = batch
+        self.cache_len = cache_len
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().nrp_cache_destroy(self.handle)
+        except Exception:
+            pass
+
+    def reset(self):
+        _check(lib().nrp_cache_reset(self.handle, _stream()))
+
+    def export_h(self):
+        import torch
+        out = torch.empty((self.batch, self.cache_len, self.attn.d_model), dtype=torch.float32,
+                          device="cuda")
+        _check(lib().nrp_cache_export_h(self.handle, out.data_ptr(), _stream()))
+        return out
+
+    def import_h(self, h):
+        h = h.float().contiguous().cuda()
+        _check(lib().nrp_cache_import_h(self.handle, h.data_ptr(), _stream()))
+
+
+class EncoderCache:
+    """streaming/core.rs:117-187: dimensions of the three cache tensors and
+    the host fill level last_channel_len."""
+
+    def __init__(self, num_layers, batch_size, channel_cache_size, time_cache_size, d_model):
+        self._dims = (num_layers, batch_size, channel_cache_size, time_cache_size, d_model)
+        self.last_channel_len = np.zeros(batch_size, np.int64)
+
+    def batch_size(self):
+        return self._dims[1]
+
+    def num_layers(self):
+        return self._dims[0]
+
+    def channel_cache_size(self):
+        return self._dims[2]
+
+    def time_cache_size(self):
+        return self._dims[3]
+
+
+@dataclass
+class StreamingConfig:
+    """streaming/core.rs:27-108."""
+    chunk_size: Tuple[int, int]
+    shift_size: Tuple[int, int]
+    cache_drop_size: int
+    last_channel_cache_size: int
+    last_time_cache_size: int
+    valid_out_len: int
+    pre_encode_cache_size: Tuple[int, int]
+    drop_extra_pre_encoded: int
+    lookahead_frames: int
+    mode_idx: int
+    left_context: int
+    right_context: int
+
+    def chunk_size_for_step(self, is_first):
+        return self.chunk_size[0] if is_first else self.chunk_size[1]
+
+    def shift_size_for_step(self, is_first):
+        return self.shift_size[0] if is_first else self.shift_size[1]
+
+    def pre_encode_cache_for_step(self, is_first):
+        return self.pre_encode_cache_size[0] if is_first else self.pre_encode_cache_size[1]
+
+    def drop_extra_for_step(self, is_first):
+        return 0 if is_first else self.drop_extra_pre_encoded
+
+
+def compute_streaming_config(left: int, right: int, style: str, n_layers: int,
+                             subsampling_factor: int = 8, conv_kernel_size: int = 9,
+                             causal_conv: bool = True, mode_idx: int = 0,
+                             max_context: int = 10000) -> StreamingConfig:
+    """streaming/core.rs:247-362 for one (left, right) mode."""
+    c = _StreamCfg()
+    _check(lib().nrp_streaming_config_compute(left, right, int(style == "chunked_limited"),
+                                              n_layers, subsampling_factor, conv_kernel_size,
+                                              int(causal_conv), mode_idx, max_context,
+                                              C.byref(c)))
+    return StreamingConfig(tuple(c.chunk_size), tuple(c.shift_size), c.cache_drop_size,
+                           c.last_channel_cache_size, c.last_time_cache_size, c.valid_out_len,
+                           tuple(c.pre_encode_cache_size), c.drop_extra_pre_encoded,
+                           c.lookahead_frames, c.mode_idx, c.left_context, c.right_context)
+
+
+@dataclass
+class StreamingModeInfo:
+    """streaming/core.rs:190-243."""
+    mode_idx: int
+    left_context: int
+    right_context: int
+    latency_ms: float
+    description: str
+
+    @staticmethod
+    def from_context(mode_idx, left_context, right_context, frame_duration_ms):
+        latency = right_context * frame_duration_ms if right_context >= 0 else math.inf
+        if right_context == 0:
+            d = f"Zero lookahead (lowest latency), left={left_context}"
+        elif right_context < 0:
+            d = f"Unlimited lookahead, left={left_context}"
+        else:
+            d = f"Lookahead={right_context} frames (~{latency:.0f}ms), left={left_context}"
+        return StreamingModeInfo(mode_idx, left_context, right_context, latency, d)
+
+
+# ----------------------------------------------------- linear primitives
+def linear(x, w, bias=None, ctx: Optional[Context] = None, out=None):
+    """LinearLayer::forward Standard arm on device tensors (f32 or bf16)."""
+    import torch
+    ctx = ctx or Context.default()
+    M, K = x.reshape(-1, x.shape[-1]).shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((*x.shape[:-1], N), dtype=x.dtype, device=x.device)
+    dt = BF16 if x.dtype == torch.bfloat16 else F32
+    _check(lib().nrp_linear(ctx.handle, _stream(), dt, x.data_ptr(), M, K, w.data_ptr(), N,
+                            _ptr(bias), out.data_ptr()))
+    return out
+
+
+def qlinear(x, wq, scales, biases, bias=None, group_size=64, bits=8,
+            ctx: Optional[Context] = None, out=None):
+    """LinearLayer::forward Quantized arm (bf16 activations, u32 packed W)."""
+    import torch
+    ctx = ctx or Context.default()
+    M, K = x.reshape(-1, x.shape[-1]).shape
+    N = wq.shape[0]
+    if out is None:
+        out = torch.empty((*x.shape[:-1], N), dtype=torch.bfloat16, device=x.device)
+    _check(lib().nrp_qlinear(ctx.handle, _stream(), x.data_ptr(), M, K, wq.data_ptr(),
+                             scales.data_ptr(), biases.data_ptr(), N, group_size, bits,
+                             _ptr(bias), out.data_ptr()))
+    return out

@@ -1,0 +1,956 @@
+// api.cpp -- the C ABI of libnemo_relpos.so (declared in include/nemo_relpos.h).
+//
+// Host-side logic of the drop-in: parameter loading and dtype casts
+// (RelPositionMultiHeadAttention::{load_weights,set_dtype},
+// src/asr/modules/encoders/attention.rs:409-423, 863-893; LinearLayer::cast,
+// src/core/quantization.rs:92-114), the positional table
+// (attention.rs:59-177), masks (attention.rs:210-294,
+// src/asr/modules/encoders/conformer.rs:97-323), the streaming cache
+// bookkeeping (attention.rs:606-816, conformer.rs:883-1037) and
+// compute_streaming_config (src/asr/streaming/core.rs:247-362).  All
+// arithmetic on tensors runs in the CUDA kernels; nothing here computes on
+// the host what the device path computes.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/nemo_relpos.h"
+#include "gemm.h"
+
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int ok() { return NRP_OK; }
+
+#define CUDA_TRY(expr)                                                                    \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));        \
+  } while (0)
+
+uint16_t bf16_bits(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return static_cast<uint16_t>((u >> 16) | ((u & 0xffff) ? 0x40 : 0));
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+float bf16_round(float x) {
+  uint32_t u = static_cast<uint32_t>(bf16_bits(x)) << 16;
+  float y;
+  memcpy(&y, &u, 4);
+  return y;
+}
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  cudaError_t ensure(size_t n) {
+    if (n <= bytes && p) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&p, n ? n : 16);
+    if (e == cudaSuccess) bytes = n;
+    return e;
+  }
+  template <typename T>
+  T* as() const { return static_cast<T*>(p); }
+};
+
+struct Linear {
+  bool loaded = false;
+  bool quant = false;
+  int bits = 8, group = 64;
+  std::vector<float> w;        // f32 master [N, K] (standard)
+  std::vector<uint32_t> wq;    // packed [N, K*bits/32] (quantised)
+  std::vector<float> qs, qb;   // [N, K/group]
+  std::vector<float> bias;     // [N] or empty
+};
+
+}  // namespace
+
+// Optional per-launch timing: CUDA events recorded on the launching stream
+// around each kernel the library launches, summed per kernel kind.
+struct ProfRec {
+  int kind;
+  cudaEvent_t start, stop;
+};
+
+struct nrp_context {
+  int device = 0;
+  int num_sms = 148;
+  int* d_err = nullptr;
+  bool prof = false;
+  std::vector<ProfRec> recs;
+  std::vector<cudaEvent_t> pool;
+  double prof_ms[NRP_KERNEL_KINDS] = {};
+  int64_t prof_n[NRP_KERNEL_KINDS] = {};
+};
+
+struct nrp_attn {
+  nrp_context* ctx = nullptr;
+  int D = 0, H = 0, dh = 0;
+  int use_bias = 1;
+  int dtype = NRP_DTYPE_F32;
+  int cache_drop = 0;
+  Linear lin[5];
+  std::vector<float> u, v;
+  bool dirty = true;
+  // device parameters in the module dtype
+  bool qkv_quant = false;
+  DevBuf w_qkv, s_qkv, z_qkv, b_qkv;  // weights (or u8 codes), scales, zero-points, bias
+  bool has_b_qkv = false;
+  DevBuf w_out, s_out, z_out, b_out;
+  bool out_quant = false, has_b_out = false;
+  DevBuf w_pos, s_pos, z_pos;
+  bool pos_quant = false;
+  DevBuf u_dev, v_dev;
+  // workspace
+  DevBuf qkv, cbuf, pbuf;
+  // projected streaming positions, reused while pos_len is unchanged
+  int spos_len = -1;
+  DevBuf spos;
+};
+
+struct nrp_cache {
+  nrp_attn* attn = nullptr;
+  int B = 0, C = 0, D = 0, dtype = 0;
+  int head = 0;  // ring slot of the oldest frame
+  DevBuf kc, vc, hc;
+  DevBuf tmp;
+};
+
+namespace {
+
+cudaEvent_t take_event(nrp_context* c) {
+  if (!c->pool.empty()) {
+    cudaEvent_t e = c->pool.back();
+    c->pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Scope guard: records start/stop events around one launch when enabled.
+struct ProfScope {
+  nrp_context* c;
+  int kind;
+  cudaStream_t st;
+  cudaEvent_t a = nullptr;
+  ProfScope(nrp_context* c_, int kind_, cudaStream_t st_) : c(c_), kind(kind_), st(st_) {
+    if (c && c->prof) {
+      a = take_event(c);
+      cudaEventRecord(a, st);
+    }
+  }
+  ~ProfScope() {
+    if (a) {
+      cudaEvent_t b = take_event(c);
+      cudaEventRecord(b, st);
+      c->recs.push_back({kind, a, b});
+    }
+  }
+};
+
+// Folds finished records into the per-kind totals.
+int prof_collect(nrp_context* c) {
+  for (auto& r : c->recs) {
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return fail(NRP_ERR_CUDA, "cudaEventSynchronize: %s", cudaGetErrorString(e));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.start, r.stop);
+    c->prof_ms[r.kind] += ms;
+    c->prof_n[r.kind] += 1;
+    c->pool.push_back(r.start);
+    c->pool.push_back(r.stop);
+  }
+  c->recs.clear();
+  return NRP_OK;
+}
+
+size_t esize(int dtype) { return dtype == NRP_DTYPE_BF16 ? 2 : 4; }
+
+// Upload a float vector in the module dtype.
+cudaError_t upload(DevBuf& dst, const float* src, size_t n, int dtype) {
+  cudaError_t e = dst.ensure(n * esize(dtype));
+  if (e != cudaSuccess) return e;
+  if (dtype == NRP_DTYPE_BF16) {
+    std::vector<uint16_t> h(n);
+    for (size_t i = 0; i < n; ++i) h[i] = bf16_bits(src[i]);
+    return cudaMemcpy(dst.p, h.data(), n * 2, cudaMemcpyHostToDevice);
+  }
+  return cudaMemcpy(dst.p, src, n * 4, cudaMemcpyHostToDevice);
+}
+
+// MLX affine dequantisation on the host (f32 modules run quantised layers
+// through the f32 GEMM): w = scale * q + bias (quantization.rs:4-8).
+void dequant_host(const Linear& L, int N, int K, std::vector<float>& w) {
+  w.resize(static_cast<size_t>(N) * K);
+  const int per = 32 / L.bits, kg = K / L.group;
+  const uint32_t mask = (1u << L.bits) - 1u;
+  for (int n = 0; n < N; ++n)
+    for (int k = 0; k < K; ++k) {
+      const uint32_t q = (L.wq[static_cast<size_t>(n) * (K / per) + k / per] >> (L.bits * (k % per))) & mask;
+      w[static_cast<size_t>(n) * K + k] =
+          L.qs[static_cast<size_t>(n) * kg + k / L.group] * static_cast<float>(q) +
+          L.qb[static_cast<size_t>(n) * kg + k / L.group];
+    }
+}
+
+// Device copies of the parameters in the module dtype.  Q, K and V are
+// concatenated into one [3D, D] projection so the three run as one GEMM.
+int sync_params(nrp_attn* a) {
+  if (!a->dirty) return ok();
+  const int D = a->D;
+  const size_t DD = static_cast<size_t>(D) * D;
+  const bool bf = a->dtype == NRP_DTYPE_BF16;
+  for (int i = 0; i < 5; ++i)
+    if (!a->lin[i].loaded) return fail(NRP_ERR_INVALID, "linear %d has no weights loaded", i);
+  const Linear* qkv[3] = {&a->lin[0], &a->lin[1], &a->lin[2]};
+  const bool q0 = qkv[0]->quant;
+  if (qkv[1]->quant != q0 || qkv[2]->quant != q0)
+    return fail(NRP_ERR_UNSUPPORTED, "linear_q/k/v must all be quantized or all standard");
+  // quantised layers run quantised only in bf16 modules
+  a->qkv_quant = bf && q0;
+  a->out_quant = bf && a->lin[3].quant;
+  a->pos_quant = bf && a->lin[4].quant;
+
+  auto stage_std = [&](const Linear& L, std::vector<float>& w) {
+    if (L.quant) dequant_host(L, D, D, w);
+    else w = L.w;
+  };
+  auto upload_quant = [&](const Linear* const* Ls, int n, DevBuf& wq, DevBuf& sc, DevBuf& zp)
+      -> cudaError_t {
+    const int kg = D / 64;
+    std::vector<uint8_t> codes(static_cast<size_t>(n) * DD);
+    std::vector<float> s(static_cast<size_t>(n) * D * kg), z(static_cast<size_t>(n) * D * kg);
+    for (int i = 0; i < n; ++i) {
+      memcpy(codes.data() + i * DD, Ls[i]->wq.data(), DD);
+      memcpy(s.data() + static_cast<size_t>(i) * D * kg, Ls[i]->qs.data(), sizeof(float) * D * kg);
+      memcpy(z.data() + static_cast<size_t>(i) * D * kg, Ls[i]->qb.data(), sizeof(float) * D * kg);
+    }
+    cudaError_t e = wq.ensure(codes.size());
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(wq.p, codes.data(), codes.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return e;
+    e = upload(sc, s.data(), s.size(), NRP_DTYPE_BF16);
+    if (e != cudaSuccess) return e;
+    return upload(zp, z.data(), z.size(), NRP_DTYPE_BF16);
+  };
+
+  // --- fused Q|K|V
+  if (a->qkv_quant) {
+    for (int i = 0; i < 3; ++i)
+      if (qkv[i]->bits != 8 || qkv[i]->group != 64)
+        return fail(NRP_ERR_UNSUPPORTED, "quantized layers need bits 8, group 64");
+    CUDA_TRY(upload_quant(qkv, 3, a->w_qkv, a->s_qkv, a->z_qkv));
+  } else {
+    std::vector<float> w(3 * DD), tmp;
+    for (int i = 0; i < 3; ++i) {
+      stage_std(*qkv[i], tmp);
+      memcpy(w.data() + i * DD, tmp.data(), sizeof(float) * DD);
+    }
+    CUDA_TRY(upload(a->w_qkv, w.data(), w.size(), a->dtype));
+  }
+  a->has_b_qkv = !qkv[0]->bias.empty() || !qkv[1]->bias.empty() || !qkv[2]->bias.empty();
+  if (a->has_b_qkv) {
+    std::vector<float> b(3 * static_cast<size_t>(D), 0.f);
+    for (int i = 0; i < 3; ++i)
+      if (!qkv[i]->bias.empty()) memcpy(b.data() + i * D, qkv[i]->bias.data(), sizeof(float) * D);
+    CUDA_TRY(upload(a->b_qkv, b.data(), b.size(), a->dtype));
+  }
+  // --- out
+  const Linear* lo = &a->lin[3];
+  if (a->out_quant) {
+    if (lo->bits != 8 || lo->group != 64)
+      return fail(NRP_ERR_UNSUPPORTED, "quantized layers need bits 8, group 64");
+    CUDA_TRY(upload_quant(&lo, 1, a->w_out, a->s_out, a->z_out));
+  } else {
+    std::vector<float> w;
+    stage_std(*lo, w);
+    CUDA_TRY(upload(a->w_out, w.data(), w.size(), a->dtype));
+  }
+  a->has_b_out = !lo->bias.empty();
+  if (a->has_b_out) CUDA_TRY(upload(a->b_out, lo->bias.data(), D, a->dtype));
+  // --- pos (no bias)
+  const Linear* lp = &a->lin[4];
+  if (a->pos_quant) {
+    if (lp->bits != 8 || lp->group != 64)
+      return fail(NRP_ERR_UNSUPPORTED, "quantized layers need bits 8, group 64");
+    CUDA_TRY(upload_quant(&lp, 1, a->w_pos, a->s_pos, a->z_pos));
+  } else {
+    std::vector<float> w;
+    stage_std(*lp, w);
+    CUDA_TRY(upload(a->w_pos, w.data(), w.size(), a->dtype));
+  }
+  // --- position biases: kept in f32 on the device, rounded like the cast
+  std::vector<float> u = a->u, v = a->v;
+  if (u.empty()) u.assign(D, 0.f);
+  if (v.empty()) v.assign(D, 0.f);
+  if (bf)
+    for (int i = 0; i < D; ++i) {
+      u[i] = bf16_round(u[i]);
+      v[i] = bf16_round(v[i]);
+    }
+  CUDA_TRY(upload(a->u_dev, u.data(), D, NRP_DTYPE_F32));
+  CUDA_TRY(upload(a->v_dev, v.data(), D, NRP_DTYPE_F32));
+  a->dirty = false;
+  a->spos_len = -1;
+  return ok();
+}
+
+// y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias) in the module dtype; W is
+// either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
+int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
+               const void* w, bool quant, const void* qs, const void* qb, int N,
+               const void* bias, void* y, int ldy) {
+  if (M <= 0) return ok();
+  if (dtype == NRP_DTYPE_F32) {
+    ProfScope ps(ctx, NRP_KERNEL_GEMM_F32, st);
+    CUDA_TRY(nrp::launch_gemm_f32(static_cast<const float*>(x), M, K, static_cast<const float*>(w),
+                                  N, static_cast<const float*>(bias), static_cast<float*>(y), ldy,
+                                  st));
+    return ok();
+  }
+  if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)
+    return fail(NRP_ERR_UNSUPPORTED, "bf16 linear needs K %% 64 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
+  if (quant && M <= 16) {
+    ProfScope ps(ctx, NRP_KERNEL_QGEMV, st);
+    CUDA_TRY(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
+                               static_cast<const uint8_t*>(w),
+                               static_cast<const __nv_bfloat16*>(qs),
+                               static_cast<const __nv_bfloat16*>(qb),
+                               static_cast<const __nv_bfloat16*>(bias),
+                               static_cast<__nv_bfloat16*>(y), ldy, N, st));
+    return ok();
+  }
+  CUtensorMap mx, mw;
+  if (!nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
+                         static_cast<uint64_t>(K) * 2, 64, 128, true))
+    return fail(NRP_ERR_CUDA, "TMA descriptor for x rejected");
+  if (quant) {
+    ProfScope ps(ctx, NRP_KERNEL_GEMM_Q8, st);
+    CUDA_TRY(nrp::launch_gemm_q8(mx, static_cast<const uint8_t*>(w),
+                                 static_cast<const __nv_bfloat16*>(qs),
+                                 static_cast<const __nv_bfloat16*>(qb),
+                                 static_cast<const __nv_bfloat16*>(bias),
+                                 static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
+                                 ctx->d_err, st));
+  } else {
+    if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
+                           static_cast<uint64_t>(K) * 2, 64, 256, true))
+      return fail(NRP_ERR_CUDA, "TMA descriptor for W rejected");
+    ProfScope ps(ctx, NRP_KERNEL_GEMM_BF16, st);
+    CUDA_TRY(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
+                                   static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
+                                   ctx->d_err, st));
+  }
+  return ok();
+}
+
+int check_device(nrp_context* ctx) {
+  int cur = -1;
+  CUDA_TRY(cudaGetDevice(&cur));
+  if (cur != ctx->device) CUDA_TRY(cudaSetDevice(ctx->device));
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int nrp_abi_version(void) { return NRP_ABI_VERSION; }
+
+const char* nrp_last_error(void) { return g_err.c_str(); }
+
+// ------------------------------------------------------------ host logic
+int nrp_pe_encoding_host(int d_model, int max_len, int seq_len, float* out) {
+  if (!out || d_model <= 0 || d_model % 2 || max_len <= 0)
+    return fail(NRP_ERR_INVALID, "invalid positional encoding arguments");
+  if (seq_len <= 0) return fail(NRP_ERR_INVALID, "positional encoding requested for an empty sequence");
+  // A table of length L holds positions (L-1)..-(L-1); get_encoding slices
+  // positions (seq_len-1)..-(seq_len-1) from it, or rebuilds at seq_len.
+  const int half = d_model / 2;
+  std::vector<float> div(half);
+  const float lnf = logf(10000.0f) / static_cast<float>(d_model);
+  for (int k = 0; k < half; ++k) div[k] = expf(-static_cast<float>(2 * k) * lnf);
+  for (int r = 0; r < 2 * seq_len - 1; ++r) {
+    const float pos = static_cast<float>(seq_len - 1 - r);
+    float* row = out + static_cast<size_t>(r) * d_model;
+    for (int k = 0; k < half; ++k) {
+      const float ang = pos * div[k];
+      row[2 * k] = sinf(ang);
+      row[2 * k + 1] = cosf(ang);
+    }
+  }
+  return ok();
+}
+
+float nrp_pe_xscale(int d_model, int xscaling) {
+  return xscaling ? sqrtf(static_cast<float>(d_model)) : 1.0f;
+}
+
+int nrp_att_context_new(int left, int right, const char* style, nrp_att_context* out) {
+  if (left < 0 && right < 0) return 0;
+  if (out) {
+    out->left = left;
+    out->right = right;
+    out->chunked = (style && strcmp(style, "chunked_limited") == 0) ? 1 : 0;
+  }
+  return 1;
+}
+
+static inline int ctx_visible(const nrp_att_context* c, int i, int j) {
+  if (c->chunked && c->right >= 0) {
+    const int chunk = c->right + 1;
+    const int lc = c->left >= 0 ? c->left / chunk : 10000;
+    const int diff = i / chunk - j / chunk;
+    return diff >= 0 && diff <= lc;
+  }
+  const int off = j - i;
+  int vis = c->left < 0 ? 1 : off >= -std::max(c->left, 0);
+  if (!c->chunked && c->right >= 0) vis = vis && off <= c->right;
+  return vis;
+}
+
+int nrp_block_mask_host(const nrp_att_context* context, int start, int end, int seq_len,
+                        uint8_t* vis) {
+  if (!context || !vis || end < start || seq_len < 0) return fail(NRP_ERR_INVALID, "invalid mask arguments");
+  for (int i = start; i < end; ++i)
+    for (int j = 0; j < seq_len; ++j)
+      vis[static_cast<size_t>(i - start) * seq_len + j] = static_cast<uint8_t>(ctx_visible(context, i, j));
+  return ok();
+}
+
+int nrp_key_padding_mask_host(const int32_t* lengths, int batch, int seq_len, float* mask) {
+  if (!lengths || batch < 0) return fail(NRP_ERR_INVALID, "invalid key padding arguments");
+  bool any = false;
+  for (int b = 0; b < batch; ++b) any = any || lengths[b] < seq_len;
+  if (!any) return 0;
+  if (mask)
+    for (int b = 0; b < batch; ++b) {
+      const int len = std::max(lengths[b], 1);
+      for (int j = 0; j < seq_len; ++j)
+        mask[static_cast<size_t>(b) * seq_len + j] = j < len ? 0.0f : -INFINITY;
+    }
+  return 1;
+}
+
+int nrp_streaming_mask_host(const nrp_att_context* context, int max_audio_length, int cache_len,
+                            int filled_cache_len, int tensor_seq_len, int valid_seq_len,
+                            uint8_t* vis) {
+  if (!vis || tensor_seq_len < 0 || max_audio_length < cache_len + tensor_seq_len)
+    return fail(NRP_ERR_INVALID, "invalid streaming mask arguments");
+  const int offset = cache_len - filled_cache_len;
+  for (int ii = 0; ii < tensor_seq_len; ++ii) {
+    const int i = cache_len + ii;
+    for (int j = 0; j < max_audio_length; ++j) {
+      int m = 1;
+      if (context) {
+        if (context->chunked && context->right == -1) {
+          if (context->left >= 0) m = (j - i) >= -context->left;
+        } else {
+          m = ctx_visible(context, i, j);
+        }
+      }
+      if (offset > 0) m = m && j >= offset;
+      if (valid_seq_len < tensor_seq_len) m = m && ii < valid_seq_len;
+      vis[static_cast<size_t>(ii) * max_audio_length + j] = static_cast<uint8_t>(m);
+    }
+  }
+  return ok();
+}
+
+int nrp_streaming_config_compute(int left, int right, int chunked, int n_layers,
+                                 int subsampling_factor, int conv_kernel_size, int causal_conv,
+                                 int mode_idx, int max_context, nrp_streaming_config* out) {
+  if (!out || subsampling_factor <= 0 || conv_kernel_size <= 0 || n_layers < 0)
+    return fail(NRP_ERR_INVALID, "invalid streaming config arguments");
+  const int ctx0 = causal_conv ? conv_kernel_size - 1 : (conv_kernel_size - 1) / 2;
+  const int ctx1 = causal_conv ? 0 : (conv_kernel_size - 1) / 2;
+  int la, drop;
+  if (chunked) {
+    la = std::max(right, 0);
+    drop = 0;
+  } else {
+    la = right >= 0 ? right * n_layers + ctx1 * n_layers : 0;
+    drop = la;
+  }
+  const int sf = subsampling_factor;
+  out->cache_drop_size = drop;
+  out->last_channel_cache_size = left >= 0 ? left : max_context;
+  out->last_time_cache_size = ctx0;
+  out->chunk_size[0] = 1 + sf * la;
+  out->chunk_size[1] = sf + sf * la;
+  const int shift_steps = std::max(la - drop, 0);
+  out->shift_size[0] = 1 + sf * shift_steps;
+  out->shift_size[1] = sf + sf * shift_steps;
+  out->valid_out_len = (out->shift_size[1] - sf) / sf + 1;
+  out->pre_encode_cache_size[0] = 0;
+  out->pre_encode_cache_size[1] = sf + 1;
+  out->drop_extra_pre_encoded = 1 + (out->pre_encode_cache_size[1] - 1) / sf;
+  out->lookahead_frames = la;
+  out->mode_idx = mode_idx;
+  out->left_context = left;
+  out->right_context = right;
+  return ok();
+}
+
+// --------------------------------------------------------------- context
+int nrp_context_create(int device, nrp_context** out) {
+  if (!out) return fail(NRP_ERR_INVALID, "null output handle");
+  int n = 0;
+  CUDA_TRY(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return fail(NRP_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+  CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(NRP_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                device, prop.major, prop.minor);
+  auto* c = new nrp_context;
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  cudaError_t e = cudaMalloc(&c->d_err, sizeof(int));
+  if (e != cudaSuccess) {
+    delete c;
+    return fail(NRP_ERR_NOMEM, "cudaMalloc: %s", cudaGetErrorString(e));
+  }
+  cudaMemset(c->d_err, 0, sizeof(int));
+  *out = c;
+  return ok();
+}
+
+int nrp_context_destroy(nrp_context* ctx) {
+  if (!ctx) return ok();
+  cudaSetDevice(ctx->device);
+  prof_collect(ctx);
+  for (cudaEvent_t e : ctx->pool) cudaEventDestroy(e);
+  cudaFree(ctx->d_err);
+  delete ctx;
+  return ok();
+}
+
+int nrp_context_check(nrp_context* ctx, void* stream) {
+  if (!ctx) return fail(NRP_ERR_INVALID, "null context");
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int e = 0;
+  CUDA_TRY(cudaMemcpy(&e, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(ctx->d_err, 0, sizeof(int));
+    return fail(NRP_ERR_DEVICE, "a kernel gave up on a bounded wait (code %d)", e);
+  }
+  return ok();
+}
+
+int nrp_pe_encoding(nrp_context* ctx, int d_model, int max_len, int seq_len, int dtype,
+                    void* dev_out, void* stream) {
+  if (!ctx || !dev_out) return fail(NRP_ERR_INVALID, "null argument");
+  std::vector<float> h(static_cast<size_t>(2 * std::max(seq_len, 1) - 1) * std::max(d_model, 1));
+  int rc = nrp_pe_encoding_host(d_model, max_len, seq_len, h.data());
+  if (rc) return rc;
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == NRP_DTYPE_BF16) {
+    std::vector<uint16_t> b(h.size());
+    for (size_t i = 0; i < h.size(); ++i) b[i] = bf16_bits(h[i]);
+    CUDA_TRY(cudaMemcpyAsync(dev_out, b.data(), b.size() * 2, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));  // host staging buffer goes out of scope
+  } else {
+    CUDA_TRY(cudaMemcpyAsync(dev_out, h.data(), h.size() * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  return ok();
+}
+
+// ------------------------------------------------------------- attention
+int nrp_attn_create(nrp_context* ctx, int d_model, int n_heads, int use_bias, nrp_attn** out) {
+  if (!ctx || !out) return fail(NRP_ERR_INVALID, "null argument");
+  if (d_model <= 0 || n_heads <= 0 || d_model % n_heads)
+    return fail(NRP_ERR_INVALID, "d_model %d not divisible by n_heads %d", d_model, n_heads);
+  if (d_model / n_heads > 128)
+    return fail(NRP_ERR_UNSUPPORTED, "head_dim %d > 128", d_model / n_heads);
+  auto* a = new nrp_attn;
+  a->ctx = ctx;
+  a->D = d_model;
+  a->H = n_heads;
+  a->dh = d_model / n_heads;
+  a->use_bias = use_bias;
+  // zero parameters, like RelPositionMultiHeadAttention::new
+  for (int i = 0; i < 5; ++i) {
+    a->lin[i].loaded = true;
+    a->lin[i].w.assign(static_cast<size_t>(d_model) * d_model, 0.f);
+    if (use_bias && i != NRP_LINEAR_POS) a->lin[i].bias.assign(d_model, 0.f);
+  }
+  a->u.assign(d_model, 0.f);
+  a->v.assign(d_model, 0.f);
+  *out = a;
+  return ok();
+}
+
+int nrp_attn_destroy(nrp_attn* attn) {
+  if (attn) {
+    cudaSetDevice(attn->ctx->device);
+    delete attn;
+  }
+  return ok();
+}
+
+int nrp_attn_set_dtype(nrp_attn* attn, int dtype) {
+  if (!attn) return fail(NRP_ERR_INVALID, "null module");
+  if (dtype != NRP_DTYPE_F32 && dtype != NRP_DTYPE_BF16)
+    return fail(NRP_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (dtype == NRP_DTYPE_BF16 && attn->dh != 128)
+    return fail(NRP_ERR_UNSUPPORTED, "bf16 kernels need head_dim 128 (got %d)", attn->dh);
+  attn->dtype = dtype;
+  attn->dirty = true;
+  attn->spos_len = -1;
+  return ok();
+}
+
+int nrp_attn_set_cache_drop_size(nrp_attn* attn, int cache_drop_size) {
+  if (!attn || cache_drop_size < 0) return fail(NRP_ERR_INVALID, "invalid cache_drop_size");
+  attn->cache_drop = cache_drop_size;
+  return ok();
+}
+
+int nrp_attn_load_linear(nrp_attn* attn, int which, const float* weight, const float* bias) {
+  if (!attn || !weight || which < 0 || which > 4) return fail(NRP_ERR_INVALID, "invalid linear arguments");
+  Linear& L = attn->lin[which];
+  const size_t n = static_cast<size_t>(attn->D) * attn->D;
+  L = Linear();
+  L.loaded = true;
+  L.w.assign(weight, weight + n);
+  if (bias) L.bias.assign(bias, bias + attn->D);
+  attn->dirty = true;
+  return ok();
+}
+
+int nrp_attn_load_linear_quantized(nrp_attn* attn, int which, int bits, int group_size,
+                                   const uint32_t* wq, const float* scales, const float* biases,
+                                   const float* bias) {
+  if (!attn || !wq || !scales || !biases || which < 0 || which > 4)
+    return fail(NRP_ERR_INVALID, "invalid quantized linear arguments");
+  if (bits != 8 || group_size != 64)
+    return fail(NRP_ERR_UNSUPPORTED, "quantized linear: bits %d group %d (supported: 8, 64)", bits, group_size);
+  const int D = attn->D;
+  if (D % 64) return fail(NRP_ERR_UNSUPPORTED, "d_model %d not a multiple of the group size", D);
+  Linear& L = attn->lin[which];
+  L = Linear();
+  L.loaded = true;
+  L.quant = true;
+  L.bits = bits;
+  L.group = group_size;
+  L.wq.assign(wq, wq + static_cast<size_t>(D) * D / 4);
+  L.qs.assign(scales, scales + static_cast<size_t>(D) * (D / 64));
+  L.qb.assign(biases, biases + static_cast<size_t>(D) * (D / 64));
+  if (bias) L.bias.assign(bias, bias + D);
+  attn->dirty = true;
+  return ok();
+}
+
+int nrp_attn_load_pos_bias(nrp_attn* attn, const float* u, const float* v) {
+  if (!attn || !u || !v) return fail(NRP_ERR_INVALID, "null pos bias");
+  attn->u.assign(u, u + attn->D);
+  attn->v.assign(v, v + attn->D);
+  attn->dirty = true;
+  return ok();
+}
+
+int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, const void* pos_emb,
+                     const int32_t* lengths, const nrp_att_context* context, void* out) {
+  if (!a || !x || !pos_emb || !out) return fail(NRP_ERR_INVALID, "null argument");
+  if (B <= 0 || T <= 0) return fail(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  nrp_context* ctx = a->ctx;
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  int rc = sync_params(a);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int D = a->D, P = 2 * T - 1;
+  const size_t es = esize(a->dtype);
+  const size_t BT = static_cast<size_t>(B) * T;
+  CUDA_TRY(a->qkv.ensure(BT * 3 * D * es));
+  CUDA_TRY(a->cbuf.ensure(BT * D * es));
+  CUDA_TRY(a->pbuf.ensure(static_cast<size_t>(P) * D * es));
+  // 478-480: q, k, v in one GEMM; 493: linear_pos
+  rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
+                  a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p, 3 * D);
+  if (rc) return rc;
+  rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
+                  a->z_pos.p, D, nullptr, a->pbuf.p, D);
+  if (rc) return rc;
+  nrp::AttnContextDev cd{0, -1, -1, 0};
+  if (context) cd = {1, context->left, context->right, context->chunked};
+  if (a->dtype == NRP_DTYPE_BF16) {
+    ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
+    CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->u_dev.as<float>(),
+                                          a->v_dev.as<float>(), lengths, cd, a->cbuf.p, B, T,
+                                          a->H, ctx->d_err, ctx->num_sms, st));
+  } else {
+    const float* q = a->qkv.as<float>();
+    nrp::StreamMaskDev none{};
+    ProfScope ps(ctx, NRP_KERNEL_ATTN_SIMT, st);
+    CUDA_TRY(nrp::launch_relpos_attn_f32(q, 3 * D, q + D, 3 * D, q + 2 * D, 3 * D,
+                                         a->pbuf.as<float>(), a->u_dev.as<float>(),
+                                         a->v_dev.as<float>(), lengths, cd, none,
+                                         a->cbuf.as<float>(), B, T, T, D, a->H, st));
+  }
+  // 565: linear_out
+  return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
+                    a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
+                    out, D);
+}
+
+// -------------------------------------------------------------- caches
+int nrp_cache_create(nrp_attn* attn, int batch, int cache_len, nrp_cache** out) {
+  if (!attn || !out || batch <= 0 || cache_len <= 0) return fail(NRP_ERR_INVALID, "invalid cache arguments");
+  if (check_device(attn->ctx)) return NRP_ERR_CUDA;
+  auto* c = new nrp_cache;
+  c->attn = attn;
+  c->B = batch;
+  c->C = cache_len;
+  c->D = attn->D;
+  c->dtype = attn->dtype;
+  const size_t n = static_cast<size_t>(batch) * cache_len * attn->D * esize(c->dtype);
+  if (c->kc.ensure(n) || c->vc.ensure(n) || c->hc.ensure(n)) {
+    delete c;
+    return fail(NRP_ERR_NOMEM, "cache allocation failed");
+  }
+  cudaMemset(c->kc.p, 0, n);
+  cudaMemset(c->vc.p, 0, n);
+  cudaMemset(c->hc.p, 0, n);
+  *out = c;
+  return ok();
+}
+
+int nrp_cache_destroy(nrp_cache* cache) {
+  if (cache) {
+    cudaSetDevice(cache->attn->ctx->device);
+    delete cache;
+  }
+  return ok();
+}
+
+int nrp_cache_reset(nrp_cache* c, void* stream) {
+  if (!c) return fail(NRP_ERR_INVALID, "null cache");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemsetAsync(c->kc.p, 0, c->kc.bytes, st));
+  CUDA_TRY(cudaMemsetAsync(c->vc.p, 0, c->vc.bytes, st));
+  CUDA_TRY(cudaMemsetAsync(c->hc.p, 0, c->hc.bytes, st));
+  c->head = 0;
+  return ok();
+}
+
+int nrp_cache_export_h(nrp_cache* c, float* h, void* stream) {
+  if (!c || !h) return fail(NRP_ERR_INVALID, "null argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t es = esize(c->dtype);
+  const size_t row = static_cast<size_t>(c->D) * es;
+  const size_t pitch = row * c->C;
+  void* dst = h;
+  if (c->dtype != NRP_DTYPE_F32) {
+    CUDA_TRY(c->tmp.ensure(pitch * c->B));
+    dst = c->tmp.p;
+  }
+  // oldest frame first: slots head..C-1, then 0..head-1
+  const int n1 = c->C - c->head;
+  CUDA_TRY(cudaMemcpy2DAsync(dst, pitch, static_cast<uint8_t*>(c->hc.p) + c->head * row, pitch,
+                             n1 * row, c->B, cudaMemcpyDeviceToDevice, st));
+  if (c->head)
+    CUDA_TRY(cudaMemcpy2DAsync(static_cast<uint8_t*>(dst) + n1 * row, pitch, c->hc.p, pitch,
+                               c->head * row, c->B, cudaMemcpyDeviceToDevice, st));
+  if (c->dtype != NRP_DTYPE_F32)
+    CUDA_TRY(nrp::launch_bf16_to_f32(c->tmp.as<__nv_bfloat16>(), h,
+                                     static_cast<int64_t>(c->B) * c->C * c->D, st));
+  return ok();
+}
+
+int nrp_cache_import_h(nrp_cache* c, const float* h, void* stream) {
+  if (!c || !h) return fail(NRP_ERR_INVALID, "null argument");
+  nrp_attn* a = c->attn;
+  if (a->dtype != c->dtype) return fail(NRP_ERR_INVALID, "module dtype changed since the cache was created");
+  int rc = sync_params(a);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int D = c->D;
+  const size_t n = static_cast<size_t>(c->B) * c->C * D;
+  if (c->dtype == NRP_DTYPE_F32) {
+    CUDA_TRY(cudaMemcpyAsync(c->hc.p, h, n * 4, cudaMemcpyDeviceToDevice, st));
+  } else {
+    CUDA_TRY(nrp::launch_f32_to_bf16(h, c->hc.as<__nv_bfloat16>(), static_cast<int64_t>(n), st));
+  }
+  c->head = 0;
+  // K/V of the cached frames: the K and V blocks of the fused projection
+  const size_t es = esize(c->dtype);
+  const size_t DD = static_cast<size_t>(D) * D;
+  const int M = c->B * c->C;
+  for (int which = 1; which <= 2; ++which) {
+    const void* w = static_cast<const uint8_t*>(a->w_qkv.p) + (a->qkv_quant ? which * DD : which * DD * es);
+    const void* s = a->qkv_quant ? static_cast<const uint8_t*>(a->s_qkv.p) + which * static_cast<size_t>(D) * (D / 64) * 2 : nullptr;
+    const void* z = a->qkv_quant ? static_cast<const uint8_t*>(a->z_qkv.p) + which * static_cast<size_t>(D) * (D / 64) * 2 : nullptr;
+    const void* bias = a->has_b_qkv ? static_cast<const uint8_t*>(a->b_qkv.p) + which * D * es : nullptr;
+    rc = run_linear(a->ctx, st, c->dtype, c->hc.p, M, D, w, a->qkv_quant, s, z, D, bias,
+                    which == 1 ? c->kc.p : c->vc.p, D);
+    if (rc) return rc;
+  }
+  return ok();
+}
+
+int nrp_attn_forward_with_cache(nrp_attn* a, void* stream, const void* x, int B, int T,
+                                const void* pos_emb, nrp_cache* c, int filled, int valid,
+                                const nrp_att_context* context, void* out) {
+  if (!a || !x || !pos_emb || !c || !out) return fail(NRP_ERR_INVALID, "null argument");
+  if (c->attn != a) return fail(NRP_ERR_INVALID, "cache belongs to another module");
+  if (B != c->B || T <= 0) return fail(NRP_ERR_INVALID, "batch %d / seq_len %d do not match the cache", B, T);
+  if (a->dtype != c->dtype) return fail(NRP_ERR_INVALID, "module dtype changed since the cache was created");
+  nrp_context* ctx = a->ctx;
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  int rc = sync_params(a);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int D = a->D, C = c->C, Tk = C + T, P = 2 * Tk - 1;
+  const size_t es = esize(a->dtype);
+  const size_t BT = static_cast<size_t>(B) * T;
+  CUDA_TRY(a->qkv.ensure(BT * 3 * D * es));
+  CUDA_TRY(a->cbuf.ensure(BT * D * es));
+  rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
+                  a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p, 3 * D);
+  if (rc) return rc;
+  if (a->spos_len != P) {  // 749-761: projected positions reused per pos_len
+    CUDA_TRY(a->spos.ensure(static_cast<size_t>(P) * D * es));
+    rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
+                    a->z_pos.p, D, nullptr, a->spos.p, D);
+    if (rc) return rc;
+    a->spos_len = P;
+  }
+  nrp::StreamMaskDev sm{};
+  sm.has = 1;
+  sm.cache_len = C;
+  sm.filled = std::min(std::max(filled, 0), C);
+  sm.valid = std::min(std::max(valid, 0), T);
+  sm.ctx_has = context ? 1 : 0;
+  sm.left = context ? context->left : -1;
+  sm.right = context ? context->right : -1;
+  sm.chunked = context ? context->chunked : 0;
+  ProfScope ps_attn(ctx, NRP_KERNEL_ATTN_STREAM, st);
+  if (a->dtype == NRP_DTYPE_BF16) {
+    const auto* q = a->qkv.as<__nv_bfloat16>();
+    CUDA_TRY(nrp::launch_relpos_attn_stream_simt<__nv_bfloat16>(
+        q, 3 * D, q + D, q + 2 * D, 3 * D, c->kc.as<__nv_bfloat16>(), c->vc.as<__nv_bfloat16>(), C,
+        c->head, a->spos.as<__nv_bfloat16>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm,
+        a->cbuf.as<__nv_bfloat16>(), B, T, D, a->H, st));
+  } else {
+    const auto* q = a->qkv.as<float>();
+    CUDA_TRY(nrp::launch_relpos_attn_stream_simt<float>(
+        q, 3 * D, q + D, q + 2 * D, 3 * D, c->kc.as<float>(), c->vc.as<float>(), C, c->head,
+        a->spos.as<float>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm, a->cbuf.as<float>(),
+        B, T, D, a->H, st));
+  }
+  // slide the window: the first q_keep new frames replace the oldest
+  // (661-684); more than C of them keep only the newest C (992-996)
+  const int q_keep = std::max(T - a->cache_drop, 0);
+  const int n_app = std::min(q_keep, C);
+  const int src0 = q_keep - n_app;
+  if (n_app > 0) {
+    ProfScope ps(ctx, NRP_KERNEL_RING_APPEND, st);
+    const uint8_t* qkv = static_cast<const uint8_t*>(a->qkv.p);
+    const int64_t sb = static_cast<int64_t>(T) * 3 * D, sr = 3 * D;
+    CUDA_TRY(nrp::launch_ring_append(qkv + (src0 * 3 * D + D) * es, sb, sr, c->kc.p,
+                                     static_cast<int64_t>(C) * D, C, c->head, n_app, B, D,
+                                     static_cast<int>(es), st));
+    CUDA_TRY(nrp::launch_ring_append(qkv + (src0 * 3 * D + 2 * D) * es, sb, sr, c->vc.p,
+                                     static_cast<int64_t>(C) * D, C, c->head, n_app, B, D,
+                                     static_cast<int>(es), st));
+    CUDA_TRY(nrp::launch_ring_append(static_cast<const uint8_t*>(x) + src0 * D * es,
+                                     static_cast<int64_t>(T) * D, D, c->hc.p,
+                                     static_cast<int64_t>(C) * D, C, c->head, n_app, B, D,
+                                     static_cast<int>(es), st));
+    c->head = (c->head + n_app) % C;
+  }
+  return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
+                    a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
+                    out, D);
+}
+
+// ------------------------------------------------------------ profiling
+int nrp_profile_enable(nrp_context* ctx, int enable) {
+  if (!ctx) return fail(NRP_ERR_INVALID, "null context");
+  ctx->prof = enable != 0;
+  return ok();
+}
+
+int nrp_profile_reset(nrp_context* ctx) {
+  if (!ctx) return fail(NRP_ERR_INVALID, "null context");
+  int rc = prof_collect(ctx);
+  for (int k = 0; k < NRP_KERNEL_KINDS; ++k) {
+    ctx->prof_ms[k] = 0.0;
+    ctx->prof_n[k] = 0;
+  }
+  return rc;
+}
+
+int nrp_profile_read(nrp_context* ctx, int kind, int64_t* launches, double* total_ms) {
+  if (!ctx || kind < 0 || kind >= NRP_KERNEL_KINDS) return fail(NRP_ERR_INVALID, "bad kernel kind");
+  int rc = prof_collect(ctx);
+  if (rc) return rc;
+  if (launches) *launches = ctx->prof_n[kind];
+  if (total_ms) *total_ms = ctx->prof_ms[kind];
+  return ok();
+}
+
+// ------------------------------------------------------- linear entries
+int nrp_linear(nrp_context* ctx, void* stream, int dtype, const void* x, int M, int K,
+               const void* w, int N, const void* bias, void* y) {
+  if (!ctx || !x || !w || !y || M < 0 || K <= 0 || N <= 0) return fail(NRP_ERR_INVALID, "invalid linear arguments");
+  if (dtype != NRP_DTYPE_F32 && dtype != NRP_DTYPE_BF16) return fail(NRP_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  return run_linear(ctx, static_cast<cudaStream_t>(stream), dtype, x, M, K, w, false, nullptr,
+                    nullptr, N, bias, y, N);
+}
+
+int nrp_qlinear(nrp_context* ctx, void* stream, const void* x, int M, int K, const uint32_t* wq,
+                const void* scales, const void* biases, int N, int group_size, int bits,
+                const void* bias, void* y) {
+  if (!ctx || !x || !wq || !scales || !biases || !y || M < 0 || K <= 0 || N <= 0)
+    return fail(NRP_ERR_INVALID, "invalid quantized linear arguments");
+  if (bits != 8 || group_size != 64)
+    return fail(NRP_ERR_UNSUPPORTED, "quantized linear: bits %d group %d (supported: 8, 64)", bits, group_size);
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  return run_linear(ctx, static_cast<cudaStream_t>(stream), NRP_DTYPE_BF16, x, M, K, wq, true,
+                    scales, biases, N, bias, y, N);
+}
+
+}  // extern "C"

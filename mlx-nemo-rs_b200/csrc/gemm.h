@@ -1,0 +1,102 @@
+// gemm.h -- launchers of the library's kernels (internal, not the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nrp {
+
+// ---- TMA descriptors (driver entry point resolved through the runtime) ----
+// Row-major 2-D tensor [outer, inner] of `elem_bytes` elements, row stride in
+// bytes; box (box_inner, box_outer); 128-byte swizzle when box_inner *
+// elem_bytes == 128.  Returns false when the driver rejects the map.
+bool make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                  uint32_t box_outer, bool swizzle128);
+// 3-D tensor [d2, d1, d0] (d0 innermost) with strides in bytes for d1, d2.
+bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                  uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2,
+                  bool swizzle128);
+
+// ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
+// x map: bf16 [M, K], box (64, 128), swizzle 128.  W map: bf16 [N, K], box
+// (64, 256), swizzle 128.  Requires K % 64 == 0 and N % 32 == 0.
+int gemm_smem_bytes();
+cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
+                             const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
+                             int K, int num_sms, int* err, cudaStream_t stream);
+// Quantised W: MLX affine 8-bit, group 64: wq [N, K] bytes (the packed u32
+// words read as little-endian bytes), scales/biases bf16 [N, K/64].
+cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
+                           const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
+                           int ldy, int M, int N, int K, int num_sms, int* err,
+                           cudaStream_t stream);
+
+// ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
+cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
+                         const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                         const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
+                         cudaStream_t stream);
+
+// ---- fp32 CUDA-core GEMM (fp32 module dtype): y = x . W^T (+ bias) ----
+cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
+                            const float* bias, float* y, int ldy, cudaStream_t stream);
+
+// ---- offline fused rel-pos attention, bf16, tcgen05 ----
+// qkv: [B, T, 3*D] bf16 (q | k | v along the last axis, heads of 128);
+// p: [P, D] bf16 projected positions for relative positions (T-1)..-(T-1)
+// (P = 2T-1); u, v: [H, 128] f32 position biases; key_len: [B] int32 (key j
+// visible iff j < max(key_len[b], 1)) or null; context (left, right, chunked,
+// has); out: [B, T, D] bf16.
+struct AttnContextDev {
+  int has, left, right, chunked;
+};
+cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* u,
+                                    const float* v, const int32_t* key_len, AttnContextDev ctx,
+                                    void* out, int B, int T, int H, int* err, int num_sms,
+                                    cudaStream_t stream);
+
+// ---- generic CUDA-core attention (fp32 module dtype, any head_dim <= 128) ----
+// q [B,Tq,D] (row stride ldq), k/v [B,Tk,D] (row strides ldk, ldv), p
+// [2Tk-1, D]; masks: key_len (offline pad), ctx (offline context on absolute
+// query positions q_off + i), stream (streaming mask: cache C, filled,
+// valid, ctx).  Rows without a visible key are 0.
+struct StreamMaskDev {
+  int has;        // 1: streaming mask in force
+  int cache_len;  // C (keys 0..C-1 come from the cache)
+  int filled;     // keys j < C - filled are hidden
+  int valid;      // query rows i >= valid see nothing
+  int left, right, chunked, ctx_has;
+};
+cudaError_t launch_relpos_attn_f32(const float* q, int ldq, const float* k, int ldk,
+                                   const float* v, int ldv, const float* p, const float* u,
+                                   const float* vb, const int32_t* key_len, AttnContextDev ctx,
+                                   StreamMaskDev sm, float* out, int B, int Tq, int Tk, int D,
+                                   int H, cudaStream_t stream);
+
+// ---- streaming attention against ring caches (T = float or bf16 storage) ----
+// q [B, T, ldq] (head h at column h*dh), knew/vnew [B, T, ldkv] the chunk's
+// projected keys/values, ring caches kc/vc [B, C, D] with the oldest frame at
+// slot `head`, p [2(C+T)-1, D], out [B, T, D].
+template <typename T>
+cudaError_t launch_relpos_attn_stream_simt(const T* q, int ldq, const T* knew, const T* vnew,
+                                           int ldkv, const T* kc, const T* vc, int C, int head,
+                                           const T* p, const float* u, const float* vb,
+                                           StreamMaskDev sm, T* out, int B, int T_, int D, int H,
+                                           cudaStream_t stream);
+
+// ---- small elementwise helpers ----
+cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,
+                               cudaStream_t stream);
+cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n,
+                               cudaStream_t stream);
+// Ring append of rows: dst[b, (head + i) % C, :] = src[b, src_off + i, :] for
+// i in [0, n), row length `cols` elements of `elem_bytes`.
+cudaError_t launch_ring_append(const void* src, int64_t src_bstride, int64_t src_rstride,
+                               void* dst, int64_t dst_bstride, int C, int head, int n, int B,
+                               int cols, int elem_bytes, cudaStream_t stream);
+
+}  // namespace nrp

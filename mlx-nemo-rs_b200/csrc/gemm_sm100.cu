@@ -1,0 +1,303 @@
+// gemm_sm100.cu -- Y[M,N] = X[M,K] . W[N,K]^T (+ bias[N]) on tcgen05.
+//
+// Serves LinearLayer::forward (reference: src/core/quantization.rs:126-162)
+// for the rel-pos MHA projections: the Standard arm (bf16 W staged by TMA)
+// and the Quantized arm (MLX affine 8-bit, group 64: W = scale*q + bias),
+// where producer warps dequantise u8 weights straight into the swizzled
+// shared-memory B tile, so the dequantised matrix never exists in HBM.
+//
+// Tiling: 128 x 256 output tile per CTA step, K in 64-element stages (one
+// 128-byte swizzle atom per row; also exactly one quantisation group), a
+// 4-deep TMA/mbarrier pipeline, and two 256-column TMEM accumulators so the
+// epilogue of tile t overlaps the MMAs of tile t+1.  The grid is persistent
+// (one CTA per SM, tiles strided by gridDim.x).
+//
+// Warp roles (bf16: 6 warps; quantised: 10 warps):
+//   warp 0      TMA producer for X (and W in the bf16 case)
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 2-5   epilogue: TMEM -> registers -> +bias -> bf16 -> global
+//   warps 6-9   (quantised only) u8 -> bf16 dequantising producer for W
+#include "gemm.h"
+#include "sm100.cuh"
+
+namespace nrp {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kEpiWarp0 = 2;
+constexpr int kDeqWarp0 = 6;
+
+struct GemmSmem {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * (kABytes + kBBytes) + 256;
+
+template <bool kQuant>
+__global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap map_x,
+                   const __grid_constant__ CUtensorMap map_w,
+                   const uint8_t* __restrict__ wq,         // quantised: [N, K] bytes
+                   const __nv_bfloat16* __restrict__ qs,   // [N, K/64]
+                   const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
+                   const __nv_bfloat16* __restrict__ bias, // [N] or null
+                   __nv_bfloat16* __restrict__ y, int ldy, int M, int N, int K, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sA = base;
+  uint8_t* sB = base + kStages * kABytes;
+  GemmSmem* ss = reinterpret_cast<GemmSmem*>(sB + kStages * kBBytes);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (N + kBN - 1) / kBN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = K / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ss->full[s], kQuant ? 1 + 128 : 1);
+      mbar_init(&ss->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ss->tfull[b], 1);
+      mbar_init(&ss->tempty[b], 4);
+    }
+    ss->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ss->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&map_x);
+    if (!kQuant) prefetch_tensormap(&map_w);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ss->tmem_base;
+  volatile int* abort_flag = &ss->abort;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * kBM;
+        const int n0 = (tile % tiles_n) * kBN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t round = it / kStages;
+          if (!mbar_wait(&ss->empty[s], (round & 1) ^ 1, err, kDevTimeoutLoad)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&ss->full[s], kQuant ? kABytes : kABytes + kBBytes);
+          tma_load_2d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0);
+          if (!kQuant) tma_load_2d(sB + s * kBBytes, &map_w, &ss->full[s], kb * kBK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN, 0, 0);
+      uint32_t it = 0;
+      int tc = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tc) {
+        const int buf = tc & 1;
+        const uint32_t use = tc >> 1;
+        if (!mbar_wait(&ss->tempty[buf], (use & 1) ^ 1, err, kDevTimeoutEpi)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dcol = tmem + buf * kBN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t round = it / kStages;
+          if (!mbar_wait(&ss->full[s], round & 1, err, kDevTimeoutLoad)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * kABytes);
+          const uint32_t b0 = smem_u32(sB + s * kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
+            umma_ss(dcol, ad, bd, idesc, (kb | k) != 0);
+          }
+          umma_commit(&ss->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&ss->tfull[buf]);
+      }
+    }
+  } else if (warp < kEpiWarp0 + 4) {
+    // --------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int tc = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tc) {
+      const int m0 = (tile / tiles_n) * kBM;
+      const int n0 = (tile % tiles_n) * kBN;
+      const int buf = tc & 1;
+      const uint32_t use = tc >> 1;
+      if (!mbar_wait(&ss->tfull[buf], use & 1, err, kDevTimeoutMma)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = m0 + row_in_tile;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_ld_wait();
+        const int n = n0 + c;
+        if (m < M && n < N) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float lo = __uint_as_float(r[2 * e]);
+            float hi = __uint_as_float(r[2 * e + 1]);
+            if (bias) {
+              lo += __bfloat162float(bias[n + 2 * e]);
+              hi += __bfloat162float(bias[n + 2 * e + 1]);
+            }
+            packed[e] = pack_bf16x2(lo, hi);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * ldy + n);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
+                                packed[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ss->tempty[buf]);
+    }
+  } else if (kQuant) {
+    // ------------------------------------------ dequantising W producer
+    // 4 threads per W row, 16 bytes (16 weights) each; 32 rows per pass.
+    const int t = threadIdx.x - kDeqWarp0 * 32;  // 0..127
+    const int sub = t & 3;
+    const int row0 = t >> 2;
+    const int kgroups = K / 64;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      const int n0 = (tile % tiles_n) * kBN;
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t round = it / kStages;
+        if (!mbar_wait(&ss->empty[s], (round & 1) ^ 1, err, kDevTimeoutLoad)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* tileB = sB + s * kBBytes;
+#pragma unroll 2
+        for (int pass = 0; pass < kBN / 32; ++pass) {
+          const int r = row0 + pass * 32;
+          const int n = n0 + r;
+          uint4 q = make_uint4(0, 0, 0, 0);
+          float sc = 0.f, bi = 0.f;
+          if (n < N) {
+            q = *reinterpret_cast<const uint4*>(wq + static_cast<size_t>(n) * K + kb * kBK +
+                                                sub * 16);
+            sc = __bfloat162float(qs[static_cast<size_t>(n) * kgroups + kb]);
+            bi = __bfloat162float(qb[static_cast<size_t>(n) * kgroups + kb]);
+          }
+          const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+          uint32_t outw[8];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t v = words[w];
+            const float f0 = fmaf(sc, static_cast<float>(v & 0xFF), bi);
+            const float f1 = fmaf(sc, static_cast<float>((v >> 8) & 0xFF), bi);
+            const float f2 = fmaf(sc, static_cast<float>((v >> 16) & 0xFF), bi);
+            const float f3 = fmaf(sc, static_cast<float>(v >> 24), bi);
+            outw[2 * w] = pack_bf16x2(f0, f1);
+            outw[2 * w + 1] = pack_bf16x2(f2, f3);
+          }
+          // elements [sub*16, sub*16+16) of the row = 16-byte chunks 2*sub, 2*sub+1
+          *reinterpret_cast<uint4*>(tileB + sw128_offset(r, 2 * sub)) =
+              make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          *reinterpret_cast<uint4*>(tileB + sw128_offset(r, 2 * sub + 1)) =
+              make_uint4(outw[4], outw[5], outw[6], outw[7]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&ss->full[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+int gemm_smem_bytes() { return static_cast<int>(kSmemBytes); }
+
+cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
+                             const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
+                             int K, int num_sms, int* err, cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, nullptr, nullptr,
+                                                           nullptr, bias, y, ldy, M, N, K, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
+                           const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
+                           int ldy, int M, int N, int K, int num_sms, int* err,
+                           cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, wq, qs, qb, bias, y, ldy,
+                                                          M, N, K, err);
+  return cudaGetLastError();
+}
+
+}  // namespace nrp

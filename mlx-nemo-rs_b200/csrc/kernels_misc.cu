@@ -1,0 +1,280 @@
+// kernels_misc.cu -- the small kernels around the hot path:
+//  * fp32 CUDA-core GEMM for modules whose dtype is f32 (LinearLayer's
+//    Standard arm, src/core/quantization.rs:128-135, at f32 parity);
+//  * the small-M MLX-affine 8-bit GEMV (quantized_matmul for streaming-size
+//    M, quantization.rs:137-160), HBM-bound on the packed weights;
+//  * dtype conversions and the ring-buffer row append of the streaming cache;
+//  * TMA descriptor construction (driver entry point via the runtime).
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "gemm.h"
+#include "sm100.cuh"
+
+namespace nrp {
+
+// -------------------------------------------------------------- TMA maps
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+bool make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                  uint32_t box_outer, bool swizzle128) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  (void)elem_bytes;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                  uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2,
+                  bool swizzle128) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  (void)elem_bytes;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dtype, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------ fp32 SIMT GEMM
+namespace {
+constexpr int kFT = 64, kFK = 16;
+
+__global__ void __launch_bounds__(256)
+    gemm_f32_kernel(const float* __restrict__ x, int M, int K, const float* __restrict__ w, int N,
+                    const float* __restrict__ bias, float* __restrict__ y, int ldy) {
+  __shared__ float sx[kFK][kFT + 4];
+  __shared__ float sw[kFK][kFT + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * kFT, n0 = blockIdx.x * kFT;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += kFK) {
+    for (int e = threadIdx.x; e < kFT * kFK; e += 256) {
+      const int r = e / kFK, c = e % kFK;
+      const int m = m0 + r, n = n0 + r, k = k0 + c;
+      sx[c][r] = (m < M && k < K) ? x[static_cast<size_t>(m) * K + k] : 0.f;
+      sw[c][r] = (n < N && k < K) ? w[static_cast<size_t>(n) * K + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < kFK; ++c) {
+      float a[4], bb[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        a[u] = sx[c][ty * 4 + u];
+        bb[u] = sw[c][tx * 4 + u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(a[u], bb[v], acc[u][v]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int m = m0 + ty * 4 + u;
+    if (m >= M) continue;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int n = n0 + tx * 4 + v;
+      if (n < N) y[static_cast<size_t>(m) * ldy + n] = acc[u][v] + (bias ? bias[n] : 0.f);
+    }
+  }
+}
+}  // namespace
+
+cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
+                            const float* bias, float* y, int ldy, cudaStream_t stream) {
+  dim3 grid((N + kFT - 1) / kFT, (M + kFT - 1) / kFT);
+  gemm_f32_kernel<<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------- small-M quantised GEMV
+// One warp per output column n.  Lane l reads 16 packed weights at a time
+// (a 16-byte load; 32 lanes cover 512 contiguous bytes of the row), all in
+// one group of 64, and FMAs them against every input row staged in shared
+// memory as f32.  K is processed in slices of kQK columns.
+namespace {
+constexpr int kQMaxM = 16;
+constexpr int kQK = 1024;
+constexpr int kQWarps = 8;
+
+__global__ void __launch_bounds__(kQWarps * 32)
+    qgemv_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                 const uint8_t* __restrict__ wq, const __nv_bfloat16* __restrict__ qs,
+                 const __nv_bfloat16* __restrict__ qb, const __nv_bfloat16* __restrict__ bias,
+                 __nv_bfloat16* __restrict__ y, int ldy, int N) {
+  extern __shared__ float sxq[];  // [M][kQK]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kQWarps + warp;
+  const int kg = K / 64;
+  float acc[kQMaxM];
+#pragma unroll
+  for (int m = 0; m < kQMaxM; ++m) acc[m] = 0.f;
+  for (int k0 = 0; k0 < K; k0 += kQK) {
+    const int kw = min(kQK, K - k0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < M * kw; e += blockDim.x) {
+      const int m = e / kw, c = e % kw;
+      sxq[m * kQK + c] = __bfloat162float(x[static_cast<size_t>(m) * K + k0 + c]);
+    }
+    __syncthreads();
+    if (n < N) {
+      for (int c = lane * 16; c < kw; c += 32 * 16) {
+        const int k = k0 + c;
+        const uint4 q = *reinterpret_cast<const uint4*>(wq + static_cast<size_t>(n) * K + k);
+        const float s = __bfloat162float(qs[static_cast<size_t>(n) * kg + k / 64]);
+        const float bz = __bfloat162float(qb[static_cast<size_t>(n) * kg + k / 64]);
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+        float wv[16];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            wv[4 * u + e] = fmaf(s, static_cast<float>((words[u] >> (8 * e)) & 0xFFu), bz);
+        }
+#pragma unroll
+        for (int m = 0; m < kQMaxM; ++m) {
+          if (m < M) {
+            const float4* xr = reinterpret_cast<const float4*>(sxq + m * kQK + c);
+            float a = acc[m];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const float4 xv = xr[v];
+              a = fmaf(xv.x, wv[4 * v], a);
+              a = fmaf(xv.y, wv[4 * v + 1], a);
+              a = fmaf(xv.z, wv[4 * v + 2], a);
+              a = fmaf(xv.w, wv[4 * v + 3], a);
+            }
+            acc[m] = a;
+          }
+        }
+      }
+    }
+  }
+  if (n >= N) return;
+#pragma unroll
+  for (int m = 0; m < kQMaxM; ++m) {
+    if (m >= M) break;
+    float a = acc[m];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    if (lane == 0) {
+      if (bias) a += __bfloat162float(bias[n]);
+      y[static_cast<size_t>(m) * ldy + n] = __float2bfloat16_rn(a);
+    }
+  }
+}
+}  // namespace
+
+cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
+                         const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                         const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
+                         cudaStream_t stream) {
+  if (M > kQMaxM || K % 512 != 0) return cudaErrorInvalidValue;
+  static bool attr = false;
+  const int smem = kQMaxM * kQK * 4;
+  if (!attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(qgemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  qgemv_kernel<<<(N + kQWarps - 1) / kQWarps, kQWarps * 32, smem, stream>>>(x, M, K, wq, qs, qb,
+                                                                           bias, y, ldy, N);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ conversions
+namespace {
+__global__ void f32_to_bf16_kernel(const float* __restrict__ s, __nv_bfloat16* __restrict__ d,
+                                   int64_t n) {
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    d[e] = __float2bfloat16_rn(s[e]);
+}
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ s, float* __restrict__ d,
+                                   int64_t n) {
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    d[e] = __bfloat162float(s[e]);
+}
+int grid_for(int64_t n) {
+  int64_t g = (n + 255) / 256;
+  return static_cast<int>(g < 148 * 16 ? (g < 1 ? 1 : g) : 148 * 16);
+}
+
+// dst[b, (head + i) % C, :] = src[b, i, :]; one block per (i, b), 16-byte
+// vectors when the row allows it.
+__global__ void ring_append_kernel(const uint8_t* __restrict__ src, int64_t sb, int64_t sr,
+                                   uint8_t* __restrict__ dst, int64_t db, int C, int head,
+                                   int row_bytes) {
+  const int i = blockIdx.x, b = blockIdx.y;
+  const uint8_t* s = src + b * sb + i * sr;
+  uint8_t* d = dst + b * db + static_cast<int64_t>((head + i) % C) * row_bytes;
+  if ((row_bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(s) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+    for (int e = threadIdx.x; e < row_bytes / 16; e += blockDim.x)
+      reinterpret_cast<uint4*>(d)[e] = reinterpret_cast<const uint4*>(s)[e];
+  } else {
+    for (int e = threadIdx.x; e < row_bytes; e += blockDim.x) d[e] = s[e];
+  }
+}
+}  // namespace
+
+cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,
+                               cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  f32_to_bf16_kernel<<<grid_for(n), 256, 0, stream>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n,
+                               cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  bf16_to_f32_kernel<<<grid_for(n), 256, 0, stream>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ring_append(const void* src, int64_t src_bstride, int64_t src_rstride,
+                               void* dst, int64_t dst_bstride, int C, int head, int n, int B,
+                               int cols, int elem_bytes, cudaStream_t stream) {
+  if (n <= 0 || B <= 0) return cudaSuccess;
+  dim3 grid(n, B);
+  ring_append_kernel<<<grid, 128, 0, stream>>>(
+      static_cast<const uint8_t*>(src), src_bstride * elem_bytes, src_rstride * elem_bytes,
+      static_cast<uint8_t*>(dst), dst_bstride * elem_bytes, C, head, cols * elem_bytes);
+  return cudaGetLastError();
+}
+
+}  // namespace nrp
