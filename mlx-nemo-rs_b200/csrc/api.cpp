@@ -137,7 +137,6 @@ struct nrp_attn {
   DevBuf u_dev, v_dev;
   // workspace
   DevBuf qkv, cbuf, pbuf;
-  DevBuf kbuf, pbbuf;  // u.k_j and v.p_r from the projection epilogues (bf16 path)
   // projected streaming positions, reused while pos_len is unchanged
   int spos_len = -1;
   DevBuf spos;
@@ -336,7 +335,7 @@ int sync_params(nrp_attn* a) {
 // either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
 int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
                const void* w, bool quant, const void* qs, const void* qb, int N,
-               const void* bias, void* y, int ldy, const nrp::HeadDot& hd = nrp::HeadDot()) {
+               const void* bias, void* y, int ldy) {
   if (M <= 0) return ok();
   if (dtype == NRP_DTYPE_F32) {
     ProfScope ps(ctx, NRP_KERNEL_GEMM_F32, st);
@@ -347,7 +346,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   }
   if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)
     return fail(NRP_ERR_UNSUPPORTED, "bf16 linear needs K %% 64 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
-  if (quant && M <= 16 && !hd.vec) {
+  if (quant && M <= 16) {
     ProfScope ps(ctx, NRP_KERNEL_QGEMV, st);
     CUDA_TRY(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
                                static_cast<const uint8_t*>(w),
@@ -368,7 +367,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                  static_cast<const __nv_bfloat16*>(qb),
                                  static_cast<const __nv_bfloat16*>(bias),
                                  static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                 ctx->d_err, st, hd));
+                                 ctx->d_err, st));
   } else {
     if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
                            static_cast<uint64_t>(K) * 2, 64, 256, true))
@@ -376,7 +375,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
     ProfScope ps(ctx, NRP_KERNEL_GEMM_BF16, st);
     CUDA_TRY(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
                                    static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                   ctx->d_err, st, hd));
+                                   ctx->d_err, st));
   }
   return ok();
 }
@@ -709,44 +708,18 @@ int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, con
   nrp::AttnContextDev cd{0, -1, -1, 0};
   if (context) cd = {1, context->left, context->right, context->chunked};
   if (a->dtype == NRP_DTYPE_BF16) {
-    // 478-480: q, k, v in one GEMM whose epilogue also writes u.k_j per
-    // head; 493: linear_pos, whose epilogue writes v.p_r per head
-    const int H = a->H;
-    const int kb_ld = (T + 3) & ~3;
-    const int pb_off = nrp::relpos_attn_pb_off(T);
-    const int pb_ld = (P + pb_off + 3) & ~3;
-    CUDA_TRY(a->kbuf.ensure(static_cast<size_t>(B) * H * kb_ld * 4));
-    const size_t pb_bytes = static_cast<size_t>(H) * pb_ld * 4;
-    if (pb_bytes > a->pbbuf.bytes) {
-      CUDA_TRY(a->pbbuf.ensure(pb_bytes));
-      CUDA_TRY(cudaMemsetAsync(a->pbbuf.p, 0, pb_bytes, st));  // the off-prefix is never written
-    }
-    nrp::HeadDot hk;
-    hk.vec = a->u_dev.as<float>();
-    hk.out = a->kbuf.as<float>();
-    hk.col0 = D;
-    hk.heads = H;
-    hk.rows_per_batch = T;
-    hk.ld = kb_ld;
+    // 478-480: q, k, v in one GEMM; 493: linear_pos
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
-                    3 * D, hk);
+                    3 * D);
     if (rc) return rc;
-    nrp::HeadDot hp;
-    hp.vec = a->v_dev.as<float>();
-    hp.out = a->pbbuf.as<float>();
-    hp.col0 = 0;
-    hp.heads = H;
-    hp.rows_per_batch = P;
-    hp.ld = pb_ld;
-    hp.off = pb_off;
     rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
-                    a->z_pos.p, D, nullptr, a->pbuf.p, D, hp);
+                    a->z_pos.p, D, nullptr, a->pbuf.p, D);
     if (rc) return rc;
     ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
-    CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->kbuf.as<float>(), kb_ld,
-                                          a->pbbuf.as<float>(), pb_ld, lengths, cd, a->cbuf.p,
-                                          B, T, H, ctx->d_err, ctx->num_sms, st));
+    CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->u_dev.as<float>(),
+                                          a->v_dev.as<float>(), lengths, cd, a->cbuf.p, B, T,
+                                          a->H, ctx->d_err, ctx->num_sms, st));
   } else {
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,

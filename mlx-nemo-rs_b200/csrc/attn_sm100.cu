@@ -21,18 +21,20 @@
 // at offset 127-il: a per-lane skew, done in registers with a 5-stage
 // predicated barrel shift over a 64-column window.
 //
-// Biases.  (q+u).k_j = q.k_j + u.k_j and (q+v).p_r = q.p_r + v.p_r; the
-// scalars u.k_j (kb) and v.p_r (pb) come from the projection GEMMs'
-// epilogues and are staged per tile with the K / P tiles.
+// Biases.  The CTA's query tile is staged once and turned into two bf16
+// tiles, q+u (A operand of the content product) and q+v (A operand of the
+// positional product) -- the same bf16 adds as the reference's
+// q_with_bias_u / q_with_bias_v (attention.rs:506-508).
 //
 // Masks.  Key padding (attention.rs:280-294) and AttentionContext windows
 // (attention.rs:232-272) reduce to one visible key interval per query row.
 //
-// Memory.  Shared: Q, 2 x K, 2 x P chunk, V, probabilities (the bf16 A
-// operand of P.V), kb/pb rings -- 226 KB.  TMEM: S [0,128), BD slots
-// [128,256) and [256,384), O [384,512).  The MMAs of key tile t+1 run while
-// the softmax of tile t finishes (its TMEM reads come first), and the loads
-// of tile t+1 are issued a tile ahead.
+// Memory.  Shared: q+u, q+v, one {K tile, P chunk} stage, 2 x V,
+// probabilities (the bf16 A operand of P.V) -- 224 KB.  TMEM: S [0,128), BD
+// slots [128,256) and [256,384), O [384,512).  The MMAs of key tile t+1 run
+// while the softmax of tile t finishes (its TMEM reads come first); the
+// next {K, P} stage loads as soon as the tile's MMAs have read it and V is
+// loaded a tile ahead.
 //
 // Warps 0-7 (softmax): warp w owns TMEM lane quadrant w&3 (one query row
 // per thread) and key half w>>2 (64 keys); the two threads of a row swap
@@ -55,25 +57,24 @@ constexpr uint32_t kTileBytes = 2 * kHalf;  // 32 KB: 128 rows x 128 bf16
 constexpr int kSoftmaxThreads = 256;
 constexpr int kThreads = kSoftmaxThreads + 32;
 
-// shared-memory map (1024-aligned base)
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kTileBytes;       // 2 slots
-constexpr uint32_t kOffP = kOffK + 2 * kTileBytes;   // 2 slots
-constexpr uint32_t kOffV = kOffP + 2 * kTileBytes;
-constexpr uint32_t kOffPr = kOffV + kTileBytes;
-constexpr uint32_t kOffKb = kOffPr + kTileBytes;     // 2 x 128 f32
-constexpr uint32_t kOffPb = kOffKb + 2 * 512;        // 3 x 128 f32
-constexpr uint32_t kOffBar = kOffPb + 3 * 512;
+// shared-memory map (offsets from a 1024-aligned base)
+constexpr uint32_t kOffQu = 0;
+constexpr uint32_t kOffQv = kOffQu + kTileBytes;
+constexpr uint32_t kOffK = kOffQv + kTileBytes;
+constexpr uint32_t kOffP = kOffK + kTileBytes;
+constexpr uint32_t kOffV = kOffP + kTileBytes;       // 2 slots
+constexpr uint32_t kOffPr = kOffV + 2 * kTileBytes;
+constexpr uint32_t kOffBar = kOffPr + kTileBytes;
 
 struct Bars {
-  uint64_t q, p0, kp[2], v, s, sfree, p, o, x1, x2;
+  uint64_t q, prep, p0, kp, v[2], s, sfree, p, o, x1, x2;
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t kSmemBytes = kOffBar + sizeof(Bars);
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kOffBar + sizeof(Bars);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-constexpr uint32_t kStageTx = 2 * kTileBytes + 2 * 512;  // K, P chunk, kb, pb
+constexpr uint32_t kStageTx = 2 * kTileBytes;  // K tile + P chunk
 
 // Bounded wait whose outcome is the same for every lane of the warp (the
 // tcgen05 loads/stores that follow are warp-collective).
@@ -116,23 +117,19 @@ __device__ __forceinline__ void mma_k128(uint32_t tmem_d, uint32_t a, uint32_t b
 __global__ void __launch_bounds__(kThreads, 1)
     relpos_attn_kernel(const __grid_constant__ CUtensorMap map_qkv,  // [B][T][3D] bf16
                        const __grid_constant__ CUtensorMap map_p,    // [2T-1][D] bf16
-                       const __grid_constant__ CUtensorMap map_kb,   // [B*H][T] f32
-                       const __grid_constant__ CUtensorMap map_pb,   // [H][2T-1+off] f32
+                       const float* __restrict__ pos_u, const float* __restrict__ pos_v,
                        const int32_t* __restrict__ key_len, AttnContextDev ctx,
-                       __nv_bfloat16* __restrict__ out, int T, int H, int pb_off, int* err) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+                       __nv_bfloat16* __restrict__ out, int T, int H, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-  if ((smem_u32(smem) & 1023u) != 0) {  // the swizzle atoms need 1024-byte alignment
-    if (threadIdx.x == 0) atomicCAS(err, 0, kDevBadArgs);
-    return;
-  }
-  uint8_t* sQ = smem + kOffQ;
+  uint8_t* sQu = smem + kOffQu;
+  uint8_t* sQv = smem + kOffQv;
   uint8_t* sK = smem + kOffK;
   uint8_t* sP = smem + kOffP;
   uint8_t* sV = smem + kOffV;
   uint8_t* sPr = smem + kOffPr;
-  float* skb = reinterpret_cast<float*>(smem + kOffKb);
-  float* spb = reinterpret_cast<float*>(smem + kOffPb);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -156,16 +153,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   // outputs are unspecified in the reference (conformer.rs:1590-1593) and
   // are written as zeros here.
   const bool padded_tile = key_len && i0 >= kend;
-  const int j0 = jlo & ~3;  // 16-byte aligned kb rows
+  const int j0 = jlo;
   const int nt = (jhi > jlo && !padded_tile) ? (jhi - j0 + kTile - 1) / kTile : 0;
   const int rbase = T - kTile - i0 + j0;  // first P row of chunk 0
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q, 1);
+    mbar_init(&bars->prep, kSoftmaxThreads);
     mbar_init(&bars->p0, 1);
-    mbar_init(&bars->kp[0], 1);
-    mbar_init(&bars->kp[1], 1);
-    mbar_init(&bars->v, 1);
+    mbar_init(&bars->kp, 1);
+    mbar_init(&bars->v[0], 1);
+    mbar_init(&bars->v[1], 1);
     mbar_init(&bars->s, 1);
     mbar_init(&bars->sfree, kSoftmaxThreads);
     mbar_init(&bars->p, kSoftmaxThreads);
@@ -189,95 +187,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ TMA + MMA issuer
     if (lane == 0 && nt > 0) {
       const int qcol = h * kDh, kcol = D + h * kDh, vcol = 2 * D + h * kDh;
-      const int bh = b * H + h;
       prefetch_tensormap(&map_qkv);
       prefetch_tensormap(&map_p);
-      prefetch_tensormap(&map_kb);
-      prefetch_tensormap(&map_pb);
-      auto load_stage = [&](int t) {  // K_t, kb_t, P chunk t+1, pb_{t+1}
-        const int s = t & 1, c = t + 1;
-        uint64_t* bar = &bars->kp[s];
-        mbar_arrive_expect_tx(bar, kStageTx);
+      auto load_stage = [&](int t) {  // K_t and P chunk t+1
+        mbar_arrive_expect_tx(&bars->kp, kStageTx);
         const int jt = j0 + t * kTile;
-        tma_load_3d(sK + s * kTileBytes, &map_qkv, bar, kcol, jt, b);
-        tma_load_3d(sK + s * kTileBytes + kHalf, &map_qkv, bar, kcol + 64, jt, b);
-        tma_load_2d(skb + s * kTile, &map_kb, bar, jt, bh);
-        uint8_t* dst = sP + (c & 1) * kTileBytes;
-        const int prow = rbase + c * kTile;
-        tma_load_2d(dst, &map_p, bar, h * kDh, prow);
-        tma_load_2d(dst + kHalf, &map_p, bar, h * kDh + 64, prow);
-        tma_load_2d(spb + (c % 3) * kTile, &map_pb, bar, prow + pb_off, h);
+        tma_load_3d(sK, &map_qkv, &bars->kp, kcol, jt, b);
+        tma_load_3d(sK + kHalf, &map_qkv, &bars->kp, kcol + 64, jt, b);
+        const int prow = rbase + (t + 1) * kTile;
+        tma_load_2d(sP, &map_p, &bars->kp, h * kDh, prow);
+        tma_load_2d(sP + kHalf, &map_p, &bars->kp, h * kDh + 64, prow);
+      };
+      auto load_v = [&](int t) {
+        uint64_t* bar = &bars->v[t & 1];
+        uint8_t* dst = sV + (t & 1) * kTileBytes;
+        mbar_arrive_expect_tx(bar, kTileBytes);
+        tma_load_3d(dst, &map_qkv, bar, vcol, j0 + t * kTile, b);
+        tma_load_3d(dst + kHalf, &map_qkv, bar, vcol + 64, j0 + t * kTile, b);
       };
       mbar_arrive_expect_tx(&bars->q, kTileBytes);
-      tma_load_3d(sQ, &map_qkv, &bars->q, qcol, i0, b);
-      tma_load_3d(sQ + kHalf, &map_qkv, &bars->q, qcol + 64, i0, b);
-      // P chunk 0 and pb_0: chunk 0 is only read by the first BD MMA, so it
-      // is staged in the probability buffer, which is free until then.
-      mbar_arrive_expect_tx(&bars->p0, kTileBytes + 512);
+      tma_load_3d(sQu, &map_qkv, &bars->q, qcol, i0, b);
+      tma_load_3d(sQu + kHalf, &map_qkv, &bars->q, qcol + 64, i0, b);
+      // P chunk 0 is only read by the first BD MMA, so it is staged in the
+      // probability buffer, which is free until the first softmax.
+      mbar_arrive_expect_tx(&bars->p0, kTileBytes);
       tma_load_2d(sPr, &map_p, &bars->p0, h * kDh, rbase);
       tma_load_2d(sPr + kHalf, &map_p, &bars->p0, h * kDh + 64, rbase);
-      tma_load_2d(spb, &map_pb, &bars->p0, rbase + pb_off, h);
       load_stage(0);
-      if (nt > 1) load_stage(1);
-      mbar_arrive_expect_tx(&bars->v, kTileBytes);
-      tma_load_3d(sV, &map_qkv, &bars->v, vcol, j0, b);
-      tma_load_3d(sV + kHalf, &map_qkv, &bars->v, vcol + 64, j0, b);
+      load_v(0);
+      if (nt > 1) load_v(1);
 
       constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, 0, 1);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-      const uint32_t aP = smem_u32(sP), aPr = smem_u32(sPr);
-      bool ok = mbar_wait(&bars->q, 0, err, kDevTimeoutLoad) &&
+      const uint32_t aQu = smem_u32(sQu), aQv = smem_u32(sQv), aK = smem_u32(sK);
+      const uint32_t aV = smem_u32(sV), aP = smem_u32(sP), aPr = smem_u32(sPr);
+      auto pv = [&](int t) {  // O (+)= probabilities(t) . V_t
+        tc_fence_after();
+        const uint32_t vb = aV + (t & 1) * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t offa = (k >> 2) * kHalf + (k & 3) * 32;
+          umma_ss(tmem + 384, sdesc_sw128(aPr + offa, 16, 1024),
+                  sdesc_sw128(vb + k * 2048, kHalf, 1024), idesc_pv, (t > 0) || (k > 0));
+        }
+        umma_commit(&bars->o);
+      };
+      bool ok = mbar_wait(&bars->prep, 0, err, kDevTimeoutEpi) &&
                 mbar_wait(&bars->p0, 0, err, kDevTimeoutLoad);
       if (ok) {
         tc_fence_after();
-        mma_k128(tmem + 128, aQ, aPr, idesc_kk, false);  // BD_0 -> slot 0
+        mma_k128(tmem + 128, aQv, aPr, idesc_kk, false);  // BD_0 -> slot 0
       }
       for (int t = 0; t < nt && ok; ++t) {
-        const int s = t & 1;
-        ok = mbar_wait(&bars->kp[s], (t >> 1) & 1, err, kDevTimeoutLoad);
+        ok = mbar_wait(&bars->kp, t & 1, err, kDevTimeoutLoad);
         if (ok && t > 0) ok = mbar_wait(&bars->sfree, (t - 1) & 1, err, kDevTimeoutEpi);
         if (!ok) break;
-        if (t > 0 && t + 1 < nt) load_stage(t + 1);
         tc_fence_after();
-        mma_k128(tmem, aQ, aK + s * kTileBytes, idesc_kk, false);  // S_t
-        mma_k128(tmem + 128 + 128 * ((t + 1) & 1), aQ, aP + ((t + 1) & 1) * kTileBytes, idesc_kk,
-                 false);  // BD_{t+1}
+        mma_k128(tmem, aQu, aK, idesc_kk, false);  // S_t
+        mma_k128(tmem + 128 + 128 * ((t + 1) & 1), aQv, aP, idesc_kk, false);  // BD_{t+1}
         umma_commit(&bars->s);
-        if (t > 0) {  // P.V of the previous tile
+        // the stage is free once these MMAs have read it
+        ok = mbar_wait(&bars->s, t & 1, err, kDevTimeoutMma);
+        if (!ok) break;
+        if (t + 1 < nt) load_stage(t + 1);
+        if (t > 0) {  // P.V of the previous tile, then V for tile t+1 into its slot
           ok = mbar_wait(&bars->p, (t - 1) & 1, err, kDevTimeoutEpi) &&
-               mbar_wait(&bars->v, (t - 1) & 1, err, kDevTimeoutLoad);
+               mbar_wait(&bars->v[(t - 1) & 1], ((t - 1) >> 1) & 1, err, kDevTimeoutLoad);
           if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t offa = (k >> 2) * kHalf + (k & 3) * 32;
-            umma_ss(tmem + 384, sdesc_sw128(aPr + offa, 16, 1024),
-                    sdesc_sw128(aV + k * 2048, kHalf, 1024), idesc_pv, (t > 1) || (k > 0));
-          }
-          umma_commit(&bars->o);
+          pv(t - 1);
           ok = mbar_wait(&bars->o, (t - 1) & 1, err, kDevTimeoutMma);
           if (!ok) break;
-          mbar_arrive_expect_tx(&bars->v, kTileBytes);
-          const int jn = j0 + t * kTile;
-          tma_load_3d(sV, &map_qkv, &bars->v, vcol, jn, b);
-          tma_load_3d(sV + kHalf, &map_qkv, &bars->v, vcol + 64, jn, b);
+          if (t + 1 < nt) load_v(t + 1);
         }
       }
       if (ok) {  // P.V of the last tile
         const int t = nt - 1;
         ok = mbar_wait(&bars->p, t & 1, err, kDevTimeoutEpi) &&
-             mbar_wait(&bars->v, t & 1, err, kDevTimeoutLoad);
-        if (ok) {
-          tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t offa = (k >> 2) * kHalf + (k & 3) * 32;
-            umma_ss(tmem + 384, sdesc_sw128(aPr + offa, 16, 1024),
-                    sdesc_sw128(aV + k * 2048, kHalf, 1024), idesc_pv, (t > 0) || (k > 0));
-          }
-          umma_commit(&bars->o);
-        }
+             mbar_wait(&bars->v[t & 1], (t >> 1) & 1, err, kDevTimeoutLoad);
+        if (ok) pv(t);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -293,20 +280,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale_log2 = 1.4426950408889634f * rsqrtf(static_cast<float>(kDh));
     const int shift = 31 - lane;
     const bool s16 = shift & 16, s8 = shift & 8, s4 = shift & 4, s2 = shift & 2, s1 = shift & 1;
+    // keys every row of this warp sees: no per-element mask inside it
+    const int wlo = __reduce_max_sync(0xffffffffu, rlo);
+    const int whi = __reduce_min_sync(0xffffffffu, rhi);
     float* xbuf = reinterpret_cast<float*>(sPr + kTileBytes - 1024);  // [2][128] exchange
     uint32_t xphase = 0;
     float m_ref = -INFINITY;  // log2-domain maximum the output is scaled by
     float l = 0.f;            // this thread's share of the row sum
     bool ok = true;
-    for (int t = 0; t < nt; ++t) {
+    // ---- q+u and q+v tiles (bf16 adds, attention.rs:506-508), once per CTA
+    if (nt > 0) {
+      ok = warp_wait(&bars->q, 0, err, kDevTimeoutLoad);
+      if (ok) {
+        const int tid = threadIdx.x;  // 0..255: row tid/2, 64-column half tid&1
+        const int row = tid >> 1, half = tid & 1;
+        const float* u = pos_u + h * kDh + half * 64;
+        const float* v = pos_v + h * kDh + half * 64;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const uint32_t off = half * kHalf + sw128_offset(row, ch);
+          const uint4 q = *reinterpret_cast<const uint4*>(sQu + off);
+          const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+          uint32_t wu[4], wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[e]));
+            const int c = ch * 8 + 2 * e;
+            wu[e] = pack_bf16x2(f.x + u[c], f.y + u[c + 1]);
+            wv[e] = pack_bf16x2(f.x + v[c], f.y + v[c + 1]);
+          }
+          *reinterpret_cast<uint4*>(sQu + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+          *reinterpret_cast<uint4*>(sQv + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(&bars->prep);
+    }
+    for (int t = 0; t < nt && ok; ++t) {
       const uint32_t par = t & 1;
       if (__any_sync(0xffffffffu, *abort_flag)) { ok = false; break; }
-      if (t == 0 && !warp_wait(&bars->p0, 0, err, kDevTimeoutLoad)) { ok = false; break; }
-      if (!warp_wait(&bars->kp[t & 1], (t >> 1) & 1, err, kDevTimeoutLoad)) { ok = false; break; }
       if (!warp_wait(&bars->s, par, err, kDevTimeoutMma)) { ok = false; break; }
       tc_fence_after();
       const int jt = j0 + t * kTile;
-      const float* kbt = skb + (t & 1) * kTile;
       // ---- pass 1: 64 scores (log2 domain, masked) into registers
       float sc[64];
       float mx = -INFINITY;
@@ -337,16 +352,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int x = 0; x < 33; ++x) a[x] = s2 ? a[x + 2] : a[x];
 #pragma unroll
         for (int x = 0; x < 32; ++x) a[x] = s1 ? a[x + 1] : a[x];
+        const int jb = jt + jl0;
+        if (jb >= wlo && jb + 32 <= whi) {  // every key visible to every row
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int jl = jl0 + e;
-          const int j = jt + jl;
-          const int x = 127 - il + jl;  // P row within the 256-row window
-          const float pbv = spb[((t + (x >> 7)) % 3) * kTile + (x & 127)];
-          float v = (__uint_as_float(sr[e]) + kbt[jl] + a[e] + pbv) * scale_log2;
-          v = (j >= rlo && j < rhi) ? v : -INFINITY;
-          mx = fmaxf(mx, v);
-          sc[32 * sub + e] = v;
+          for (int e = 0; e < 32; ++e) {
+            const float v = (__uint_as_float(sr[e]) + a[e]) * scale_log2;
+            mx = fmaxf(mx, v);
+            sc[32 * sub + e] = v;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int j = jb + e;
+            float v = (__uint_as_float(sr[e]) + a[e]) * scale_log2;
+            v = (j >= rlo && j < rhi) ? v : -INFINITY;
+            mx = fmaxf(mx, v);
+            sc[32 * sub + e] = v;
+          }
         }
       }
       tc_fence_before();
@@ -452,12 +474,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-int relpos_attn_pb_off(int T) { return (4 - T % 4) % 4; }
-
-cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* kb, int kb_ld,
-                                    const float* pb, int pb_ld, const int32_t* key_len,
-                                    AttnContextDev ctx, void* out, int B, int T, int H, int* err,
-                                    int num_sms, cudaStream_t stream) {
+cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* u,
+                                    const float* v, const int32_t* key_len, AttnContextDev ctx,
+                                    void* out, int B, int T, int H, int* err, int num_sms,
+                                    cudaStream_t stream) {
   (void)num_sms;
   static bool attr = false;
   if (!attr) {
@@ -468,22 +488,15 @@ cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float*
     attr = true;
   }
   const int D = H * kDh;
-  const int off = relpos_attn_pb_off(T);
-  CUtensorMap map_qkv, map_p, map_kb, map_pb;
+  CUtensorMap map_qkv, map_p;
   if (!make_tmap_3d(&map_qkv, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3ull * D, T, B,
                     3ull * D * 2, 3ull * D * 2 * T, 64, kTile, 1, true) ||
       !make_tmap_2d(&map_p, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, 2ull * T - 1,
-                    static_cast<uint64_t>(D) * 2, 64, kTile, true) ||
-      !make_tmap_2d(&map_kb, kb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, T,
-                    static_cast<uint64_t>(B) * H, static_cast<uint64_t>(kb_ld) * 4, kTile, 1,
-                    false) ||
-      !make_tmap_2d(&map_pb, pb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 2ull * T - 1 + off, H,
-                    static_cast<uint64_t>(pb_ld) * 4, kTile, 1, false))
+                    static_cast<uint64_t>(D) * 2, 64, kTile, true))
     return cudaErrorInvalidValue;
   dim3 grid((T + kTile - 1) / kTile, H, B);
   relpos_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      map_qkv, map_p, map_kb, map_pb, key_len, ctx, static_cast<__nv_bfloat16*>(out), T, H, off,
-      err);
+      map_qkv, map_p, u, v, key_len, ctx, static_cast<__nv_bfloat16*>(out), T, H, err);
   return cudaGetLastError();
 }
 

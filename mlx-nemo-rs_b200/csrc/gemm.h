@@ -21,30 +21,19 @@ bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, 
                   uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2,
                   bool swizzle128);
 
-// Optional epilogue: for output columns [col0, col0 + heads*128), write the
-// dot of each row's 128-column head block (after the bias) with vec[0 ..
-// heads*128) to out[(b*heads + head) * ld + t + off], where row m = b *
-// rows_per_batch + t.  vec == null disables it.
-struct HeadDot {
-  const float* vec = nullptr;
-  float* out = nullptr;
-  int col0 = 0, heads = 0, rows_per_batch = 1, ld = 0, off = 0;
-};
-
 // ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
 // x map: bf16 [M, K], box (64, 128), swizzle 128.  W map: bf16 [N, K], box
 // (64, 256), swizzle 128.  Requires K % 64 == 0 and N % 32 == 0.
 int gemm_smem_bytes();
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
-                             int K, int num_sms, int* err, cudaStream_t stream,
-                             HeadDot hd = HeadDot());
+                             int K, int num_sms, int* err, cudaStream_t stream);
 // Quantised W: MLX affine 8-bit, group 64: wq [N, K] bytes (the packed u32
 // words read as little-endian bytes), scales/biases bf16 [N, K/64].
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
-                           cudaStream_t stream, HeadDot hd = HeadDot());
+                           cudaStream_t stream);
 
 // ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
@@ -59,20 +48,17 @@ cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
 // ---- offline fused rel-pos attention, bf16, tcgen05 ----
 // qkv: [B, T, 3*D] bf16 (q | k | v along the last axis, heads of 128);
 // p: [P, D] bf16 projected positions for relative positions (T-1)..-(T-1)
-// (P = 2T-1); u, v: [H, 128] f32 position biases; key_len: [B] int32 (key j
+// (P = 2T-1); u, v: [H, 128] f32 position biases (bf16-rounded values, added
+// to q in bf16 inside the kernel); key_len: [B] int32 (key j
 // visible iff j < max(key_len[b], 1)) or null; context (left, right, chunked,
 // has); out: [B, T, D] bf16.
 struct AttnContextDev {
   int has, left, right, chunked;
 };
-// kb: f32 [B*H, kb_ld] with kb[b*H+h][j] = u_h . k_j; pb: f32 [H, pb_ld]
-// with pb[h][r + pb_off] = v_h . p_r, pb_off = (4 - T % 4) % 4 (keeps the
-// kernel's TMA row offsets 16-byte aligned); kb_ld, pb_ld multiples of 4.
-int relpos_attn_pb_off(int T);
-cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* kb, int kb_ld,
-                                    const float* pb, int pb_ld, const int32_t* key_len,
-                                    AttnContextDev ctx, void* out, int B, int T, int H, int* err,
-                                    int num_sms, cudaStream_t stream);
+cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* u,
+                                    const float* v, const int32_t* key_len, AttnContextDev ctx,
+                                    void* out, int B, int T, int H, int* err, int num_sms,
+                                    cudaStream_t stream);
 
 // ---- generic CUDA-core attention (fp32 module dtype, any head_dim <= 128) ----
 // q [B,Tq,D] (row stride ldq), k/v [B,Tk,D] (row strides ldk, ldv), p

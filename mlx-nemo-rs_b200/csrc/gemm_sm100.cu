@@ -15,10 +15,7 @@
 // Warp roles (bf16: 6 warps; quantised: 10 warps):
 //   warp 0      TMA producer for X (and W in the bf16 case)
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2-5   epilogue: TMEM -> registers -> +bias -> bf16 -> global, and
-//               optionally a per-head dot of each output row with a vector
-//               (u . k_j and v . p_r for the attention kernel, whose biased
-//               queries (q+u).k = q.k + u.k split this way)
+//   warps 2-5   epilogue: TMEM -> registers -> +bias -> bf16 -> global
 //   warps 6-9   (quantised only) u8 -> bf16 dequantising producer for W
 #include "gemm.h"
 #include "sm100.cuh"
@@ -54,8 +51,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                    const __nv_bfloat16* __restrict__ qs,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ bias, // [N] or null
-                   __nv_bfloat16* __restrict__ y, int ldy, int M, int N, int K, HeadDot hd,
-                   int* err) {
+                   __nv_bfloat16* __restrict__ y, int ldy, int M, int N, int K, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -172,7 +168,6 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
       tc_fence_after();
       const int m = m0 + row_in_tile;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
-      float hsum = 0.f;  // running per-head dot for the head-dot epilogue
 #pragma unroll 1
       for (int c = 0; c < kBN; c += 32) {
         uint32_t r[32];
@@ -181,8 +176,6 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         const int n = n0 + c;
         if (m < M && n < N) {
           uint32_t packed[16];
-          const int hcol = n - hd.col0;
-          const bool dot = hd.vec && hcol >= 0 && hcol < hd.heads * 128;
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             float lo = __uint_as_float(r[2 * e]);
@@ -191,17 +184,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
               lo += __bfloat162float(bias[n + 2 * e]);
               hi += __bfloat162float(bias[n + 2 * e + 1]);
             }
-            if (dot) {
-              const float2 hv = __ldg(reinterpret_cast<const float2*>(hd.vec + hcol + 2 * e));
-              hsum = fmaf(lo, hv.x, fmaf(hi, hv.y, hsum));
-            }
             packed[e] = pack_bf16x2(lo, hi);
-          }
-          if (dot && (hcol & 127) == 96) {  // last 32 columns of a head
-            const int head = hcol >> 7;
-            const int bb = m / hd.rows_per_batch, tt = m - bb * hd.rows_per_batch;
-            hd.out[static_cast<size_t>(bb * hd.heads + head) * hd.ld + tt + hd.off] = hsum;
-            hsum = 0.f;
           }
           uint4* dst = reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * ldy + n);
 #pragma unroll
@@ -282,7 +265,7 @@ int gemm_smem_bytes() { return static_cast<int>(kSmemBytes); }
 
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
-                             int K, int num_sms, int* err, cudaStream_t stream, HeadDot hd) {
+                             int K, int num_sms, int* err, cudaStream_t stream) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<false>,
@@ -294,15 +277,14 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, nullptr, nullptr,
-                                                           nullptr, bias, y, ldy, M, N, K, hd,
-                                                           err);
+                                                           nullptr, bias, y, ldy, M, N, K, err);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
-                           cudaStream_t stream, HeadDot hd) {
+                           cudaStream_t stream) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<true>,
@@ -314,7 +296,7 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, wq, qs, qb, bias, y, ldy,
-                                                          M, N, K, hd, err);
+                                                          M, N, K, err);
   return cudaGetLastError();
 }
 
