@@ -64,17 +64,25 @@ constexpr uint32_t kOffK = kOffQv + kTileBytes;
 constexpr uint32_t kOffP = kOffK + kTileBytes;
 constexpr uint32_t kOffV = kOffP + kTileBytes;       // 2 slots
 constexpr uint32_t kOffPr = kOffV + 2 * kTileBytes;
-constexpr uint32_t kOffBar = kOffPr + kTileBytes;
+constexpr uint32_t kOffX = kOffPr + kTileBytes;      // [2 parity][2 halves][128] f32
+constexpr uint32_t kOffBar = kOffX + 2048;
 
 struct Bars {
-  uint64_t q, prep, p0, kp, v[2], s, sfree, p, o, x1, x2;
+  uint64_t q, prep, p0, kp, v[2], s, sfree, p, o, x;
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kOffBar + sizeof(Bars);
+constexpr size_t kSmemBytes = kOffBar + sizeof(Bars);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr uint32_t kStageTx = 2 * kTileBytes;  // K tile + P chunk
+
+// 2^x with the MUFU approximation (flush-to-zero; inputs here are <= 8).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // Bounded wait whose outcome is the same for every lane of the warp (the
 // tcgen05 loads/stores that follow are warp-collective).
@@ -120,10 +128,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const float* __restrict__ pos_u, const float* __restrict__ pos_v,
                        const int32_t* __restrict__ key_len, AttnContextDev ctx,
                        __nv_bfloat16* __restrict__ out, int T, int H, int* err) {
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  // Dynamic shared memory starts 1024-byte aligned when, as here, the kernel
+  // has no static shared memory; checked, since the swizzle atoms need it.
+  extern __shared__ __align__(1024) uint8_t smem[];
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(err, 0, kDevBadArgs);
+    return;
+  }
   uint8_t* sQu = smem + kOffQu;
   uint8_t* sQv = smem + kOffQv;
   uint8_t* sK = smem + kOffK;
@@ -168,8 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->sfree, kSoftmaxThreads);
     mbar_init(&bars->p, kSoftmaxThreads);
     mbar_init(&bars->o, 1);
-    mbar_init(&bars->x1, kSoftmaxThreads);
-    mbar_init(&bars->x2, kSoftmaxThreads);
+    mbar_init(&bars->x, kSoftmaxThreads);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -283,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // keys every row of this warp sees: no per-element mask inside it
     const int wlo = __reduce_max_sync(0xffffffffu, rlo);
     const int whi = __reduce_min_sync(0xffffffffu, rhi);
-    float* xbuf = reinterpret_cast<float*>(sPr + kTileBytes - 1024);  // [2][128] exchange
+    float* xbuf = reinterpret_cast<float*>(smem + kOffX);  // [parity][half][row] exchange
     uint32_t xphase = 0;
     float m_ref = -INFINITY;  // log2-domain maximum the output is scaled by
     float l = 0.f;            // this thread's share of the row sum
@@ -324,7 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int jt = j0 + t * kTile;
       // ---- pass 1: 64 scores (log2 domain, masked) into registers
       float sc[64];
-      float mx = -INFINITY;
+      float mxp[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mxp[e] = -INFINITY;
 #pragma unroll
       for (int sub = 0; sub < 2; ++sub) {
         const int jl0 = 64 * kh + 32 * sub;
@@ -357,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float v = (__uint_as_float(sr[e]) + a[e]) * scale_log2;
-            mx = fmaxf(mx, v);
+            mxp[e & 7] = fmaxf(mxp[e & 7], v);
             sc[32 * sub + e] = v;
           }
         } else {
@@ -366,22 +379,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int j = jb + e;
             float v = (__uint_as_float(sr[e]) + a[e]) * scale_log2;
             v = (j >= rlo && j < rhi) ? v : -INFINITY;
-            mx = fmaxf(mx, v);
+            mxp[e & 7] = fmaxf(mxp[e & 7], v);
             sc[32 * sub + e] = v;
           }
         }
       }
+      float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       tc_fence_before();
       mbar_arrive(&bars->sfree);  // S and BD slot t&1 may be overwritten
       // ---- previous P.V done: O is stable, the probability buffer is free
       if (t > 0 && !warp_wait(&bars->o, par ^ 1, err, kDevTimeoutMma)) { ok = false; break; }
-      // ---- swap row maxima with the other key half's thread
-      xbuf[kh * 128 + il] = mx;
-      mbar_arrive(&bars->x1);
-      if (!warp_wait(&bars->x1, xphase, err, kDevTimeoutEpi)) { ok = false; break; }
-      mx = fmaxf(mx, xbuf[(kh ^ 1) * 128 + il]);
-      mbar_arrive(&bars->x2);
-      if (!warp_wait(&bars->x2, xphase, err, kDevTimeoutEpi)) { ok = false; break; }
+      // ---- swap row maxima with the other key half's thread; the two parity
+      // buffers let one sync per tile suffice (a thread cannot write the
+      // buffer of parity p again before its partner passed this sync)
+      xbuf[xphase * 256 + kh * 128 + il] = mx;
+      mbar_arrive(&bars->x);
+      if (!warp_wait(&bars->x, xphase, err, kDevTimeoutEpi)) { ok = false; break; }
+      mx = fmaxf(mx, xbuf[xphase * 256 + (kh ^ 1) * 128 + il]);
       xphase ^= 1;
       float alpha = 1.f;
       if (mx > m_ref + 8.f) {  // also taken when m_ref is -inf and mx finite
@@ -406,21 +421,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // ---- pass 2: probabilities -> shared memory (bf16 A operand of P.V)
-      const bool live = m_ref != -INFINITY;
+      // a row that has seen no key yet keeps m_ref = -inf: subtract 0 so
+      // its -inf scores give exp2(-inf) = 0 rather than NaN
+      const float msub = m_ref == -INFINITY ? 0.f : m_ref;
       uint8_t* prow = sPr + kh * kHalf;
+      float lp[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) lp[e] = 0.f;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = live ? exp2f(sc[8 * ch + 2 * e] - m_ref) : 0.f;
-          const float p1 = live ? exp2f(sc[8 * ch + 2 * e + 1] - m_ref) : 0.f;
-          l += p0 + p1;
+          const float p0 = fast_exp2(sc[8 * ch + 2 * e] - msub);
+          const float p1 = fast_exp2(sc[8 * ch + 2 * e + 1] - msub);
+          lp[2 * e] += p0;
+          lp[2 * e + 1] += p1;
           pk[e] = pack_bf16x2(p0, p1);
         }
         *reinterpret_cast<uint4*>(prow + sw128_offset(il, ch)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+      l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p);
@@ -430,11 +452,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float inv = 0.f;
     if (ok && nt > 0) {
       tc_fence_after();
-      xbuf[kh * 128 + il] = l;
-      mbar_arrive(&bars->x1);
-      ok = warp_wait(&bars->x1, xphase, err, kDevTimeoutEpi);
+      xbuf[xphase * 256 + kh * 128 + il] = l;
+      mbar_arrive(&bars->x);
+      ok = warp_wait(&bars->x, xphase, err, kDevTimeoutEpi);
       if (ok) {
-        const float lt = l + xbuf[(kh ^ 1) * 128 + il];
+        const float lt = l + xbuf[xphase * 256 + (kh ^ 1) * 128 + il];
         inv = lt > 0.f ? 1.f / lt : 0.f;
       }
     }
