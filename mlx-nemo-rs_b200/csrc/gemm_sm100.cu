@@ -15,7 +15,9 @@
 // Warp roles (bf16: 6 warps; quantised: 10 warps):
 //   warp 0      TMA producer for X (and W in the bf16 case)
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2-5   epilogue: TMEM -> registers -> +bias -> bf16 -> global
+//   warps 2-5   epilogue: TMEM -> registers -> +bias -> bf16 -> a 32 x 64
+//               swizzled shared-memory slab per warp (double-buffered) ->
+//               TMA tensor store (full-sector writes; M/N tails clipped)
 //   warps 6-9   (quantised only) u8 -> bf16 dequantising producer for W
 #include "gemm.h"
 #include "sm100.cuh"
@@ -41,12 +43,16 @@ struct GemmSmem {
   int abort;
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * (kABytes + kBBytes) + 256;
+constexpr uint32_t kSlabBytes = 32 * 128;  // 32 rows x 64 bf16, 128B-swizzled
+constexpr uint32_t kEpiBytes = 4 * 2 * kSlabBytes;  // 4 warps x 2 buffers
+constexpr size_t kSmemBytes =
+    1024 /*align slack*/ + kStages * (kABytes + kBBytes) + kEpiBytes + 256;
 
 template <bool kQuant>
 __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ CUtensorMap map_w,
+                   const __grid_constant__ CUtensorMap map_y,  // [M, N] bf16, box (64, 32)
                    const uint8_t* __restrict__ wq,         // quantised: [N, K] bytes
                    const __nv_bfloat16* __restrict__ qs,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
@@ -57,7 +63,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sA = base;
   uint8_t* sB = base + kStages * kABytes;
-  GemmSmem* ss = reinterpret_cast<GemmSmem*>(sB + kStages * kBBytes);
+  uint8_t* sE = sB + kStages * kBBytes;
+  GemmSmem* ss = reinterpret_cast<GemmSmem*>(sE + kEpiBytes);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -154,8 +161,10 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   } else if (warp < kEpiWarp0 + 4) {
     // --------------------------------------------------------- epilogue
     const int quad = warp & 3;
-    const int row_in_tile = quad * 32 + lane;
+    uint8_t* slab = sE + (warp - kEpiWarp0) * 2 * kSlabBytes;
+    if (lane == 0) prefetch_tensormap(&map_y);
     int tc = 0;
+    uint32_t nslab = 0;
     for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tc) {
       const int m0 = (tile / tiles_n) * kBM;
       const int n0 = (tile % tiles_n) * kBN;
@@ -166,37 +175,49 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         break;
       }
       tc_fence_after();
-      const int m = m0 + row_in_tile;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
 #pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
+      for (int c = 0; c < kBN; c += 64) {
+        uint32_t r[64];
+        tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+        tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
         tmem_ld_wait();
-        const int n = n0 + c;
-        if (m < M && n < N) {
-          uint32_t packed[16];
+        if (n0 + c >= N) continue;  // whole slab past N (warp-uniform)
+        uint8_t* sb = slab + (nslab & 1) * kSlabBytes;
+        // the store issued two slabs ago must have finished reading sb
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float lo = __uint_as_float(r[2 * e]);
-            float hi = __uint_as_float(r[2 * e + 1]);
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int col = ch * 8 + 2 * e;
+            float lo = __uint_as_float(r[col]);
+            float hi = __uint_as_float(r[col + 1]);
             if (bias) {
-              lo += __bfloat162float(bias[n + 2 * e]);
-              hi += __bfloat162float(bias[n + 2 * e + 1]);
+              const int n = n0 + c + col;
+              lo += n < N ? __bfloat162float(bias[n]) : 0.f;
+              hi += n + 1 < N ? __bfloat162float(bias[n + 1]) : 0.f;
             }
-            packed[e] = pack_bf16x2(lo, hi);
+            pk[e] = pack_bf16x2(lo, hi);
           }
-          uint4* dst = reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * ldy + n);
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
-                                packed[4 * v + 3]);
+          *reinterpret_cast<uint4*>(sb + sw128_offset(lane, ch)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_y, sb, n0 + c, m0 + quad * 32);
+          bulk_commit();
+        }
+        ++nslab;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ss->tempty[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // stores read shared memory until done
   } else if (kQuant) {
     // ------------------------------------------ dequantising W producer
     // 4 threads per W row, 16 bytes (16 weights) each; 32 rows per pass.
@@ -263,6 +284,13 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
 
 int gemm_smem_bytes() { return static_cast<int>(kSmemBytes); }
 
+namespace {
+bool make_y_map(CUtensorMap* map, __nv_bfloat16* y, int ldy, int M, int N) {
+  return make_tmap_2d(map, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M,
+                      static_cast<uint64_t>(ldy) * 2, 64, 32, true);
+}
+}  // namespace
+
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
                              int K, int num_sms, int* err, cudaStream_t stream) {
@@ -276,7 +304,9 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
   }
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, nullptr, nullptr,
+  CUtensorMap map_y;
+  if (!make_y_map(&map_y, y, ldy, M, N)) return cudaErrorInvalidValue;
+  gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, map_y, nullptr, nullptr,
                                                            nullptr, bias, y, ldy, M, N, K, err);
   return cudaGetLastError();
 }
@@ -295,8 +325,10 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
   }
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, wq, qs, qb, bias, y, ldy,
-                                                          M, N, K, err);
+  CUtensorMap map_y;
+  if (!make_y_map(&map_y, y, ldy, M, N)) return cudaErrorInvalidValue;
+  gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, map_y, wq, qs, qb, bias, y,
+                                                          ldy, M, N, K, err);
   return cudaGetLastError();
 }
 
