@@ -55,6 +55,7 @@ constexpr int kTile = 128;
 constexpr uint32_t kHalf = kTile * 64 * 2;  // 16 KB: 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kHalf;  // 32 KB: 128 rows x 128 bf16
 constexpr int kSoftmaxThreads = 256;
+constexpr int kSoftmaxWarps = kSoftmaxThreads / 32;
 constexpr int kThreads = kSoftmaxThreads + 32;
 
 // shared-memory map (offsets from a 1024-aligned base)
@@ -82,6 +83,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// One arrival per warp, after every lane's prior writes (each lane fenced
+// what it needs before calling this).
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
 // Bounded wait whose outcome is the same for every lane of the warp (the
@@ -171,16 +179,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q, 1);
-    mbar_init(&bars->prep, kSoftmaxThreads);
+    mbar_init(&bars->prep, kSoftmaxWarps);
     mbar_init(&bars->p0, 1);
     mbar_init(&bars->kp, 1);
     mbar_init(&bars->v[0], 1);
     mbar_init(&bars->v[1], 1);
     mbar_init(&bars->s, 1);
-    mbar_init(&bars->sfree, kSoftmaxThreads);
-    mbar_init(&bars->p, kSoftmaxThreads);
+    mbar_init(&bars->sfree, kSoftmaxWarps);
+    mbar_init(&bars->p, kSoftmaxWarps);
     mbar_init(&bars->o, 1);
-    mbar_init(&bars->x, kSoftmaxThreads);
+    mbar_init(&bars->x, kSoftmaxWarps);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -325,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async_smem();
       }
-      mbar_arrive(&bars->prep);
+      warp_arrive(&bars->prep);
     }
     for (int t = 0; t < nt && ok; ++t) {
       const uint32_t par = t & 1;
@@ -387,14 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                        fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       tc_fence_before();
-      mbar_arrive(&bars->sfree);  // S and BD slot t&1 may be overwritten
+      warp_arrive(&bars->sfree);  // S and BD slot t&1 may be overwritten
       // ---- previous P.V done: O is stable, the probability buffer is free
       if (t > 0 && !warp_wait(&bars->o, par ^ 1, err, kDevTimeoutMma)) { ok = false; break; }
       // ---- swap row maxima with the other key half's thread; the two parity
       // buffers let one sync per tile suffice (a thread cannot write the
       // buffer of parity p again before its partner passed this sync)
       xbuf[xphase * 256 + kh * 128 + il] = mx;
-      mbar_arrive(&bars->x);
+      warp_arrive(&bars->x);
       if (!warp_wait(&bars->x, xphase, err, kDevTimeoutEpi)) { ok = false; break; }
       mx = fmaxf(mx, xbuf[xphase * 256 + (kh ^ 1) * 128 + il]);
       xphase ^= 1;
@@ -445,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->p);
+      warp_arrive(&bars->p);
     }
     // ---- epilogue: out = O / l over both key halves
     if (ok && nt > 0) ok = warp_wait(&bars->o, (nt - 1) & 1, err, kDevTimeoutMma);
@@ -453,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && nt > 0) {
       tc_fence_after();
       xbuf[xphase * 256 + kh * 128 + il] = l;
-      mbar_arrive(&bars->x);
+      warp_arrive(&bars->x);
       ok = warp_wait(&bars->x, xphase, err, kDevTimeoutEpi);
       if (ok) {
         const float lt = l + xbuf[xphase * 256 + (kh ^ 1) * 128 + il];

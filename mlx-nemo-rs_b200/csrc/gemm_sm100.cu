@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ss->full[s], kQuant ? 1 + 128 : 1);
+      mbar_init(&ss->full[s], kQuant ? 1 + 4 : 1);  // TMA + one arrival per dequant warp
       mbar_init(&ss->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
               make_uint4(outw[4], outw[5], outw[6], outw[7]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&ss->full[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ss->full[s]);
       }
     }
   }

@@ -58,14 +58,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Suspend-time hint of one try_wait (ns): the waiting thread sleeps until
+// the phase completes or the hint expires, instead of spinning and taking
+// issue slots from the warps that do the work.
+constexpr uint32_t kTryWaitHintNs = 100000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitHintNs)
       : "memory");
   return ok != 0;
 }
@@ -77,7 +82,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
+    if ((it & 7u) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }
