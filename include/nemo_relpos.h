@@ -178,6 +178,25 @@ int nrp_attn_forward(nrp_attn* attn, void* stream, const void* x, int batch, int
                      const void* pos_emb, const int32_t* lengths,
                      const nrp_att_context* context, void* out);
 
+/* No counterpart in the reference.  The same computation as nrp_attn_forward
+ * (same arguments and outputs), for callers that cannot let the library
+ * allocate device memory -- e.g. an audio thread with a real-time deadline,
+ * which cannot wait on cudaMalloc's device synchronisation, or a process
+ * whose device memory is handed out by another runtime's allocator.  Its
+ * intermediate tensors live in a fixed 32 MiB array in the library's device
+ * memory (held by every GPU that loads the library, until exit), so it
+ * allocates nothing; sizes whose intermediates need more
+ * (about 8 KB per frame plus 2 KB per position at d_model 1024, bf16) are
+ * rejected with NRP_ERR_INVALID.  The module's parameters must already be on
+ * the device (one nrp_attn_forward or nrp_attn_forward_with_cache call
+ * uploads them); otherwise NRP_ERR_INVALID.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  All calls share the array: calls
+ * whose work overlaps on the GPU race and must be serialised by the caller. */
+int nrp_attn_forward_noalloc(nrp_attn* attn, void* stream, const void* x, int batch, int seq_len,
+                             const void* pos_emb, const int32_t* lengths,
+                             const nrp_att_context* context, void* out);
+
 /* ---------------------------------------------------- streaming caches */
 /* One layer's share of EncoderCache (src/asr/streaming/core.rs:117-127):
  * the attention-input cache last_channel[layer] ([batch, cache_len,

@@ -20,7 +20,8 @@ NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]
-SOURCES = ["gemm_sm100.cu", "attn_sm100.cu", "attn_simt.cu", "kernels_misc.cu", "api.cpp"]
+SOURCES = ["gemm_sm100.cu", "attn_sm100.cu", "attn_simt.cu", "kernels_misc.cu", "noalloc.cu",
+           "api.cpp"]
 
 
 def _stale(out, deps):

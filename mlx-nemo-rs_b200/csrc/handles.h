@@ -1,0 +1,102 @@
+// handles.h -- definitions of the C ABI's opaque handles and the small
+// host-side types they hold (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "../../include/nemo_relpos.h"
+
+namespace nrp {
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  cudaError_t ensure(size_t n) {
+    if (n <= bytes && p) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&p, n ? n : 16);
+    if (e == cudaSuccess) bytes = n;
+    return e;
+  }
+  template <typename T>
+  T* as() const { return static_cast<T*>(p); }
+};
+
+struct Linear {
+  bool loaded = false;
+  bool quant = false;
+  int bits = 8, group = 64;
+  std::vector<float> w;        // f32 master [N, K] (standard)
+  std::vector<uint32_t> wq;    // packed [N, K*bits/32] (quantised)
+  std::vector<float> qs, qb;   // [N, K/group]
+  std::vector<float> bias;     // [N] or empty
+};
+
+// Optional per-launch timing: CUDA events recorded on the launching stream
+// around each kernel the library launches, summed per kernel kind.
+struct ProfRec {
+  int kind;
+  cudaEvent_t start, stop;
+};
+
+// Sets this thread's nrp_last_error() message and returns `code`.
+int report_error(int code, const char* msg);
+
+}  // namespace nrp
+
+struct nrp_context {
+  int device = 0;
+  int num_sms = 148;
+  int* d_err = nullptr;
+  bool prof = false;
+  std::vector<nrp::ProfRec> recs;
+  std::vector<cudaEvent_t> pool;
+  double prof_ms[NRP_KERNEL_KINDS] = {};
+  int64_t prof_n[NRP_KERNEL_KINDS] = {};
+};
+
+struct nrp_attn {
+  nrp_context* ctx = nullptr;
+  int D = 0, H = 0, dh = 0;
+  int use_bias = 1;
+  int dtype = NRP_DTYPE_F32;
+  int cache_drop = 0;
+  nrp::Linear lin[5];
+  std::vector<float> u, v;
+  bool dirty = true;
+  // device parameters in the module dtype
+  bool qkv_quant = false;
+  nrp::DevBuf w_qkv, s_qkv, z_qkv, b_qkv;  // weights (or u8 codes), scales, zero-points, bias
+  bool has_b_qkv = false;
+  nrp::DevBuf w_out, s_out, z_out, b_out;
+  bool out_quant = false, has_b_out = false;
+  nrp::DevBuf w_pos, s_pos, z_pos;
+  bool pos_quant = false;
+  nrp::DevBuf u_dev, v_dev;
+  // workspace
+  nrp::DevBuf qkv, cbuf, pbuf;
+  // projected streaming positions, reused while pos_len is unchanged
+  int spos_len = -1;
+  nrp::DevBuf spos;
+};
+
+struct nrp_cache {
+  nrp_attn* attn = nullptr;
+  int B = 0, C = 0, D = 0, dtype = 0;
+  int head = 0;  // ring slot of the oldest frame
+  nrp::DevBuf kc, vc, hc;
+  nrp::DevBuf tmp;
+};
+

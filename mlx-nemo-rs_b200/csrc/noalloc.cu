@@ -1,0 +1,170 @@
+// noalloc.cu -- nrp_attn_forward_noalloc: the rel-pos MHA forward without any
+// device allocation.
+//
+// nrp_attn_forward keeps its intermediate tensors (the fused q|k|v
+// projections, the projected positions and the attention context) in
+// buffers it grows with cudaMalloc.  Some callers cannot let a library call
+// cudaMalloc: an audio thread with a real-time deadline cannot wait on it
+// (it synchronises the device), and a host process whose device memory is
+// handed out by another runtime's allocator has none to give.  For them
+// this entry point takes the same inputs and output as nrp_attn_forward and
+// places its intermediates in g_static_scratch, a fixed array in the
+// library's own device memory, so the call allocates nothing.
+//
+// The array is kStaticScratchBytes (32 MiB).  Every GPU that loads this
+// library holds it until the process exits, and every call shares it: a call
+// overwrites what the previous call left there (it clears nothing because
+// every byte it reads is written earlier in the same call), and two calls
+// whose work overlaps on the GPU (different streams, or different modules on
+// one device) race on it.  Callers serialise such calls themselves.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "gemm.h"
+#include "handles.h"
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
+int report(int code, const char* fmt, long long a = 0, long long b = 0) {
+  char buf[256];
+  snprintf(buf, sizeof buf, fmt, a, b);
+  return nrp::report_error(code, buf);
+}
+
+// Device address of g_static_scratch on `device` (the current device).  The
+// host-side name of the array is not a device address, so it is looked up
+// once per device with cudaGetSymbolAddress and cached.
+int scratch_address(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return report(NRP_ERR_UNSUPPORTED, "device %lld beyond the scratch table", device);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return nrp::report_error(NRP_ERR_CUDA, cudaGetErrorString(e));
+    g_scratch_addr[device] = p;
+  }
+  *out = g_scratch_addr[device];
+  return NRP_OK;
+}
+
+#define TRY_CUDA(expr)                                                         \
+  do {                                                                         \
+    const cudaError_t e_ = (expr);                                             \
+    if (e_ != cudaSuccess) return nrp::report_error(NRP_ERR_CUDA, cudaGetErrorString(e_)); \
+  } while (0)
+
+// y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias), as nrp_attn_forward runs
+// its projections, with nothing allocated.
+int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
+           const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
+           void* y, int ldy) {
+  if (M <= 0) return NRP_OK;
+  if (dtype == NRP_DTYPE_F32) {
+    TRY_CUDA(nrp::launch_gemm_f32(static_cast<const float*>(x), M, K, static_cast<const float*>(w),
+                                  N, static_cast<const float*>(bias), static_cast<float*>(y), ldy,
+                                  st));
+    return NRP_OK;
+  }
+  if (quant && M <= 16) {
+    TRY_CUDA(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
+                               static_cast<const uint8_t*>(w),
+                               static_cast<const __nv_bfloat16*>(qs),
+                               static_cast<const __nv_bfloat16*>(qb),
+                               static_cast<const __nv_bfloat16*>(bias),
+                               static_cast<__nv_bfloat16*>(y), ldy, N, st));
+    return NRP_OK;
+  }
+  CUtensorMap mx, mw;
+  if (!nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
+                         static_cast<uint64_t>(K) * 2, 64, 128, true))
+    return report(NRP_ERR_CUDA, "TMA descriptor for x rejected");
+  if (quant) {
+    TRY_CUDA(nrp::launch_gemm_q8(mx, static_cast<const uint8_t*>(w),
+                                 static_cast<const __nv_bfloat16*>(qs),
+                                 static_cast<const __nv_bfloat16*>(qb),
+                                 static_cast<const __nv_bfloat16*>(bias),
+                                 static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
+                                 ctx->d_err, st));
+    return NRP_OK;
+  }
+  if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
+                         static_cast<uint64_t>(K) * 2, 64, 256, true))
+    return report(NRP_ERR_CUDA, "TMA descriptor for W rejected");
+  TRY_CUDA(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
+                                 static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
+                                 ctx->d_err, st));
+  return NRP_OK;
+}
+
+}  // namespace
+
+extern "C" int nrp_attn_forward_noalloc(nrp_attn* a, void* stream, const void* x, int B, int T,
+                                        const void* pos_emb, const int32_t* lengths,
+                                        const nrp_att_context* context, void* out) {
+  if (!a || !x || !pos_emb || !out) return report(NRP_ERR_INVALID, "null argument");
+  if (B <= 0 || T <= 0) return report(NRP_ERR_INVALID, "empty input [%lld, %lld]", B, T);
+  if (a->dirty)
+    return report(NRP_ERR_INVALID,
+                  "the module's parameters are not on the device yet: one nrp_attn_forward or "
+                  "nrp_attn_forward_with_cache call (which allocates them) must come first");
+  nrp_context* ctx = a->ctx;
+  int cur = -1;
+  TRY_CUDA(cudaGetDevice(&cur));
+  if (cur != ctx->device) TRY_CUDA(cudaSetDevice(ctx->device));
+  const int D = a->D, P = 2 * T - 1;
+  const size_t es = a->dtype == NRP_DTYPE_BF16 ? 2 : 4;
+  const size_t BT = static_cast<size_t>(B) * T;
+  const size_t qkv_bytes = round256(BT * 3 * D * es);
+  const size_t ctx_bytes = round256(BT * D * es);
+  const size_t pos_bytes = round256(static_cast<size_t>(P) * D * es);
+  const size_t need = qkv_bytes + ctx_bytes + pos_bytes;
+  if (need > kStaticScratchBytes)
+    return report(NRP_ERR_INVALID,
+                  "batch x seq_len needs %lld bytes of intermediates, more than the %lld-byte "
+                  "static scratch of nrp_attn_forward_noalloc (use nrp_attn_forward)",
+                  static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes));
+  void* base = nullptr;
+  int rc = scratch_address(ctx->device, &base);
+  if (rc) return rc;
+  uint8_t* qkv = static_cast<uint8_t*>(base);
+  uint8_t* cbuf = qkv + qkv_bytes;
+  uint8_t* pbuf = cbuf + ctx_bytes;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant, a->s_qkv.p,
+              a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, qkv, 3 * D);
+  if (rc) return rc;
+  rc = linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p,
+              D, nullptr, pbuf, D);
+  if (rc) return rc;
+  nrp::AttnContextDev cd{0, -1, -1, 0};
+  if (context) cd = {1, context->left, context->right, context->chunked};
+  if (a->dtype == NRP_DTYPE_BF16) {
+    TRY_CUDA(nrp::launch_relpos_attn_bf16(qkv, pbuf, a->u_dev.as<float>(), a->v_dev.as<float>(),
+                                          lengths, cd, cbuf, B, T, a->H, ctx->d_err,
+                                          ctx->num_sms, st));
+  } else {
+    const float* q = reinterpret_cast<const float*>(qkv);
+    nrp::StreamMaskDev none{};
+    TRY_CUDA(nrp::launch_relpos_attn_f32(q, 3 * D, q + D, 3 * D, q + 2 * D, 3 * D,
+                                         reinterpret_cast<const float*>(pbuf),
+                                         a->u_dev.as<float>(), a->v_dev.as<float>(), lengths, cd,
+                                         none, reinterpret_cast<float*>(cbuf), B, T, T, D, a->H,
+                                         st));
+  }
+  return linear(ctx, st, a->dtype, cbuf, static_cast<int>(BT), D, a->w_out.p, a->out_quant,
+                a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr, out, D);
+}
