@@ -267,7 +267,7 @@ int sync_params(nrp_attn* a) {
 // either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
 int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
                const void* w, bool quant, const void* qs, const void* qb, int N,
-               const void* bias, void* y, int ldy) {
+               const void* bias, void* y, int ldy, const nrp::RowTiling& rt = nrp::RowTiling()) {
   if (M <= 0) return ok();
   if (dtype == NRP_DTYPE_F32) {
     ProfScope ps(ctx, NRP_KERNEL_GEMM_F32, st);
@@ -289,9 +289,13 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
     return ok();
   }
   CUtensorMap mx, mw;
-  if (!nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
-                         static_cast<uint64_t>(K) * 2, 64, 128, true))
-    return fail(NRP_ERR_CUDA, "TMA descriptor for x rejected");
+  const bool xmap_ok =
+      rt.T > 0 ? nrp::make_tmap_3d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, rt.T, rt.B,
+                                   static_cast<uint64_t>(K) * 2,
+                                   static_cast<uint64_t>(K) * 2 * rt.T, 64, 128, 1, true)
+               : nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
+                                   static_cast<uint64_t>(K) * 2, 64, 128, true);
+  if (!xmap_ok) return fail(NRP_ERR_CUDA, "TMA descriptor for x rejected");
   if (quant) {
     ProfScope ps(ctx, NRP_KERNEL_GEMM_Q8, st);
     CUDA_TRY(nrp::launch_gemm_q8(mx, static_cast<const uint8_t*>(w),
@@ -299,7 +303,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                  static_cast<const __nv_bfloat16*>(qb),
                                  static_cast<const __nv_bfloat16*>(bias),
                                  static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                 ctx->d_err, st));
+                                 ctx->d_err, st, rt));
   } else {
     if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
                            static_cast<uint64_t>(K) * 2, 64, 256, true))
@@ -307,7 +311,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
     ProfScope ps(ctx, NRP_KERNEL_GEMM_BF16, st);
     CUDA_TRY(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
                                    static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                   ctx->d_err, st));
+                                   ctx->d_err, st, rt));
   }
   return ok();
 }
@@ -639,11 +643,16 @@ int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, con
   CUDA_TRY(a->pbuf.ensure(static_cast<size_t>(P) * D * es));
   nrp::AttnContextDev cd{0, -1, -1, 0};
   if (context) cd = {1, context->left, context->right, context->chunked};
+  // With a key padding mask the row tiles of the per-frame GEMMs follow the
+  // utterances and skip frames past each length (their rows are zeros:
+  // padded rows are unspecified in the reference, conformer.rs:1590-1593).
+  nrp::RowTiling rows;
+  if (lengths && B <= 256) rows = {lengths, T, B};
   if (a->dtype == NRP_DTYPE_BF16) {
     // 478-480: q, k, v in one GEMM; 493: linear_pos
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
-                    3 * D);
+                    3 * D, rows);
     if (rc) return rc;
     rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
                     a->z_pos.p, D, nullptr, a->pbuf.p, D);
@@ -671,7 +680,7 @@ int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, con
   // 565: linear_out
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
-                    out, D);
+                    out, D, rows);
 }
 
 // -------------------------------------------------------------- caches

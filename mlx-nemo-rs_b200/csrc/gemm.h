@@ -21,19 +21,31 @@ bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, 
                   uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2,
                   bool swizzle128);
 
+// Row tiling of a GEMM whose M rows are B utterances of T frames (T > 0):
+// row tiles never straddle utterances, and with len != null a tile whose
+// first frame is at or past len[b] (device int32 [B]) is skipped -- its
+// output rows are written as zeros.  T == 0: flat rows.  In the batched
+// form the x map is 3-D [B][T][K] with box (64, 128, 1).
+struct RowTiling {
+  const int32_t* len = nullptr;
+  int T = 0;
+  int B = 0;
+};
+
 // ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
 // x map: bf16 [M, K], box (64, 128), swizzle 128.  W map: bf16 [N, K], box
 // (64, 256), swizzle 128.  Requires K % 64 == 0 and N % 32 == 0.
 int gemm_smem_bytes();
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
-                             int K, int num_sms, int* err, cudaStream_t stream);
+                             int K, int num_sms, int* err, cudaStream_t stream,
+                             RowTiling rt = RowTiling());
 // Quantised W: MLX affine 8-bit, group 64: wq [N, K] bytes (the packed u32
 // words read as little-endian bytes), scales/biases bf16 [N, K/64].
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
-                           cudaStream_t stream);
+                           cudaStream_t stream, RowTiling rt = RowTiling());
 
 // ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,

@@ -45,8 +45,10 @@ struct GemmSmem {
 
 constexpr uint32_t kSlabBytes = 32 * 128;  // 32 rows x 64 bf16, 128B-swizzled
 constexpr uint32_t kEpiBytes = 4 * 2 * kSlabBytes;  // 4 warps x 2 buffers
-constexpr size_t kSmemBytes =
-    1024 /*align slack*/ + kStages * (kABytes + kBBytes) + kEpiBytes + 256;
+constexpr int kMaxBatch = 256;  // batched tiling: utterances per GEMM
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * (kABytes + kBBytes) + kEpiBytes +
+                              256 + 4 * (kMaxBatch + 1);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 template <bool kQuant>
 __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
@@ -57,7 +59,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                    const __nv_bfloat16* __restrict__ qs,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ bias, // [N] or null
-                   __nv_bfloat16* __restrict__ y, int ldy, int M, int N, int K, int* err) {
+                   __nv_bfloat16* __restrict__ y, int ldy, int M, int N, int K, RowTiling rt,
+                   int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -68,11 +71,62 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int tiles_m = (M + kBM - 1) / kBM;
+  // Row tiles: flat over M, or (batched) per utterance so a tile never
+  // straddles two.  In the batched form with lengths, the persistent tile
+  // list holds every row tile that has a valid frame first, then the tiles
+  // wholly past their utterance's length (which only write zeros), so the
+  // skipped work is not left as holes in the static assignment.
+  const bool batched = rt.T > 0;
+  const int tpb = batched ? (rt.T + kBM - 1) / kBM : 0;
+  const int tiles_m = batched ? rt.B * tpb : (M + kBM - 1) / kBM;
   const int tiles_n = (N + kBN - 1) / kBN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = K / kBK;
-
+  int* live_pre = reinterpret_cast<int*>(sE + kEpiBytes + sizeof(GemmSmem));  // [B+1]
+  int live_m = tiles_m;
+  if (batched && rt.len) {
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int b = 0; b < rt.B; ++b) {
+        live_pre[b] = acc;
+        const int L = rt.len[b];
+        acc += L <= 0 ? 0 : min(tpb, (L + kBM - 1) / kBM);
+      }
+      live_pre[rt.B] = acc;
+    }
+    __syncthreads();
+    live_m = live_pre[rt.B];
+  }
+  // list index -> (first row of the tile, its utterance); true = zero-fill tile
+  auto tile_rows = [&](int tile, int& r0, int& bb) -> bool {
+    const int tm = tile / tiles_n;
+    if (!batched) {
+      r0 = tm * kBM;
+      bb = 0;
+      return false;
+    }
+    if (!rt.len) {
+      bb = tm / tpb;
+      r0 = (tm - bb * tpb) * kBM;
+      return false;
+    }
+    if (tm < live_m) {  // k-th live row tile
+      int b = 0;
+      while (live_pre[b + 1] <= tm) ++b;
+      bb = b;
+      r0 = (tm - live_pre[b]) * kBM;
+      return false;
+    }
+    int k = tm - live_m, b = 0;  // k-th dead row tile
+    for (;; ++b) {
+      const int dead = tpb - (live_pre[b + 1] - live_pre[b]);
+      if (k < dead) break;
+      k -= dead;
+    }
+    bb = b;
+    r0 = (live_pre[b + 1] - live_pre[b] + k) * kBM;
+    return true;
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&ss->full[s], kQuant ? 1 + 4 : 1);  // TMA + one arrival per dequant warp
@@ -104,7 +158,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile / tiles_n) * kBM;
+        int m0, bb;
+        if (tile_rows(tile, m0, bb)) continue;
         const int n0 = (tile % tiles_n) * kBN;
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % kStages;
@@ -114,7 +169,10 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             break;
           }
           mbar_arrive_expect_tx(&ss->full[s], kQuant ? kABytes : kABytes + kBBytes);
-          tma_load_2d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0);
+          if (batched)
+            tma_load_3d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0, bb);
+          else
+            tma_load_2d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0);
           if (!kQuant) tma_load_2d(sB + s * kBBytes, &map_w, &ss->full[s], kb * kBK, n0);
         }
       }
@@ -125,9 +183,12 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
       constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN, 0, 0);
       uint32_t it = 0;
       int tc = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tc) {
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int m0, bb;
+        if (tile_rows(tile, m0, bb)) continue;
         const int buf = tc & 1;
         const uint32_t use = tc >> 1;
+        ++tc;
         if (!mbar_wait(&ss->tempty[buf], (use & 1) ^ 1, err, kDevTimeoutEpi)) {
           *abort_flag = 1;
           break;
@@ -165,23 +226,32 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     if (lane == 0) prefetch_tensormap(&map_y);
     int tc = 0;
     uint32_t nslab = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tc) {
-      const int m0 = (tile / tiles_n) * kBM;
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      int m0, bb;
+      const bool skip = tile_rows(tile, m0, bb);
       const int n0 = (tile % tiles_n) * kBN;
       const int buf = tc & 1;
       const uint32_t use = tc >> 1;
-      if (!mbar_wait(&ss->tfull[buf], use & 1, err, kDevTimeoutMma)) {
-        *abort_flag = 1;
-        break;
+      if (!skip) {
+        ++tc;
+        if (!mbar_wait(&ss->tfull[buf], use & 1, err, kDevTimeoutMma)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
       }
-      tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
 #pragma unroll 1
       for (int c = 0; c < kBN; c += 64) {
         uint32_t r[64];
-        tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(r));
-        tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
-        tmem_ld_wait();
+        if (!skip) {
+          tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+          tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) r[e] = 0u;
+        }
         if (n0 + c >= N) continue;  // whole slab past N (warp-uniform)
         uint8_t* sb = slab + (nslab & 1) * kSlabBytes;
         // the store issued two slabs ago must have finished reading sb
@@ -195,7 +265,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             const int col = ch * 8 + 2 * e;
             float lo = __uint_as_float(r[col]);
             float hi = __uint_as_float(r[col + 1]);
-            if (bias) {
+            if (bias && !skip) {
               const int n = n0 + c + col;
               lo += n < N ? __bfloat162float(bias[n]) : 0.f;
               hi += n + 1 < N ? __bfloat162float(bias[n + 1]) : 0.f;
@@ -208,14 +278,19 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&map_y, sb, n0 + c, m0 + quad * 32);
+          if (batched)
+            tma_store_3d(&map_y, sb, n0 + c, m0 + quad * 32, bb);
+          else
+            tma_store_2d(&map_y, sb, n0 + c, m0 + quad * 32);
           bulk_commit();
         }
         ++nslab;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ss->tempty[buf]);
+      if (!skip) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ss->tempty[buf]);
+      }
     }
     if (lane == 0) bulk_wait_all();  // stores read shared memory until done
   } else if (kQuant) {
@@ -227,6 +302,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     const int kgroups = K / 64;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      int m0, bb;
+      if (tile_rows(tile, m0, bb)) continue;
       const int n0 = (tile % tiles_n) * kBN;
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         const int s = it % kStages;
@@ -286,15 +363,24 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
 int gemm_smem_bytes() { return static_cast<int>(kSmemBytes); }
 
 namespace {
-bool make_y_map(CUtensorMap* map, __nv_bfloat16* y, int ldy, int M, int N) {
+bool make_y_map(CUtensorMap* map, __nv_bfloat16* y, int ldy, int M, int N, const RowTiling& rt) {
+  if (rt.T > 0)
+    return make_tmap_3d(map, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, rt.T, rt.B,
+                        static_cast<uint64_t>(ldy) * 2, static_cast<uint64_t>(ldy) * 2 * rt.T, 64,
+                        32, 1, true);
   return make_tmap_2d(map, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M,
                       static_cast<uint64_t>(ldy) * 2, 64, 32, true);
+}
+int grid_size(int M, int N, const RowTiling& rt, int num_sms) {
+  const int tiles_m = rt.T > 0 ? rt.B * ((rt.T + kBM - 1) / kBM) : (M + kBM - 1) / kBM;
+  const int tiles = tiles_m * ((N + kBN - 1) / kBN);
+  return tiles < num_sms ? tiles : num_sms;
 }
 }  // namespace
 
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
-                             int K, int num_sms, int* err, cudaStream_t stream) {
+                             int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<false>,
@@ -303,19 +389,19 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  const int grid = tiles < num_sms ? tiles : num_sms;
+  if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
+  const int grid = grid_size(M, N, rt, num_sms);
   CUtensorMap map_y;
-  if (!make_y_map(&map_y, y, ldy, M, N)) return cudaErrorInvalidValue;
+  if (!make_y_map(&map_y, y, ldy, M, N, rt)) return cudaErrorInvalidValue;
   gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, map_y, nullptr, nullptr,
-                                                           nullptr, bias, y, ldy, M, N, K, err);
+                                                           nullptr, bias, y, ldy, M, N, K, rt, err);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, RowTiling rt) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<true>,
@@ -324,12 +410,12 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  const int grid = tiles < num_sms ? tiles : num_sms;
+  if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
+  const int grid = grid_size(M, N, rt, num_sms);
   CUtensorMap map_y;
-  if (!make_y_map(&map_y, y, ldy, M, N)) return cudaErrorInvalidValue;
+  if (!make_y_map(&map_y, y, ldy, M, N, rt)) return cudaErrorInvalidValue;
   gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, map_y, wq, qs, qb, bias, y,
-                                                          ldy, M, N, K, err);
+                                                          ldy, M, N, K, rt, err);
   return cudaGetLastError();
 }
 
