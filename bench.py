@@ -35,6 +35,9 @@ LEN_LO, LEN_HI = 375, 750
 WORKLOAD = ("BASELINE config 1: offline batched full-context rel-pos MHA layer, bf16, "
             "B=16 T=750 d_model=1024 8x128 heads, lengths U[375,750] with key padding mask")
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) per launch from one ncu capture of this workload,
+# per kernel kind (profiles/relpos_attn_kernel_config1.md); None = not captured.
+TRAFFIC_BYTES = {"attn_sm100": 62.479e6 + 4.606e6, "gemm_bf16": None}
 
 
 def workload(seed: int):
@@ -325,14 +328,17 @@ def main():
         flop_per_launch = per_kind_flops[dominant] * args.steps / n
         achieved = flop_per_launch / (ms / n / 1e3) / 1e12
         roof = {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": tflops_peak,
-                "unit": "TFLOP/s", "frac": achieved / tflops_peak, "traffic": None,
+                "unit": "TFLOP/s", "frac": achieved / tflops_peak,
+                "traffic": TRAFFIC_BYTES.get(dominant),
                 "peak_source": peak_src,
                 "algorithmic_flop_per_launch": flop_per_launch}
     attn_roof = None
     if "attn_sm100" in prof:
         n, ms = prof["attn_sm100"]
         a = attn_f * args.steps / n / (ms / n / 1e3) / 1e12
-        attn_roof = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s"}
+        attn_roof = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s",
+                     "traffic": TRAFFIC_BYTES["attn_sm100"],
+                     "algorithmic_flop_per_launch": attn_f * args.steps / n}
     gemm_roof = None
     if "gemm_bf16" in prof:
         n, ms = prof["gemm_bf16"]
