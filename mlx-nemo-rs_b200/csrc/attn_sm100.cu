@@ -307,26 +307,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;  // log2-domain maximum the output is scaled by
     float l = 0.f;            // this thread's share of the row sum
     bool ok = true;
-    // ---- q+u and q+v tiles (bf16 adds, attention.rs:506-508), once per CTA
+    // ---- q+u and q+v tiles (bf16 adds, attention.rs:506-508), once per CTA.
+    // This thread's 64 u and v values are fetched before the wait for the Q
+    // tile, so their latency overlaps the TMA.
     if (nt > 0) {
+      const int tid = threadIdx.x;  // 0..255: row tid/2, 64-column half tid&1
+      const int row = tid >> 1, half = tid & 1;
+      float4 u4[16], v4[16];
+      const float4* ug = reinterpret_cast<const float4*>(pos_u + h * kDh + half * 64);
+      const float4* vg = reinterpret_cast<const float4*>(pos_v + h * kDh + half * 64);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        u4[k] = __ldg(ug + k);
+        v4[k] = __ldg(vg + k);
+      }
       ok = warp_wait(&bars->q, 0, err, kDevTimeoutLoad);
       if (ok) {
-        const int tid = threadIdx.x;  // 0..255: row tid/2, 64-column half tid&1
-        const int row = tid >> 1, half = tid & 1;
-        const float* u = pos_u + h * kDh + half * 64;
-        const float* v = pos_v + h * kDh + half * 64;
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
           const uint32_t off = half * kHalf + sw128_offset(row, ch);
           const uint4 q = *reinterpret_cast<const uint4*>(sQu + off);
           const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+          const float uu[8] = {u4[2 * ch].x, u4[2 * ch].y, u4[2 * ch].z, u4[2 * ch].w,
+                               u4[2 * ch + 1].x, u4[2 * ch + 1].y, u4[2 * ch + 1].z,
+                               u4[2 * ch + 1].w};
+          const float vv[8] = {v4[2 * ch].x, v4[2 * ch].y, v4[2 * ch].z, v4[2 * ch].w,
+                               v4[2 * ch + 1].x, v4[2 * ch + 1].y, v4[2 * ch + 1].z,
+                               v4[2 * ch + 1].w};
           uint32_t wu[4], wv[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[e]));
-            const int c = ch * 8 + 2 * e;
-            wu[e] = pack_bf16x2(f.x + u[c], f.y + u[c + 1]);
-            wv[e] = pack_bf16x2(f.x + v[c], f.y + v[c + 1]);
+            wu[e] = pack_bf16x2(f.x + uu[2 * e], f.y + uu[2 * e + 1]);
+            wv[e] = pack_bf16x2(f.x + vv[2 * e], f.y + vv[2 * e + 1]);
           }
           *reinterpret_cast<uint4*>(sQu + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
           *reinterpret_cast<uint4*>(sQv + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
