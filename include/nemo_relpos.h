@@ -225,6 +225,68 @@ int nrp_attn_forward_with_cache(nrp_attn* attn, void* stream, const void* x, int
                                 int seq_len, const void* pos_emb, nrp_cache* cache, int filled,
                                 int valid, const nrp_att_context* context, void* out);
 
+/* ------------------------------------- sequence split over several GPUs */
+/* Long-form windowed attention with the sequence cut into contiguous
+ * segments, one per GPU (one process per GPU).  The reference runs one
+ * device and has no counterpart; each rank computes exactly the rows
+ * RelPositionMultiHeadAttention::forward (attention.rs:446-573) gives for its
+ * segment, with the keys and values of the frames its window reaches on the
+ * neighbouring segments (the halo) received over NCCL. */
+typedef struct nrp_halo nrp_halo;
+#define NRP_HALO_ID_BYTES 128
+
+/* Segment of `rank`: [start, start + len) of seq_len frames cut into nranks
+ * pieces of ceil(seq_len / nranks) (the last one ragged; len may be 0). */
+int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len);
+
+/* The halo plan of `rank` under `context` (NULL: full context): its
+ * segment, the frames it receives from rank-1 (halo_left) and rank+1
+ * (halo_right), and the frames it sends them (its first send_prev and last
+ * send_next frames).  The halo of a segment [s, e) is the part of
+ * [s + dmin, e + dmax) within the sequence outside it, where dmin..dmax are
+ * the key offsets j - i the context makes visible.  NRP_ERR_UNSUPPORTED
+ * when a rank would have no frames or a halo would reach past a neighbour. */
+typedef struct {
+  int start, len;
+  int halo_left, halo_right;
+  int send_prev, send_next;
+} nrp_seq_plan;
+int nrp_seq_shard_plan(int seq_len, int nranks, int rank, const nrp_att_context* context,
+                       nrp_seq_plan* out);
+
+/* The communicator's unique id (ncclGetUniqueId), made on one rank and
+ * handed to every rank by the caller's own means (a store, a broadcast). */
+int nrp_halo_unique_id(unsigned char id[NRP_HALO_ID_BYTES]);
+
+/* Joins the communicator of nranks ranks (one per process and device, the
+ * context's device).  NCCL (libnccl.so.2) is loaded on first use.  Every
+ * wait of the communicator's host side is bounded by timeout_ms: a rank
+ * that does not join or answer in time makes the call fail (NRP_ERR_DEVICE)
+ * and the communicator is aborted. */
+int nrp_halo_comm_create(nrp_context* ctx, const unsigned char id[NRP_HALO_ID_BYTES], int rank,
+                         int nranks, int timeout_ms, nrp_halo** out);
+int nrp_halo_comm_destroy(nrp_halo* halo);
+
+/* Waits up to the communicator's timeout for the work queued on `stream`;
+ * if it has not finished (a peer that never sent its halo), aborts the
+ * communicator -- which ends its kernels -- and returns NRP_ERR_DEVICE.
+ * An aborted communicator fails every later call. */
+int nrp_halo_comm_check(nrp_halo* halo, void* stream);
+
+/* This rank's share of nrp_attn_forward on [batch, seq_len, d_model]:
+ * x_local device [batch, len, d_model] = frames [start, start + len) of the
+ * sequence (nrp_seq_shard); pos_emb device [2*seq_len-1, d_model], the whole
+ * table (only the rows the window reaches are read); lengths device int32
+ * [batch] in frames of the whole sequence, or NULL; context: a window that
+ * reaches no further than the neighbouring segments (NRP_ERR_UNSUPPORTED
+ * otherwise, and for full context); out_local device [batch, len, d_model].
+ * bf16 only.  Every rank calls it with the same batch, seq_len and context,
+ * in the same order. */
+int nrp_attn_forward_seq_sharded(nrp_attn* attn, nrp_halo* halo, void* stream,
+                                 const void* x_local, int batch, int seq_len,
+                                 const void* pos_emb, const int32_t* lengths,
+                                 const nrp_att_context* context, void* out_local);
+
 /* --------------------------------------------------- linear primitives */
 /* LinearLayer::forward, Standard arm (quantization.rs:128-135) on device
  * buffers: y[M,N] = x[M,K] . w[N,K]^T (+ bias[N]), dtype f32 or bf16 for

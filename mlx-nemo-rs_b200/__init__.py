@@ -54,6 +54,11 @@ class _AttCtx(C.Structure):
     _fields_ = [("left", C.c_int32), ("right", C.c_int32), ("chunked", C.c_int32)]
 
 
+class _SeqPlan(C.Structure):
+    _fields_ = [("start", C.c_int32), ("len", C.c_int32), ("halo_left", C.c_int32),
+                ("halo_right", C.c_int32), ("send_prev", C.c_int32), ("send_next", C.c_int32)]
+
+
 class _StreamCfg(C.Structure):
     _fields_ = [("chunk_size", C.c_int32 * 2), ("shift_size", C.c_int32 * 2),
                 ("cache_drop_size", C.c_int32), ("last_channel_cache_size", C.c_int32),
@@ -105,6 +110,13 @@ def lib():
             "nrp_attn_forward_with_cache": ([vp, vp, vp, i, i, vp, vp, i, i, vp, vp], i),
             "nrp_linear": ([vp, vp, i, vp, i, i, vp, i, vp, vp], i),
             "nrp_qlinear": ([vp, vp, vp, i, i, vp, vp, vp, i, i, i, vp, vp], i),
+            "nrp_seq_shard": ([i, i, i, vp, vp], i),
+            "nrp_seq_shard_plan": ([i, i, i, vp, vp], i),
+            "nrp_halo_unique_id": ([vp], i),
+            "nrp_halo_comm_create": ([vp, vp, i, i, i, vp], i),
+            "nrp_halo_comm_destroy": ([vp], i),
+            "nrp_halo_comm_check": ([vp, vp], i),
+            "nrp_attn_forward_seq_sharded": ([vp, vp, vp, vp, i, i, vp, vp, vp, vp], i),
             "nrp_profile_enable": ([vp, i], i),
             "nrp_profile_reset": ([vp], i),
             "nrp_profile_read": ([vp, i, vp, vp], i),
@@ -456,6 +468,122 @@ class RelPositionMultiHeadAttention:
             int(cache_filled_len), T if valid_len is None else int(valid_len),
             C.byref(c) if c is not None else None, out.data_ptr()))
         return out
+
+
+    def forward_seq_sharded(self, x_local, pos_emb, seq_len: int, halo: "HaloComm",
+                            context: Optional[AttentionContext] = None,
+                            key_mask: Optional[KeyPaddingMask] = None, out=None):
+        """This rank's rows of forward() on a sequence of seq_len frames cut
+        into one segment per rank (seq_shard): x_local [B, len, D] holds the
+        segment's frames, pos_emb the whole [2*seq_len-1, D] table, key_mask
+        the whole-sequence lengths.  No reference counterpart (the reference
+        runs on one device); every rank calls it in the same order."""
+        import torch
+        B, T, D = x_local.shape
+        pe = pos_emb.reshape(-1, D)
+        if out is None:
+            out = torch.empty_like(x_local)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_attn_forward_seq_sharded(
+            self.handle, halo.handle, _stream(), x_local.data_ptr(), B, int(seq_len),
+            pe.data_ptr(), key_mask.lengths.data_ptr() if key_mask is not None else None,
+            C.byref(c) if c is not None else None, out.data_ptr()))
+        return out
+
+
+# ------------------------------------------- sequence split (several GPUs)
+@dataclass
+class SeqPlan:
+    """A rank's segment [start, start + len) and its halo: frames received
+    from rank-1 / rank+1 and frames sent to them (nrp_seq_shard_plan)."""
+    start: int
+    len: int
+    halo_left: int
+    halo_right: int
+    send_prev: int
+    send_next: int
+
+
+def seq_shard(seq_len: int, nranks: int, rank: int) -> Tuple[int, int]:
+    """(start, len) of rank's segment: ceil(seq_len / nranks) frames each,
+    the last one ragged."""
+    s, n = C.c_int(), C.c_int()
+    _check(lib().nrp_seq_shard(seq_len, nranks, rank, C.byref(s), C.byref(n)))
+    return s.value, n.value
+
+
+def seq_shard_plan(seq_len: int, nranks: int, rank: int,
+                   context: Optional[AttentionContext] = None) -> SeqPlan:
+    p = _SeqPlan()
+    c = context._c() if context is not None else None
+    _check(lib().nrp_seq_shard_plan(seq_len, nranks, rank, C.byref(c) if c is not None else None,
+                                    C.byref(p)))
+    return SeqPlan(p.start, p.len, p.halo_left, p.halo_right, p.send_prev, p.send_next)
+
+
+class HaloComm:
+    """The NCCL communicator of a sequence split (nrp_halo): one rank per
+    process and GPU.  Every host-side wait is bounded by timeout_ms; a peer
+    that does not join or answer in time aborts the communicator and raises
+    NrpError(NRP_ERR_DEVICE)."""
+
+    ID_BYTES = 128
+
+    def __init__(self, rank: int, nranks: int, unique_id: bytes,
+                 ctx: Optional[Context] = None, timeout_ms: int = 30000):
+        self.handle = None
+        self.ctx = ctx or Context.default()
+        if len(unique_id) != self.ID_BYTES:
+            raise NrpError(NRP_ERR_INVALID, "unique id must be 128 bytes")
+        uid = (C.c_ubyte * self.ID_BYTES).from_buffer_copy(unique_id)
+        h = C.c_void_p()
+        _check(lib().nrp_halo_comm_create(self.ctx.handle, uid, rank, nranks, timeout_ms,
+                                          C.byref(h)))
+        self.handle = h
+        self.rank, self.nranks = rank, nranks
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_ubyte * HaloComm.ID_BYTES)()
+        _check(lib().nrp_halo_unique_id(buf))
+        return bytes(buf)
+
+    @staticmethod
+    def share_unique_id(group=None) -> bytes:
+        """Makes the id on the group's first rank and broadcasts it over
+        torch.distributed (any backend)."""
+        import torch.distributed as dist
+        first = dist.get_global_rank(group, 0) if group is not None else 0
+        obj = [HaloComm.unique_id() if dist.get_rank() == first else None]
+        dist.broadcast_object_list(obj, src=first, group=group)
+        return obj[0]
+
+    @classmethod
+    def from_process_group(cls, ctx: Optional[Context] = None, group=None,
+                           timeout_ms: int = 30000) -> "HaloComm":
+        import torch.distributed as dist
+        uid = cls.share_unique_id(group)
+        return cls(dist.get_rank(group), dist.get_world_size(group), uid, ctx, timeout_ms)
+
+    def plan(self, seq_len: int, context: Optional[AttentionContext] = None) -> SeqPlan:
+        return seq_shard_plan(seq_len, self.nranks, self.rank, context)
+
+    def check(self, stream=None):
+        """Waits (bounded) for `stream`; raises NRP_ERR_DEVICE if a peer never
+        answered (the communicator is then aborted)."""
+        _check(lib().nrp_halo_comm_check(self.handle,
+                                         stream if stream is not None else _stream()))
+
+    def close(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check(lib().nrp_halo_comm_destroy(h))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class AttentionCache:

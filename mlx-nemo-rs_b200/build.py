@@ -21,7 +21,23 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]
 SOURCES = ["gemm_sm100.cu", "attn_sm100.cu", "attn_simt.cu", "kernels_misc.cu", "noalloc.cu",
-           "api.cpp"]
+           "api.cpp", "halo.cpp"]
+
+
+def _nccl_include():
+    """Directory of nccl.h for halo.cpp (types and the config initializer
+    only: the library is loaded with dlopen at run time).  The header of the
+    NCCL that torch ships comes first, as that is the copy a torch process
+    has loaded."""
+    import sysconfig
+    for base in (sysconfig.get_paths()["purelib"], sysconfig.get_paths()["platlib"]):
+        d = os.path.join(base, "nvidia", "nccl", "include")
+        if os.path.exists(os.path.join(d, "nccl.h")):
+            return d
+    for d in ("/usr/include", "/usr/local/cuda/include"):
+        if os.path.exists(os.path.join(d, "nccl.h")):
+            return d
+    raise RuntimeError("nccl.h not found (needed to build halo.cpp)")
 
 
 def _stale(out, deps):
@@ -41,6 +57,8 @@ def _compile(src, force):
     cmd = [NVCC, *ARCH, *FLAGS, "-c", path, "-o", obj]
     if src.endswith(".cpp"):
         cmd = [NVCC, *FLAGS, "-x", "c++", "-c", path, "-o", obj]
+        if src == "halo.cpp":
+            cmd[1:1] = ["-I", _nccl_include()]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"compile failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
@@ -57,7 +75,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
             if log.strip():
                 print(log)
     if force or _stale(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
+        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

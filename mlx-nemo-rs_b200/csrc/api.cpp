@@ -278,7 +278,8 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   }
   if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)
     return fail(NRP_ERR_UNSUPPORTED, "bf16 linear needs K %% 64 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
-  if (quant && M <= 16) {
+  // (the GEMV writes flat rows: not for an output with its own batch stride)
+  if (quant && M <= 16 && rt.y_bstride == 0) {
     ProfScope ps(ctx, NRP_KERNEL_QGEMV, st);
     CUDA_TRY(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
                                static_cast<const uint8_t*>(w),
@@ -654,12 +655,21 @@ int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, con
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
                     3 * D, rows);
     if (rc) return rc;
-    rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
-                    a->z_pos.p, D, nullptr, a->pbuf.p, D);
+    // linear_pos only over the P rows the context's relative positions
+    // reach (all 2T-1 without a window; 257 for a (128, 128) window)
+    nrp::AttnGeom g = nrp::full_geom(T, D);
+    int dmin, dmax;
+    nrp::visible_offsets(cd, T, dmin, dmax);
+    g.p_base = T - 1 + dmin;
+    g.p_rows = dmax - dmin + 1;
+    rc = run_linear(ctx, st, a->dtype,
+                    static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * es,
+                    g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr,
+                    a->pbuf.p, D);
     if (rc) return rc;
     ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
     CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->u_dev.as<float>(),
-                                          a->v_dev.as<float>(), lengths, cd, a->cbuf.p, B, T,
+                                          a->v_dev.as<float>(), lengths, cd, g, a->cbuf.p, B,
                                           a->H, ctx->d_err, ctx->num_sms, st));
   } else {
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
@@ -681,6 +691,175 @@ int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, con
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
                     out, D, rows);
+}
+
+// ------------------------------------------------------ sequence split
+int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len) {
+  if (!start || !len) return fail(NRP_ERR_INVALID, "null output");
+  if (seq_len <= 0 || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(NRP_ERR_INVALID, "seq_len %d, rank %d of %d", seq_len, rank, nranks);
+  const int seg = (seq_len + nranks - 1) / nranks;
+  const long long s = std::min<long long>(seq_len, static_cast<long long>(rank) * seg);
+  *start = static_cast<int>(s);
+  *len = static_cast<int>(std::min<long long>(seq_len, s + seg) - s);
+  return ok();
+}
+
+int nrp_seq_shard_plan(int T, int n, int r, const nrp_att_context* context, nrp_seq_plan* out) {
+  if (!out) return fail(NRP_ERR_INVALID, "null output");
+  int s = 0, len = 0, s_last = 0, len_last = 0;
+  int rc = nrp_seq_shard(T, n, r, &s, &len);
+  if (rc) return rc;
+  nrp_seq_shard(T, n, n - 1, &s_last, &len_last);
+  if (len_last <= 0)
+    return fail(NRP_ERR_UNSUPPORTED, "%d frames leave some of %d ranks without frames", T, n);
+  nrp::AttnContextDev cd{0, -1, -1, 0};
+  if (context) cd = {1, context->left, context->right, context->chunked};
+  int dmin, dmax;
+  nrp::visible_offsets(cd, T, dmin, dmax);
+  // the part of [s0 + dmin, e0 + dmax) within the sequence outside [s0, e0)
+  auto left_halo = [&](int s0) { return s0 - std::max(0, std::min(s0, s0 + dmin)); };
+  auto right_halo = [&](int e0) { return std::max(e0, std::min(T, e0 + dmax)) - e0; };
+  const int e = s + len;
+  nrp_seq_plan p{s, len, left_halo(s), right_halo(e), 0, 0};
+  int tmp = 0, len_prev = 0, len_next = 0;
+  if (r > 0) {
+    nrp_seq_shard(T, n, r - 1, &tmp, &len_prev);
+    p.send_prev = right_halo(s);  // rank r-1's right halo: my first frames
+  }
+  if (r + 1 < n) {
+    nrp_seq_shard(T, n, r + 1, &tmp, &len_next);
+    p.send_next = left_halo(e);  // rank r+1's left halo: my last frames
+  }
+  if (p.halo_left > len_prev || p.halo_right > len_next || p.send_prev > len ||
+      p.send_next > len)
+    return fail(NRP_ERR_UNSUPPORTED,
+                "the attention window (key offsets %d..%d) reaches past the neighbouring "
+                "segments of %d frames", dmin, dmax, len);
+  *out = p;
+  return ok();
+}
+
+int nrp_attn_forward_seq_sharded(nrp_attn* a, nrp_halo* h, void* stream, const void* x, int B,
+                                 int T, const void* pos_emb, const int32_t* lengths,
+                                 const nrp_att_context* context, void* out) {
+  if (!a || !h || !x || !pos_emb || !out) return fail(NRP_ERR_INVALID, "null argument");
+  if (B <= 0 || T <= 0) return fail(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  if (h->dead) return fail(NRP_ERR_DEVICE, "the halo communicator was aborted");
+  nrp_context* ctx = a->ctx;
+  if (h->ctx->device != ctx->device)
+    return fail(NRP_ERR_INVALID, "halo communicator on device %d, module on %d",
+                h->ctx->device, ctx->device);
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  int rc = sync_params(a);
+  if (rc) return rc;
+  if (a->dtype != NRP_DTYPE_BF16)
+    return fail(NRP_ERR_UNSUPPORTED, "the sequence-split forward runs in bf16");
+  if (B > 256) return fail(NRP_ERR_UNSUPPORTED, "sequence split supports batch <= 256");
+  nrp_seq_plan plan;
+  rc = nrp_seq_shard_plan(T, h->nranks, h->rank, context, &plan);
+  if (rc) return rc;
+  const int D = a->D;
+  const int s = plan.start, len = plan.len, e = s + len;
+  const int hl = plan.halo_left, hr = plan.halo_right;
+  const int send_prev = plan.send_prev, send_next = plan.send_next;
+  nrp::AttnContextDev cd{0, -1, -1, 0};
+  if (context) cd = {1, context->left, context->right, context->chunked};
+  int dmin, dmax;
+  nrp::visible_offsets(cd, T, dmin, dmax);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int tbuf = hl + len + hr;
+  const size_t row = static_cast<size_t>(B) * 3 * D * 2;  // one time-major frame, all utterances
+  CUDA_TRY(h->buf.ensure(static_cast<size_t>(tbuf) * row));
+  CUDA_TRY(a->cbuf.ensure(static_cast<size_t>(B) * len * D * 2));
+  nrp::AttnGeom g;
+  g.Tg = T;
+  g.tbuf = tbuf;
+  g.base = s - hl;
+  g.qkv_ts = static_cast<int64_t>(B) * 3 * D;
+  g.qkv_bs = 3 * D;
+  g.q_lo = s;
+  g.q_hi = e;
+  g.k_lo = s - hl;
+  g.k_hi = e + hr;
+  g.p_base = T - 1 + dmin;
+  g.p_rows = dmax - dmin + 1;
+  g.out_base = s;
+  g.out_bs = static_cast<int64_t>(len) * D;
+  CUDA_TRY(a->pbuf.ensure(static_cast<size_t>(g.p_rows) * D * 2));
+  // linear_pos over the window's P rows (attention.rs:493)
+  rc = run_linear(ctx, st, a->dtype,
+                  static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * 2,
+                  g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr,
+                  a->pbuf.p, D);
+  if (rc) return rc;
+  // q|k|v of the local frames into the buffer's middle rows (478-480)
+  nrp::RowTiling rt;
+  rt.T = len;
+  rt.B = B;
+  rt.y_bstride = 3 * D;
+  uint8_t* buf = static_cast<uint8_t*>(h->buf.p);
+  rc = run_linear(ctx, st, a->dtype, x, B * len, D, a->w_qkv.p, a->qkv_quant, a->s_qkv.p,
+                  a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr,
+                  buf + static_cast<size_t>(hl) * row, B * 3 * D, rt);
+  if (rc) return rc;
+  const bool exchange = hl + hr + send_prev + send_next > 0;
+  if (exchange) {
+    const size_t send_off[2] = {static_cast<size_t>(hl) * row,
+                                static_cast<size_t>(hl + len - send_next) * row};
+    const size_t send_bytes[2] = {static_cast<size_t>(send_prev) * row,
+                                  static_cast<size_t>(send_next) * row};
+    const size_t recv_off[2] = {0, static_cast<size_t>(hl + len) * row};
+    const size_t recv_bytes[2] = {static_cast<size_t>(hl) * row, static_cast<size_t>(hr) * row};
+    rc = nrp::halo_exchange(h, send_off, send_bytes, recv_off, recv_bytes, st);
+    if (rc) return rc;
+  }
+  // Query tiles (128 frames from s) whose keys are all local run while the
+  // halo is in flight; the others after it has arrived.
+  const int ntiles = (len + 127) / 128;
+  int first = 0, last = ntiles;  // local tiles [first, last)
+  if (hl > 0) first = std::min(ntiles, (-dmin + 127) / 128);
+  if (hr > 0) last = std::max(0, (len - dmax) / 128);
+  // A launch that runs while the halo is in flight sees only the segment's
+  // own frames: its tensor map starts at the segment and ends with it, so the
+  // key tiles that overhang the segment load zeros instead of halo rows that
+  // are being written (or were never written) -- masked keys still meet the
+  // P.V product with probability 0, which must not see a NaN.
+  auto attend = [&](int q_lo, int q_hi, bool local_only) -> int {
+    if (q_hi <= q_lo) return ok();
+    nrp::AttnGeom gi = g;
+    gi.q_lo = q_lo;
+    gi.q_hi = q_hi;
+    const void* qkv = h->buf.p;
+    if (local_only) {
+      gi.base = s;
+      gi.tbuf = len;
+      gi.k_lo = s;
+      gi.k_hi = e;
+      qkv = buf + static_cast<size_t>(hl) * row;
+    }
+    ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
+    CUDA_TRY(nrp::launch_relpos_attn_bf16(qkv, a->pbuf.p, a->u_dev.as<float>(),
+                                          a->v_dev.as<float>(), lengths, cd, gi, a->cbuf.p, B,
+                                          a->H, ctx->d_err, ctx->num_sms, st));
+    return ok();
+  };
+  if (!exchange || first >= last) {
+    if (exchange) CUDA_TRY(cudaStreamWaitEvent(st, h->done, 0));
+    rc = attend(s, e, false);
+    if (rc) return rc;
+  } else {
+    const int mid_lo = s + 128 * first, mid_hi = std::min(e, s + 128 * last);
+    rc = attend(mid_lo, mid_hi, true);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamWaitEvent(st, h->done, 0));
+    rc = attend(s, mid_lo, false);
+    if (!rc) rc = attend(mid_hi, e, false);
+    if (rc) return rc;
+  }
+  // linear_out (565)
+  return run_linear(ctx, st, a->dtype, a->cbuf.p, B * len, D, a->w_out.p, a->out_quant,
+                    a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr, out, D);
 }
 
 // -------------------------------------------------------------- caches

@@ -29,6 +29,13 @@
 // Masks.  Key padding (attention.rs:280-294) and AttentionContext windows
 // (attention.rs:232-272) reduce to one visible key interval per query row.
 //
+// Geometry.  Frame indices are global (AttnGeom): a launch may cover a
+// slice of the query rows, read q|k|v from a buffer that starts at any frame
+// and has any row and batch strides (the time-major halo buffer of a
+// sequence-split forward), and read only the slice of the P table that its
+// relative positions reach -- TMA loads of P rows outside that slice, and of
+// frames outside the buffer, return zeros, and every pair they feed is masked.
+//
 // Memory.  Shared: q+u, q+v, one {K tile, P chunk} stage, 2 x V,
 // probabilities (the bf16 A operand of P.V) -- 224 KB.  TMEM: S [0,128), BD
 // slots [128,256) and [256,384), O [384,512).  The MMAs of key tile t+1 run
@@ -101,9 +108,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 
 // Visible key interval [lo, hi) of query row i (AttentionContext::block_mask,
 // attention.rs:232-272, intersected with key_padding_mask, 280-294).
-__device__ __forceinline__ void row_interval(const AttnContextDev& c, int i, int kend, int& lo,
-                                             int& hi) {
-  lo = 0;
+__device__ __forceinline__ void row_interval(const AttnContextDev& c, int i, int kbeg, int kend,
+                                             int& lo, int& hi) {
+  lo = kbeg;
   hi = kend;
   if (!c.has) return;
   if (c.chunked && c.right >= 0) {
@@ -131,11 +138,11 @@ __device__ __forceinline__ void mma_k128(uint32_t tmem_d, uint32_t a, uint32_t b
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    relpos_attn_kernel(const __grid_constant__ CUtensorMap map_qkv,  // [B][T][3D] bf16
-                       const __grid_constant__ CUtensorMap map_p,    // [2T-1][D] bf16
+    relpos_attn_kernel(const __grid_constant__ CUtensorMap map_qkv,  // [B][tbuf][3D] bf16
+                       const __grid_constant__ CUtensorMap map_p,    // [p_rows][D] bf16
                        const float* __restrict__ pos_u, const float* __restrict__ pos_v,
-                       const int32_t* __restrict__ key_len, AttnContextDev ctx,
-                       __nv_bfloat16* __restrict__ out, int T, int H, int* err) {
+                       const int32_t* __restrict__ key_len, AttnContextDev ctx, AttnGeom g,
+                       __nv_bfloat16* __restrict__ out, int H, int* err) {
   // Dynamic shared memory starts 1024-byte aligned when, as here, the kernel
   // has no static shared memory; checked, since the swizzle atoms need it.
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -155,27 +162,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = lane_id();
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int D = H * kDh;
-  const int i0 = qt * kTile;
+  const int i0 = g.q_lo + qt * kTile;  // global frame of the tile's first row
 
-  // Keys visible to any row of this tile: one interval [jlo, jhi).
-  int kend = T;
-  if (key_len) kend = min(T, max(key_len[b], 1));
+  // Keys visible to any row of this tile: one interval [jlo, jhi) of global
+  // frames, within the frames the buffer holds.
+  int klen = g.Tg;
+  if (key_len) klen = min(g.Tg, max(key_len[b], 1));
+  const int kend = min(klen, g.k_hi);
   int jlo, jhi;
   {
     int lo0, hi0, lo1, hi1;
-    const int i1 = min(i0 + kTile - 1, T - 1);
-    row_interval(ctx, i0, kend, lo0, hi0);
-    row_interval(ctx, i1, kend, lo1, hi1);
-    jlo = max(0, min(lo0, lo1));
-    jhi = min(kend, max(hi0, hi1));
+    const int i1 = min(i0 + kTile - 1, g.q_hi - 1);
+    row_interval(ctx, i0, g.k_lo, kend, lo0, hi0);
+    row_interval(ctx, i1, g.k_lo, kend, lo1, hi1);
+    jlo = min(lo0, lo1);
+    jhi = max(hi0, hi1);
   }
   // Query tiles wholly past the utterance's length are padding: their
   // outputs are unspecified in the reference (conformer.rs:1590-1593) and
   // are written as zeros here.
-  const bool padded_tile = key_len && i0 >= kend;
+  const bool padded_tile = key_len && i0 >= klen;
   const int j0 = jlo;
   const int nt = (jhi > jlo && !padded_tile) ? (jhi - j0 + kTile - 1) / kTile : 0;
-  const int rbase = T - kTile - i0 + j0;  // first P row of chunk 0
+  // first P row of chunk 0, as a row of the p buffer (may be negative:
+  // rows outside the buffer load as zeros and only meet masked pairs)
+  const int rbase = g.Tg - kTile - i0 + j0 - g.p_base;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q, 1);
@@ -210,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&map_p);
       auto load_stage = [&](int t) {  // K_t and P chunk t+1
         mbar_arrive_expect_tx(&bars->kp, kStageTx);
-        const int jt = j0 + t * kTile;
+        const int jt = j0 + t * kTile - g.base;
         tma_load_3d(sK, &map_qkv, &bars->kp, kcol, jt, b);
         tma_load_3d(sK + kHalf, &map_qkv, &bars->kp, kcol + 64, jt, b);
         const int prow = rbase + (t + 1) * kTile;
@@ -221,12 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t* bar = &bars->v[t & 1];
         uint8_t* dst = sV + (t & 1) * kTileBytes;
         mbar_arrive_expect_tx(bar, kTileBytes);
-        tma_load_3d(dst, &map_qkv, bar, vcol, j0 + t * kTile, b);
-        tma_load_3d(dst + kHalf, &map_qkv, bar, vcol + 64, j0 + t * kTile, b);
+        tma_load_3d(dst, &map_qkv, bar, vcol, j0 + t * kTile - g.base, b);
+        tma_load_3d(dst + kHalf, &map_qkv, bar, vcol + 64, j0 + t * kTile - g.base, b);
       };
       mbar_arrive_expect_tx(&bars->q, kTileBytes);
-      tma_load_3d(sQu, &map_qkv, &bars->q, qcol, i0, b);
-      tma_load_3d(sQu + kHalf, &map_qkv, &bars->q, qcol + 64, i0, b);
+      tma_load_3d(sQu, &map_qkv, &bars->q, qcol, i0 - g.base, b);
+      tma_load_3d(sQu + kHalf, &map_qkv, &bars->q, qcol + 64, i0 - g.base, b);
       // P chunk 0 is only read by the first BD MMA, so it is staged in the
       // probability buffer, which is free until the first softmax.
       mbar_arrive_expect_tx(&bars->p0, kTileBytes);
@@ -295,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i = i0 + il;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     int rlo, rhi;
-    row_interval(ctx, min(i, T - 1), kend, rlo, rhi);
+    row_interval(ctx, min(i, g.q_hi - 1), g.k_lo, kend, rlo, rhi);
     const float scale_log2 = 1.4426950408889634f * rsqrtf(static_cast<float>(kDh));
     const int shift = 31 - lane;
     const bool s16 = shift & 16, s8 = shift & 8, s4 = shift & 4, s2 = shift & 2, s1 = shift & 1;
@@ -492,12 +503,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = 0u;
       }
-      if (i < T) {
+      if (i < g.q_hi) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           pk[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-        uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(b) * T + i) * D +
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(b) * g.out_bs +
+                                              static_cast<size_t>(i - g.out_base) * D +
                                               h * kDh + col);
 #pragma unroll
         for (int v = 0; v < 4; ++v)
@@ -517,29 +529,68 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
+AttnGeom full_geom(int T, int D) {
+  AttnGeom g;
+  g.Tg = T;
+  g.tbuf = T;
+  g.base = 0;
+  g.qkv_ts = 3ll * D;
+  g.qkv_bs = 3ll * D * T;
+  g.q_lo = 0;
+  g.q_hi = T;
+  g.k_lo = 0;
+  g.k_hi = T;
+  g.p_base = 0;
+  g.p_rows = 2 * T - 1;
+  g.out_base = 0;
+  g.out_bs = static_cast<int64_t>(T) * D;
+  return g;
+}
+
+void visible_offsets(const AttnContextDev& c, int T, int& dmin, int& dmax) {
+  dmin = -(T - 1);
+  dmax = T - 1;
+  if (!c.has) return;
+  if (c.chunked && c.right >= 0) {
+    // row i of chunk ci sees keys [(ci - lc) * chunk, (ci + 1) * chunk)
+    const long long chunk = c.right + 1;
+    const long long lc = c.left >= 0 ? c.left / chunk : 10000;
+    const long long lo = -(lc * chunk + chunk - 1);
+    if (lo > dmin) dmin = static_cast<int>(lo);
+    dmax = static_cast<int>(chunk - 1 < dmax ? chunk - 1 : dmax);
+  } else {
+    if (c.left >= 0) dmin = -c.left;
+    if (!c.chunked && c.right >= 0) dmax = c.right;
+  }
+  dmin = dmin < -(T - 1) ? -(T - 1) : dmin;
+  dmax = dmax > T - 1 ? T - 1 : dmax;
+  if (dmax < dmin) dmax = dmin;  // nothing visible: keep a valid 1-row window
+}
+
 cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* u,
                                     const float* v, const int32_t* key_len, AttnContextDev ctx,
-                                    void* out, int B, int T, int H, int* err, int num_sms,
-                                    cudaStream_t stream) {
+                                    const AttnGeom& g, void* out, int B, int H, int* err,
+                                    int num_sms, cudaStream_t stream) {
   (void)num_sms;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(relpos_attn_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  if (cudaError_t e = smem_attr_once(relpos_attn_kernel, static_cast<int>(kSmemBytes), attr))
+    return e;
   const int D = H * kDh;
+  if (g.q_hi <= g.q_lo || g.tbuf <= 0 || g.p_rows <= 0 || B <= 0 || B > 65535)
+    return cudaErrorInvalidValue;
+  if (g.q_lo < g.base || g.q_hi > g.base + g.tbuf || g.k_lo < g.base ||
+      g.k_hi > g.base + g.tbuf || g.k_lo < 0 || g.k_hi > g.Tg || g.q_lo < g.out_base)
+    return cudaErrorInvalidValue;
   CUtensorMap map_qkv, map_p;
-  if (!make_tmap_3d(&map_qkv, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3ull * D, T, B,
-                    3ull * D * 2, 3ull * D * 2 * T, 64, kTile, 1, true) ||
-      !make_tmap_2d(&map_p, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, 2ull * T - 1,
+  if (!make_tmap_3d(&map_qkv, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3ull * D, g.tbuf, B,
+                    static_cast<uint64_t>(g.qkv_ts) * 2, static_cast<uint64_t>(g.qkv_bs) * 2, 64,
+                    kTile, 1, true) ||
+      !make_tmap_2d(&map_p, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, g.p_rows,
                     static_cast<uint64_t>(D) * 2, 64, kTile, true))
     return cudaErrorInvalidValue;
-  dim3 grid((T + kTile - 1) / kTile, H, B);
+  dim3 grid((g.q_hi - g.q_lo + kTile - 1) / kTile, H, B);
   relpos_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      map_qkv, map_p, u, v, key_len, ctx, static_cast<__nv_bfloat16*>(out), T, H, err);
+      map_qkv, map_p, u, v, key_len, ctx, g, static_cast<__nv_bfloat16*>(out), H, err);
   return cudaGetLastError();
 }
 

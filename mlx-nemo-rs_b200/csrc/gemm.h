@@ -6,7 +6,24 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace nrp {
+
+// Raises a kernel's dynamic shared-memory limit once per device (function
+// attributes belong to each device's context; `done` holds one bit per
+// device ordinal).
+template <typename F>
+cudaError_t smem_attr_once(F* func, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 // ---- TMA descriptors (driver entry point resolved through the runtime) ----
 // Row-major 2-D tensor [outer, inner] of `elem_bytes` elements, row stride in
@@ -30,6 +47,10 @@ struct RowTiling {
   const int32_t* len = nullptr;
   int T = 0;
   int B = 0;
+  // Output rows of utterance b start at y + b * y_bstride (elements); 0
+  // means T * ldy (utterances stacked).  A time-major output [T][B][N] is
+  // ldy = B * N, y_bstride = N.  Rows t >= T are never written.
+  int64_t y_bstride = 0;
 };
 
 // ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
@@ -58,19 +79,43 @@ cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
                             const float* bias, float* y, int ldy, cudaStream_t stream);
 
 // ---- offline fused rel-pos attention, bf16, tcgen05 ----
-// qkv: [B, T, 3*D] bf16 (q | k | v along the last axis, heads of 128);
-// p: [P, D] bf16 projected positions for relative positions (T-1)..-(T-1)
-// (P = 2T-1); u, v: [H, 128] f32 position biases (bf16-rounded values, added
-// to q in bf16 inside the kernel); key_len: [B] int32 (key j
-// visible iff j < max(key_len[b], 1)) or null; context (left, right, chunked,
-// has); out: [B, T, D] bf16.
+// Where a launch's rows sit in the sequence.  All frame indices are global
+// (frames of the whole utterance, Tg per utterance): the P row of query i
+// and key j is Tg-1-i+j, key_len and the attention context are in global
+// frames.  The launch computes query rows [q_lo, q_hi) of each utterance
+// from a q|k|v buffer holding global frames [base, base + tbuf) (row of
+// frame g of utterance b at (g - base) * qkv_ts + b * qkv_bs elements, each
+// row q | k | v of D each), and keys only from [k_lo, k_hi) (the frames the
+// buffer really holds).  p holds P rows [p_base, p_base + p_rows) of the
+// global table; rows outside read as zero, so a windowed context needs only
+// the rows its relative positions reach.
+struct AttnGeom {
+  int Tg;
+  int tbuf, base;
+  int64_t qkv_ts, qkv_bs;  // elements
+  int q_lo, q_hi;
+  int k_lo, k_hi;
+  int p_base, p_rows;
+  int out_base;     // global frame of output row 0
+  int64_t out_bs;   // output batch stride (elements); rows are D apart
+};
+// The whole sequence in one buffer [B, T, 3D] and the full P table.
+AttnGeom full_geom(int T, int D);
+// Relative offsets d = j - i visible under a context: [dmin, dmax] within
+// [-(T-1), T-1] (AttentionContext::block_mask, attention.rs:232-272).
 struct AttnContextDev {
   int has, left, right, chunked;
 };
+void visible_offsets(const AttnContextDev& ctx, int T, int& dmin, int& dmax);
+
+// qkv per geom; p: projected positions per geom; u, v: [H, 128] f32
+// position biases (bf16-rounded values, added to q in bf16 inside the
+// kernel); key_len: [B] int32 (key j visible iff j < max(key_len[b], 1)) or
+// null; out: bf16, row of frame i of utterance b at b * out_bs + (i - out_base) * D.
 cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* u,
                                     const float* v, const int32_t* key_len, AttnContextDev ctx,
-                                    void* out, int B, int T, int H, int* err, int num_sms,
-                                    cudaStream_t stream);
+                                    const AttnGeom& g, void* out, int B, int H, int* err,
+                                    int num_sms, cudaStream_t stream);
 
 // ---- generic CUDA-core attention (fp32 module dtype, any head_dim <= 128) ----
 // q [B,Tq,D] (row stride ldq), k/v [B,Tk,D] (row strides ldk, ldv), p

@@ -364,10 +364,12 @@ int gemm_smem_bytes() { return static_cast<int>(kSmemBytes); }
 
 namespace {
 bool make_y_map(CUtensorMap* map, __nv_bfloat16* y, int ldy, int M, int N, const RowTiling& rt) {
-  if (rt.T > 0)
+  if (rt.T > 0) {
+    const uint64_t bstride = rt.y_bstride > 0 ? static_cast<uint64_t>(rt.y_bstride)
+                                              : static_cast<uint64_t>(ldy) * rt.T;
     return make_tmap_3d(map, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, rt.T, rt.B,
-                        static_cast<uint64_t>(ldy) * 2, static_cast<uint64_t>(ldy) * 2 * rt.T, 64,
-                        32, 1, true);
+                        static_cast<uint64_t>(ldy) * 2, bstride * 2, 64, 32, 1, true);
+  }
   return make_tmap_2d(map, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M,
                       static_cast<uint64_t>(ldy) * 2, 64, 32, true);
 }
@@ -381,14 +383,9 @@ int grid_size(int M, int N, const RowTiling& rt, int num_sms) {
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
                              int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<false>, static_cast<int>(kSmemBytes), attr))
+    return e;
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
   const int grid = grid_size(M, N, rt, num_sms);
   CUtensorMap map_y;
@@ -402,14 +399,9 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
                            cudaStream_t stream, RowTiling rt) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tn_kernel<true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<true>, static_cast<int>(kSmemBytes), attr))
+    return e;
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
   const int grid = grid_size(M, N, rt, num_sms);
   CUtensorMap map_y;

@@ -100,3 +100,26 @@ struct nrp_cache {
   nrp::DevBuf tmp;
 };
 
+// Sequence-split communicator (halo.cpp).  `comm` is the ncclComm_t; the
+// exchange runs on its own high-priority stream so that it overlaps the
+// attention of the query tiles that need no halo.
+struct nrp_halo {
+  nrp_context* ctx = nullptr;
+  void* comm = nullptr;
+  int rank = 0, nranks = 1;
+  int timeout_ms = 10000;
+  bool dead = false;  // aborted after a timeout or an NCCL error
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ready = nullptr, done = nullptr;
+  nrp::DevBuf buf;  // time-major q|k|v [halo + len + halo][batch][3 d_model]
+};
+
+namespace nrp {
+// Queues on halo->stream, after the work queued so far on `st`: for side s
+// (0: rank - 1, 1: rank + 1; skipped when that rank does not exist or both
+// byte counts are 0) send send_bytes[s] bytes from buf + send_off[s] and
+// receive recv_bytes[s] bytes into buf + recv_off[s] (one NCCL group); then
+// records halo->done.  Offsets in bytes into halo->buf.
+int halo_exchange(nrp_halo* halo, const size_t send_off[2], const size_t send_bytes[2],
+                  const size_t recv_off[2], const size_t recv_bytes[2], cudaStream_t st);
+}  // namespace nrp

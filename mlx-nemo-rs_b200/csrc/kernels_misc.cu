@@ -202,14 +202,10 @@ cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq
                          const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
                          cudaStream_t stream) {
   if (M > kQMaxM || K % 512 != 0) return cudaErrorInvalidValue;
-  static bool attr = false;
   const int smem = kQMaxM * kQK * 4;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(qgemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  if (cudaError_t e = smem_attr_once(qgemv_kernel, smem, attr))
+    return e;
   qgemv_kernel<<<(N + kQWarps - 1) / kQWarps, kQWarps * 32, smem, stream>>>(x, M, K, wq, qs, qb,
                                                                            bias, y, ldy, N);
   return cudaGetLastError();

@@ -147,16 +147,27 @@ extern "C" int nrp_attn_forward_noalloc(nrp_attn* a, void* stream, const void* x
   rc = linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant, a->s_qkv.p,
               a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, qkv, 3 * D);
   if (rc) return rc;
-  rc = linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p,
-              D, nullptr, pbuf, D);
-  if (rc) return rc;
   nrp::AttnContextDev cd{0, -1, -1, 0};
   if (context) cd = {1, context->left, context->right, context->chunked};
   if (a->dtype == NRP_DTYPE_BF16) {
+    // linear_pos over the P rows the context reaches, as nrp_attn_forward
+    nrp::AttnGeom g = nrp::full_geom(T, D);
+    int dmin, dmax;
+    nrp::visible_offsets(cd, T, dmin, dmax);
+    g.p_base = T - 1 + dmin;
+    g.p_rows = dmax - dmin + 1;
+    rc = linear(ctx, st, a->dtype,
+                static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * es,
+                g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr, pbuf,
+                D);
+    if (rc) return rc;
     TRY_CUDA(nrp::launch_relpos_attn_bf16(qkv, pbuf, a->u_dev.as<float>(), a->v_dev.as<float>(),
-                                          lengths, cd, cbuf, B, T, a->H, ctx->d_err,
+                                          lengths, cd, g, cbuf, B, a->H, ctx->d_err,
                                           ctx->num_sms, st));
   } else {
+    rc = linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
+                a->z_pos.p, D, nullptr, pbuf, D);
+    if (rc) return rc;
     const float* q = reinterpret_cast<const float*>(qkv);
     nrp::StreamMaskDev none{};
     TRY_CUDA(nrp::launch_relpos_attn_f32(q, 3 * D, q + D, 3 * D, q + 2 * D, 3 * D,
