@@ -64,6 +64,27 @@ def algorithmic_flops(lengths):
     return proj, pos, attn
 
 
+# long-form windowed attention, sequence split across ranks
+LONG_B, LONG_T, LONG_WINDOW = 4, 12500, (128, 128)
+LONG_WORKLOAD = ("BASELINE config 4: long-form rel-pos local attention, window [128,128], bf16, "
+                 "B=4 T=12500 d_model=1024 8x128 heads; the sequence is split across the ranks "
+                 "with a 128-frame K/V halo exchanged over NCCL")
+
+
+def long_flops():
+    """Per forward (all frames valid): projections Q,K,V,out 2*K*N per
+    frame, linear_pos over the 2*128+1 positions the window reaches,
+    attention 3 products x 2*dh per visible (query, key) pair."""
+    dh = D // H
+    left, right = LONG_WINDOW
+    i = np.arange(LONG_T)
+    pairs = int(np.sum(np.minimum(LONG_T - 1, i + right) - np.maximum(0, i - left) + 1))
+    proj = 4 * 2 * LONG_B * LONG_T * D * D
+    pos = 2 * (left + right + 1) * D * D
+    attn = 3 * 2 * dh * H * LONG_B * pairs
+    return proj, pos, attn
+
+
 def env_int(name, default):
     try:
         return int(os.environ.get(name, default))
@@ -194,9 +215,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="offline", choices=["offline", "long"],
+                    help="offline: BASELINE config 1 (the headline line); long: config 4, "
+                         "the sequence split across the ranks")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "long":
+        return main_long(args)
 
     import torch
     import torch.distributed as dist
@@ -372,6 +398,206 @@ def main():
             "gpu_launches": launches,
             "roofline": roof,
             "roofline_kernels": {"attn_sm100": attn_roof, "gemm_bf16": gemm_roof},
+            "kernels": kern,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def _peak():
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    p = peaks.get("bf16_tflops_sustained")
+    if p:
+        return p, "measured (bf16_tflops_sustained, MEASURED_PEAKS.json)"
+    return 1400.0, "fallback 1.4 PFLOP/s sustained"
+
+
+def main_long(args):
+    """Config 4: one step = the windowed forward over [4, 12500, 1024]; with
+    N ranks each rank runs its segment of the sequence
+    (nrp_attn_forward_seq_sharded: local projections, 128-frame K/V halo
+    over NCCL, attention, linear_out).  Strong scaling: the total work is
+    fixed; value = all frames / the slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(4321)
+    f = lambda *sh: (rng.standard_normal(sh) * 0.02).astype(np.float32)
+    w = {"wq": f(D, D), "bq": f(D), "wk": f(D, D), "bk": f(D), "wv": f(D, D), "bv": f(D),
+         "wo": f(D, D), "bo": f(D), "wp": f(D, D), "pos_bias_u": f(H, D // H),
+         "pos_bias_v": f(H, D // H)}
+    attn = nrp.RelPositionMultiHeadAttention(D, H, True, ctx=ctx)
+    for which, (wk, bk) in enumerate((("wq", "bq"), ("wk", "bk"), ("wv", "bv"), ("wo", "bo"),
+                                      ("wp", None))):
+        attn.set_linear(which, nrp.LinearLayer.standard(w[wk], w[bk] if bk else None))
+    attn.set_pos_bias(w["pos_bias_u"], w["pos_bias_v"])
+    attn.set_dtype(nrp.BF16)
+    actx = nrp.AttentionContext.new(LONG_WINDOW, "regular")
+    pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
+    pe.set_dtype(nrp.BF16)
+    pos = pe.get_encoding(LONG_T)
+    dev = torch.device("cuda", local)
+    # every rank draws the whole sequence (same seed) and keeps its segment
+    x = np.random.default_rng(8765).standard_normal((LONG_B, LONG_T, D)).astype(np.float32)
+    halo = None
+    if world > 1:
+        halo = nrp.HaloComm.from_process_group(ctx=ctx, timeout_ms=120000)
+        plan = halo.plan(LONG_T, actx)
+        s0, n0 = plan.start, plan.len
+    else:
+        s0, n0 = 0, LONG_T
+    x_loc = np.ascontiguousarray(x[:, s0:s0 + n0])
+    xd = torch.from_numpy(x_loc).to(dev, torch.bfloat16)
+    out = torch.empty_like(xd)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(o=out, xin=xd):
+        if halo is None:
+            attn.forward(xin, pos, actx, None, out=o)
+        else:
+            attn.forward_seq_sharded(xin, pos, LONG_T, halo, actx, None, out=o)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    if halo is not None:
+        halo.check()
+    ctx.check()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            step()
+            ends[k].record(stream)
+        if halo is not None:
+            halo.check()
+        torch.cuda.synchronize()
+    barrier()
+    ctx.check()
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)))
+    frames = LONG_B * LONG_T
+    value = frames * args.steps / (total_ms / 1e3)
+
+    ctx.profile(True)
+    ctx.profile_reset()
+    for k in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    launches = sum(n for n, _ in prof.values())
+
+    x_host = torch.from_numpy(x_loc).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev2 = torch.empty_like(xd)
+    e_s = torch.cuda.Event(enable_timing=True)
+    e_e = torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        x_dev2.copy_(x_host, non_blocking=True)
+        step(out, x_dev2)
+        out_host.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e_s.record(stream)
+    for _ in range(args.steps):
+        x_dev2.copy_(x_host, non_blocking=True)
+        step(out, x_dev2)
+        out_host.copy_(out, non_blocking=True)
+    e_e.record(stream)
+    if halo is not None:
+        halo.check()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e_s.elapsed_time(e_e))
+    e2e_value = frames * args.steps / (e2e_ms / 1e3)
+
+    tflops_peak, peak_src = _peak()
+    proj, pos_f, attn_f = long_flops()
+    share = {"gemm_bf16": (proj + pos_f) / world, "attn_sm100": attn_f / world}
+    kern, rk = {}, {}
+    tot = max(sum(m for _, m in prof.values()), 1e-9)
+    for name, (n, ms) in prof.items():
+        kern[name] = {"launches": n, "ms_total": ms, "share": ms / tot}
+        if name in share:
+            a = share[name] * args.steps / (ms / 1e3) / 1e12
+            rk[name] = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s",
+                        "algorithmic_flop_per_launch": share[name] * args.steps / n}
+    dominant = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
+    roof = None
+    if dominant in rk:
+        roof = {"bound": "tensor", "kernel": dominant, "achieved": rk[dominant]["achieved"],
+                "peak": tflops_peak, "unit": "TFLOP/s", "frac": rk[dominant]["frac"],
+                "traffic": None, "peak_source": peak_src,
+                "algorithmic_flop_per_launch": rk[dominant]["algorithmic_flop_per_launch"]}
+    whole = (proj + pos_f + attn_f) * args.steps / (total_ms / 1e3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        threads = os.cpu_count() or 1
+        orc.set_threads(threads)
+        pe_h = orc.get_encoding(D, 5000, LONG_T)
+        t0 = time.perf_counter()
+        orc.mha_forward(x[:1], w, pe_h, H, context=(*LONG_WINDOW, False), bf16=True)
+        dt = time.perf_counter() - t0
+        cpu = {"value": LONG_T / dt, "unit": "frames/s", "cores": threads, "kind": "port",
+               "sample": f"1 of the 4 utterances ({LONG_T} frames), one run; CPU restatement "
+                         f"(ORC_DIRECT: window-skipping attention, every P row projected as "
+                         f"the reference does), host CPU: {cpu_model()}"}
+
+    if halo is not None:
+        halo.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": LONG_WORKLOAD, "batch": LONG_B, "seq_len": LONG_T,
+                       "d_model": D, "heads": H, "window": list(LONG_WINDOW),
+                       "frames_per_rank": n0 * LONG_B,
+                       "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                       "parallelism": f"sequence split x{world}, K/V halo over NCCL"
+                                      if world > 1 else "one GPU"},
+            "e2e": {"value": e2e_value, "unit": "frames/s",
+                    "h2d_bytes_per_step": x_host.numel() * 2,
+                    "d2h_bytes_per_step": out_host.numel() * 2},
+            "gpu_launches": launches,
+            "whole_step_tflops": whole,
+            "roofline": roof,
+            "roofline_kernels": rk,
             "kernels": kern,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
