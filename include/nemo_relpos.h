@@ -287,6 +287,85 @@ int nrp_attn_forward_seq_sharded(nrp_attn* attn, nrp_halo* halo, void* stream,
                                  const void* pos_emb, const int32_t* lengths,
                                  const nrp_att_context* context, void* out_local);
 
+/* ------------------------------------------------------ conformer block */
+/* ConformerBlock (src/asr/modules/encoders/conformer.rs:1617-2028):
+ *   x += 0.5 * FF1(LN x); x += MHA(LN x); x += Conv(LN x);
+ *   x += 0.5 * FF2(LN x); x = LN x
+ * with FeedForward = linear2(SiLU(linear1 x)) (2033-2088) and
+ * ConvolutionModule = pointwise_conv2(SiLU(norm(depthwise(GLU(pointwise_conv1
+ * x) with padded frames zeroed)))) (2108-2330).  LayerNorms have eps 1e-5;
+ * the conv norm is BatchNorm in inference mode (eps 1e-5) or a LayerNorm.
+ * Every linear may be standard or MLX 8-bit quantised, like the attention's.
+ * The block runs in bf16 (nrp_block_set_dtype(NRP_DTYPE_BF16)) and needs
+ * d_model in {256, 512, 1024, 2048}, head_dim 128 and ff_dim % 64 == 0. */
+typedef struct nrp_block nrp_block;
+typedef enum {
+  NRP_BLOCK_FF1_LINEAR1 = 0, /* feed_forward1.linear1 [ff_dim, d_model] */
+  NRP_BLOCK_FF1_LINEAR2 = 1, /* feed_forward1.linear2 [d_model, ff_dim] */
+  NRP_BLOCK_CONV_PW1 = 2,    /* conv.pointwise_conv1 [2*d_model, d_model] */
+  NRP_BLOCK_CONV_PW2 = 3,    /* conv.pointwise_conv2 [d_model, d_model] */
+  NRP_BLOCK_FF2_LINEAR1 = 4,
+  NRP_BLOCK_FF2_LINEAR2 = 5
+} nrp_block_linear_id;
+typedef enum {
+  NRP_BLOCK_NORM_FF1 = 0,  /* norm_feed_forward1 */
+  NRP_BLOCK_NORM_ATT = 1,  /* norm_self_att */
+  NRP_BLOCK_NORM_CONV = 2, /* norm_conv */
+  NRP_BLOCK_NORM_FF2 = 3,  /* norm_feed_forward2 */
+  NRP_BLOCK_NORM_OUT = 4   /* norm_out */
+} nrp_block_norm_id;
+/* ConformerBlock::new (1661-1692): conv_norm 0 = batch_norm, 1 = layer_norm;
+ * causal_conv pads the depthwise conv on the left only. */
+int nrp_block_create(nrp_context* ctx, int d_model, int n_heads, int ff_dim, int conv_kernel,
+                     int causal_conv, int conv_norm, int use_bias, nrp_block** out);
+int nrp_block_destroy(nrp_block* block);
+int nrp_block_set_dtype(nrp_block* block, int dtype);
+/* The block's RelPositionMultiHeadAttention (owned by the block): load its
+ * parameters with nrp_attn_load_*. */
+int nrp_block_attn(nrp_block* block, nrp_attn** attn);
+/* Weights::fetch_linear for one of the block's linears (FeedForward::
+ * load_weights 2074-2088, ConvolutionModule::load_weights 2404-2437): host
+ * f32 weight [out, in], bias [out] or NULL; quantised: u32 codes
+ * [out, in*bits/32], scales/biases [out, in/group]. */
+int nrp_block_load_linear(nrp_block* block, int which, const float* weight, const float* bias);
+int nrp_block_load_linear_quantized(nrp_block* block, int which, int bits, int group_size,
+                                    const uint32_t* wq, const float* scales,
+                                    const float* biases, const float* bias);
+/* load_layer_norm (src/core/loading.rs:203-214): gamma, beta host f32 [d_model]. */
+int nrp_block_load_norm(nrp_block* block, int which, const float* gamma, const float* beta);
+/* load_conv1d for conv.depthwise_conv (loading.rs:216-223): weight host f32
+ * in the MLX layout [d_model, kernel, 1]; bias [d_model] or NULL. */
+int nrp_block_load_depthwise(nrp_block* block, const float* weight, const float* bias);
+/* load_batch_norm for conv.batch_norm (loading.rs:234-252); with conv_norm
+ * = layer_norm, gamma/beta are that LayerNorm's and mean/var are ignored. */
+int nrp_block_load_conv_norm(nrp_block* block, const float* gamma, const float* beta,
+                             const float* running_mean, const float* running_var);
+/* ConformerBlock::forward (1693-1870): x, out device [batch, seq_len,
+ * d_model] bf16 (out may be x); pos_emb device [2*seq_len-1, d_model];
+ * lengths device int32 [batch] or NULL (PaddingMask, 1594-1615: padded keys
+ * hidden, padded frames zeroed before the depthwise conv); context NULL
+ * for full attention.  Rows past a length are unspecified. */
+int nrp_block_forward(nrp_block* block, void* stream, const void* x, int batch, int seq_len,
+                      const void* pos_emb, const int32_t* lengths,
+                      const nrp_att_context* context, void* out);
+
+/* ConformerEncoder::forward_from_embeddings (conformer.rs:694-722) over
+ * n_layers blocks: x * xscale (sqrt(d_model) when xscaling), the positional
+ * table of RelPositionalEncoding(d_model, max_len) for seq_len, every block,
+ * then the transpose to [batch, d_model, seq_len]. */
+typedef struct nrp_encoder nrp_encoder;
+int nrp_encoder_create(nrp_context* ctx, int n_layers, int d_model, int n_heads, int ff_dim,
+                       int conv_kernel, int causal_conv, int conv_norm, int use_bias,
+                       int xscaling, int max_len, nrp_encoder** out);
+int nrp_encoder_destroy(nrp_encoder* enc);
+int nrp_encoder_block(nrp_encoder* enc, int layer, nrp_block** block);
+int nrp_encoder_set_dtype(nrp_encoder* enc, int dtype);
+/* x device [batch, seq_len, d_model] bf16 (left unchanged); lengths device
+ * int32 [batch] or NULL; out device [batch, d_model, seq_len] bf16. */
+int nrp_encoder_forward_from_embeddings(nrp_encoder* enc, void* stream, const void* x, int batch,
+                                        int seq_len, const int32_t* lengths,
+                                        const nrp_att_context* context, void* out);
+
 /* --------------------------------------------------- linear primitives */
 /* LinearLayer::forward, Standard arm (quantization.rs:128-135) on device
  * buffers: y[M,N] = x[M,K] . w[N,K]^T (+ bias[N]), dtype f32 or bf16 for
@@ -316,7 +395,10 @@ typedef enum {
   NRP_KERNEL_ATTN_SIMT = 5,   /* f32 offline attention, CUDA cores */
   NRP_KERNEL_ATTN_STREAM = 6, /* streaming attention against the ring cache */
   NRP_KERNEL_RING_APPEND = 7, /* streaming cache slide */
-  NRP_KERNEL_KINDS = 8
+  NRP_KERNEL_LAYERNORM = 8,   /* the block's LayerNorms */
+  NRP_KERNEL_DWCONV = 9,      /* depthwise conv + BatchNorm + SiLU */
+  NRP_KERNEL_ELEMENTWISE = 10, /* input scaling, transposes, copies */
+  NRP_KERNEL_KINDS = 11
 } nrp_kernel_kind;
 int nrp_profile_enable(nrp_context* ctx, int enable);
 int nrp_profile_reset(nrp_context* ctx);

@@ -117,6 +117,21 @@ def lib():
             "nrp_halo_comm_destroy": ([vp], i),
             "nrp_halo_comm_check": ([vp, vp], i),
             "nrp_attn_forward_seq_sharded": ([vp, vp, vp, vp, i, i, vp, vp, vp, vp], i),
+            "nrp_block_create": ([vp, i, i, i, i, i, i, i, vp], i),
+            "nrp_block_destroy": ([vp], i),
+            "nrp_block_set_dtype": ([vp, i], i),
+            "nrp_block_attn": ([vp, vp], i),
+            "nrp_block_load_linear": ([vp, i, vp, vp], i),
+            "nrp_block_load_linear_quantized": ([vp, i, i, i, vp, vp, vp, vp], i),
+            "nrp_block_load_norm": ([vp, i, vp, vp], i),
+            "nrp_block_load_depthwise": ([vp, vp, vp], i),
+            "nrp_block_load_conv_norm": ([vp, vp, vp, vp, vp], i),
+            "nrp_block_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
+            "nrp_encoder_create": ([vp] + [i] * 10 + [vp], i),
+            "nrp_encoder_destroy": ([vp], i),
+            "nrp_encoder_block": ([vp, i, vp], i),
+            "nrp_encoder_set_dtype": ([vp, i], i),
+            "nrp_encoder_forward_from_embeddings": ([vp, vp, vp, i, i, vp, vp, vp], i),
             "nrp_profile_enable": ([vp, i], i),
             "nrp_profile_reset": ([vp], i),
             "nrp_profile_read": ([vp, i, vp, vp], i),
@@ -179,7 +194,7 @@ class Context:
         _check(lib().nrp_context_check(self.handle, stream if stream is not None else _stream()))
 
     KERNELS = ("gemm_bf16", "gemm_q8", "qgemv", "gemm_f32", "attn_sm100", "attn_simt",
-               "attn_stream", "ring_append")
+               "attn_stream", "ring_append", "layernorm", "dwconv", "elementwise")
 
     def profile(self, enable: bool = True):
         _check(lib().nrp_profile_enable(self.handle, int(enable)))
@@ -369,15 +384,30 @@ class RelPositionMultiHeadAttention:
         _check(lib().nrp_attn_create(self.ctx.handle, d_model, n_heads, int(bool(use_bias)),
                                      C.byref(h)))
         self.handle = h
+        self._owned = True
         self.d_model = d_model
         self._n_heads = n_heads
         self.dtype = F32
         self._cache_drop_size = 0
         self.att_context_size: Optional[Tuple[int, int]] = None
 
+    @classmethod
+    def _view(cls, handle, d_model: int, n_heads: int, ctx: Context):
+        """A module owned by a ConformerBlock (not freed by this object)."""
+        self = cls.__new__(cls)
+        self.ctx = ctx
+        self.handle = handle
+        self._owned = False
+        self.d_model = d_model
+        self._n_heads = n_heads
+        self.dtype = F32
+        self._cache_drop_size = 0
+        self.att_context_size = None
+        return self
+
     def __del__(self):
         try:
-            if self.handle:
+            if self.handle and self._owned:
                 lib().nrp_attn_destroy(self.handle)
         except Exception:
             pass
@@ -489,6 +519,183 @@ class RelPositionMultiHeadAttention:
             pe.data_ptr(), key_mask.lengths.data_ptr() if key_mask is not None else None,
             C.byref(c) if c is not None else None, out.data_ptr()))
         return out
+
+
+# ------------------------------------------------------- conformer block
+BLOCK_LINEARS = ("feed_forward1.linear1", "feed_forward1.linear2", "conv.pointwise_conv1",
+                 "conv.pointwise_conv2", "feed_forward2.linear1", "feed_forward2.linear2")
+BLOCK_NORMS = ("norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2",
+               "norm_out")
+
+
+class ConformerBlock:
+    """ConformerBlock (src/asr/modules/encoders/conformer.rs:1617-2028): the
+    macaron feed-forwards, the rel-pos attention, the convolution module and
+    the final norm, in bf16 on the device.  conv_norm: "batch_norm" or
+    "layer_norm"."""
+
+    def __init__(self, d_model: int, n_heads: int, ff_dim: int, conv_kernel: int = 9,
+                 causal_conv: bool = False, conv_norm: str = "batch_norm",
+                 use_bias: bool = True, ctx: Optional[Context] = None, _handle=None,
+                 _owner=None):
+        self.ctx = ctx or Context.default()
+        self.d_model, self.n_heads, self.ff_dim, self.conv_kernel = d_model, n_heads, ff_dim, \
+            conv_kernel
+        self.conv_norm = conv_norm
+        self._owner = _owner
+        if _handle is None:
+            h = C.c_void_p()
+            _check(lib().nrp_block_create(self.ctx.handle, d_model, n_heads, ff_dim, conv_kernel,
+                                          int(causal_conv), int(conv_norm == "layer_norm"),
+                                          int(use_bias), C.byref(h)))
+            self.handle, self._owned = h, True
+        else:
+            self.handle, self._owned = _handle, False
+        a = C.c_void_p()
+        _check(lib().nrp_block_attn(self.handle, C.byref(a)))
+        self.self_attn = RelPositionMultiHeadAttention._view(a, d_model, n_heads, self.ctx)
+
+    def __del__(self):
+        try:
+            if self._owned and self.handle:
+                lib().nrp_block_destroy(self.handle)
+        except Exception:
+            pass
+
+    def set_dtype(self, dtype: int):
+        _check(lib().nrp_block_set_dtype(self.handle, dtype))
+        self.self_attn.dtype = dtype
+
+    def set_linear(self, which: int, layer: LinearLayer):
+        if layer.is_quantized():
+            wq = np.ascontiguousarray(layer.weight, np.uint32)
+            sc, bi = _np_f32(layer.scales), _np_f32(layer.biases)
+            b = _np_f32(layer.bias) if layer.bias is not None else None
+            _check(lib().nrp_block_load_linear_quantized(
+                self.handle, which, layer.bits, layer.group_size, wq.ctypes.data, sc.ctypes.data,
+                bi.ctypes.data, b.ctypes.data if b is not None else None))
+        else:
+            w = _np_f32(layer.weight)
+            b = _np_f32(layer.bias) if layer.bias is not None else None
+            _check(lib().nrp_block_load_linear(self.handle, which, w.ctypes.data,
+                                               b.ctypes.data if b is not None else None))
+
+    def set_norm(self, which: int, gamma, beta):
+        g, b = _np_f32(gamma), _np_f32(beta)
+        _check(lib().nrp_block_load_norm(self.handle, which, g.ctypes.data, b.ctypes.data))
+
+    def set_depthwise(self, weight, bias=None):
+        """weight in the MLX Conv1d layout [d_model, kernel, 1] (or [d_model, kernel])."""
+        w = _np_f32(weight).reshape(self.d_model, self.conv_kernel)
+        b = _np_f32(bias) if bias is not None else None
+        _check(lib().nrp_block_load_depthwise(self.handle, w.ctypes.data,
+                                              b.ctypes.data if b is not None else None))
+
+    def set_conv_norm(self, gamma, beta, running_mean=None, running_var=None):
+        g, b = _np_f32(gamma), _np_f32(beta)
+        m = _np_f32(running_mean) if running_mean is not None else None
+        v = _np_f32(running_var) if running_var is not None else None
+        _check(lib().nrp_block_load_conv_norm(self.handle, g.ctypes.data, b.ctypes.data,
+                                              m.ctypes.data if m is not None else None,
+                                              v.ctypes.data if v is not None else None))
+
+    def load_weights(self, weights: Dict[str, object], prefix: str,
+                     quant: Optional[QuantizationConfig] = None):
+        """ConformerBlock::load_weights (conformer.rs:1978-2028) with the
+        NeMo key names."""
+        for which, name in enumerate(BLOCK_LINEARS):
+            layer = load_linear_layer(weights, f"{prefix}.{name}", quant)
+            if layer is not None:
+                self.set_linear(which, layer)
+        for which, name in enumerate(BLOCK_NORMS):
+            g = weights.get(f"{prefix}.{name}.weight")
+            b = weights.get(f"{prefix}.{name}.bias")
+            if g is not None or b is not None:
+                n = self.d_model
+                self.set_norm(which, g if g is not None else np.ones(n, np.float32),
+                              b if b is not None else np.zeros(n, np.float32))
+        self.self_attn.load_weights(weights, f"{prefix}.self_attn", quant)
+        w = weights.get(f"{prefix}.conv.depthwise_conv.weight")
+        if w is not None:
+            self.set_depthwise(w, weights.get(f"{prefix}.conv.depthwise_conv.bias"))
+        bn = f"{prefix}.conv.batch_norm"
+        g = weights.get(f"{bn}.weight")
+        if g is not None:
+            self.set_conv_norm(g, weights[f"{bn}.bias"], weights.get(f"{bn}.running_mean"),
+                               weights.get(f"{bn}.running_var"))
+
+    def forward(self, x, pos_emb, context: Optional[AttentionContext] = None,
+                lengths=None, out=None):
+        """conformer.rs:1693-1870.  x [B, T, D] bf16; lengths: device int32
+        [B] (a KeyPaddingMask's) or None."""
+        import torch
+        B, T, D = x.shape
+        pe = pos_emb.reshape(-1, D)
+        if out is None:
+            out = torch.empty_like(x)
+        if isinstance(lengths, KeyPaddingMask):
+            lengths = lengths.lengths
+        c = context._c() if context is not None else None
+        _check(lib().nrp_block_forward(self.handle, _stream(), x.data_ptr(), B, T, pe.data_ptr(),
+                                       _ptr(lengths), C.byref(c) if c is not None else None,
+                                       out.data_ptr()))
+        return out
+
+
+class ConformerEncoder:
+    """The conformer stack of ConformerEncoder (conformer.rs:381-722):
+    forward_from_embeddings on post-subsampling embeddings."""
+
+    def __init__(self, n_layers: int, d_model: int, n_heads: int, ff_dim: int,
+                 conv_kernel: int = 9, causal_conv: bool = False,
+                 conv_norm: str = "batch_norm", use_bias: bool = True, xscaling: bool = True,
+                 max_len: int = 5000, ctx: Optional[Context] = None):
+        self.ctx = ctx or Context.default()
+        self.d_model = d_model
+        h = C.c_void_p()
+        _check(lib().nrp_encoder_create(self.ctx.handle, n_layers, d_model, n_heads, ff_dim,
+                                        conv_kernel, int(causal_conv),
+                                        int(conv_norm == "layer_norm"), int(use_bias),
+                                        int(xscaling), max_len, C.byref(h)))
+        self.handle = h
+        self.layers = []
+        for i in range(n_layers):
+            b = C.c_void_p()
+            _check(lib().nrp_encoder_block(h, i, C.byref(b)))
+            self.layers.append(ConformerBlock(d_model, n_heads, ff_dim, conv_kernel, causal_conv,
+                                              conv_norm, use_bias, self.ctx, _handle=b,
+                                              _owner=self))
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().nrp_encoder_destroy(self.handle)
+        except Exception:
+            pass
+
+    def set_dtype(self, dtype: int):
+        _check(lib().nrp_encoder_set_dtype(self.handle, dtype))
+
+    def load_weights(self, weights: Dict[str, object],
+                     quant: Optional[QuantizationConfig] = None):
+        """conformer.rs:590-605: layer i from encoder.layers.{i}."""
+        for i, layer in enumerate(self.layers):
+            layer.load_weights(weights, f"encoder.layers.{i}", quant)
+
+    def forward_from_embeddings(self, x, lengths, context: Optional[AttentionContext] = None,
+                                out=None):
+        """conformer.rs:694-722: returns ([B, D, T] bf16, lengths)."""
+        import torch
+        B, T, D = x.shape
+        if out is None:
+            out = torch.empty((B, D, T), dtype=x.dtype, device=x.device)
+        mask = key_padding_mask(np.asarray(lengths, np.int32), T)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_encoder_forward_from_embeddings(
+            self.handle, _stream(), x.data_ptr(), B, T,
+            mask.lengths.data_ptr() if mask is not None else None,
+            C.byref(c) if c is not None else None, out.data_ptr()))
+        return out, lengths
 
 
 # ------------------------------------------- sequence split (several GPUs)

@@ -25,10 +25,13 @@
 #include "../../include/nemo_relpos.h"
 #include "gemm.h"
 #include "handles.h"
+#include "internal.h"
 
 using nrp::DevBuf;
 using nrp::Linear;
 using nrp::ProfRec;
+using nrp::ProfScope;
+using nrp::take_event;
 
 
 namespace {
@@ -54,6 +57,15 @@ int report_error(int code, const char* msg) {
   g_err = msg;
   return code;
 }
+int failf(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
 }  // namespace nrp
 
 namespace {
@@ -65,56 +77,12 @@ namespace {
       return fail(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));        \
   } while (0)
 
-uint16_t bf16_bits(float x) {
-  uint32_t u;
-  memcpy(&u, &x, 4);
-  if ((u & 0x7f800000u) == 0x7f800000u) return static_cast<uint16_t>((u >> 16) | ((u & 0xffff) ? 0x40 : 0));
-  u += 0x7fffu + ((u >> 16) & 1u);
-  return static_cast<uint16_t>(u >> 16);
-}
-
-float bf16_round(float x) {
-  uint32_t u = static_cast<uint32_t>(bf16_bits(x)) << 16;
-  float y;
-  memcpy(&y, &u, 4);
-  return y;
-}
+using nrp::bf16_bits;
+using nrp::bf16_round;
 
 }  // namespace
 
 namespace {
-
-cudaEvent_t take_event(nrp_context* c) {
-  if (!c->pool.empty()) {
-    cudaEvent_t e = c->pool.back();
-    c->pool.pop_back();
-    return e;
-  }
-  cudaEvent_t e = nullptr;
-  cudaEventCreate(&e);
-  return e;
-}
-
-// Scope guard: records start/stop events around one launch when enabled.
-struct ProfScope {
-  nrp_context* c;
-  int kind;
-  cudaStream_t st;
-  cudaEvent_t a = nullptr;
-  ProfScope(nrp_context* c_, int kind_, cudaStream_t st_) : c(c_), kind(kind_), st(st_) {
-    if (c && c->prof) {
-      a = take_event(c);
-      cudaEventRecord(a, st);
-    }
-  }
-  ~ProfScope() {
-    if (a) {
-      cudaEvent_t b = take_event(c);
-      cudaEventRecord(b, st);
-      c->recs.push_back({kind, a, b});
-    }
-  }
-};
 
 // Folds finished records into the per-kind totals.
 int prof_collect(nrp_context* c) {
@@ -267,9 +235,12 @@ int sync_params(nrp_attn* a) {
 // either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
 int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
                const void* w, bool quant, const void* qs, const void* qb, int N,
-               const void* bias, void* y, int ldy, const nrp::RowTiling& rt = nrp::RowTiling()) {
+               const void* bias, void* y, int ldy, const nrp::RowTiling& rt = nrp::RowTiling(),
+               const nrp::Epilogue& ep = nrp::Epilogue()) {
   if (M <= 0) return ok();
   if (dtype == NRP_DTYPE_F32) {
+    if (ep.mode != nrp::kEpiBias)
+      return fail(NRP_ERR_UNSUPPORTED, "fused epilogues run in bf16 modules only");
     ProfScope ps(ctx, NRP_KERNEL_GEMM_F32, st);
     CUDA_TRY(nrp::launch_gemm_f32(static_cast<const float*>(x), M, K, static_cast<const float*>(w),
                                   N, static_cast<const float*>(bias), static_cast<float*>(y), ldy,
@@ -279,7 +250,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)
     return fail(NRP_ERR_UNSUPPORTED, "bf16 linear needs K %% 64 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
   // (the GEMV writes flat rows: not for an output with its own batch stride)
-  if (quant && M <= 16 && rt.y_bstride == 0) {
+  if (quant && M <= 16 && rt.y_bstride == 0 && ep.mode == nrp::kEpiBias) {
     ProfScope ps(ctx, NRP_KERNEL_QGEMV, st);
     CUDA_TRY(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
                                static_cast<const uint8_t*>(w),
@@ -304,7 +275,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                  static_cast<const __nv_bfloat16*>(qb),
                                  static_cast<const __nv_bfloat16*>(bias),
                                  static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                 ctx->d_err, st, rt));
+                                 ctx->d_err, st, rt, ep));
   } else {
     if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
                            static_cast<uint64_t>(K) * 2, 64, 256, true))
@@ -312,7 +283,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
     ProfScope ps(ctx, NRP_KERNEL_GEMM_BF16, st);
     CUDA_TRY(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
                                    static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                   ctx->d_err, st, rt));
+                                   ctx->d_err, st, rt, ep));
   }
   return ok();
 }
@@ -629,13 +600,23 @@ int nrp_attn_load_pos_bias(nrp_attn* attn, const float* u, const float* v) {
 
 int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, const void* pos_emb,
                      const int32_t* lengths, const nrp_att_context* context, void* out) {
+  return nrp::attn_forward(a, static_cast<cudaStream_t>(stream), x, B, T, pos_emb, lengths,
+                           context, out, nrp::Epilogue());
+}
+
+}  // extern "C"
+
+namespace nrp {
+
+int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, const void* pos_emb,
+                 const int32_t* lengths, const nrp_att_context* context, void* out,
+                 const Epilogue& out_ep) {
   if (!a || !x || !pos_emb || !out) return fail(NRP_ERR_INVALID, "null argument");
   if (B <= 0 || T <= 0) return fail(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
   nrp_context* ctx = a->ctx;
   if (check_device(ctx)) return NRP_ERR_CUDA;
   int rc = sync_params(a);
   if (rc) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int D = a->D, P = 2 * T - 1;
   const size_t es = esize(a->dtype);
   const size_t BT = static_cast<size_t>(B) * T;
@@ -687,11 +668,23 @@ int nrp_attn_forward(nrp_attn* a, void* stream, const void* x, int B, int T, con
                                          a->v_dev.as<float>(), lengths, cd, none,
                                          a->cbuf.as<float>(), B, T, T, D, a->H, st));
   }
-  // 565: linear_out
+  // 565: linear_out (the caller's epilogue: a block adds its residual here)
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
-                    out, D, rows);
+                    out, D, rows, out_ep);
 }
+
+int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
+           const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
+           void* y, int ldy, const RowTiling& rt, const Epilogue& ep) {
+  return run_linear(ctx, st, dtype, x, M, K, w, quant, qs, qb, N, bias, y, ldy, rt, ep);
+}
+
+int select_device(nrp_context* ctx) { return check_device(ctx); }
+
+}  // namespace nrp
+
+extern "C" {
 
 // ------------------------------------------------------ sequence split
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len) {

@@ -1,0 +1,535 @@
+// block.cpp -- the Conformer block and encoder around the rel-pos attention
+// (src/asr/modules/encoders/conformer.rs:694-722, 1617-2437).
+//
+// One block forward, x updated in place in bf16 (M = batch * seq_len rows):
+//   LayerNorm                       -> h
+//   FF1 linear1, epilogue SiLU      -> hid
+//   FF1 linear2, epilogue x += 0.5 * (.)
+//   LayerNorm -> h; the attention with linear_out's epilogue x += (.)
+//   LayerNorm -> h; pointwise_conv1, epilogue GLU + padded frames zeroed -> glu
+//   depthwise conv + BatchNorm affine + SiLU -> dw
+//   pointwise_conv2, epilogue x += (.)
+//   LayerNorm -> h; FF2 as FF1; final LayerNorm in place
+// With lengths, every per-frame GEMM tiles rows per utterance and skips the
+// row tiles past each length (padded rows are unspecified, conformer.rs:
+// 1590-1593), as the attention's own projections do.  pointwise_conv1's rows
+// are uploaded permuted ([128 value rows | their 128 gate rows] per 256-row
+// tile) so the GLU happens inside one output tile.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "../../include/nemo_relpos.h"
+#include "gemm.h"
+#include "handles.h"
+#include "internal.h"
+
+namespace {
+
+using nrp::failf;
+
+#define TRY_CUDA(expr)                                                                \
+  do {                                                                                \
+    const cudaError_t e_ = (expr);                                                    \
+    if (e_ != cudaSuccess)                                                            \
+      return failf(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));     \
+  } while (0)
+
+constexpr int kNumLinears = 6;
+constexpr int kNumNorms = 5;
+
+struct DevLinear {
+  nrp::DevBuf w, s, z, b;  // bf16 weight (or u8 codes), bf16 scales, zero points, bias
+  bool quant = false, has_b = false;
+};
+
+cudaError_t upload_bf16(nrp::DevBuf& dst, const float* src, size_t n) {
+  std::vector<uint16_t> h(n);
+  for (size_t i = 0; i < n; ++i) h[i] = nrp::bf16_bits(src[i]);
+  cudaError_t e = dst.ensure(n * 2);
+  if (e == cudaSuccess) e = cudaMemcpy(dst.p, h.data(), n * 2, cudaMemcpyHostToDevice);
+  return e;
+}
+
+cudaError_t upload_f32(nrp::DevBuf& dst, const std::vector<float>& v) {
+  cudaError_t e = dst.ensure(v.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(dst.p, v.data(), v.size() * 4, cudaMemcpyHostToDevice);
+  return e;
+}
+
+// Row order of pointwise_conv1 on the device: tile k (256 rows) holds value
+// rows 128k.. and gate rows D + 128k.. (GLU splits the 2D outputs in halves).
+int glu_source_row(int n, int D) {
+  const int k = n / 256, j = n % 256;
+  return j < 128 ? 128 * k + j : D + 128 * k + (j - 128);
+}
+
+}  // namespace
+
+struct nrp_block {
+  nrp_context* ctx = nullptr;
+  int D = 0, H = 0, ff = 0, K = 0;
+  bool causal = false;
+  int conv_norm = 0;  // 0 batch norm, 1 layer norm
+  int use_bias = 1;
+  int dtype = NRP_DTYPE_F32;
+  nrp_attn* attn = nullptr;
+  nrp::Linear lin[kNumLinears];
+  std::vector<float> ng[kNumNorms], nb[kNumNorms];
+  std::vector<float> dw_w, dw_b;            // [D][K], [D]
+  std::vector<float> cn_g, cn_b, cn_m, cn_v;  // conv norm
+  bool dirty = true;
+  DevLinear dl[kNumLinears];
+  nrp::DevBuf d_ng[kNumNorms], d_nb[kNumNorms];
+  nrp::DevBuf d_dw_w, d_dw_b, d_cn_scale, d_cn_shift, d_cn_g, d_cn_b;
+  nrp::DevBuf h, hid, glu, dw;  // workspace
+};
+
+struct nrp_encoder {
+  nrp_context* ctx = nullptr;
+  int D = 0, H = 0, max_len = 5000;
+  float xscale = 1.f;
+  int dtype = NRP_DTYPE_F32;
+  std::vector<nrp_block*> blocks;
+  nrp::DevBuf x, pos;
+  int pos_T = -1, pos_dtype = -1;
+};
+
+namespace {
+
+// Output and input sizes of each block linear.
+void linear_shape(const nrp_block* k, int which, int& N, int& Kin) {
+  switch (which) {
+    case NRP_BLOCK_FF1_LINEAR1:
+    case NRP_BLOCK_FF2_LINEAR1: N = k->ff; Kin = k->D; return;
+    case NRP_BLOCK_FF1_LINEAR2:
+    case NRP_BLOCK_FF2_LINEAR2: N = k->D; Kin = k->ff; return;
+    case NRP_BLOCK_CONV_PW1: N = 2 * k->D; Kin = k->D; return;
+    default: N = k->D; Kin = k->D; return;
+  }
+}
+
+// Device copies of the block's parameters in bf16 (LinearLayer::cast and
+// cast_module of ConformerBlock::set_dtype, conformer.rs:1639-1659: every
+// parameter rounded to bf16; the BatchNorm is then folded to
+// scale = gamma / sqrt(var + eps), shift = beta - mean * scale).
+int sync_block(nrp_block* k) {
+  if (!k->dirty) return NRP_OK;
+  const int D = k->D;
+  for (int i = 0; i < kNumLinears; ++i) {
+    const nrp::Linear& L = k->lin[i];
+    if (!L.loaded) return failf(NRP_ERR_INVALID, "block linear %d has no weights loaded", i);
+    int N, Kin;
+    linear_shape(k, i, N, Kin);
+    const bool glu = i == NRP_BLOCK_CONV_PW1;
+    auto src_row = [&](int n) { return glu ? glu_source_row(n, D) : n; };
+    DevLinear& d = k->dl[i];
+    d.quant = L.quant;
+    if (L.quant) {
+      if (L.bits != 8 || L.group != 64)
+        return failf(NRP_ERR_UNSUPPORTED, "quantized layers need bits 8, group 64");
+      const int kg = Kin / 64;
+      std::vector<uint8_t> codes(static_cast<size_t>(N) * Kin);
+      std::vector<float> sc(static_cast<size_t>(N) * kg), zp(static_cast<size_t>(N) * kg);
+      const uint8_t* wb = reinterpret_cast<const uint8_t*>(L.wq.data());
+      for (int n = 0; n < N; ++n) {
+        const int r = src_row(n);
+        memcpy(codes.data() + static_cast<size_t>(n) * Kin, wb + static_cast<size_t>(r) * Kin, Kin);
+        memcpy(sc.data() + static_cast<size_t>(n) * kg, L.qs.data() + static_cast<size_t>(r) * kg,
+               sizeof(float) * kg);
+        memcpy(zp.data() + static_cast<size_t>(n) * kg, L.qb.data() + static_cast<size_t>(r) * kg,
+               sizeof(float) * kg);
+      }
+      TRY_CUDA(d.w.ensure(codes.size()));
+      TRY_CUDA(cudaMemcpy(d.w.p, codes.data(), codes.size(), cudaMemcpyHostToDevice));
+      TRY_CUDA(upload_bf16(d.s, sc.data(), sc.size()));
+      TRY_CUDA(upload_bf16(d.z, zp.data(), zp.size()));
+    } else {
+      std::vector<float> w(static_cast<size_t>(N) * Kin);
+      for (int n = 0; n < N; ++n)
+        memcpy(w.data() + static_cast<size_t>(n) * Kin, L.w.data() + static_cast<size_t>(src_row(n)) * Kin,
+               sizeof(float) * Kin);
+      TRY_CUDA(upload_bf16(d.w, w.data(), w.size()));
+    }
+    d.has_b = !L.bias.empty();
+    if (d.has_b) {
+      std::vector<float> b(N);
+      for (int n = 0; n < N; ++n) b[n] = L.bias[src_row(n)];
+      TRY_CUDA(upload_bf16(d.b, b.data(), b.size()));
+    }
+  }
+  auto rounded = [](const std::vector<float>& v) {
+    std::vector<float> r(v.size());
+    for (size_t i = 0; i < v.size(); ++i) r[i] = nrp::bf16_round(v[i]);
+    return r;
+  };
+  for (int i = 0; i < kNumNorms; ++i) {
+    TRY_CUDA(upload_f32(k->d_ng[i], rounded(k->ng[i])));
+    TRY_CUDA(upload_f32(k->d_nb[i], rounded(k->nb[i])));
+  }
+  // depthwise weight: MLX [D, K, 1] == [D][K]
+  TRY_CUDA(upload_f32(k->d_dw_w, rounded(k->dw_w)));
+  if (!k->dw_b.empty()) TRY_CUDA(upload_f32(k->d_dw_b, rounded(k->dw_b)));
+  if (k->conv_norm == 0) {
+    std::vector<float> scale(D), shift(D);
+    const float eps = nrp::bf16_round(1e-5f);
+    for (int c = 0; c < D; ++c) {
+      const float g = nrp::bf16_round(k->cn_g[c]), b = nrp::bf16_round(k->cn_b[c]);
+      const float m = nrp::bf16_round(k->cn_m[c]), v = nrp::bf16_round(k->cn_v[c]);
+      scale[c] = g / sqrtf(v + eps);
+      shift[c] = b - m * scale[c];
+    }
+    TRY_CUDA(upload_f32(k->d_cn_scale, scale));
+    TRY_CUDA(upload_f32(k->d_cn_shift, shift));
+  } else {
+    TRY_CUDA(upload_f32(k->d_cn_g, rounded(k->cn_g)));
+    TRY_CUDA(upload_f32(k->d_cn_b, rounded(k->cn_b)));
+  }
+  k->dirty = false;
+  return NRP_OK;
+}
+
+int block_linear(nrp_block* k, cudaStream_t st, int which, const void* x, int M, void* y,
+                 int ldy, const nrp::RowTiling& rt, const nrp::Epilogue& ep) {
+  int N, Kin;
+  linear_shape(k, which, N, Kin);
+  const DevLinear& d = k->dl[which];
+  return nrp::linear(k->ctx, st, NRP_DTYPE_BF16, x, M, Kin, d.w.p, d.quant, d.s.p, d.z.p, N,
+                     d.has_b ? d.b.p : nullptr, y, ldy, rt, ep);
+}
+
+int layer_norm(nrp_block* k, cudaStream_t st, int which, const void* x, void* y, int64_t rows) {
+  nrp::ProfScope ps(k->ctx, NRP_KERNEL_LAYERNORM, st);
+  TRY_CUDA(nrp::launch_layernorm(static_cast<const __nv_bfloat16*>(x), k->d_ng[which].as<float>(),
+                                 k->d_nb[which].as<float>(), static_cast<__nv_bfloat16*>(y), rows,
+                                 k->D, 1e-5f, false, st));
+  return NRP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nrp_block_create(nrp_context* ctx, int d_model, int n_heads, int ff_dim, int conv_kernel,
+                     int causal_conv, int conv_norm, int use_bias, nrp_block** out) {
+  if (!ctx || !out) return failf(NRP_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (d_model <= 0 || n_heads <= 0 || d_model % n_heads || ff_dim <= 0 || conv_kernel <= 0 ||
+      (conv_norm != 0 && conv_norm != 1))
+    return failf(NRP_ERR_INVALID, "invalid block configuration");
+  // a symmetric ("same") padding keeps T frames only for an odd kernel
+  if (!causal_conv && conv_kernel % 2 == 0)
+    return failf(NRP_ERR_UNSUPPORTED, "non-causal conv needs an odd kernel (%d)", conv_kernel);
+  auto* k = new nrp_block;
+  k->ctx = ctx;
+  k->D = d_model;
+  k->H = n_heads;
+  k->ff = ff_dim;
+  k->K = conv_kernel;
+  k->causal = causal_conv != 0;
+  k->conv_norm = conv_norm;
+  k->use_bias = use_bias;
+  int rc = nrp_attn_create(ctx, d_model, n_heads, use_bias, &k->attn);
+  if (rc) {
+    delete k;
+    return rc;
+  }
+  // nn::LayerNorm::new / BatchNorm::new defaults: weight 1, bias 0, running
+  // mean 0, running var 1; the linears start as zeros with biases
+  // (FeedForward::new 2046-2063, ConvolutionModule::new 2137-2196).
+  for (int i = 0; i < kNumNorms; ++i) {
+    k->ng[i].assign(d_model, 1.f);
+    k->nb[i].assign(d_model, 0.f);
+  }
+  k->cn_g.assign(d_model, 1.f);
+  k->cn_b.assign(d_model, 0.f);
+  k->cn_m.assign(d_model, 0.f);
+  k->cn_v.assign(d_model, 1.f);
+  k->dw_w.assign(static_cast<size_t>(d_model) * conv_kernel, 0.f);
+  if (use_bias) k->dw_b.assign(d_model, 0.f);
+  for (int i = 0; i < kNumLinears; ++i) {
+    int N, Kin;
+    linear_shape(k, i, N, Kin);
+    nrp::Linear& L = k->lin[i];
+    L.loaded = true;
+    L.w.assign(static_cast<size_t>(N) * Kin, 0.f);
+    const bool conv = i == NRP_BLOCK_CONV_PW1 || i == NRP_BLOCK_CONV_PW2;
+    if (use_bias || conv) L.bias.assign(N, 0.f);
+  }
+  *out = k;
+  return NRP_OK;
+}
+
+int nrp_block_destroy(nrp_block* k) {
+  if (!k) return NRP_OK;
+  nrp_attn_destroy(k->attn);
+  delete k;
+  return NRP_OK;
+}
+
+int nrp_block_set_dtype(nrp_block* k, int dtype) {
+  if (!k) return failf(NRP_ERR_INVALID, "null block");
+  if (dtype != NRP_DTYPE_F32 && dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_INVALID, "dtype %d", dtype);
+  k->dtype = dtype;
+  k->dirty = true;
+  return nrp_attn_set_dtype(k->attn, dtype);
+}
+
+int nrp_block_attn(nrp_block* k, nrp_attn** attn) {
+  if (!k || !attn) return failf(NRP_ERR_INVALID, "null argument");
+  *attn = k->attn;
+  return NRP_OK;
+}
+
+int nrp_block_load_linear(nrp_block* k, int which, const float* w, const float* bias) {
+  if (!k || !w) return failf(NRP_ERR_INVALID, "null argument");
+  if (which < 0 || which >= kNumLinears) return failf(NRP_ERR_INVALID, "linear %d", which);
+  int N, Kin;
+  linear_shape(k, which, N, Kin);
+  nrp::Linear& L = k->lin[which];
+  L = nrp::Linear();
+  L.loaded = true;
+  L.w.assign(w, w + static_cast<size_t>(N) * Kin);
+  if (bias) L.bias.assign(bias, bias + N);
+  k->dirty = true;
+  return NRP_OK;
+}
+
+int nrp_block_load_linear_quantized(nrp_block* k, int which, int bits, int group_size,
+                                    const uint32_t* wq, const float* scales,
+                                    const float* biases, const float* bias) {
+  if (!k || !wq || !scales || !biases) return failf(NRP_ERR_INVALID, "null argument");
+  if (which < 0 || which >= kNumLinears) return failf(NRP_ERR_INVALID, "linear %d", which);
+  if (bits != 8 || group_size != 64)
+    return failf(NRP_ERR_UNSUPPORTED, "quantized layers need bits 8, group 64");
+  int N, Kin;
+  linear_shape(k, which, N, Kin);
+  if (Kin % 64) return failf(NRP_ERR_UNSUPPORTED, "in features %d not a multiple of 64", Kin);
+  nrp::Linear& L = k->lin[which];
+  L = nrp::Linear();
+  L.loaded = true;
+  L.quant = true;
+  L.bits = bits;
+  L.group = group_size;
+  L.wq.assign(wq, wq + static_cast<size_t>(N) * Kin / 4);
+  L.qs.assign(scales, scales + static_cast<size_t>(N) * (Kin / 64));
+  L.qb.assign(biases, biases + static_cast<size_t>(N) * (Kin / 64));
+  if (bias) L.bias.assign(bias, bias + N);
+  k->dirty = true;
+  return NRP_OK;
+}
+
+int nrp_block_load_norm(nrp_block* k, int which, const float* gamma, const float* beta) {
+  if (!k || !gamma || !beta) return failf(NRP_ERR_INVALID, "null argument");
+  if (which < 0 || which >= kNumNorms) return failf(NRP_ERR_INVALID, "norm %d", which);
+  k->ng[which].assign(gamma, gamma + k->D);
+  k->nb[which].assign(beta, beta + k->D);
+  k->dirty = true;
+  return NRP_OK;
+}
+
+int nrp_block_load_depthwise(nrp_block* k, const float* w, const float* bias) {
+  if (!k || !w) return failf(NRP_ERR_INVALID, "null argument");
+  k->dw_w.assign(w, w + static_cast<size_t>(k->D) * k->K);
+  if (bias) k->dw_b.assign(bias, bias + k->D);
+  else k->dw_b.clear();
+  k->dirty = true;
+  return NRP_OK;
+}
+
+int nrp_block_load_conv_norm(nrp_block* k, const float* gamma, const float* beta,
+                             const float* mean, const float* var) {
+  if (!k || !gamma || !beta) return failf(NRP_ERR_INVALID, "null argument");
+  k->cn_g.assign(gamma, gamma + k->D);
+  k->cn_b.assign(beta, beta + k->D);
+  if (k->conv_norm == 0) {
+    if (!mean || !var) return failf(NRP_ERR_INVALID, "batch norm needs running statistics");
+    k->cn_m.assign(mean, mean + k->D);
+    k->cn_v.assign(var, var + k->D);
+  }
+  k->dirty = true;
+  return NRP_OK;
+}
+
+int nrp_block_forward(nrp_block* k, void* stream, const void* x, int B, int T,
+                      const void* pos_emb, const int32_t* lengths,
+                      const nrp_att_context* context, void* out) {
+  if (!k || !x || !pos_emb || !out) return failf(NRP_ERR_INVALID, "null argument");
+  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  if (k->dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_UNSUPPORTED, "the conformer block runs in bf16 (nrp_block_set_dtype)");
+  const int D = k->D;
+  if (D != 256 && D != 512 && D != 1024 && D != 2048)
+    return failf(NRP_ERR_UNSUPPORTED, "d_model %d (the block needs 256, 512, 1024 or 2048)", D);
+  if (k->ff % 64) return failf(NRP_ERR_UNSUPPORTED, "ff_dim %d not a multiple of 64", k->ff);
+  // padded frames are zeroed by the GEMMs' per-utterance row tiling
+  if (lengths && B > 256)
+    return failf(NRP_ERR_UNSUPPORTED, "the block with lengths supports batch <= 256");
+  if (nrp::select_device(k->ctx)) return NRP_ERR_CUDA;
+  int rc = sync_block(k);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t M = static_cast<int64_t>(B) * T;
+  if (M > INT32_MAX / 4) return failf(NRP_ERR_UNSUPPORTED, "batch x seq_len too large");
+  const int Mi = static_cast<int>(M);
+  TRY_CUDA(k->h.ensure(M * D * 2));
+  TRY_CUDA(k->hid.ensure(M * k->ff * 2));
+  TRY_CUDA(k->glu.ensure(M * D * 2));
+  TRY_CUDA(k->dw.ensure(M * D * 2));
+  if (out != x) {
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(cudaMemcpyAsync(out, x, M * D * 2, cudaMemcpyDeviceToDevice, st));
+  }
+  nrp::RowTiling rows;
+  if (lengths && B <= 256) rows = {lengths, T, B};
+  auto residual = [&](float alpha) {
+    nrp::Epilogue e;
+    e.mode = nrp::kEpiResidual;
+    e.res = static_cast<const __nv_bfloat16*>(out);
+    e.ldr = D;
+    e.alpha = alpha;
+    return e;
+  };
+  nrp::Epilogue silu;
+  silu.mode = nrp::kEpiSilu;
+  auto feed_forward = [&](int norm, int l1, int l2) -> int {
+    int r = layer_norm(k, st, norm, out, k->h.p, M);
+    if (!r) r = block_linear(k, st, l1, k->h.p, Mi, k->hid.p, k->ff, rows, silu);
+    if (!r) r = block_linear(k, st, l2, k->hid.p, Mi, out, D, rows, residual(0.5f));
+    return r;
+  };
+  // 1703-1733: x += 0.5 * FF1(LN x)
+  rc = feed_forward(NRP_BLOCK_NORM_FF1, NRP_BLOCK_FF1_LINEAR1, NRP_BLOCK_FF1_LINEAR2);
+  if (rc) return rc;
+  // 1750-1785: x += MHA(LN x)
+  rc = layer_norm(k, st, NRP_BLOCK_NORM_ATT, out, k->h.p, M);
+  if (rc) return rc;
+  rc = nrp::attn_forward(k->attn, st, k->h.p, B, T, pos_emb, lengths, context, out, residual(1.f));
+  if (rc) return rc;
+  // 1797-1824, 2249-2330: x += Conv(LN x)
+  rc = layer_norm(k, st, NRP_BLOCK_NORM_CONV, out, k->h.p, M);
+  if (rc) return rc;
+  nrp::Epilogue glu;
+  glu.mode = nrp::kEpiGlu;
+  glu.len = rows.len;
+  rc = block_linear(k, st, NRP_BLOCK_CONV_PW1, k->h.p, Mi, k->glu.p, D, rows, glu);
+  if (rc) return rc;
+  {
+    const bool bn = k->conv_norm == 0;
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_DWCONV, st);
+    TRY_CUDA(nrp::launch_dwconv(k->glu.as<__nv_bfloat16>(), k->d_dw_w.as<float>(),
+                                k->dw_b.empty() ? nullptr : k->d_dw_b.as<float>(),
+                                bn ? k->d_cn_scale.as<float>() : nullptr,
+                                bn ? k->d_cn_shift.as<float>() : nullptr,
+                                k->dw.as<__nv_bfloat16>(), B, T, D, k->K, k->causal, bn, st));
+  }
+  if (k->conv_norm == 1) {  // LayerNorm conv norm, then SiLU
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_LAYERNORM, st);
+    TRY_CUDA(nrp::launch_layernorm(k->dw.as<__nv_bfloat16>(), k->d_cn_g.as<float>(),
+                                   k->d_cn_b.as<float>(), k->dw.as<__nv_bfloat16>(), M, D, 1e-5f,
+                                   true, st));
+  }
+  rc = block_linear(k, st, NRP_BLOCK_CONV_PW2, k->dw.p, Mi, out, D, rows, residual(1.f));
+  if (rc) return rc;
+  // 1826-1858: x += 0.5 * FF2(LN x)
+  rc = feed_forward(NRP_BLOCK_NORM_FF2, NRP_BLOCK_FF2_LINEAR1, NRP_BLOCK_FF2_LINEAR2);
+  if (rc) return rc;
+  // 1861: final LayerNorm
+  return layer_norm(k, st, NRP_BLOCK_NORM_OUT, out, out, M);
+}
+
+// ---------------------------------------------------------------- encoder
+int nrp_encoder_create(nrp_context* ctx, int n_layers, int d_model, int n_heads, int ff_dim,
+                       int conv_kernel, int causal_conv, int conv_norm, int use_bias,
+                       int xscaling, int max_len, nrp_encoder** out) {
+  if (!ctx || !out) return failf(NRP_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (n_layers <= 0 || max_len <= 0) return failf(NRP_ERR_INVALID, "invalid encoder configuration");
+  auto* e = new nrp_encoder;
+  e->ctx = ctx;
+  e->D = d_model;
+  e->H = n_heads;
+  e->max_len = max_len;
+  e->xscale = nrp_pe_xscale(d_model, xscaling);
+  for (int i = 0; i < n_layers; ++i) {
+    nrp_block* b = nullptr;
+    const int rc = nrp_block_create(ctx, d_model, n_heads, ff_dim, conv_kernel, causal_conv,
+                                    conv_norm, use_bias, &b);
+    if (rc) {
+      nrp_encoder_destroy(e);
+      return rc;
+    }
+    e->blocks.push_back(b);
+  }
+  *out = e;
+  return NRP_OK;
+}
+
+int nrp_encoder_destroy(nrp_encoder* e) {
+  if (!e) return NRP_OK;
+  for (nrp_block* b : e->blocks) nrp_block_destroy(b);
+  delete e;
+  return NRP_OK;
+}
+
+int nrp_encoder_block(nrp_encoder* e, int layer, nrp_block** block) {
+  if (!e || !block) return failf(NRP_ERR_INVALID, "null argument");
+  if (layer < 0 || layer >= static_cast<int>(e->blocks.size()))
+    return failf(NRP_ERR_INVALID, "layer %d of %d", layer, static_cast<int>(e->blocks.size()));
+  *block = e->blocks[layer];
+  return NRP_OK;
+}
+
+int nrp_encoder_set_dtype(nrp_encoder* e, int dtype) {
+  if (!e) return failf(NRP_ERR_INVALID, "null encoder");
+  for (nrp_block* b : e->blocks) {
+    const int rc = nrp_block_set_dtype(b, dtype);
+    if (rc) return rc;
+  }
+  e->dtype = dtype;
+  return NRP_OK;
+}
+
+int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void* x, int B, int T,
+                                        const int32_t* lengths, const nrp_att_context* context,
+                                        void* out) {
+  if (!e || !x || !out) return failf(NRP_ERR_INVALID, "null argument");
+  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  if (e->dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_UNSUPPORTED, "the encoder runs in bf16 (nrp_encoder_set_dtype)");
+  if (nrp::select_device(e->ctx)) return NRP_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int D = e->D;
+  const int64_t n = static_cast<int64_t>(B) * T * D;
+  TRY_CUDA(e->x.ensure(n * 2));
+  // 707-708: the positional table for this length (built once per length;
+  // nrp_pe_encoding stages it through the host)
+  if (e->pos_T != T) {
+    TRY_CUDA(e->pos.ensure(static_cast<size_t>(2 * T - 1) * D * 2));
+    const int rc = nrp_pe_encoding(e->ctx, D, e->max_len, T, NRP_DTYPE_BF16, e->pos.p, stream);
+    if (rc) return rc;
+    e->pos_T = T;
+  }
+  {
+    nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(cudaMemcpyAsync(e->x.p, x, n * 2, cudaMemcpyDeviceToDevice, st));
+    // 701-704: x * xscale
+    if (e->xscale != 1.f)
+      TRY_CUDA(nrp::launch_scale(e->x.as<__nv_bfloat16>(), n, nrp::bf16_round(e->xscale), st));
+  }
+  for (nrp_block* b : e->blocks) {
+    const int rc = nrp_block_forward(b, stream, e->x.p, B, T, e->pos.p, lengths, context, e->x.p);
+    if (rc) return rc;
+  }
+  // 717: transpose to [B, D, T]
+  nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
+  TRY_CUDA(nrp::launch_transpose_btd(e->x.as<__nv_bfloat16>(), static_cast<__nv_bfloat16*>(out), B,
+                                     T, D, st));
+  return NRP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,234 @@
+// block_kernels.cu -- the HBM-bound kernels of the Conformer block
+// (src/asr/modules/encoders/conformer.rs:1693-1870, 2120-2330) that are not
+// fused into a GEMM epilogue: LayerNorm, the depthwise convolution with the
+// inference BatchNorm and SiLU, the input scaling of forward_from_embeddings
+// and the final [B, T, D] -> [B, D, T] transpose.  All bf16 in HBM, f32 in
+// registers, one rounding per output.
+#include <cuda_bf16.h>
+
+#include "gemm.h"
+#include "sm100.cuh"
+
+namespace nrp {
+namespace {
+
+__device__ __forceinline__ void unpack8(const uint4& q, float* f) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+
+__device__ __forceinline__ float silu(float v) { return v * __fdividef(1.f, 1.f + __expf(-v)); }
+
+// nn::LayerNorm (eps 1e-5, affine): one warp per row of D = 256 * kChunks,
+// the row held in registers (each lane 8 consecutive values per chunk);
+// mean first, then the variance about it.  y may alias x.
+template <int kChunks>
+__global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* x,
+                                                        const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta,
+                                                        __nv_bfloat16* y, int64_t rows, float eps,
+                                                        int act_silu) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  constexpr int D = 256 * kChunks;
+  const __nv_bfloat16* xr = x + row * D;
+  float v[kChunks][8];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    unpack8(*reinterpret_cast<const uint4*>(xr + c * 256 + lane * 8), v[c]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += v[c][e];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float d = v[c][e] - mean;
+      q += d * d;
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float inv = rsqrtf(q * (1.f / D) + eps);
+  __nv_bfloat16* yr = y + row * D;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = c * 256 + lane * 8;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float t = (v[c][e] - mean) * inv * gamma[col + e] + beta[col + e];
+      o[e] = act_silu ? silu(t) : t;
+    }
+    *reinterpret_cast<uint4*>(yr + col) = pack8(o);
+  }
+}
+
+// Depthwise Conv1d over time (groups = D, kernel K, zero padding `pad_left`
+// frames before and K-1-pad_left after: (K-1)/2 each side offline, K-1 on the
+// left when causal), + bias, then optionally the inference BatchNorm folded
+// to a per-channel affine and SiLU.  A CTA covers kTT output frames of one
+// utterance; its input rows (kTT + K - 1) are staged in shared memory and
+// each thread owns 8 channels.
+constexpr int kTT = 32;
+__global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __restrict__ x,
+                                                     const float* __restrict__ w,  // [D][K]
+                                                     const float* __restrict__ bias,
+                                                     const float* __restrict__ bn_scale,
+                                                     const float* __restrict__ bn_shift,
+                                                     __nv_bfloat16* __restrict__ y, int T, int D,
+                                                     int K, int pad_left, int act_silu) {
+  extern __shared__ __align__(16) uint8_t dw_smem[];
+  __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(dw_smem);  // [kTT + K - 1][D]
+  const int b = blockIdx.y;
+  const int t0 = blockIdx.x * kTT;
+  const int rows = kTT + K - 1;
+  const int vecs = D / 8;
+  const __nv_bfloat16* xb = x + static_cast<int64_t>(b) * T * D;
+  for (int i = threadIdx.x; i < rows * vecs; i += blockDim.x) {
+    const int r = i / vecs, cv = i - r * vecs;
+    const int t = t0 - pad_left + r;
+    uint4 q = make_uint4(0u, 0u, 0u, 0u);
+    if (t >= 0 && t < T) q = *reinterpret_cast<const uint4*>(xb + static_cast<int64_t>(t) * D + cv * 8);
+    *reinterpret_cast<uint4*>(tile + r * D + cv * 8) = q;
+  }
+  __syncthreads();
+  __nv_bfloat16* yb = y + static_cast<int64_t>(b) * T * D;
+  for (int cv = threadIdx.x; cv < vecs; cv += blockDim.x) {
+    const int c0 = cv * 8;
+    float sc[8], sh[8], bi[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      bi[e] = bias ? bias[c0 + e] : 0.f;
+      sc[e] = bn_scale ? bn_scale[c0 + e] : 1.f;
+      sh[e] = bn_shift ? bn_shift[c0 + e] : 0.f;
+    }
+    const int tn = min(kTT, T - t0);
+    for (int tt = 0; tt < tn; ++tt) {
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int k = 0; k < K; ++k) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += w[(c0 + e) * K + k] * f[e];
+      }
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float t = (acc[e] + bi[e]) * sc[e] + sh[e];
+        o[e] = act_silu ? silu(t) : t;
+      }
+      *reinterpret_cast<uint4*>(yb + static_cast<int64_t>(t0 + tt) * D + c0) = pack8(o);
+    }
+  }
+}
+
+__global__ void scale_kernel(__nv_bfloat16* x, int64_t n8, float s) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float f[8];
+    unpack8(reinterpret_cast<const uint4*>(x)[i], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] *= s;
+    reinterpret_cast<uint4*>(x)[i] = pack8(f);
+  }
+}
+
+// [B, T, D] -> [B, D, T], 32 x 32 tiles through shared memory.
+__global__ void transpose_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                                 int T, int D) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const __nv_bfloat16* xb = x + static_cast<int64_t>(b) * T * D;
+  __nv_bfloat16* yb = y + static_cast<int64_t>(b) * T * D;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int t = t0 + r, d = d0 + threadIdx.x;
+    if (t < T && d < D) tile[r][threadIdx.x] = xb[static_cast<int64_t>(t) * D + d];
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int d = d0 + r, t = t0 + threadIdx.x;
+    if (t < T && d < D) yb[static_cast<int64_t>(d) * T + t] = tile[threadIdx.x][r];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_layernorm(const __nv_bfloat16* x, const float* gamma, const float* beta,
+                             __nv_bfloat16* y, int64_t rows, int D, float eps, bool act_silu,
+                             cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
+  switch (D) {
+    case 256:
+      layernorm_kernel<1><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
+      break;
+    case 512:
+      layernorm_kernel<2><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
+      break;
+    case 1024:
+      layernorm_kernel<4><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
+      break;
+    case 2048:
+      layernorm_kernel<8><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+size_t dwconv_smem_bytes(int D, int K) { return static_cast<size_t>(kTT + K - 1) * D * 2; }
+
+cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* w, const float* bias,
+                          const float* bn_scale, const float* bn_shift, __nv_bfloat16* y, int B,
+                          int T, int D, int K, bool causal, bool act_silu, cudaStream_t stream) {
+  if (B <= 0 || T <= 0) return cudaSuccess;
+  if (D % 8 != 0 || K < 1 || B > 65535) return cudaErrorInvalidValue;
+  const size_t smem = dwconv_smem_bytes(D, K);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr{0};
+  if (smem > 48 * 1024)
+    if (cudaError_t e = smem_attr_once(dwconv_kernel, 227 * 1024, attr)) return e;
+  const dim3 grid((T + kTT - 1) / kTT, B);
+  const int threads = D / 8 < 256 ? D / 8 : 256;
+  dwconv_kernel<<<grid, threads, smem, stream>>>(x, w, bias, bn_scale, bn_shift, y, T, D, K,
+                                                  causal ? K - 1 : (K - 1) / 2, act_silu);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  if (n % 8 != 0) return cudaErrorInvalidValue;
+  scale_kernel<<<592, 256, 0, stream>>>(x, n / 8, s);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D,
+                                 cudaStream_t stream) {
+  if (B <= 0 || T <= 0) return cudaSuccess;
+  if (B > 65535) return cudaErrorInvalidValue;
+  const dim3 grid((T + 31) / 32, (D + 31) / 32, B);
+  transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(x, y, T, D);
+  return cudaGetLastError();
+}
+
+}  // namespace nrp

@@ -53,6 +53,26 @@ struct RowTiling {
   int64_t y_bstride = 0;
 };
 
+// What the GEMM epilogue does with v = acc + bias (f32) before the single
+// rounding to bf16:
+//   kEpiBias      y = v
+//   kEpiSilu      y = v * sigmoid(v)                      (FeedForward::forward)
+//   kEpiResidual  y = res + alpha * v; res may alias y     (the block's residuals)
+//   kEpiGlu       W's rows come in 256-row tiles [128 value rows | their 128
+//                 gate rows]; tile k writes output columns [128k, 128k + 128)
+//                 = value * sigmoid(gate), so y has N/2 columns; with len,
+//                 rows t >= len[b] are written as zeros (ConvolutionModule's
+//                 GLU and padded-frame zeroing)
+enum EpiMode { kEpiBias = 0, kEpiSilu = 1, kEpiResidual = 2, kEpiGlu = 3 };
+struct Epilogue {
+  int mode = kEpiBias;
+  const __nv_bfloat16* res = nullptr;
+  int64_t ldr = 0;     // residual row stride (elements)
+  int64_t res_bs = 0;  // residual batch stride under batched tiling (0: T * ldr)
+  float alpha = 1.f;
+  const int32_t* len = nullptr;  // kEpiGlu, batched tiling
+};
+
 // ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
 // x map: bf16 [M, K], box (64, 128), swizzle 128.  W map: bf16 [N, K], box
 // (64, 256), swizzle 128.  Requires K % 64 == 0 and N % 32 == 0.
@@ -60,13 +80,14 @@ int gemm_smem_bytes();
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
                              int K, int num_sms, int* err, cudaStream_t stream,
-                             RowTiling rt = RowTiling());
+                             RowTiling rt = RowTiling(), const Epilogue& ep = Epilogue());
 // Quantised W: MLX affine 8-bit, group 64: wq [N, K] bytes (the packed u32
 // words read as little-endian bytes), scales/biases bf16 [N, K/64].
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
-                           cudaStream_t stream, RowTiling rt = RowTiling());
+                           cudaStream_t stream, RowTiling rt = RowTiling(),
+                           const Epilogue& ep = Epilogue());
 
 // ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
@@ -145,6 +166,21 @@ cudaError_t launch_relpos_attn_stream_simt(const T* q, int ldq, const T* knew, c
                                            const T* p, const float* u, const float* vb,
                                            StreamMaskDev sm, T* out, int B, int T_, int D, int H,
                                            cudaStream_t stream);
+
+// ---- Conformer block kernels (block_kernels.cu) ----
+// LayerNorm over rows of D in {256, 512, 1024, 2048} (gamma/beta f32 [D]),
+// optionally followed by SiLU; y may alias x.
+cudaError_t launch_layernorm(const __nv_bfloat16* x, const float* gamma, const float* beta,
+                             __nv_bfloat16* y, int64_t rows, int D, float eps, bool act_silu,
+                             cudaStream_t stream);
+// Depthwise conv over time of [B, T, D] (w f32 [D][K], bias [D] or null),
+// then y = act((conv + bias) * bn_scale + bn_shift) (scale/shift null = 1/0).
+cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* w, const float* bias,
+                          const float* bn_scale, const float* bn_shift, __nv_bfloat16* y, int B,
+                          int T, int D, int K, bool causal, bool act_silu, cudaStream_t stream);
+cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stream);
+cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D,
+                                 cudaStream_t stream);
 
 // ---- small elementwise helpers ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,

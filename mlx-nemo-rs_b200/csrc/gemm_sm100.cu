@@ -59,8 +59,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                    const __nv_bfloat16* __restrict__ qs,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ bias, // [N] or null
-                   __nv_bfloat16* __restrict__ y, int ldy, int M, int N, int K, RowTiling rt,
-                   int* err) {
+                   int M, int N, int K, RowTiling rt, Epilogue ep, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -241,18 +240,74 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         tc_fence_after();
       }
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
+      const bool glu = ep.mode == kEpiGlu;
+      const int ncols = glu ? kBN / 2 : kBN;  // output columns of the tile
+      const int on0 = glu ? n0 / 2 : n0;      // its first output column
+      const int n_out = glu ? N / 2 : N;
+      const int row = m0 + quad * 32 + lane;  // this thread's row (in its utterance)
+      const bool row_in = row < (batched ? rt.T : M);
+      bool keep = true;  // GLU: padded frames are zeros
+      if (glu && ep.len && batched && !skip) keep = row < ep.len[bb];
 #pragma unroll 1
-      for (int c = 0; c < kBN; c += 64) {
-        uint32_t r[64];
-        if (!skip) {
+      for (int c = 0; c < ncols; c += 64) {
+        float v[64];
+        if (!skip && glu) {
+#pragma unroll
+          for (int h = 0; h < 64; h += 32) {  // value columns c+h.., gate columns 128+c+h..
+            uint32_t ar[32], gr[32];
+            tmem_ld32(taddr + c + h, ar);
+            tmem_ld32(taddr + 128 + c + h, gr);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              float a = __uint_as_float(ar[e]);
+              float g = __uint_as_float(gr[e]);
+              if (bias) {
+                a += __bfloat162float(bias[n0 + c + h + e]);
+                g += __bfloat162float(bias[n0 + 128 + c + h + e]);
+              }
+              v[h + e] = keep ? a * __fdividef(1.f, 1.f + __expf(-g)) : 0.f;
+            }
+          }
+        } else if (!skip) {
+          uint32_t r[64];
           tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(r));
           tmem_ld32(taddr + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
-          tmem_ld_wait();
+          {
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 64; ++e) {
+              const int n = n0 + c + e;
+              v[e] = __uint_as_float(r[e]) +
+                     ((bias && n < N) ? __bfloat162float(bias[n]) : 0.f);
+            }
+            if (ep.mode == kEpiSilu) {
+#pragma unroll
+              for (int e = 0; e < 64; ++e) v[e] = v[e] * __fdividef(1.f, 1.f + __expf(-v[e]));
+            } else if (ep.mode == kEpiResidual && row_in) {
+              const int64_t bs = ep.res_bs ? ep.res_bs : static_cast<int64_t>(rt.T) * ep.ldr;
+              const __nv_bfloat16* rp =
+                  ep.res + (batched ? bb * bs : 0) + static_cast<int64_t>(row) * ep.ldr + on0 + c;
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch) {
+                if (on0 + c + ch * 8 >= n_out) break;
+                const uint4 q = *reinterpret_cast<const uint4*>(rp + ch * 8);
+                const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f =
+                      __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[e]));
+                  v[ch * 8 + 2 * e] = f.x + ep.alpha * v[ch * 8 + 2 * e];
+                  v[ch * 8 + 2 * e + 1] = f.y + ep.alpha * v[ch * 8 + 2 * e + 1];
+                }
+              }
+            }
+          }
         } else {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) r[e] = 0u;
+          for (int e = 0; e < 64; ++e) v[e] = 0.f;
         }
-        if (n0 + c >= N) continue;  // whole slab past N (warp-uniform)
+        if (on0 + c >= n_out) continue;  // whole slab past N (warp-uniform)
         uint8_t* sb = slab + (nslab & 1) * kSlabBytes;
         // the store issued two slabs ago must have finished reading sb
         if (lane == 0) bulk_wait_read<1>();
@@ -261,17 +316,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         for (int ch = 0; ch < 8; ++ch) {
           uint32_t pk[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int col = ch * 8 + 2 * e;
-            float lo = __uint_as_float(r[col]);
-            float hi = __uint_as_float(r[col + 1]);
-            if (bias && !skip) {
-              const int n = n0 + c + col;
-              lo += n < N ? __bfloat162float(bias[n]) : 0.f;
-              hi += n + 1 < N ? __bfloat162float(bias[n + 1]) : 0.f;
-            }
-            pk[e] = pack_bf16x2(lo, hi);
-          }
+          for (int e = 0; e < 4; ++e) pk[e] = pack_bf16x2(v[ch * 8 + 2 * e], v[ch * 8 + 2 * e + 1]);
           *reinterpret_cast<uint4*>(sb + sw128_offset(lane, ch)) =
               make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
@@ -279,9 +324,9 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         __syncwarp();
         if (lane == 0) {
           if (batched)
-            tma_store_3d(&map_y, sb, n0 + c, m0 + quad * 32, bb);
+            tma_store_3d(&map_y, sb, on0 + c, m0 + quad * 32, bb);
           else
-            tma_store_2d(&map_y, sb, n0 + c, m0 + quad * 32);
+            tma_store_2d(&map_y, sb, on0 + c, m0 + quad * 32);
           bulk_commit();
         }
         ++nslab;
@@ -373,6 +418,15 @@ bool make_y_map(CUtensorMap* map, __nv_bfloat16* y, int ldy, int M, int N, const
   return make_tmap_2d(map, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M,
                       static_cast<uint64_t>(ldy) * 2, 64, 32, true);
 }
+// The residual is read with 16-byte loads; GLU tiles pair 128 value and 128
+// gate columns.
+bool epilogue_ok(const Epilogue& ep, int N) {
+  if (ep.mode == kEpiResidual)
+    return ep.res && ep.ldr % 8 == 0 && ep.res_bs % 8 == 0 && N % 8 == 0 &&
+           (reinterpret_cast<uintptr_t>(ep.res) & 15) == 0;
+  if (ep.mode == kEpiGlu) return N % kBN == 0;
+  return ep.mode == kEpiBias || ep.mode == kEpiSilu;
+}
 int grid_size(int M, int N, const RowTiling& rt, int num_sms) {
   const int tiles_m = rt.T > 0 ? rt.B * ((rt.T + kBM - 1) / kBM) : (M + kBM - 1) / kBM;
   const int tiles = tiles_m * ((N + kBN - 1) / kBN);
@@ -382,32 +436,37 @@ int grid_size(int M, int N, const RowTiling& rt, int num_sms) {
 
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
-                             int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt) {
+                             int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt,
+                             const Epilogue& ep) {
   static std::atomic<uint64_t> attr{0};
   if (cudaError_t e = smem_attr_once(gemm_tn_kernel<false>, static_cast<int>(kSmemBytes), attr))
     return e;
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
+  if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
   const int grid = grid_size(M, N, rt, num_sms);
   CUtensorMap map_y;
-  if (!make_y_map(&map_y, y, ldy, M, N, rt)) return cudaErrorInvalidValue;
+  if (!make_y_map(&map_y, y, ldy, M, ep.mode == kEpiGlu ? N / 2 : N, rt))
+    return cudaErrorInvalidValue;
   gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, map_y, nullptr, nullptr,
-                                                           nullptr, bias, y, ldy, M, N, K, rt, err);
+                                                           nullptr, bias, M, N, K, rt, ep, err);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
-                           cudaStream_t stream, RowTiling rt) {
+                           cudaStream_t stream, RowTiling rt, const Epilogue& ep) {
   static std::atomic<uint64_t> attr{0};
   if (cudaError_t e = smem_attr_once(gemm_tn_kernel<true>, static_cast<int>(kSmemBytes), attr))
     return e;
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
+  if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
   const int grid = grid_size(M, N, rt, num_sms);
   CUtensorMap map_y;
-  if (!make_y_map(&map_y, y, ldy, M, N, rt)) return cudaErrorInvalidValue;
-  gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, map_y, wq, qs, qb, bias, y,
-                                                          ldy, M, N, K, rt, err);
+  if (!make_y_map(&map_y, y, ldy, M, ep.mode == kEpiGlu ? N / 2 : N, rt))
+    return cudaErrorInvalidValue;
+  gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, map_y, wq, qs, qb, bias, M,
+                                                          N, K, rt, ep, err);
   return cudaGetLastError();
 }
 

@@ -32,6 +32,16 @@ class _Weights(C.Structure):
                  "pos_bias_u", "pos_bias_v")]
 
 
+class _Lin(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("b", C.c_void_p)]
+
+
+class _BlockWeights(C.Structure):
+    _fields_ = ([(n, _Lin) for n in ("ff1_1", "ff1_2", "pw1", "pw2", "ff2_1", "ff2_2")] +
+                [(n, C.c_void_p) for n in ("dw_w", "dw_b", "cn_g", "cn_b", "cn_m", "cn_v")] +
+                [("norm_g", C.c_void_p * 5), ("norm_b", C.c_void_p * 5), ("attn", _Weights)])
+
+
 class _Ctx(C.Structure):
     _fields_ = [("has", C.c_int), ("left", C.c_int), ("right", C.c_int),
                 ("chunked", C.c_int)]
@@ -77,6 +87,10 @@ def lib():
             _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
             C.c_int, C.c_int, C.c_int, _f32p]
         L.orc_stream_layer_step.restype = C.c_int
+        L.orc_block_forward.argtypes = [
+            _f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+            C.POINTER(_BlockWeights), _f32p, C.c_void_p, C.c_void_p, C.c_int, _f32p]
+        L.orc_block_forward.restype = C.c_int
         L.orc_bf16_round_array.argtypes = [_f32p, C.c_int64]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
@@ -257,3 +271,49 @@ def stream_layer_step(x, w, pos_emb, n_heads, h_cache, filled, valid, left,
         x, B, T, D, n_heads, C.byref(st), _f32(pos_emb), h_cache, Cc, filled,
         valid, left, right, int(chunked), cache_drop_size, int(bool(bf16)), out)
     return out, nxt
+
+
+BLOCK_LINEARS = ("ff1_1", "ff1_2", "pw1", "pw2", "ff2_1", "ff2_2")
+BLOCK_NORMS = ("ff1", "att", "conv", "ff2", "out")
+
+
+def block_forward(x, bw, pos_emb, n_heads, ff_dim, kernel, causal=False, conv_norm=0,
+                  lengths=None, context=None, bf16=True):
+    """ConformerBlock::forward (conformer.rs:1693-1870).
+
+    bw: {"ff1_1": (w, b), ... (BLOCK_LINEARS, f32 weights [out, in]; a
+    quantised layer gives its dequantised weights), "dw": (w [D, K], b),
+    "conv_norm": (gamma, beta, mean, var) (mean/var None for a layer norm),
+    "norms": {name: (gamma, beta)} for BLOCK_NORMS, "attn": the mha_forward
+    weight dict}."""
+    x = _f32(x)
+    B, T, D = x.shape
+    keep = []
+
+    def ptr(a):
+        if a is None:
+            return None
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    st = _BlockWeights()
+    for name in BLOCK_LINEARS:
+        w, b = bw[name]
+        setattr(st, name, _Lin(ptr(w), ptr(b)))
+    st.dw_w, st.dw_b = ptr(np.asarray(bw["dw"][0]).reshape(D, kernel)), ptr(bw["dw"][1])
+    g, b, m, v = bw["conv_norm"]
+    st.cn_g, st.cn_b, st.cn_m, st.cn_v = ptr(g), ptr(b), ptr(m), ptr(v)
+    for i, name in enumerate(BLOCK_NORMS):
+        st.norm_g[i] = ptr(bw["norms"][name][0])
+        st.norm_b[i] = ptr(bw["norms"][name][1])
+    st.attn = _weights_struct(bw["attn"], keep)
+    ln = np.ascontiguousarray(lengths, np.int32) if lengths is not None else None
+    cs = _ctx_struct(context)
+    out = np.empty_like(x)
+    rc = lib().orc_block_forward(
+        x, B, T, D, n_heads, ff_dim, kernel, int(bool(causal)), int(conv_norm), C.byref(st),
+        _f32(pos_emb), ln.ctypes.data if ln is not None else None,
+        C.cast(C.pointer(cs), C.c_void_p) if cs is not None else None, int(bool(bf16)), out)
+    assert rc == 0
+    return out

@@ -653,3 +653,150 @@ int orc_stream_layer_step(const float *x, int B, int T, int D, int H,
   const int next = filled + q_keep < C ? filled + q_keep : C;
   return next;
 }
+
+/* ------------------------------------------------------ Conformer block */
+
+static inline float rnd(float v, int bf16) { return bf16 ? orc_bf16_round(v) : v; }
+
+/* nn::LayerNorm (eps 1e-5): f32 statistics, one rounding of the output
+ * (MLX's fused layer norm). g, b already in the compute dtype. */
+static void layer_norm_r(const float *x, int64_t rows, int D, const float *g,
+                         const float *b, int bf16, float *y) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const float *xr = x + r * D;
+    double s = 0.0;
+    for (int c = 0; c < D; ++c) s += xr[c];
+    const float mean = (float)(s / D);
+    double q = 0.0;
+    for (int c = 0; c < D; ++c) {
+      const double d = xr[c] - mean;
+      q += d * d;
+    }
+    const float inv = 1.0f / sqrtf((float)(q / D) + 1e-5f);
+    for (int c = 0; c < D; ++c)
+      y[r * D + c] = rnd((xr[c] - mean) * inv * g[c] + b[c], bf16);
+  }
+}
+
+/* sigmoid and x * sigmoid(x) as two rounded ops (mlx nn::silu). */
+static inline float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+static void silu_r(float *x, int64_t n, int bf16) {
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < n; ++e) x[e] = rnd(x[e] * rnd(sigm(x[e]), bf16), bf16);
+}
+
+/* FeedForward (2081-2087) and the half-step residual (1723-1726). */
+static void ff_residual(float *xx, int64_t M, int D, int ff, const orc_lin *l1,
+                        const orc_lin *l2, const float *g, const float *b, int bf16,
+                        float *h, float *hid, float *tmp) {
+  layer_norm_r(xx, M, D, g, b, bf16, h);
+  linear_r(h, (int)M, D, l1->w, ff, l1->b, bf16, hid);
+  silu_r(hid, M * ff, bf16);
+  linear_r(hid, (int)M, ff, l2->w, D, l2->b, bf16, tmp);
+  const float half = 0.5f;
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < M * D; ++e) xx[e] = rnd(xx[e] + rnd(half * tmp[e], bf16), bf16);
+}
+
+int orc_block_forward(const float *x, int B, int T, int D, int H, int ff, int K,
+                      int causal, int conv_norm, const orc_block_weights *w,
+                      const float *pos_emb, const int32_t *lengths,
+                      const orc_context *ctx, int bf16, float *out) {
+  if (B <= 0 || T <= 0 || D <= 0 || H <= 0 || D % H || ff <= 0 || K <= 0) return -1;
+  const int64_t M = (int64_t)B * T;
+  const size_t n = (size_t)M * D;
+  /* set_dtype: every block parameter in the compute dtype */
+  float *ng[5], *nb[5];
+  for (int i = 0; i < 5; ++i) {
+    ng[i] = dup_round(w->norm_g[i], D, bf16);
+    nb[i] = dup_round(w->norm_b[i], D, bf16);
+  }
+  const orc_lin *src[6] = {&w->ff1_1, &w->ff1_2, &w->pw1, &w->pw2, &w->ff2_1, &w->ff2_2};
+  const int lin_n[6] = {ff, D, 2 * D, D, ff, D}, lin_k[6] = {D, ff, D, D, D, ff};
+  orc_lin L[6];
+  for (int i = 0; i < 6; ++i) {
+    L[i].w = dup_round(src[i]->w, (size_t)lin_n[i] * lin_k[i], bf16);
+    L[i].b = dup_round(src[i]->b, (size_t)lin_n[i], bf16);
+  }
+  float *dw_w = dup_round(w->dw_w, (size_t)D * K, bf16);
+  float *dw_b = dup_round(w->dw_b, D, bf16);
+  float *cn_g = dup_round(w->cn_g, D, bf16), *cn_b = dup_round(w->cn_b, D, bf16);
+  float *cn_m = conv_norm == 0 ? dup_round(w->cn_m, D, bf16) : NULL;
+  float *cn_v = conv_norm == 0 ? dup_round(w->cn_v, D, bf16) : NULL;
+  const float eps = rnd(1e-5f, bf16);  /* bn.eps cast to the dtype (2130) */
+  /* PaddingMask::new (1604-1614): None when nothing is padded */
+  const int32_t *kl = NULL;
+  if (lengths)
+    for (int b = 0; b < B; ++b)
+      if (lengths[b] < T) kl = lengths;
+
+  float *xx = dup_round(x, n, bf16);
+  float *h = (float *)malloc(sizeof(float) * n);
+  float *tmp = (float *)malloc(sizeof(float) * n);
+  float *hid = (float *)malloc(sizeof(float) * (size_t)M * (ff > 2 * D ? ff : 2 * D));
+  float *glu = (float *)malloc(sizeof(float) * n);
+
+  /* 1703-1726 */
+  ff_residual(xx, M, D, ff, &L[0], &L[1], ng[0], nb[0], bf16, h, hid, tmp);
+  /* 1750-1785: x += self_attn(LN x) */
+  layer_norm_r(xx, M, D, ng[1], nb[1], bf16, h);
+  orc_mha_forward(h, B, T, D, H, &w->attn, pos_emb, kl, ctx, ORC_DIRECT, bf16,
+                  0, tmp);
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < (int64_t)n; ++e) xx[e] = rnd(xx[e] + tmp[e], bf16);
+  /* 1797-1824: x += conv(LN x) */
+  layer_norm_r(xx, M, D, ng[2], nb[2], bf16, h);
+  linear_r(h, (int)M, D, L[2].w, 2 * D, L[2].b, bf16, hid); /* pointwise_conv1 */
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < M; ++r) {
+    const int b = (int)(r / T), t = (int)(r % T);
+    const int valid = !kl || t < kl[b];
+    for (int c = 0; c < D; ++c) {
+      const float a = hid[r * 2 * D + c], g = hid[r * 2 * D + D + c];
+      const float v = rnd(a * rnd(sigm(g), bf16), bf16); /* GLU 2275-2281 */
+      glu[r * D + c] = valid ? v : 0.0f;                 /* 2282-2285 */
+    }
+  }
+  const int pad = causal ? K - 1 : (K - 1) / 2;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int b = 0; b < B; ++b)
+    for (int t = 0; t < T; ++t)
+      for (int c = 0; c < D; ++c) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k) {
+          const int ts = t + k - pad;
+          if (ts >= 0 && ts < T) acc += dw_w[(size_t)c * K + k] * glu[((size_t)b * T + ts) * D + c];
+        }
+        if (dw_b) acc = rnd(acc, bf16) + dw_b[c];
+        h[((size_t)b * T + t) * D + c] = rnd(acc, bf16);
+      }
+  if (conv_norm == 0) {
+    /* BatchNorm, inference: (x - mean) * rsqrt(var + eps) * weight + bias */
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < (int64_t)n; ++e) {
+      const int c = (int)(e % D);
+      const float xm = rnd(h[e] - cn_m[c], bf16);
+      const float inv = rnd(1.0f / sqrtf(rnd(cn_v[c] + eps, bf16)), bf16);
+      const float nv = rnd(xm * inv, bf16);
+      h[e] = rnd(rnd(nv * cn_g[c], bf16) + cn_b[c], bf16);
+    }
+  } else {
+    layer_norm_r(h, M, D, cn_g, cn_b, bf16, h);
+  }
+  silu_r(h, (int64_t)n, bf16);
+  linear_r(h, (int)M, D, L[3].w, D, L[3].b, bf16, tmp); /* pointwise_conv2 */
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < (int64_t)n; ++e) xx[e] = rnd(xx[e] + tmp[e], bf16);
+  /* 1826-1858 */
+  ff_residual(xx, M, D, ff, &L[4], &L[5], ng[3], nb[3], bf16, h, hid, tmp);
+  /* 1861: final norm */
+  layer_norm_r(xx, M, D, ng[4], nb[4], bf16, out);
+
+  free(xx); free(h); free(tmp); free(hid); free(glu);
+  for (int i = 0; i < 5; ++i) { free(ng[i]); free(nb[i]); }
+  for (int i = 0; i < 6; ++i) { free((void *)L[i].w); free((void *)L[i].b); }
+  free(dw_w); free(dw_b); free(cn_g); free(cn_b); free(cn_m); free(cn_v);
+  return 0;
+}

@@ -134,6 +134,33 @@ int orc_stream_layer_step(const float *x, int B, int T, int D, int H,
                           int left, int right, int chunked, int cache_drop_size,
                           int bf16, float *out);
 
+/* One linear of a Conformer block: w [N, K] f32 (a quantised layer passes
+ * its dequantised weights), b [N] or NULL. */
+typedef struct {
+  const float *w, *b;
+} orc_lin;
+
+typedef struct {
+  orc_lin ff1_1, ff1_2, pw1, pw2, ff2_1, ff2_2;
+  const float *dw_w, *dw_b;               /* depthwise conv [D][K], [D] or NULL */
+  const float *cn_g, *cn_b, *cn_m, *cn_v; /* conv norm (m, v: batch norm only) */
+  const float *norm_g[5], *norm_b[5];     /* ff1, self_att, conv, ff2, out */
+  orc_mha_weights attn;
+} orc_block_weights;
+
+/* ConformerBlock::forward (conformer.rs:1693-1870) with FeedForward
+ * (2033-2088) and ConvolutionModule::forward (2249-2330): LayerNorm eps
+ * 1e-5, SiLU, GLU, padded frames (t >= lengths[b]) zeroed before the
+ * depthwise conv (non-causal: (K-1)/2 zeros each side; causal: K-1 on the
+ * left), BatchNorm in inference mode (conv_norm 0, eps 1e-5) or LayerNorm
+ * (conv_norm 1).  With bf16, every parameter is rounded (set_dtype) and
+ * every op's output is rounded as the reference's bf16 graph does.
+ * x, out [B, T, D]; pos_emb [2T-1, D]. */
+int orc_block_forward(const float *x, int B, int T, int D, int H, int ff, int K,
+                      int causal, int conv_norm, const orc_block_weights *w,
+                      const float *pos_emb, const int32_t *lengths,
+                      const orc_context *ctx, int bf16, float *out);
+
 /* bfloat16 round-to-nearest-even of a float (what an MLX astype does). */
 float orc_bf16_round(float x);
 void orc_bf16_round_array(float *x, int64_t n);

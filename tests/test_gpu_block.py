@@ -1,0 +1,114 @@
+"""Device parity of the Conformer block and encoder (BASELINE config 3's
+layer: macaron FF 1024->4096->1024 with SiLU, rel-pos MHA 8x128, conv module
+with depthwise kernel 9, GLU and BatchNorm, all linears MLX 8-bit) against
+the CPU oracle (oracle.block_forward, conformer.rs:1693-1870), through the
+C ABI.  bf16 tolerance 2e-2 of the output scale over valid rows."""
+import numpy as np
+import pytest
+
+from conftest import rand_block
+from __graft_entry__ import load_package
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 2e-2
+
+
+@pytest.fixture(scope="module")
+def nrp():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return load_package()
+
+
+def rel_err(got, ref, lengths):
+    err = 0.0
+    for b, L in enumerate(lengths):
+        err = max(err, float(np.abs(got[b, :L] - ref[b, :L]).max() / np.abs(ref[b, :L]).max()))
+    return err
+
+
+def make_block(nrp, wd, D, H, ff, K, causal, conv_norm, quant):
+    blk = nrp.ConformerBlock(D, H, ff, K, causal, conv_norm)
+    blk.load_weights(wd, "b", nrp.QuantizationConfig(8, 64) if quant else None)
+    blk.set_dtype(nrp.BF16)
+    return blk
+
+
+@pytest.mark.parametrize("B,T,D,H,ff,K,causal,conv_norm,quant,lengths,context", [
+    (3, 300, 256, 2, 1024, 9, False, "batch_norm", False, [300, 171, 245], None),
+    (2, 260, 256, 2, 1024, 9, False, "batch_norm", True, [260, 130], None),
+    (2, 200, 256, 2, 512, 5, True, "layer_norm", False, None, (64, 0, False)),
+    (1, 129, 512, 4, 2048, 31, False, "batch_norm", True, None, (70, 13, True)),
+    (2, 500, 1024, 8, 4096, 9, False, "batch_norm", True, [500, 313], None),
+])
+def test_block_matches_oracle(nrp, orc, B, T, D, H, ff, K, causal, conv_norm, quant, lengths,
+                              context):
+    import torch
+    rng = np.random.default_rng(B * 100 + T + D)
+    bw, wd = rand_block(rng, D, H, ff, K, conv_norm, quant=quant, orc=orc)
+    blk = make_block(nrp, wd, D, H, ff, K, causal, conv_norm, quant)
+    x = rng.standard_normal((B, T, D)).astype(np.float32)
+    pe = nrp.RelPositionalEncoding(D, 5000, True)
+    pe.set_dtype(nrp.BF16)
+    ln = np.array(lengths, np.int32) if lengths is not None else None
+    mask = nrp.key_padding_mask(ln, T) if ln is not None else None
+    ctx = nrp.AttentionContext.new(context[:2], "chunked_limited" if context[2] else "regular") \
+        if context is not None else None
+    xd = torch.from_numpy(x).cuda().bfloat16()
+    got = blk.forward(xd, pe.get_encoding(T), ctx, mask)
+    blk.ctx.check()
+    got = got.float().cpu().numpy()
+    ref = orc.block_forward(x, bw, pe.get_encoding_host(T)[0], H, ff, K, causal=causal,
+                            conv_norm=0 if conv_norm == "batch_norm" else 1, lengths=ln,
+                            context=context, bf16=True)
+    rows = lengths or [T] * B
+    assert all(np.isfinite(got[b, :L]).all() for b, L in enumerate(rows))
+    err = rel_err(got, ref, rows)
+    assert err < TOL_BF16, err
+
+
+def test_block_in_place_equals_out_of_place(nrp, orc):
+    import torch
+    rng = np.random.default_rng(2)
+    B, T, D, H, ff, K = 2, 150, 256, 2, 1024, 9
+    _, wd = rand_block(rng, D, H, ff, K)
+    blk = make_block(nrp, wd, D, H, ff, K, False, "batch_norm", False)
+    pe = nrp.RelPositionalEncoding(D, 5000, True)
+    pe.set_dtype(nrp.BF16)
+    pos = pe.get_encoding(T)
+    x = torch.from_numpy(rng.standard_normal((B, T, D)).astype(np.float32)).cuda().bfloat16()
+    a = blk.forward(x, pos)
+    y = x.clone()
+    blk.forward(y, pos, out=y)
+    blk.ctx.check()
+    assert torch.equal(a, y)
+
+
+def test_encoder_forward_from_embeddings(nrp, orc):
+    """Two layers of forward_from_embeddings (conformer.rs:694-722): x *
+    sqrt(d_model), the blocks, the [B, D, T] transpose."""
+    import torch
+    rng = np.random.default_rng(4)
+    B, T, D, H, ff, K, L = 2, 180, 256, 2, 1024, 9, 2
+    enc = nrp.ConformerEncoder(L, D, H, ff, K)
+    bws, wd = [], {}
+    for i in range(L):
+        bw, w = rand_block(rng, D, H, ff, K, quant=True, orc=orc, prefix=f"encoder.layers.{i}")
+        bws.append(bw)
+        wd.update(w)
+    enc.load_weights(wd, nrp.QuantizationConfig(8, 64))
+    enc.set_dtype(nrp.BF16)
+    x = rng.standard_normal((B, T, D)).astype(np.float32)
+    lengths = np.array([180, 97], np.int32)
+    out, out_len = enc.forward_from_embeddings(torch.from_numpy(x).cuda().bfloat16(), lengths)
+    enc.ctx.check()
+    assert tuple(out.shape) == (B, D, T) and np.array_equal(out_len, lengths)
+    got = out.float().cpu().numpy().transpose(0, 2, 1)
+    h = orc.bf16_round(orc.bf16_round(x) * np.float32(np.sqrt(D)))
+    pe = orc.get_encoding(D, 5000, T)
+    for bw in bws:
+        h = orc.block_forward(h, bw, pe, H, ff, K, lengths=lengths, bf16=True)
+    err = rel_err(got, h, lengths)
+    assert err < TOL_BF16, err
