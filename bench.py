@@ -215,14 +215,22 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="offline", choices=["offline", "long"],
+    ap.add_argument("--workload", default="offline",
+                    choices=["offline", "long", "encoder", "stream", "single"],
                     help="offline: BASELINE config 1 (the headline line); long: config 4, "
-                         "the sequence split across the ranks")
+                         "the sequence split across the ranks; encoder: config 3; stream: "
+                         "config 2; single: config 0")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "long":
         return main_long(args)
+    if args.workload == "encoder":
+        return main_encoder(args)
+    if args.workload == "stream":
+        return main_stream(args)
+    if args.workload == "single":
+        return main_single(args)
 
     import torch
     import torch.distributed as dist
@@ -403,6 +411,429 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+# the 24-layer encoder, all linears MLX 8-bit
+ENC_LAYERS, ENC_B, ENC_T, ENC_FF, ENC_K = 24, 32, 500, 4096, 9
+ENC_LEN_LO, ENC_LEN_HI = 250, 500
+ENC_WORKLOAD = ("BASELINE config 3: 24-layer FastConformer encoder (forward_from_embeddings), "
+                "macaron FF 1024->4096->1024 SiLU, rel-pos MHA 8x128, conv module (depthwise 9, "
+                "GLU, BatchNorm affine), every linear MLX 8-bit g64 from N(0,0.02^2) masters, "
+                "bf16 activations, B=32 T=500 lengths U[250,500]")
+# streaming attention over 24 layers
+STR_LAYERS, STR_SESS, STR_CHUNK, STR_CACHE, STR_CHUNKS = 24, 64, 14, 70, 50
+STR_WORKLOAD = ("BASELINE config 2: cache-aware streaming rel-pos attention, 24 layers, "
+                "64 sessions, chunk 14 (13 lookahead + 1), 70-frame left K/V cache, "
+                "chunked_limited [70,13], bf16; a step is one chunk through the 24 layers, the "
+                "caches restart empty every 50 chunks")
+# one fp32 layer, batch 1, T=125
+SGL_T = 125
+SGL_WORKLOAD = ("BASELINE config 0: one rel-pos MHA layer, fp32, B=1 T=125 d_model=1024 "
+                "8x128 heads, no mask")
+
+
+def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, workload,
+             config, scaling, e2e, dtype, cpu=None, hbm_bytes=None, reset=None):
+    """Common timing for the secondary workloads: W warm-up steps, K steps
+    timed with CUDA events (L2 flushed between steps, outside the events),
+    max over ranks; per-kernel device time from the library's events over K
+    more steps; e2e = K steps of `e2e()` (host copies inside); one JSON line.
+    flops / hbm_bytes: per step, per kernel kind (algorithmic)."""
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for k in range(max(args.warmup, 3)):
+        step(k)
+    ctx.check()
+    if reset:
+        reset()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            step(k)
+            ends[k].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ctx.check()
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)))
+    value = world * frames * args.steps / (total_ms / 1e3)
+    if reset:
+        reset()
+    ctx.profile(True)
+    ctx.profile_reset()
+    for k in range(args.steps):
+        flush.zero_()
+        step(k)
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    launches = sum(n for n, _ in prof.values())
+    e2e_fn, h2d, d2h = e2e
+    if reset:
+        reset()
+    for k in range(2):
+        e2e_fn(k)
+    torch.cuda.synchronize()
+    barrier()
+    e_s = torch.cuda.Event(enable_timing=True)
+    e_e = torch.cuda.Event(enable_timing=True)
+    e_s.record(stream)
+    for k in range(args.steps):
+        e2e_fn(k)
+    e_e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e_s.elapsed_time(e_e))
+    e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
+
+    tflops_peak, peak_src = _peak()
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    hbm_peak = peaks.get("hbm_gbs") or 6650.0
+    hbm_src = "measured (hbm_gbs, MEASURED_PEAKS.json)" if peaks.get("hbm_gbs") else \
+        "fallback 6.65 TB/s"
+    tot = max(sum(m for _, m in prof.values()), 1e-9)
+    kern, rk = {}, {}
+    for name, (n, ms) in prof.items():
+        kern[name] = {"launches": n, "ms_total": ms, "share": ms / tot}
+        if flops and name in flops:
+            a = flops[name] * args.steps / (ms / 1e3) / 1e12
+            rk[name] = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s",
+                        "algorithmic_flop_per_launch": flops[name] * args.steps / n}
+        if hbm_bytes and name in hbm_bytes:
+            g = hbm_bytes[name] * args.steps / (ms / 1e3) / 1e9
+            rk[name] = {"achieved": g, "frac": g / hbm_peak, "unit": "GB/s",
+                        "algorithmic_bytes_per_launch": hbm_bytes[name] * args.steps / n}
+    dominant = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
+    roof = None
+    if dominant in rk:
+        hbm = rk[dominant]["unit"] == "GB/s"
+        roof = {"bound": "hbm" if hbm else "tensor", "kernel": dominant,
+                "achieved": rk[dominant]["achieved"],
+                "peak": hbm_peak if hbm else tflops_peak, "unit": rk[dominant]["unit"],
+                "frac": rk[dominant]["frac"], "traffic": None,
+                "peak_source": hbm_src if hbm else peak_src}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": dict({"workload": workload,
+                            "l2": "flushed between timed steps (256 MiB write, outside the "
+                                  "events)"}, **config),
+            "e2e": {"value": e2e_value, "unit": "frames/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "roofline_kernels": rk,
+            "kernels": kern,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu() if (cpu and rank == 0 and world == 1 and
+                                      not args.no_cpu_baseline) else None,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def _dist_init(args):
+    import torch
+    import torch.distributed as dist
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def main_encoder(args):
+    """Config 3: forward_from_embeddings over 24 quantised blocks; weak
+    scaling (each rank its own 32-utterance batch)."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    from oracle import oracle as orc  # quantiser of the synthetic checkpoint only
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(5150 + rank)
+    enc = nrp.ConformerEncoder(ENC_LAYERS, D, H, ENC_FF, ENC_K, ctx=ctx)
+    f = lambda *sh: (rng.standard_normal(sh, dtype=np.float32) * 0.02)
+    shapes = {"feed_forward1.linear1": (ENC_FF, D), "feed_forward1.linear2": (D, ENC_FF),
+              "conv.pointwise_conv1": (2 * D, D), "conv.pointwise_conv2": (D, D),
+              "feed_forward2.linear1": (ENC_FF, D), "feed_forward2.linear2": (D, ENC_FF),
+              "self_attn.linear_q": (D, D), "self_attn.linear_k": (D, D),
+              "self_attn.linear_v": (D, D), "self_attn.linear_out": (D, D),
+              "self_attn.linear_pos": (D, D)}
+    sample_layers = []  # the oracle's CPU sample: the first two layers' weights
+    for i, blk in enumerate(enc.layers):
+        wd = {}
+        p = f"encoder.layers.{i}"
+        for name, (n, k) in shapes.items():
+            wq, sc, zp = orc.quantize(f(n, k), 64, 8)
+            wd[f"{p}.{name}.weight"] = wq
+            wd[f"{p}.{name}.scales"] = sc.astype(np.float16).astype(np.float32)
+            wd[f"{p}.{name}.biases"] = zp.astype(np.float16).astype(np.float32)
+            if not name.endswith("linear_pos"):
+                wd[f"{p}.{name}.bias"] = f(n)
+        for nm in nrp.BLOCK_NORMS:
+            wd[f"{p}.{nm}.weight"] = 1 + f(D)
+            wd[f"{p}.{nm}.bias"] = f(D)
+        wd[f"{p}.self_attn.pos_bias_u"] = f(H, D // H)
+        wd[f"{p}.self_attn.pos_bias_v"] = f(H, D // H)
+        wd[f"{p}.conv.depthwise_conv.weight"] = f(D, ENC_K, 1)
+        wd[f"{p}.conv.depthwise_conv.bias"] = f(D)
+        bn = f"{p}.conv.batch_norm"
+        wd[f"{bn}.weight"], wd[f"{bn}.bias"] = 1 + f(D), f(D)
+        wd[f"{bn}.running_mean"], wd[f"{bn}.running_var"] = f(D), 1 + np.abs(f(D))
+        blk.load_weights(wd, p, nrp.QuantizationConfig(8, 64))
+        if i < 2:
+            sample_layers.append((p, wd))
+    enc.set_dtype(nrp.BF16)
+    dev = torch.device("cuda", local)
+    x = rng.standard_normal((ENC_B, ENC_T, D), dtype=np.float32)
+    lengths = rng.integers(ENC_LEN_LO, ENC_LEN_HI + 1, ENC_B).astype(np.int32)
+    xd = torch.from_numpy(x).to(dev, torch.bfloat16)
+    out = torch.empty((ENC_B, D, ENC_T), dtype=torch.bfloat16, device=dev)
+
+    def step(k, xin=xd):
+        enc.forward_from_embeddings(xin, lengths, None, out=out)
+
+    x_host = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty_like(out, device="cpu").pin_memory()
+    x_dev2 = torch.empty_like(xd)
+
+    def e2e(k):
+        x_dev2.copy_(x_host, non_blocking=True)
+        step(k, x_dev2)
+        out_host.copy_(out, non_blocking=True)
+
+    valid = int(lengths.sum())
+    L2s = int(np.sum(lengths.astype(np.int64) ** 2))
+    per_frame = 2 * 2 * (2 * D * ENC_FF) + 4 * 2 * D * D + 2 * D * 2 * D + 2 * D * D
+    flops = {"gemm_q8": ENC_LAYERS * (per_frame * valid + 2 * (2 * ENC_T - 1) * D * D),
+             "attn_sm100": ENC_LAYERS * 3 * 2 * (D // H) * H * L2s}
+    bytes_ = {"layernorm": ENC_LAYERS * 5 * 2 * ENC_B * ENC_T * D * 2,
+              "dwconv": ENC_LAYERS * 2 * ENC_B * ENC_T * D * 2}
+
+    def cpu():
+        """The oracle on utterance 0 through the first two layers, scaled to
+        24 layers (the layers cost the same)."""
+        threads = os.cpu_count() or 1
+        orc.set_threads(threads)
+        L0 = int(lengths[0])
+        h = orc.bf16_round(orc.bf16_round(x[:1, :L0]) * np.float32(np.sqrt(D)))
+        pe_h = orc.get_encoding(D, 5000, L0)
+        deq = lambda wd, k: orc.dequantize(wd[k + ".weight"], orc.bf16_round(wd[k + ".scales"]),
+                                           orc.bf16_round(wd[k + ".biases"]), 64, 8)
+        blocks = []
+        for p, wd in sample_layers:
+            lin = lambda n: (deq(wd, f"{p}.{n}"), wd.get(f"{p}.{n}.bias"))
+            bw = {"ff1_1": lin("feed_forward1.linear1"), "ff1_2": lin("feed_forward1.linear2"),
+                  "pw1": lin("conv.pointwise_conv1"), "pw2": lin("conv.pointwise_conv2"),
+                  "ff2_1": lin("feed_forward2.linear1"), "ff2_2": lin("feed_forward2.linear2"),
+                  "dw": (wd[f"{p}.conv.depthwise_conv.weight"].reshape(D, ENC_K),
+                         wd[f"{p}.conv.depthwise_conv.bias"]),
+                  "conv_norm": tuple(wd[f"{p}.conv.batch_norm.{n}"] for n in
+                                     ("weight", "bias", "running_mean", "running_var")),
+                  "norms": {o: (wd[f"{p}.{n}.weight"], wd[f"{p}.{n}.bias"])
+                            for o, n in zip(orc.BLOCK_NORMS, nrp.BLOCK_NORMS)},
+                  "attn": {"wq": deq(wd, f"{p}.self_attn.linear_q"),
+                           "bq": wd[f"{p}.self_attn.linear_q.bias"],
+                           "wk": deq(wd, f"{p}.self_attn.linear_k"),
+                           "bk": wd[f"{p}.self_attn.linear_k.bias"],
+                           "wv": deq(wd, f"{p}.self_attn.linear_v"),
+                           "bv": wd[f"{p}.self_attn.linear_v.bias"],
+                           "wo": deq(wd, f"{p}.self_attn.linear_out"),
+                           "bo": wd[f"{p}.self_attn.linear_out.bias"],
+                           "wp": deq(wd, f"{p}.self_attn.linear_pos"),
+                           "pos_bias_u": wd[f"{p}.self_attn.pos_bias_u"],
+                           "pos_bias_v": wd[f"{p}.self_attn.pos_bias_v"]}}
+            blocks.append(bw)
+        t0 = time.perf_counter()
+        for bw in blocks:
+            h = orc.block_forward(h, bw, pe_h, H, ENC_FF, ENC_K, bf16=True)
+        dt = (time.perf_counter() - t0) * ENC_LAYERS / len(blocks)
+        return {"value": L0 / dt, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": f"utterance 0 ({L0} frames) through the first {len(blocks)} of the "
+                          f"{ENC_LAYERS} layers, time scaled to {ENC_LAYERS} layers; CPU "
+                          f"restatement (oracle block_forward, bf16 rounding), host CPU: "
+                          f"{cpu_model()}"}
+    _harness(args, world, rank, local, ctx, step, valid, flops, None, ENC_WORKLOAD,
+             {"batch_per_gpu": ENC_B, "seq_len": ENC_T, "layers": ENC_LAYERS,
+              "valid_frames_per_gpu": valid, "weights": "MLX 8-bit g64, fp16 scales",
+              "parallelism": f"utterance-parallel replicas x{world}"},
+             "weak", (e2e, x_host.numel() * 2, out_host.numel() * 2), "bf16", cpu=cpu,
+             hbm_bytes=bytes_)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main_stream(args):
+    """Config 2: one chunk of 14 frames for 64 sessions through 24 layers of
+    forward_with_cache; weak scaling (each rank its own 64 sessions)."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(777 + rank)
+    dev = torch.device("cuda", local)
+    f = lambda *sh: (rng.standard_normal(sh, dtype=np.float32) * 0.02)
+    layers, caches = [], []
+    for i in range(STR_LAYERS):
+        a = nrp.RelPositionMultiHeadAttention(D, H, True, ctx=ctx)
+        for which, bias in ((nrp.LINEAR_Q, True), (nrp.LINEAR_K, True), (nrp.LINEAR_V, True),
+                            (nrp.LINEAR_OUT, True), (nrp.LINEAR_POS, False)):
+            a.set_linear(which, nrp.LinearLayer.standard(f(D, D), f(D) if bias else None))
+        a.set_pos_bias(f(H, D // H), f(H, D // H))
+        a.set_dtype(nrp.BF16)
+        layers.append(a)
+        caches.append(nrp.AttentionCache(a, STR_SESS, STR_CACHE))
+    actx = nrp.AttentionContext.new((STR_CACHE, STR_CHUNK - 1), "chunked_limited")
+    pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
+    pe.set_dtype(nrp.BF16)
+    pos = pe.get_encoding(STR_CACHE + STR_CHUNK)
+    xs = [torch.from_numpy(rng.standard_normal((STR_SESS, STR_CHUNK, D), dtype=np.float32))
+          .to(dev, torch.bfloat16) for _ in range(4)]
+    bufs = [torch.empty_like(xs[0]) for _ in range(2)]
+    state = {"chunk": 0}
+
+    def reset():
+        for c in caches:
+            c.reset()
+        state["chunk"] = 0
+
+    def step(k, xin=None):
+        c = state["chunk"]
+        if c == STR_CHUNKS:
+            reset()
+            c = 0
+        filled = min(c * STR_CHUNK, STR_CACHE)
+        h = xin if xin is not None else xs[k % len(xs)]
+        for i, a in enumerate(layers):
+            o = bufs[i & 1]
+            a.forward_with_cache(h, pos, caches[i], filled, STR_CHUNK, actx, out=o)
+            h = o
+        state["chunk"] = c + 1
+        return h
+
+    x_host = torch.empty((STR_SESS, STR_CHUNK, D), dtype=torch.bfloat16).pin_memory()
+    x_host.copy_(xs[0].cpu())
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev2 = torch.empty_like(xs[0])
+
+    def e2e(k):
+        x_dev2.copy_(x_host, non_blocking=True)
+        h = step(k, x_dev2)
+        out_host.copy_(h, non_blocking=True)
+
+    frames = STR_SESS * STR_CHUNK
+    M = frames
+    # linear_pos runs once per positional length (attention.rs:749-761): not per step
+    flops = {"gemm_bf16": STR_LAYERS * 4 * 2 * M * D * D}
+    kv = STR_SESS * (STR_CACHE + STR_CHUNK) * D * 2 * 2
+    qo = 2 * STR_SESS * STR_CHUNK * D * 2
+    p_rows = (2 * (STR_CACHE + STR_CHUNK) - 1) * D * 2
+    hbm = {"attn_stream": STR_LAYERS * (kv + qo + p_rows),
+           "ring_append": STR_LAYERS * 3 * STR_SESS * STR_CHUNK * D * 2 * 2}
+    _harness(args, world, rank, local, ctx, step, frames, flops, None, STR_WORKLOAD,
+             {"sessions_per_gpu": STR_SESS, "chunk": STR_CHUNK, "cache": STR_CACHE,
+              "layers": STR_LAYERS,
+              "parallelism": f"session-parallel replicas x{world}"},
+             "weak", (e2e, x_host.numel() * 2, out_host.numel() * 2), "bf16", hbm_bytes=hbm,
+             reset=reset)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main_single(args):
+    """Config 0: one fp32 layer on [1, 125, 1024] (launch-bound)."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(99 + rank)
+    f = lambda *sh: (rng.standard_normal(sh, dtype=np.float32) * 0.02)
+    w = {"wq": f(D, D), "bq": f(D), "wk": f(D, D), "bk": f(D), "wv": f(D, D), "bv": f(D),
+         "wo": f(D, D), "bo": f(D), "wp": f(D, D), "pos_bias_u": f(H, D // H),
+         "pos_bias_v": f(H, D // H)}
+    attn = nrp.RelPositionMultiHeadAttention(D, H, True, ctx=ctx)
+    for which, (wk, bk) in enumerate((("wq", "bq"), ("wk", "bk"), ("wv", "bv"), ("wo", "bo"),
+                                      ("wp", None))):
+        attn.set_linear(which, nrp.LinearLayer.standard(w[wk], w[bk] if bk else None))
+    attn.set_pos_bias(w["pos_bias_u"], w["pos_bias_v"])
+    dev = torch.device("cuda", local)
+    x = rng.standard_normal((1, SGL_T, D), dtype=np.float32)
+    xd = torch.from_numpy(x).to(dev)
+    out = torch.empty_like(xd)
+    pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
+    pos = pe.get_encoding(SGL_T)
+
+    def step(k, xin=xd):
+        attn.forward(xin, pos, None, None, out=out)
+
+    x_host = torch.from_numpy(x).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev2 = torch.empty_like(xd)
+
+    def e2e(k):
+        x_dev2.copy_(x_host, non_blocking=True)
+        step(k, x_dev2)
+        out_host.copy_(out, non_blocking=True)
+
+    def cpu():
+        from oracle import oracle as orc
+        threads = os.cpu_count() or 1
+        orc.set_threads(threads)
+        pe_h = orc.get_encoding(D, 5000, SGL_T)
+        orc.mha_forward(x, w, pe_h, H)
+        runs = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            orc.mha_forward(x, w, pe_h, H, mode=orc.ORC_REFERENCE_ALGO)
+            runs.append(time.perf_counter() - t0)
+        med = statistics.median(runs)
+        return {"value": SGL_T / med, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": f"the whole config-0 forward ({SGL_T} frames), median of 5; CPU "
+                          f"restatement of the reference algorithm in f32, host CPU: "
+                          f"{cpu_model()}"}
+    flops = {"gemm_f32": 4 * 2 * SGL_T * D * D + 2 * (2 * SGL_T - 1) * D * D,
+             "attn_simt": 3 * 2 * (D // H) * H * SGL_T * SGL_T}
+    _harness(args, world, rank, local, ctx, step, SGL_T, flops, None, SGL_WORKLOAD,
+             {"batch_per_gpu": 1, "seq_len": SGL_T, "d_model": D, "heads": H,
+              "parallelism": f"replicas x{world}"},
+             "weak", (e2e, x_host.numel() * 4, out_host.numel() * 4), "f32", cpu=cpu)
     if world > 1:
         dist.destroy_process_group()
     return 0
