@@ -986,26 +986,39 @@ int nrp_attn_forward_with_cache(nrp_attn* a, void* stream, const void* x, int B,
   sm.left = context ? context->left : -1;
   sm.right = context ? context->right : -1;
   sm.chunked = context ? context->chunked : 0;
-  ProfScope ps_attn(ctx, NRP_KERNEL_ATTN_STREAM, st);
-  if (a->dtype == NRP_DTYPE_BF16) {
-    const auto* q = a->qkv.as<__nv_bfloat16>();
-    CUDA_TRY(nrp::launch_relpos_attn_stream_simt<__nv_bfloat16>(
-        q, 3 * D, q + D, q + 2 * D, 3 * D, c->kc.as<__nv_bfloat16>(), c->vc.as<__nv_bfloat16>(), C,
-        c->head, a->spos.as<__nv_bfloat16>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm,
-        a->cbuf.as<__nv_bfloat16>(), B, T, D, a->H, st));
-  } else {
-    const auto* q = a->qkv.as<float>();
-    CUDA_TRY(nrp::launch_relpos_attn_stream_simt<float>(
-        q, 3 * D, q + D, q + 2 * D, 3 * D, c->kc.as<float>(), c->vc.as<float>(), C, c->head,
-        a->spos.as<float>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm, a->cbuf.as<float>(),
-        B, T, D, a->H, st));
-  }
   // slide the window: the first q_keep new frames replace the oldest
   // (661-684); more than C of them keep only the newest C (992-996)
   const int q_keep = std::max(T - a->cache_drop, 0);
   const int n_app = std::min(q_keep, C);
   const int src0 = q_keep - n_app;
-  if (n_app > 0) {
+  bool appended = false;
+  {
+    ProfScope ps_attn(ctx, NRP_KERNEL_ATTN_STREAM, st);
+    if (a->dtype == NRP_DTYPE_BF16 && nrp::stream_attn_supported(C, T, D, a->H)) {
+      // tensor-core kernel; it also slides the ring when the chunk fits one CTA
+      const bool fuse = T <= 16;
+      const auto* q = a->qkv.as<__nv_bfloat16>();
+      CUDA_TRY(nrp::launch_relpos_attn_stream_mma(
+          q, c->kc.as<__nv_bfloat16>(), c->vc.as<__nv_bfloat16>(), c->hc.as<__nv_bfloat16>(),
+          static_cast<const __nv_bfloat16*>(x), C, c->head, fuse ? n_app : 0, src0,
+          a->spos.as<__nv_bfloat16>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm,
+          a->cbuf.as<__nv_bfloat16>(), B, T, D, a->H, st));
+      appended = fuse;
+    } else if (a->dtype == NRP_DTYPE_BF16) {
+      const auto* q = a->qkv.as<__nv_bfloat16>();
+      CUDA_TRY(nrp::launch_relpos_attn_stream_simt<__nv_bfloat16>(
+          q, 3 * D, q + D, q + 2 * D, 3 * D, c->kc.as<__nv_bfloat16>(), c->vc.as<__nv_bfloat16>(),
+          C, c->head, a->spos.as<__nv_bfloat16>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm,
+          a->cbuf.as<__nv_bfloat16>(), B, T, D, a->H, st));
+    } else {
+      const auto* q = a->qkv.as<float>();
+      CUDA_TRY(nrp::launch_relpos_attn_stream_simt<float>(
+          q, 3 * D, q + D, q + 2 * D, 3 * D, c->kc.as<float>(), c->vc.as<float>(), C, c->head,
+          a->spos.as<float>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm,
+          a->cbuf.as<float>(), B, T, D, a->H, st));
+    }
+  }
+  if (n_app > 0 && !appended) {
     ProfScope ps(ctx, NRP_KERNEL_RING_APPEND, st);
     const uint8_t* qkv = static_cast<const uint8_t*>(a->qkv.p);
     const int64_t sb = static_cast<int64_t>(T) * 3 * D, sr = 3 * D;
@@ -1019,8 +1032,8 @@ int nrp_attn_forward_with_cache(nrp_attn* a, void* stream, const void* x, int B,
                                      static_cast<int64_t>(T) * D, D, c->hc.p,
                                      static_cast<int64_t>(C) * D, C, c->head, n_app, B, D,
                                      static_cast<int>(es), st));
-    c->head = (c->head + n_app) % C;
   }
+  if (n_app > 0) c->head = (c->head + n_app) % C;
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
                     out, D);

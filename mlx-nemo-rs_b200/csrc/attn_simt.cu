@@ -13,6 +13,7 @@
 #include <math.h>
 
 #include "gemm.h"
+#include "masks.cuh"
 #include "sm100.cuh"
 
 namespace nrp {
@@ -37,40 +38,6 @@ __device__ __forceinline__ void st<float>(float* p, float v) { *p = v; }
 template <>
 __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, float v) {
   *p = __float2bfloat16_rn(v);
-}
-
-// Visible key interval of query row i: the AttentionContext window
-// (attention.rs:232-272 / conformer.rs:97-221 on absolute positions), the
-// key padding bound (attention.rs:280-294) and the unfilled-cache offset
-// (conformer.rs:153-181).
-__device__ __forceinline__ bool interval(const AttnContextDev& ctx, const StreamMaskDev& sm,
-                                         int i, int kend, int& lo, int& hi) {
-  lo = 0;
-  hi = kend;
-  int ia = i;
-  int has = ctx.has, left = ctx.left, right = ctx.right, chunked = ctx.chunked;
-  if (sm.has) {
-    if (i >= sm.valid) return false;
-    ia = sm.cache_len + i;
-    lo = max(lo, sm.cache_len - sm.filled);
-    has = sm.ctx_has;
-    left = sm.left;
-    right = sm.right;
-    chunked = sm.chunked;
-  }
-  if (has) {
-    if (chunked && right >= 0) {
-      const int chunk = right + 1;
-      const int lc = left >= 0 ? left / chunk : 10000;
-      const int ci = ia / chunk;
-      lo = max(lo, (ci - lc) * chunk);
-      hi = min(hi, (ci + 1) * chunk);
-    } else {
-      if (left >= 0) lo = max(lo, ia - left);
-      if (!chunked && right >= 0) hi = min(hi, ia + right + 1);
-    }
-  }
-  return hi > lo;
 }
 
 template <typename T>
@@ -99,7 +66,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   int kend = Tk;
   if (key_len) kend = min(Tk, max(key_len[b], 1));
   int lo, hi;
-  const bool any = interval(ctx, sm, i, kend, lo, hi);
+  const bool any = key_interval(ctx, sm, i, kend, lo, hi);
   const float scale = rsqrtf(static_cast<float>(dh));
   float m = -INFINITY, l = 0.f;
   float o[4] = {0.f, 0.f, 0.f, 0.f};

@@ -182,6 +182,19 @@ cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stre
 cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D,
                                  cudaStream_t stream);
 
+// ---- streaming attention on tensor cores (attn_stream.cu), bf16 ----
+// q|k|v [B, T, 3D] of the chunk, rings kc/vc/hc [B, C, D] (oldest frame at
+// slot `head`), p [2(C+T)-1, D], out [B, T, D].  With n_app > 0 (only when
+// T <= 16) the kernel also writes new frames src0 .. src0+n_app-1 (K, V
+// and the attention input x) into ring slots head .. head+n_app-1 (mod C).
+bool stream_attn_supported(int C, int T, int D, int H);
+cudaError_t launch_relpos_attn_stream_mma(const __nv_bfloat16* qkv, const __nv_bfloat16* kc,
+                                          const __nv_bfloat16* vc, __nv_bfloat16* hc,
+                                          const __nv_bfloat16* x, int C, int head, int n_app,
+                                          int src0, const __nv_bfloat16* p, const float* u,
+                                          const float* v, StreamMaskDev sm, __nv_bfloat16* out,
+                                          int B, int T, int D, int H, cudaStream_t stream);
+
 // ---- small elementwise helpers ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,
                                cudaStream_t stream);

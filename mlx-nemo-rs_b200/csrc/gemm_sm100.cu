@@ -50,6 +50,32 @@ constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * (kABytes + kBByte
                               256 + 4 * (kMaxBatch + 1);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
+// v[e] += bias[n + e] for e < 32 (zero past N); 16-byte loads when `vec`.
+__device__ __forceinline__ void add_bias32(float* v, const __nv_bfloat16* bias, int n, int N,
+                                           bool vec) {
+  if (vec && n + 32 <= N) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = *reinterpret_cast<const uint4*>(bias + n + q * 8);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[e]));
+        v[q * 8 + 2 * e] += f.x;
+        v[q * 8 + 2 * e + 1] += f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] += n + e < N ? __bfloat162float(bias[n + e]) : 0.f;
+  }
+}
+__device__ __forceinline__ void add_bias64(float* v, const __nv_bfloat16* bias, int n, int N,
+                                           bool vec) {
+  add_bias32(v, bias, n, N, vec);
+  add_bias32(v + 32, bias, n + 32, N, vec);
+}
+
 template <bool kQuant>
 __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap map_x,
@@ -241,6 +267,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
       }
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
       const bool glu = ep.mode == kEpiGlu;
+      // bias columns come 8 at a time (16-byte loads) when the pointer allows
+      const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
       const int ncols = glu ? kBN / 2 : kBN;  // output columns of the tile
       const int on0 = glu ? n0 / 2 : n0;      // its first output column
       const int n_out = glu ? N / 2 : N;
@@ -258,16 +286,19 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             tmem_ld32(taddr + c + h, ar);
             tmem_ld32(taddr + 128 + c + h, gr);
             tmem_ld_wait();
+            float a[32], g[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-              float a = __uint_as_float(ar[e]);
-              float g = __uint_as_float(gr[e]);
-              if (bias) {
-                a += __bfloat162float(bias[n0 + c + h + e]);
-                g += __bfloat162float(bias[n0 + 128 + c + h + e]);
-              }
-              v[h + e] = keep ? a * __fdividef(1.f, 1.f + __expf(-g)) : 0.f;
+              a[e] = __uint_as_float(ar[e]);
+              g[e] = __uint_as_float(gr[e]);
             }
+            if (bias) {
+              add_bias32(a, bias, n0 + c + h, N, bias_vec);
+              add_bias32(g, bias, n0 + 128 + c + h, N, bias_vec);
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              v[h + e] = keep ? a[e] * __fdividef(1.f, 1.f + __expf(-g[e])) : 0.f;
           }
         } else if (!skip) {
           uint32_t r[64];
@@ -276,11 +307,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
           {
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 64; ++e) {
-              const int n = n0 + c + e;
-              v[e] = __uint_as_float(r[e]) +
-                     ((bias && n < N) ? __bfloat162float(bias[n]) : 0.f);
-            }
+            for (int e = 0; e < 64; ++e) v[e] = __uint_as_float(r[e]);
+            if (bias) add_bias64(v, bias, n0 + c, N, bias_vec);
             if (ep.mode == kEpiSilu) {
 #pragma unroll
               for (int e = 0; e < 64; ++e) v[e] = v[e] * __fdividef(1.f, 1.f + __expf(-v[e]));

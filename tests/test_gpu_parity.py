@@ -225,6 +225,8 @@ def test_bf16_quantized_projections(nrp, orc):
     ("f32", 64, 2, 8, 5, (6, 1, False), 2),
     ("bf16", 256, 2, 70, 14, (70, 13, True), 0),
     ("bf16", 1024, 8, 70, 14, (70, 13, True), 0),
+    ("bf16", 256, 2, 40, 20, (40, 3, False), 3),
+    ("bf16", 256, 2, 100, 12, None, 2),
 ])
 def test_streaming_chunks(nrp, orc, dtype_name, D, H, C, T, ctx, drop):
     """forward_with_cache over consecutive chunks (attention.rs:606-816,
