@@ -636,10 +636,14 @@ def main_encoder(args):
     valid = int(lengths.sum())
     L2s = int(np.sum(lengths.astype(np.int64) ** 2))
     per_frame = 2 * 2 * (2 * D * ENC_FF) + 4 * 2 * D * D + 2 * D * 2 * D + 2 * D * D
-    flops = {"gemm_q8": ENC_LAYERS * (per_frame * valid + 2 * (2 * ENC_T - 1) * D * D),
+    # the quantised linears run as dequantise-once + bf16 GEMM at these row
+    # counts (M = 16000 > 1024 rows)
+    flops = {"gemm_bf16": ENC_LAYERS * (per_frame * valid + 2 * (2 * ENC_T - 1) * D * D),
              "attn_sm100": ENC_LAYERS * 3 * 2 * (D // H) * H * L2s}
+    w_params = 2 * 2 * D * ENC_FF + 2 * D * D + D * D + 5 * D * D  # per layer
     bytes_ = {"layernorm": ENC_LAYERS * 5 * 2 * ENC_B * ENC_T * D * 2,
-              "dwconv": ENC_LAYERS * 2 * ENC_B * ENC_T * D * 2}
+              "dwconv": ENC_LAYERS * 2 * ENC_B * ENC_T * D * 2,
+              "dequant": ENC_LAYERS * w_params * (1 + 2)}
 
     def cpu():
         """The oracle on utterance 0 through the first two layers, scaled to

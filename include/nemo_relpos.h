@@ -398,7 +398,8 @@ typedef enum {
   NRP_KERNEL_LAYERNORM = 8,   /* the block's LayerNorms */
   NRP_KERNEL_DWCONV = 9,      /* depthwise conv + BatchNorm + SiLU */
   NRP_KERNEL_ELEMENTWISE = 10, /* input scaling, transposes, copies */
-  NRP_KERNEL_KINDS = 11
+  NRP_KERNEL_DEQUANT = 11,    /* 8-bit weights to bf16 (large-M quantised GEMM) */
+  NRP_KERNEL_KINDS = 12
 } nrp_kernel_kind;
 int nrp_profile_enable(nrp_context* ctx, int enable);
 int nrp_profile_reset(nrp_context* ctx);

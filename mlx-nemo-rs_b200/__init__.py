@@ -194,7 +194,7 @@ class Context:
         _check(lib().nrp_context_check(self.handle, stream if stream is not None else _stream()))
 
     KERNELS = ("gemm_bf16", "gemm_q8", "qgemv", "gemm_f32", "attn_sm100", "attn_simt",
-               "attn_stream", "ring_append", "layernorm", "dwconv", "elementwise")
+               "attn_stream", "ring_append", "layernorm", "dwconv", "elementwise", "dequant")
 
     def profile(self, enable: bool = True):
         _check(lib().nrp_profile_enable(self.handle, int(enable)))

@@ -231,6 +231,10 @@ int sync_params(nrp_attn* a) {
   return ok();
 }
 
+// Rows from which a quantised linear dequantises its weight once per call
+// (HBM: N*K read, 2*N*K written) instead of inside the GEMM's B producer.
+constexpr int kDequantOnceMinRows = 256;
+
 // y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias) in the module dtype; W is
 // either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
 int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
@@ -259,6 +263,21 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                static_cast<const __nv_bfloat16*>(bias),
                                static_cast<__nv_bfloat16*>(y), ldy, N, st));
     return ok();
+  }
+  // Quantised weights with many rows: dequantise the weight once into the
+  // context's scratch and run the bf16 GEMM (the in-register producer would
+  // redo the dequantisation for every 128-row tile).
+  if (quant && M >= kDequantOnceMinRows) {
+    CUDA_TRY(ctx->wscratch.ensure(static_cast<size_t>(N) * K * 2));
+    {
+      ProfScope ps(ctx, NRP_KERNEL_DEQUANT, st);
+      CUDA_TRY(nrp::launch_dequant_q8(static_cast<const uint8_t*>(w),
+                                      static_cast<const __nv_bfloat16*>(qs),
+                                      static_cast<const __nv_bfloat16*>(qb),
+                                      ctx->wscratch.as<__nv_bfloat16>(), N, K, ctx->num_sms, st));
+    }
+    w = ctx->wscratch.p;
+    quant = false;
   }
   CUtensorMap mx, mw;
   const bool xmap_ok =

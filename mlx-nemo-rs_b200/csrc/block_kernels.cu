@@ -69,10 +69,16 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* x,
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
     const int col = c * 256 + lane * 8;
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + col);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + col + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(beta + col);
+    const float4 b1 = *reinterpret_cast<const float4*>(beta + col + 4);
+    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
     float o[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      float t = (v[c][e] - mean) * inv * gamma[col + e] + beta[col + e];
+      float t = (v[c][e] - mean) * inv * gg[e] + bb[e];
       o[e] = act_silu ? silu(t) : t;
     }
     *reinterpret_cast<uint4*>(yr + col) = pack8(o);
@@ -84,8 +90,11 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* x,
 // left when causal), + bias, then optionally the inference BatchNorm folded
 // to a per-channel affine and SiLU.  A CTA covers kTT output frames of one
 // utterance; its input rows (kTT + K - 1) are staged in shared memory and
-// each thread owns 8 channels.
+// each thread owns 8 channels, whose K taps it keeps in registers (kK > 0,
+// the kernel size fixed at compile time) or reads from shared memory
+// (kK == 0, any K).
 constexpr int kTT = 32;
+template <int kK>
 __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __restrict__ x,
                                                      const float* __restrict__ w,  // [D][K]
                                                      const float* __restrict__ bias,
@@ -95,6 +104,7 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
                                                      int K, int pad_left, int act_silu) {
   extern __shared__ __align__(16) uint8_t dw_smem[];
   __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(dw_smem);  // [kTT + K - 1][D]
+  float* wsm = reinterpret_cast<float*>(dw_smem + static_cast<size_t>(kTT + K - 1) * D * 2);
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * kTT;
   const int rows = kTT + K - 1;
@@ -107,6 +117,11 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
     if (t >= 0 && t < T) q = *reinterpret_cast<const uint4*>(xb + static_cast<int64_t>(t) * D + cv * 8);
     *reinterpret_cast<uint4*>(tile + r * D + cv * 8) = q;
   }
+  if (kK == 0)  // taps transposed to [K][D] for 16-byte reads
+    for (int i = threadIdx.x; i < K * D; i += blockDim.x) {
+      const int c = i / K, k = i - c * K;
+      wsm[k * D + c] = w[i];
+    }
   __syncthreads();
   __nv_bfloat16* yb = y + static_cast<int64_t>(b) * T * D;
   for (int cv = threadIdx.x; cv < vecs; cv += blockDim.x) {
@@ -118,16 +133,35 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
       sc[e] = bn_scale ? bn_scale[c0 + e] : 1.f;
       sh[e] = bn_shift ? bn_shift[c0 + e] : 0.f;
     }
+    float wr[kK > 0 ? kK : 1][8];
+    if (kK > 0)
+#pragma unroll
+      for (int k = 0; k < (kK > 0 ? kK : 1); ++k)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wr[k][e] = w[(c0 + e) * kK + k];
     const int tn = min(kTT, T - t0);
     for (int tt = 0; tt < tn; ++tt) {
       float acc[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-      for (int k = 0; k < K; ++k) {
-        float f[8];
-        unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
+      if (kK > 0) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += w[(c0 + e) * K + k] * f[e];
+        for (int k = 0; k < (kK > 0 ? kK : 1); ++k) {
+          float f[8];
+          unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = fmaf(wr[k][e], f[e], acc[e]);
+        }
+      } else {
+        for (int k = 0; k < K; ++k) {
+          float f[8];
+          unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
+          const float4 w0 = *reinterpret_cast<const float4*>(wsm + k * D + c0);
+          const float4 w1 = *reinterpret_cast<const float4*>(wsm + k * D + c0 + 4);
+          const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = fmaf(ww[e], f[e], acc[e]);
+        }
       }
       float o[8];
 #pragma unroll
@@ -196,22 +230,34 @@ cudaError_t launch_layernorm(const __nv_bfloat16* x, const float* gamma, const f
   return cudaGetLastError();
 }
 
-size_t dwconv_smem_bytes(int D, int K) { return static_cast<size_t>(kTT + K - 1) * D * 2; }
+size_t dwconv_smem_bytes(int D, int K, bool taps_in_smem) {
+  return static_cast<size_t>(kTT + K - 1) * D * 2 + (taps_in_smem ? static_cast<size_t>(K) * D * 4 : 0);
+}
 
 cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* w, const float* bias,
                           const float* bn_scale, const float* bn_shift, __nv_bfloat16* y, int B,
                           int T, int D, int K, bool causal, bool act_silu, cudaStream_t stream) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 8 != 0 || K < 1 || B > 65535) return cudaErrorInvalidValue;
-  const size_t smem = dwconv_smem_bytes(D, K);
+  const bool fixed = K == 9;  // FastConformer's kernel size: taps in registers
+  const size_t smem = dwconv_smem_bytes(D, K, !fixed);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  static std::atomic<uint64_t> attr{0};
-  if (smem > 48 * 1024)
-    if (cudaError_t e = smem_attr_once(dwconv_kernel, 227 * 1024, attr)) return e;
   const dim3 grid((T + kTT - 1) / kTT, B);
   const int threads = D / 8 < 256 ? D / 8 : 256;
-  dwconv_kernel<<<grid, threads, smem, stream>>>(x, w, bias, bn_scale, bn_shift, y, T, D, K,
-                                                  causal ? K - 1 : (K - 1) / 2, act_silu);
+  const int pad = causal ? K - 1 : (K - 1) / 2;
+  if (fixed) {
+    static std::atomic<uint64_t> attr{0};
+    if (smem > 48 * 1024)
+      if (cudaError_t e = smem_attr_once(dwconv_kernel<9>, 227 * 1024, attr)) return e;
+    dwconv_kernel<9><<<grid, threads, smem, stream>>>(x, w, bias, bn_scale, bn_shift, y, T, D, K,
+                                                      pad, act_silu);
+  } else {
+    static std::atomic<uint64_t> attr{0};
+    if (smem > 48 * 1024)
+      if (cudaError_t e = smem_attr_once(dwconv_kernel<0>, 227 * 1024, attr)) return e;
+    dwconv_kernel<0><<<grid, threads, smem, stream>>>(x, w, bias, bn_scale, bn_shift, y, T, D, K,
+                                                      pad, act_silu);
+  }
   return cudaGetLastError();
 }
 

@@ -89,6 +89,12 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
                            cudaStream_t stream, RowTiling rt = RowTiling(),
                            const Epilogue& ep = Epilogue());
 
+// ---- large-M quantised GEMM, first half: w[N,K] bf16 = dequant(wq) ----
+// (then the bf16 GEMM): each weight is dequantised once per call instead of
+// once per 128-row tile.  Requires K % 64 == 0.
+cudaError_t launch_dequant_q8(const uint8_t* wq, const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                              __nv_bfloat16* w, int N, int K, int num_sms, cudaStream_t stream);
+
 // ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
                          const __nv_bfloat16* qs, const __nv_bfloat16* qb,

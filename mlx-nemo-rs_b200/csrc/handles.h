@@ -65,6 +65,9 @@ struct nrp_context {
   std::vector<cudaEvent_t> pool;
   double prof_ms[NRP_KERNEL_KINDS] = {};
   int64_t prof_n[NRP_KERNEL_KINDS] = {};
+  // bf16 copy of one quantised weight for the large-M quantised GEMM
+  // (stream-ordered: reused by every such call on the context)
+  nrp::DevBuf wscratch;
 };
 
 struct nrp_attn {

@@ -197,6 +197,51 @@ __global__ void __launch_bounds__(kQWarps * 32)
 }
 }  // namespace
 
+namespace {
+// MLX affine dequantisation of 8-bit weights (quantization.rs:4-8, group
+// 64): w[n, k] = scale[n, k/64] * q[n, k] + bias[n, k/64], computed in f32
+// and rounded once to bf16 -- the values the in-register GEMM producer
+// writes into its B tiles.  One thread per 16 weights (a 16-byte load, two
+// 16-byte stores); HBM-bound.
+__global__ void dequant_q8_kernel(const uint8_t* __restrict__ wq, const __nv_bfloat16* __restrict__ qs,
+                                  const __nv_bfloat16* __restrict__ qb,
+                                  __nv_bfloat16* __restrict__ w, int64_t n16, int K) {
+  const int groups = K / 64;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e0 = i * 16;
+    const int64_t n = e0 / K;
+    const int k = static_cast<int>(e0 - n * K);
+    const float sc = __bfloat162float(qs[n * groups + k / 64]);
+    const float bi = __bfloat162float(qb[n * groups + k / 64]);
+    const uint4 q = reinterpret_cast<const uint4*>(wq)[i];
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t v = words[j];
+      o[2 * j] = pack_bf16x2(fmaf(sc, static_cast<float>(v & 0xFF), bi),
+                             fmaf(sc, static_cast<float>((v >> 8) & 0xFF), bi));
+      o[2 * j + 1] = pack_bf16x2(fmaf(sc, static_cast<float>((v >> 16) & 0xFF), bi),
+                                 fmaf(sc, static_cast<float>(v >> 24), bi));
+    }
+    uint4* dst = reinterpret_cast<uint4*>(w + e0);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+}  // namespace
+
+cudaError_t launch_dequant_q8(const uint8_t* wq, const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                              __nv_bfloat16* w, int N, int K, int num_sms, cudaStream_t stream) {
+  if (K % 64 != 0 || N <= 0) return cudaErrorInvalidValue;
+  const int64_t n16 = static_cast<int64_t>(N) * K / 16;
+  const int64_t want = (n16 + 255) / 256;
+  const int grid = static_cast<int>(want < num_sms * 8 ? want : num_sms * 8);
+  dequant_q8_kernel<<<grid, 256, 0, stream>>>(wq, qs, qb, w, n16, K);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
                          const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                          const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,

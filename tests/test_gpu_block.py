@@ -42,6 +42,7 @@ def make_block(nrp, wd, D, H, ff, K, causal, conv_norm, quant):
     (2, 200, 256, 2, 512, 5, True, "layer_norm", False, None, (64, 0, False)),
     (1, 129, 512, 4, 2048, 31, False, "batch_norm", True, None, (70, 13, True)),
     (2, 500, 1024, 8, 4096, 9, False, "batch_norm", True, [500, 313], None),
+    (3, 500, 1024, 8, 4096, 9, False, "batch_norm", True, [500, 250, 421], None),
 ])
 def test_block_matches_oracle(nrp, orc, B, T, D, H, ff, K, causal, conv_norm, quant, lengths,
                               context):

@@ -98,9 +98,12 @@ def test_linear_f32(nrp, orc):
     assert a < TOL_F32 and r < TOL_F32, (a, r)
 
 
-@pytest.mark.parametrize("M", [1, 14, 16, 17, 300, 896])
+@pytest.mark.parametrize("M", [1, 14, 16, 17, 300, 896, 1024, 2500])
 @pytest.mark.parametrize("K,N", [(1024, 1024), (1024, 4096), (4096, 1024)])
 def test_qlinear_mlx_affine_8bit(nrp, orc, M, K, N):
+    """M <= 16: the GEMV; up to 1023 rows: the tcgen05 GEMM with the
+    dequantising producer; from 1024 rows: the weight dequantised once, then
+    the bf16 GEMM."""
     import torch
     rng = np.random.default_rng(M * 7 + N)
     wm = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
