@@ -92,6 +92,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed f32 pairs (sm_100): (x0, x1) = (a0 + b0, a1 + b1) and
+// (x0, x1) = (a0 * m + c, a1 * m + c), one instruction for two lanes of data.
+__device__ __forceinline__ void add_f32x2(float& x0, float& x1, float a0, float a1, float b0,
+                                          float b1) {
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fma_f32x2(float& x0, float& x1, float a0, float a1, float m,
+                                          float c) {
+  asm("{\n .reg .b64 ra, rm, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rm, {%4, %4};\n"
+      " mov.b64 rc, {%5, %5};\n fma.rn.f32x2 rd, ra, rm, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(m), "f"(c));
+}
+
 // One arrival per warp, after every lane's prior writes (each lane fenced
 // what it needs before calling this).
 __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
@@ -308,6 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int rlo, rhi;
     row_interval(ctx, min(i, g.q_hi - 1), g.k_lo, kend, rlo, rhi);
     const float scale_log2 = 1.4426950408889634f * rsqrtf(static_cast<float>(kDh));
+    // the output is rescaled when a row maximum grows by more than 2^8
+    // (log2 units), i.e. 8 / scale_log2 in raw score units
+    const float rescale_raw = 8.f / scale_log2;
     const int shift = 31 - lane;
     const bool s16 = shift & 16, s8 = shift & 8, s4 = shift & 4, s2 = shift & 2, s1 = shift & 1;
     // keys every row of this warp sees: no per-element mask inside it
@@ -315,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int whi = __reduce_min_sync(0xffffffffu, rhi);
     float* xbuf = reinterpret_cast<float*>(smem + kOffX);  // [parity][half][row] exchange
     uint32_t xphase = 0;
-    float m_ref = -INFINITY;  // log2-domain maximum the output is scaled by
+    float m_ref = -INFINITY;  // raw-score maximum the output is scaled by
     float l = 0.f;            // this thread's share of the row sum
     bool ok = true;
     // ---- q+u and q+v tiles (bf16 adds, attention.rs:506-508), once per CTA.
@@ -398,23 +418,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int x = 0; x < 32; ++x) a[x] = s1 ? a[x + 1] : a[x];
         const int jb = jt + jl0;
-        if (jb >= wlo && jb + 32 <= whi) {  // every key visible to every row
+        // raw scores s + bd (the scale is applied inside exp2 below)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float v = (__uint_as_float(sr[e]) + a[e]) * scale_log2;
-            mxp[e & 7] = fmaxf(mxp[e & 7], v);
-            sc[32 * sub + e] = v;
-          }
-        } else {
+        for (int e = 0; e < 32; e += 2)
+          add_f32x2(sc[32 * sub + e], sc[32 * sub + e + 1], __uint_as_float(sr[e]),
+                    __uint_as_float(sr[e + 1]), a[e], a[e + 1]);
+        if (!(jb >= wlo && jb + 32 <= whi)) {  // some key hidden from some row
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int j = jb + e;
-            float v = (__uint_as_float(sr[e]) + a[e]) * scale_log2;
-            v = (j >= rlo && j < rhi) ? v : -INFINITY;
-            mxp[e & 7] = fmaxf(mxp[e & 7], v);
-            sc[32 * sub + e] = v;
+            sc[32 * sub + e] = (j >= rlo && j < rhi) ? sc[32 * sub + e] : -INFINITY;
           }
         }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mxp[e & 7] = fmaxf(mxp[e & 7], sc[32 * sub + e]);
       }
       float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                        fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
@@ -431,8 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mx = fmaxf(mx, xbuf[xphase * 256 + (kh ^ 1) * 128 + il]);
       xphase ^= 1;
       float alpha = 1.f;
-      if (mx > m_ref + 8.f) {  // also taken when m_ref is -inf and mx finite
-        alpha = (m_ref == -INFINITY) ? 1.f : exp2f(m_ref - mx);
+      if (mx > m_ref + rescale_raw) {  // also taken when m_ref is -inf and mx finite
+        alpha = (m_ref == -INFINITY) ? 1.f : exp2f((m_ref - mx) * scale_log2);
         m_ref = mx;
       }
       l *= alpha;
@@ -455,7 +472,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- pass 2: probabilities -> shared memory (bf16 A operand of P.V)
       // a row that has seen no key yet keeps m_ref = -inf: subtract 0 so
       // its -inf scores give exp2(-inf) = 0 rather than NaN
-      const float msub = m_ref == -INFINITY ? 0.f : m_ref;
+      // p = 2^((score - m) * scale): one packed FMA per pair, then MUFU
+      const float nms = m_ref == -INFINITY ? 0.f : -m_ref * scale_log2;
       uint8_t* prow = sPr + kh * kHalf;
       float lp[8];
 #pragma unroll
@@ -465,10 +483,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_exp2(sc[8 * ch + 2 * e] - msub);
-          const float p1 = fast_exp2(sc[8 * ch + 2 * e + 1] - msub);
-          lp[2 * e] += p0;
-          lp[2 * e + 1] += p1;
+          float x0, x1;
+          fma_f32x2(x0, x1, sc[8 * ch + 2 * e], sc[8 * ch + 2 * e + 1], scale_log2, nms);
+          const float p0 = fast_exp2(x0);
+          const float p1 = fast_exp2(x1);
+          add_f32x2(lp[2 * e], lp[2 * e + 1], lp[2 * e], lp[2 * e + 1], p0, p1);
           pk[e] = pack_bf16x2(p0, p1);
         }
         *reinterpret_cast<uint4*>(prow + sw128_offset(il, ch)) =
