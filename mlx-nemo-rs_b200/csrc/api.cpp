@@ -279,7 +279,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
     w = ctx->wscratch.p;
     quant = false;
   }
-  CUtensorMap mx, mw;
+  CUtensorMap mx;
   const bool xmap_ok =
       rt.T > 0 ? nrp::make_tmap_3d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, rt.T, rt.B,
                                    static_cast<uint64_t>(K) * 2,
@@ -296,11 +296,8 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                  static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
                                  ctx->d_err, st, rt, ep));
   } else {
-    if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
-                           static_cast<uint64_t>(K) * 2, 64, 256, true))
-      return fail(NRP_ERR_CUDA, "TMA descriptor for W rejected");
     ProfScope ps(ctx, NRP_KERNEL_GEMM_BF16, st);
-    CUDA_TRY(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
+    CUDA_TRY(nrp::launch_gemm_bf16(mx, w, static_cast<const __nv_bfloat16*>(bias),
                                    static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
                                    ctx->d_err, st, rt, ep));
   }

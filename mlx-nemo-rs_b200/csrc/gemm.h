@@ -74,10 +74,11 @@ struct Epilogue {
 };
 
 // ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
-// x map: bf16 [M, K], box (64, 128), swizzle 128.  W map: bf16 [N, K], box
-// (64, 256), swizzle 128.  Requires K % 64 == 0 and N % 32 == 0.
+// x map: bf16 [M, K], box (64, 128), swizzle 128.  w: bf16 [N, K] row-major
+// (the launcher makes its map for the tile width it picks).  Requires
+// K % 64 == 0 and N % 32 == 0.
 int gemm_smem_bytes();
-cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
+cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
                              int K, int num_sms, int* err, cudaStream_t stream,
                              RowTiling rt = RowTiling(), const Epilogue& ep = Epilogue());

@@ -26,17 +26,22 @@ namespace nrp {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBN = 256;
+// Output tiles are 128 x kBN with kBN = 256 (large problems) or 128 (problems
+// with few tiles: twice the CTAs, and 6 pipeline stages in the same budget).
 constexpr int kBK = 64;
-constexpr int kStages = 4;
+constexpr int kMaxStages = 6;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
+template <int kBN>
+struct TileCfg {
+  static constexpr int kStages = kBN == 256 ? 4 : 6;
+  static constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 / 16 KB
+};
 constexpr int kEpiWarp0 = 2;
 constexpr int kDeqWarp0 = 6;
 
 struct GemmSmem {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint32_t tmem_base;
@@ -46,9 +51,12 @@ struct GemmSmem {
 constexpr uint32_t kSlabBytes = 32 * 128;  // 32 rows x 64 bf16, 128B-swizzled
 constexpr uint32_t kEpiBytes = 4 * 2 * kSlabBytes;  // 4 warps x 2 buffers
 constexpr int kMaxBatch = 256;  // batched tiling: utterances per GEMM
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * (kABytes + kBBytes) + kEpiBytes +
-                              256 + 4 * (kMaxBatch + 1);
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+template <int kBN>
+constexpr size_t smem_bytes() {
+  return 1024 /*align slack*/ + TileCfg<kBN>::kStages * (kABytes + TileCfg<kBN>::kBBytes) +
+         kEpiBytes + 256 + 4 * (kMaxBatch + 1);
+}
+static_assert(smem_bytes<256>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory budget");
 
 // v[e] += bias[n + e] for e < 32 (zero past N); 16-byte loads when `vec`.
 __device__ __forceinline__ void add_bias32(float* v, const __nv_bfloat16* bias, int n, int N,
@@ -76,7 +84,7 @@ __device__ __forceinline__ void add_bias64(float* v, const __nv_bfloat16* bias, 
   add_bias32(v + 32, bias, n + 32, N, vec);
 }
 
-template <bool kQuant>
+template <bool kQuant, int kBN>
 __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ CUtensorMap map_w,
@@ -86,6 +94,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ bias, // [N] or null
                    int M, int N, int K, RowTiling rt, Epilogue ep, int* err) {
+  constexpr int kStages = TileCfg<kBN>::kStages;
+  constexpr uint32_t kBBytes = TileCfg<kBN>::kBBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -433,7 +443,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
 
 }  // namespace
 
-int gemm_smem_bytes() { return static_cast<int>(kSmemBytes); }
+int gemm_smem_bytes() { return static_cast<int>(smem_bytes<256>()); }
 
 namespace {
 bool make_y_map(CUtensorMap* map, __nv_bfloat16* y, int ldy, int M, int N, const RowTiling& rt) {
@@ -452,50 +462,74 @@ bool epilogue_ok(const Epilogue& ep, int N) {
   if (ep.mode == kEpiResidual)
     return ep.res && ep.ldr % 8 == 0 && ep.res_bs % 8 == 0 && N % 8 == 0 &&
            (reinterpret_cast<uintptr_t>(ep.res) & 15) == 0;
-  if (ep.mode == kEpiGlu) return N % kBN == 0;
+  if (ep.mode == kEpiGlu) return N % 256 == 0;
   return ep.mode == kEpiBias || ep.mode == kEpiSilu;
 }
-int grid_size(int M, int N, const RowTiling& rt, int num_sms) {
-  const int tiles_m = rt.T > 0 ? rt.B * ((rt.T + kBM - 1) / kBM) : (M + kBM - 1) / kBM;
-  const int tiles = tiles_m * ((N + kBN - 1) / kBN);
+int tiles_m_of(int M, const RowTiling& rt) {
+  return rt.T > 0 ? rt.B * ((rt.T + kBM - 1) / kBM) : (M + kBM - 1) / kBM;
+}
+// 128-wide tiles when 256-wide ones would not fill one wave of the persistent
+// grid (M = 896 rows of a streaming chunk: 84 tiles -> 168).  With more tiles
+// the 256-wide tile is faster per FLOP (it reads 1.5x less shared memory per
+// MMA), which outweighs the better wave fill (config 1's linear_out: 312
+// tiles ran 7% slower as 624).  GLU needs the 256-wide layout.
+int pick_bn(int M, int N, const RowTiling& rt, const Epilogue& ep, int num_sms) {
+  if (ep.mode == kEpiGlu) return 256;
+  const int tiles256 = tiles_m_of(M, rt) * ((N + 255) / 256);
+  return tiles256 < num_sms ? 128 : 256;
+}
+int grid_size(int M, int N, int bn, const RowTiling& rt, int num_sms) {
+  const int tiles = tiles_m_of(M, rt) * ((N + bn - 1) / bn);
   return tiles < num_sms ? tiles : num_sms;
 }
-}  // namespace
 
-cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const CUtensorMap& map_w,
-                             const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
-                             int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt,
-                             const Epilogue& ep) {
+template <bool kQuant, int kBN>
+cudaError_t launch_tn(const CUtensorMap& map_x, const void* w, const uint8_t* wq,
+                      const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                      const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N, int K,
+                      int num_sms, int* err, cudaStream_t stream, const RowTiling& rt,
+                      const Epilogue& ep) {
   static std::atomic<uint64_t> attr{0};
-  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<false>, static_cast<int>(kSmemBytes), attr))
-    return e;
-  if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
-  if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
-  const int grid = grid_size(M, N, rt, num_sms);
+  constexpr int kSmem = static_cast<int>(smem_bytes<kBN>());
+  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<kQuant, kBN>, kSmem, attr)) return e;
+  CUtensorMap map_w = map_x;  // unused by the quantised kernel
+  if (!kQuant && !make_tmap_2d(&map_w, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
+                               static_cast<uint64_t>(K) * 2, 64, kBN, true))
+    return cudaErrorInvalidValue;
   CUtensorMap map_y;
   if (!make_y_map(&map_y, y, ldy, M, ep.mode == kEpiGlu ? N / 2 : N, rt))
     return cudaErrorInvalidValue;
-  gemm_tn_kernel<false><<<grid, 192, kSmemBytes, stream>>>(map_x, map_w, map_y, nullptr, nullptr,
-                                                           nullptr, bias, M, N, K, rt, ep, err);
+  const int grid = grid_size(M, N, kBN, rt, num_sms);
+  gemm_tn_kernel<kQuant, kBN><<<grid, kQuant ? 320 : 192, kSmem, stream>>>(
+      map_x, map_w, map_y, wq, qs, qb, bias, M, N, K, rt, ep, err);
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
+                             const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
+                             int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt,
+                             const Epilogue& ep) {
+  if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
+  if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
+  if (pick_bn(M, N, rt, ep, num_sms) == 128)
+    return launch_tn<false, 128>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
+                                 num_sms, err, stream, rt, ep);
+  return launch_tn<false, 256>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
+                               num_sms, err, stream, rt, ep);
 }
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
                            const __nv_bfloat16* qb, const __nv_bfloat16* bias, __nv_bfloat16* y,
                            int ldy, int M, int N, int K, int num_sms, int* err,
                            cudaStream_t stream, RowTiling rt, const Epilogue& ep) {
-  static std::atomic<uint64_t> attr{0};
-  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<true>, static_cast<int>(kSmemBytes), attr))
-    return e;
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
   if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
-  const int grid = grid_size(M, N, rt, num_sms);
-  CUtensorMap map_y;
-  if (!make_y_map(&map_y, y, ldy, M, ep.mode == kEpiGlu ? N / 2 : N, rt))
-    return cudaErrorInvalidValue;
-  gemm_tn_kernel<true><<<grid, 320, kSmemBytes, stream>>>(map_x, map_x, map_y, wq, qs, qb, bias, M,
-                                                          N, K, rt, ep, err);
-  return cudaGetLastError();
+  if (pick_bn(M, N, rt, ep, num_sms) == 128)
+    return launch_tn<true, 128>(map_x, nullptr, wq, qs, qb, bias, y, ldy, M, N, K, num_sms, err,
+                                stream, rt, ep);
+  return launch_tn<true, 256>(map_x, nullptr, wq, qs, qb, bias, y, ldy, M, N, K, num_sms, err,
+                              stream, rt, ep);
 }
 
 }  // namespace nrp

@@ -88,7 +88,7 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
                                static_cast<__nv_bfloat16*>(y), ldy, N, st));
     return NRP_OK;
   }
-  CUtensorMap mx, mw;
+  CUtensorMap mx;
   if (!nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
                          static_cast<uint64_t>(K) * 2, 64, 128, true))
     return report(NRP_ERR_CUDA, "TMA descriptor for x rejected");
@@ -101,10 +101,7 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
                                  ctx->d_err, st));
     return NRP_OK;
   }
-  if (!nrp::make_tmap_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
-                         static_cast<uint64_t>(K) * 2, 64, 256, true))
-    return report(NRP_ERR_CUDA, "TMA descriptor for W rejected");
-  TRY_CUDA(nrp::launch_gemm_bf16(mx, mw, static_cast<const __nv_bfloat16*>(bias),
+  TRY_CUDA(nrp::launch_gemm_bf16(mx, w, static_cast<const __nv_bfloat16*>(bias),
                                  static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
                                  ctx->d_err, st));
   return NRP_OK;
