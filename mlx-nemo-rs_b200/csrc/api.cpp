@@ -268,15 +268,18 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   // context's scratch and run the bf16 GEMM (the in-register producer would
   // redo the dequantisation for every 128-row tile).
   if (quant && M >= kDequantOnceMinRows) {
-    CUDA_TRY(ctx->wscratch.ensure(static_cast<size_t>(N) * K * 2));
+    // one scratch per stream the library uses, so overlapping calls on the
+    // caller's stream and the side stream never share it
+    nrp::DevBuf& scratch = st == ctx->side ? ctx->wscratch_side : ctx->wscratch;
+    CUDA_TRY(scratch.ensure(static_cast<size_t>(N) * K * 2));
     {
       ProfScope ps(ctx, NRP_KERNEL_DEQUANT, st);
       CUDA_TRY(nrp::launch_dequant_q8(static_cast<const uint8_t*>(w),
                                       static_cast<const __nv_bfloat16*>(qs),
                                       static_cast<const __nv_bfloat16*>(qb),
-                                      ctx->wscratch.as<__nv_bfloat16>(), N, K, ctx->num_sms, st));
+                                      scratch.as<__nv_bfloat16>(), N, K, ctx->num_sms, st));
     }
-    w = ctx->wscratch.p;
+    w = scratch.p;
     quant = false;
   }
   CUtensorMap mx;
@@ -473,6 +476,13 @@ int nrp_context_create(int device, nrp_context** out) {
     return fail(NRP_ERR_NOMEM, "cudaMalloc: %s", cudaGetErrorString(e));
   }
   cudaMemset(c->d_err, 0, sizeof(int));
+  e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    nrp_context_destroy(c);
+    return fail(NRP_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
+  }
   *out = c;
   return ok();
 }
@@ -482,6 +492,12 @@ int nrp_context_destroy(nrp_context* ctx) {
   cudaSetDevice(ctx->device);
   prof_collect(ctx);
   for (cudaEvent_t e : ctx->pool) cudaEventDestroy(e);
+  if (ctx->side) {
+    cudaStreamSynchronize(ctx->side);
+    cudaStreamDestroy(ctx->side);
+  }
+  if (ctx->fork) cudaEventDestroy(ctx->fork);
+  if (ctx->join) cudaEventDestroy(ctx->join);
   cudaFree(ctx->d_err);
   delete ctx;
   return ok();
@@ -648,22 +664,28 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
   if (lengths && B <= 256) rows = {lengths, T, B};
   if (a->dtype == NRP_DTYPE_BF16) {
     // 478-480: q, k, v in one GEMM; 493: linear_pos
-    rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
-                    a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
-                    3 * D, rows);
-    if (rc) return rc;
     // linear_pos only over the P rows the context's relative positions
-    // reach (all 2T-1 without a window; 257 for a (128, 128) window)
+    // reach (all 2T-1 without a window; 257 for a (128, 128) window), on the
+    // side stream: it fills the SMs the q|k|v GEMM leaves idle in its last
+    // wave, and joins before the attention
     nrp::AttnGeom g = nrp::full_geom(T, D);
     int dmin, dmax;
     nrp::visible_offsets(cd, T, dmin, dmax);
     g.p_base = T - 1 + dmin;
     g.p_rows = dmax - dmin + 1;
-    rc = run_linear(ctx, st, a->dtype,
+    CUDA_TRY(cudaEventRecord(ctx->fork, st));
+    CUDA_TRY(cudaStreamWaitEvent(ctx->side, ctx->fork, 0));
+    rc = run_linear(ctx, ctx->side, a->dtype,
                     static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * es,
                     g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr,
                     a->pbuf.p, D);
     if (rc) return rc;
+    CUDA_TRY(cudaEventRecord(ctx->join, ctx->side));
+    rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
+                    a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
+                    3 * D, rows);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamWaitEvent(st, ctx->join, 0));
     ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
     CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->u_dev.as<float>(),
                                           a->v_dev.as<float>(), lengths, cd, g, a->cbuf.p, B,

@@ -68,6 +68,11 @@ struct nrp_context {
   // bf16 copy of one quantised weight for the large-M quantised GEMM
   // (stream-ordered: reused by every such call on the context)
   nrp::DevBuf wscratch;
+  nrp::DevBuf wscratch_side;  // the same for work on `side`
+  // a second stream for work that overlaps the caller's (forked and joined
+  // with events, so the caller's stream order is kept)
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 struct nrp_attn {
