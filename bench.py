@@ -85,6 +85,45 @@ def long_flops():
     return proj, pos, attn
 
 
+def run_pipelined(steps, h2d, compute, d2h):
+    """End-to-end steps as a serving loop runs them: step k's host->device
+    copy, its compute and its device->host read each on their own stream,
+    two buffer slots, so the copy engines move step k+1's input and step
+    k-1's result while step k computes.  Every step still copies its own
+    input in and reads its own result back.  h2d(slot), compute(slot) and
+    d2h(slot) issue their work on the current stream.  Returns the elapsed
+    ms from the first copy-in to the last copy-out (CUDA events)."""
+    import torch
+    s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    in_done = [torch.cuda.Event() for _ in range(steps)]
+    cmp_done = [torch.cuda.Event() for _ in range(steps)]
+    out_done = [torch.cuda.Event() for _ in range(steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(s_in)
+    for k in range(steps):
+        slot = k & 1
+        with torch.cuda.stream(s_in):
+            if k >= 2:
+                s_in.wait_event(cmp_done[k - 2])  # the slot's input buffer is free
+            h2d(slot)
+            in_done[k].record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(in_done[k])
+            if k >= 2:
+                s_cmp.wait_event(out_done[k - 2])  # the slot's output buffer is free
+            compute(slot)
+            cmp_done[k].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(cmp_done[k])
+            d2h(slot)
+            out_done[k].record(s_out)
+    end.record(s_out)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
 def env_int(name, default):
     try:
         return int(os.environ.get(name, default))
@@ -311,30 +350,30 @@ def main():
     ctx.profile(False)
     launches = sum(n for n, _ in prof.values())
 
-    # ---- end to end through the public API with host buffers
+    # ---- end to end through the public API with host buffers: each step
+    # copies its x and lengths in from pinned host memory and reads its
+    # output back (run_pipelined: copies overlap the neighbouring steps)
     x_host = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
     len_host = torch.from_numpy(lengths.copy()).pin_memory()
-    x_dev2 = torch.empty_like(xd)
-    e_s = torch.cuda.Event(enable_timing=True)
-    e_e = torch.cuda.Event(enable_timing=True)
-    for _ in range(2):
-        x_dev2.copy_(x_host, non_blocking=True)
-        mask.lengths.copy_(len_host, non_blocking=True)
-        step(out, x_dev2)
-        out_host.copy_(out, non_blocking=True)
-    torch.cuda.synchronize()
+    xs = [torch.empty_like(xd) for _ in range(2)]
+    outs = [torch.empty_like(xd) for _ in range(2)]
+    masks = [nrp.key_padding_mask(lengths, T) for _ in range(2)]
+
+    def h2d_fn(slot):
+        xs[slot].copy_(x_host, non_blocking=True)
+        masks[slot].lengths.copy_(len_host, non_blocking=True)
+
+    def compute_fn(slot):
+        attn.forward(xs[slot], pos, None, masks[slot], out=outs[slot])
+
+    def d2h_fn(slot):
+        out_host.copy_(outs[slot], non_blocking=True)
+
+    run_pipelined(4, h2d_fn, compute_fn, d2h_fn)  # warm-up
     barrier()
-    e_s.record(stream)
-    for _ in range(args.steps):
-        x_dev2.copy_(x_host, non_blocking=True)
-        mask.lengths.copy_(len_host, non_blocking=True)
-        step(out, x_dev2)
-        out_host.copy_(out, non_blocking=True)
-    e_e.record(stream)
-    torch.cuda.synchronize()
+    e2e_ms = run_pipelined(args.steps, h2d_fn, compute_fn, d2h_fn)
     barrier()
-    e2e_ms = e_s.elapsed_time(e_e)
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -440,8 +479,9 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
     """Common timing for the secondary workloads: W warm-up steps, K steps
     timed with CUDA events (L2 flushed between steps, outside the events),
     max over ranks; per-kernel device time from the library's events over K
-    more steps; e2e = K steps of `e2e()` (host copies inside); one JSON line.
-    flops / hbm_bytes: per step, per kernel kind (algorithmic)."""
+    more steps; e2e = (h2d(slot), compute(slot), d2h(slot), bytes in, bytes
+    out) run for K steps by run_pipelined (host copies inside); one JSON
+    line.  flops / hbm_bytes: per step, per kernel kind (algorithmic)."""
     import torch
     import torch.distributed as dist
     dev = torch.device("cuda", local)
@@ -490,22 +530,13 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
     prof = ctx.profile_read()
     ctx.profile(False)
     launches = sum(n for n, _ in prof.values())
-    e2e_fn, h2d, d2h = e2e
+    h2d_fn, compute_fn, d2h_fn, h2d, d2h = e2e
     if reset:
         reset()
-    for k in range(2):
-        e2e_fn(k)
-    torch.cuda.synchronize()
+    run_pipelined(2, h2d_fn, compute_fn, d2h_fn)  # warm-up
     barrier()
-    e_s = torch.cuda.Event(enable_timing=True)
-    e_e = torch.cuda.Event(enable_timing=True)
-    e_s.record(stream)
-    for k in range(args.steps):
-        e2e_fn(k)
-    e_e.record(stream)
-    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(run_pipelined(args.steps, h2d_fn, compute_fn, d2h_fn))
     barrier()
-    e2e_ms = max_over_ranks(e_s.elapsed_time(e_e))
     e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
 
     tflops_peak, peak_src = _peak()
@@ -621,17 +652,17 @@ def main_encoder(args):
     xd = torch.from_numpy(x).to(dev, torch.bfloat16)
     out = torch.empty((ENC_B, D, ENC_T), dtype=torch.bfloat16, device=dev)
 
-    def step(k, xin=xd):
-        enc.forward_from_embeddings(xin, lengths, None, out=out)
+    def step(k, xin=xd, o=out):
+        enc.forward_from_embeddings(xin, lengths, None, out=o)
 
     x_host = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
     out_host = torch.empty_like(out, device="cpu").pin_memory()
-    x_dev2 = torch.empty_like(xd)
-
-    def e2e(k):
-        x_dev2.copy_(x_host, non_blocking=True)
-        step(k, x_dev2)
-        out_host.copy_(out, non_blocking=True)
+    xs = [torch.empty_like(xd) for _ in range(2)]
+    outs = [torch.empty_like(out) for _ in range(2)]
+    e2e = (lambda slot: xs[slot].copy_(x_host, non_blocking=True),
+           lambda slot: step(0, xs[slot], outs[slot]),
+           lambda slot: out_host.copy_(outs[slot], non_blocking=True),
+           x_host.numel() * 2, out_host.numel() * 2)
 
     valid = int(lengths.sum())
     L2s = int(np.sum(lengths.astype(np.int64) ** 2))
@@ -692,7 +723,7 @@ def main_encoder(args):
              {"batch_per_gpu": ENC_B, "seq_len": ENC_T, "layers": ENC_LAYERS,
               "valid_frames_per_gpu": valid, "weights": "MLX 8-bit g64, fp16 scales",
               "parallelism": f"utterance-parallel replicas x{world}"},
-             "weak", (e2e, x_host.numel() * 2, out_host.numel() * 2), "bf16", cpu=cpu,
+             "weak", e2e, "bf16", cpu=cpu,
              hbm_bytes=bytes_)
     if world > 1:
         dist.destroy_process_group()
@@ -735,7 +766,7 @@ def main_stream(args):
             c.reset()
         state["chunk"] = 0
 
-    def step(k, xin=None):
+    def step(k, xin=None, out_last=None):
         c = state["chunk"]
         if c == STR_CHUNKS:
             reset()
@@ -743,7 +774,7 @@ def main_stream(args):
         filled = min(c * STR_CHUNK, STR_CACHE)
         h = xin if xin is not None else xs[k % len(xs)]
         for i, a in enumerate(layers):
-            o = bufs[i & 1]
+            o = out_last if (out_last is not None and i == len(layers) - 1) else bufs[i & 1]
             a.forward_with_cache(h, pos, caches[i], filled, STR_CHUNK, actx, out=o)
             h = o
         state["chunk"] = c + 1
@@ -752,12 +783,12 @@ def main_stream(args):
     x_host = torch.empty((STR_SESS, STR_CHUNK, D), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(xs[0].cpu())
     out_host = torch.empty_like(x_host).pin_memory()
-    x_dev2 = torch.empty_like(xs[0])
-
-    def e2e(k):
-        x_dev2.copy_(x_host, non_blocking=True)
-        h = step(k, x_dev2)
-        out_host.copy_(h, non_blocking=True)
+    xin = [torch.empty_like(xs[0]) for _ in range(2)]
+    outs = [torch.empty_like(xs[0]) for _ in range(2)]
+    e2e = (lambda slot: xin[slot].copy_(x_host, non_blocking=True),
+           lambda slot: step(0, xin[slot], outs[slot]),
+           lambda slot: out_host.copy_(outs[slot], non_blocking=True),
+           x_host.numel() * 2, out_host.numel() * 2)
 
     frames = STR_SESS * STR_CHUNK
     M = frames
@@ -772,7 +803,7 @@ def main_stream(args):
              {"sessions_per_gpu": STR_SESS, "chunk": STR_CHUNK, "cache": STR_CACHE,
               "layers": STR_LAYERS,
               "parallelism": f"session-parallel replicas x{world}"},
-             "weak", (e2e, x_host.numel() * 2, out_host.numel() * 2), "bf16", hbm_bytes=hbm,
+             "weak", e2e, "bf16", hbm_bytes=hbm,
              reset=reset)
     if world > 1:
         dist.destroy_process_group()
@@ -804,17 +835,17 @@ def main_single(args):
     pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
     pos = pe.get_encoding(SGL_T)
 
-    def step(k, xin=xd):
-        attn.forward(xin, pos, None, None, out=out)
+    def step(k, xin=xd, o=out):
+        attn.forward(xin, pos, None, None, out=o)
 
     x_host = torch.from_numpy(x).pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    x_dev2 = torch.empty_like(xd)
-
-    def e2e(k):
-        x_dev2.copy_(x_host, non_blocking=True)
-        step(k, x_dev2)
-        out_host.copy_(out, non_blocking=True)
+    xs = [torch.empty_like(xd) for _ in range(2)]
+    outs = [torch.empty_like(xd) for _ in range(2)]
+    e2e = (lambda slot: xs[slot].copy_(x_host, non_blocking=True),
+           lambda slot: step(0, xs[slot], outs[slot]),
+           lambda slot: out_host.copy_(outs[slot], non_blocking=True),
+           x_host.numel() * 4, out_host.numel() * 4)
 
     def cpu():
         from oracle import oracle as orc
@@ -837,7 +868,7 @@ def main_single(args):
     _harness(args, world, rank, local, ctx, step, SGL_T, flops, None, SGL_WORKLOAD,
              {"batch_per_gpu": 1, "seq_len": SGL_T, "d_model": D, "heads": H,
               "parallelism": f"replicas x{world}"},
-             "weak", (e2e, x_host.numel() * 4, out_host.numel() * 4), "f32", cpu=cpu)
+             "weak", e2e, "f32", cpu=cpu)
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -956,26 +987,25 @@ def main_long(args):
 
     x_host = torch.from_numpy(x_loc).to(torch.bfloat16).pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    x_dev2 = torch.empty_like(xd)
-    e_s = torch.cuda.Event(enable_timing=True)
-    e_e = torch.cuda.Event(enable_timing=True)
-    for _ in range(2):
-        x_dev2.copy_(x_host, non_blocking=True)
-        step(out, x_dev2)
-        out_host.copy_(out, non_blocking=True)
-    torch.cuda.synchronize()
+    xs = [torch.empty_like(xd) for _ in range(2)]
+    outs = [torch.empty_like(xd) for _ in range(2)]
+
+    def h2d_fn(slot):
+        xs[slot].copy_(x_host, non_blocking=True)
+
+    def compute_fn(slot):
+        step(outs[slot], xs[slot])
+
+    def d2h_fn(slot):
+        out_host.copy_(outs[slot], non_blocking=True)
+
+    run_pipelined(4, h2d_fn, compute_fn, d2h_fn)  # warm-up
     barrier()
-    e_s.record(stream)
-    for _ in range(args.steps):
-        x_dev2.copy_(x_host, non_blocking=True)
-        step(out, x_dev2)
-        out_host.copy_(out, non_blocking=True)
-    e_e.record(stream)
+    e2e_ms = run_pipelined(args.steps, h2d_fn, compute_fn, d2h_fn)
     if halo is not None:
         halo.check()
-    torch.cuda.synchronize()
     barrier()
-    e2e_ms = max_over_ranks(e_s.elapsed_time(e_e))
+    e2e_ms = max_over_ranks(e2e_ms)
     e2e_value = frames * args.steps / (e2e_ms / 1e3)
 
     tflops_peak, peak_src = _peak()
