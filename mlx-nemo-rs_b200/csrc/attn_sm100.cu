@@ -92,23 +92,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Packed f32 pairs (sm_100): (x0, x1) = (a0 + b0, a1 + b1) and
-// (x0, x1) = (a0 * m + c, a1 * m + c), one instruction for two lanes of data.
-__device__ __forceinline__ void add_f32x2(float& x0, float& x1, float a0, float a1, float b0,
-                                          float b1) {
-  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
-      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
-      : "=f"(x0), "=f"(x1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-__device__ __forceinline__ void fma_f32x2(float& x0, float& x1, float a0, float a1, float m,
-                                          float c) {
-  asm("{\n .reg .b64 ra, rm, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rm, {%4, %4};\n"
-      " mov.b64 rc, {%5, %5};\n fma.rn.f32x2 rd, ra, rm, rc;\n mov.b64 {%0, %1}, rd;\n}"
-      : "=f"(x0), "=f"(x1)
-      : "f"(a0), "f"(a1), "f"(m), "f"(c));
-}
-
 // One arrival per warp, after every lane's prior writes (each lane fenced
 // what it needs before calling this).
 __device__ __forceinline__ void warp_arrive(uint64_t* bar) {

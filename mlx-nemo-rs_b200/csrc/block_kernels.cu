@@ -27,7 +27,7 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
                     pack_bf16x2(f[6], f[7]));
 }
 
-__device__ __forceinline__ float silu(float v) { return v * __fdividef(1.f, 1.f + __expf(-v)); }
+__device__ __forceinline__ float silu(float v) { return v * sigmoid_approx(v); }
 
 // nn::LayerNorm (eps 1e-5, affine): one warp per row of D = 256 * kChunks,
 // the row held in registers (each lane 8 consecutive values per chunk);
@@ -110,13 +110,20 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
   const int rows = kTT + K - 1;
   const int vecs = D / 8;
   const __nv_bfloat16* xb = x + static_cast<int64_t>(b) * T * D;
+  // the input rows go in with cp.async, all of them in flight at once
   for (int i = threadIdx.x; i < rows * vecs; i += blockDim.x) {
     const int r = i / vecs, cv = i - r * vecs;
     const int t = t0 - pad_left + r;
-    uint4 q = make_uint4(0u, 0u, 0u, 0u);
-    if (t >= 0 && t < T) q = *reinterpret_cast<const uint4*>(xb + static_cast<int64_t>(t) * D + cv * 8);
-    *reinterpret_cast<uint4*>(tile + r * D + cv * 8) = q;
+    __nv_bfloat16* dst = tile + r * D + cv * 8;
+    if (t >= 0 && t < T) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)),
+                   "l"(xb + static_cast<int64_t>(t) * D + cv * 8)
+                   : "memory");
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
   if (kK == 0)  // taps transposed to [K][D] for 16-byte reads
     for (int i = threadIdx.x; i < K * D; i += blockDim.x) {
       const int c = i / K, k = i - c * K;

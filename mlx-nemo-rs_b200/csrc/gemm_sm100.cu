@@ -267,15 +267,6 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
       const int n0 = (tile % tiles_n) * kBN;
       const int buf = tc & 1;
       const uint32_t use = tc >> 1;
-      if (!skip) {
-        ++tc;
-        if (!mbar_wait(&ss->tfull[buf], use & 1, err, kDevTimeoutMma)) {
-          *abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-      }
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
       const bool glu = ep.mode == kEpiGlu;
       // bias columns come 8 at a time (16-byte loads) when the pointer allows
       const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
@@ -286,6 +277,32 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
       const bool row_in = row < (batched ? rt.T : M);
       bool keep = true;  // GLU: padded frames are zeros
       if (glu && ep.len && batched && !skip) keep = row < ep.len[bb];
+      // residual rows are read one 64-column slab ahead; the first slab's
+      // loads go out before the wait for the accumulator, under the MMAs
+      const bool resid = ep.mode == kEpiResidual && !skip && row_in;
+      const __nv_bfloat16* rrow = nullptr;
+      if (resid) {
+        const int64_t bs = ep.res_bs ? ep.res_bs : static_cast<int64_t>(rt.T) * ep.ldr;
+        rrow = ep.res + (batched ? bb * bs : 0) + static_cast<int64_t>(row) * ep.ldr + on0;
+      }
+      uint4 resv[8];
+      auto load_res = [&](int cc) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          resv[ch] = (resid && on0 + cc + ch * 8 < n_out)
+                         ? *reinterpret_cast<const uint4*>(rrow + cc + ch * 8)
+                         : make_uint4(0u, 0u, 0u, 0u);
+      };
+      load_res(0);
+      if (!skip) {
+        ++tc;
+        if (!mbar_wait(&ss->tfull[buf], use & 1, err, kDevTimeoutMma)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+      }
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBN;
 #pragma unroll 1
       for (int c = 0; c < ncols; c += 64) {
         float v[64];
@@ -308,7 +325,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             }
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              v[h + e] = keep ? a[e] * __fdividef(1.f, 1.f + __expf(-g[e])) : 0.f;
+              v[h + e] = keep ? a[e] * sigmoid_approx(g[e]) : 0.f;
           }
         } else if (!skip) {
           uint32_t r[64];
@@ -321,22 +338,18 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             if (bias) add_bias64(v, bias, n0 + c, N, bias_vec);
             if (ep.mode == kEpiSilu) {
 #pragma unroll
-              for (int e = 0; e < 64; ++e) v[e] = v[e] * __fdividef(1.f, 1.f + __expf(-v[e]));
-            } else if (ep.mode == kEpiResidual && row_in) {
-              const int64_t bs = ep.res_bs ? ep.res_bs : static_cast<int64_t>(rt.T) * ep.ldr;
-              const __nv_bfloat16* rp =
-                  ep.res + (batched ? bb * bs : 0) + static_cast<int64_t>(row) * ep.ldr + on0 + c;
+              for (int e = 0; e < 64; ++e) v[e] = v[e] * sigmoid_approx(v[e]);
+            } else if (resid) {
 #pragma unroll
               for (int ch = 0; ch < 8; ++ch) {
-                if (on0 + c + ch * 8 >= n_out) break;
-                const uint4 q = *reinterpret_cast<const uint4*>(rp + ch * 8);
+                const uint4 q = resv[ch];
                 const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float2 f =
                       __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[e]));
-                  v[ch * 8 + 2 * e] = f.x + ep.alpha * v[ch * 8 + 2 * e];
-                  v[ch * 8 + 2 * e + 1] = f.y + ep.alpha * v[ch * 8 + 2 * e + 1];
+                  fma_f32x2v(v[ch * 8 + 2 * e], v[ch * 8 + 2 * e + 1], v[ch * 8 + 2 * e],
+                             v[ch * 8 + 2 * e + 1], ep.alpha, f.x, f.y);
                 }
               }
             }
@@ -345,6 +358,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
 #pragma unroll
           for (int e = 0; e < 64; ++e) v[e] = 0.f;
         }
+        if (resid && c + 64 < ncols) load_res(c + 64);  // the next slab's residual
         if (on0 + c >= n_out) continue;  // whole slab past N (warp-uniform)
         uint8_t* sb = slab + (nslab & 1) * kSlabBytes;
         // the store issued two slabs ago must have finished reading sb

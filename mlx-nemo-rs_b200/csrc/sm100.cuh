@@ -283,6 +283,41 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
          (static_cast<uint32_t>(chunk ^ (row & 7)) << 4);
 }
 
+// Packed f32 pairs (sm_100): (x0, x1) = (a0 + b0, a1 + b1) and
+// (x0, x1) = (a0 * m + c, a1 * m + c), one instruction for two lanes of data.
+__device__ __forceinline__ void add_f32x2(float& x0, float& x1, float a0, float a1, float b0,
+                                          float b1) {
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fma_f32x2(float& x0, float& x1, float a0, float a1, float m,
+                                          float c) {
+  asm("{\n .reg .b64 ra, rm, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rm, {%4, %4};\n"
+      " mov.b64 rc, {%5, %5};\n fma.rn.f32x2 rd, ra, rm, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(m), "f"(c));
+}
+
+// (x0, x1) = (a0 * m + c0, a1 * m + c1).
+__device__ __forceinline__ void fma_f32x2v(float& x0, float& x1, float a0, float a1, float m,
+                                           float c0, float c1) {
+  asm("{\n .reg .b64 ra, rm, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rm, {%4, %4};\n"
+      " mov.b64 rc, {%5, %6};\n fma.rn.f32x2 rd, ra, rm, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(m), "f"(c0), "f"(c1));
+}
+
+// 1 / (1 + e^-x) from the hardware tanh approximation (one MUFU op):
+// sigmoid(x) = (1 + tanh(x / 2)) / 2.  Relative error ~2^-11, below a bf16
+// output's rounding.
+__device__ __forceinline__ float sigmoid_approx(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return fmaf(0.5f, t, 0.5f);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
