@@ -264,6 +264,13 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                static_cast<__nv_bfloat16*>(y), ldy, N, st));
     return ok();
   }
+  if (quant)
+    for (const auto& pr : ctx->predeq)
+      if (pr.first == w) {
+        w = pr.second;
+        quant = false;
+        break;
+      }
   // Quantised weights with many rows: dequantise the weight once into the
   // context's scratch and run the bf16 GEMM (the in-register producer would
   // redo the dequantisation for every 128-row tile).
@@ -711,6 +718,8 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
                     out, D, rows, out_ep);
 }
+
+int attn_sync(nrp_attn* a) { return sync_params(a); }
 
 int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
            const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,

@@ -141,8 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     relpos_attn_kernel(const __grid_constant__ CUtensorMap map_qkv,  // [B][tbuf][3D] bf16
                        const __grid_constant__ CUtensorMap map_p,    // [p_rows][D] bf16
                        const float* __restrict__ pos_u, const float* __restrict__ pos_v,
+                       const __grid_constant__ CUtensorMap map_out,  // [B][rows][D] bf16
                        const int32_t* __restrict__ key_len, AttnContextDev ctx, AttnGeom g,
-                       __nv_bfloat16* __restrict__ out, int H, int* err) {
+                       __nv_bfloat16* __restrict__ out, int H, int pf_stride, int* err) {
   // Dynamic shared memory starts 1024-byte aligned when, as here, the kernel
   // has no static shared memory; checked, since the swizzle atoms need it.
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -187,6 +188,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first P row of chunk 0, as a row of the p buffer (may be negative:
   // rows outside the buffer load as zeros and only meet masked pairs)
   const int rbase = g.Tg - kTile - i0 + j0 - g.p_base;
+
+  if (nt == 0) {  // no visible key (padding): zeros, without barriers or TMEM
+    const int rows = min(kTile, g.q_hi - i0);
+    __nv_bfloat16* ob = out + static_cast<size_t>(b) * g.out_bs + h * kDh;
+    for (int k = threadIdx.x; k < rows * 16; k += blockDim.x) {
+      const int rr = k >> 4, c = k & 15;
+      *reinterpret_cast<uint4*>(ob + static_cast<size_t>(i0 + rr - g.out_base) * D + c * 8) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q, 1);
@@ -244,8 +256,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d(sPr, &map_p, &bars->p0, h * kDh, rbase);
       tma_load_2d(sPr + kHalf, &map_p, &bars->p0, h * kDh + 64, rbase);
       load_stage(0);
-      load_v(0);
-      if (nt > 1) load_v(1);
+      // The CTA that will start about one CTA-duration from now (index +
+      // pf_stride, one per SM) finds its first Q, K and V tiles in L2: their
+      // DRAM latency would otherwise sit on its prologue.
+      {
+        const int nx = gridDim.x, ny = gridDim.y;
+        const int nxt = blockIdx.x + nx * (blockIdx.y + ny * blockIdx.z) + pf_stride;
+        if (nxt < nx * ny * static_cast<int>(gridDim.z)) {
+          const int qt2 = nxt % nx, h2 = (nxt / nx) % ny, b2 = nxt / (nx * ny);
+          const int i2 = g.q_lo + qt2 * kTile;
+          int klen2 = g.Tg;
+          if (key_len) klen2 = min(g.Tg, max(key_len[b2], 1));
+          if (!(key_len && i2 >= klen2)) {
+            int lo0, hi0, lo1, hi1;
+            row_interval(ctx, i2, g.k_lo, min(klen2, g.k_hi), lo0, hi0);
+            row_interval(ctx, min(i2 + kTile - 1, g.q_hi - 1), g.k_lo, min(klen2, g.k_hi), lo1,
+                         hi1);
+            const int j2 = min(lo0, lo1) - g.base;
+            for (int half = 0; half < 2; ++half) {
+              tma_prefetch_3d(&map_qkv, h2 * kDh + 64 * half, i2 - g.base, b2);
+              tma_prefetch_3d(&map_qkv, D + h2 * kDh + 64 * half, j2, b2);
+              tma_prefetch_3d(&map_qkv, 2 * D + h2 * kDh + 64 * half, j2, b2);
+            }
+          }
+        }
+      }
 
       constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, 0, 1);
@@ -276,6 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_k128(tmem, aQu, aK, idesc_kk, false);  // S_t
         mma_k128(tmem + 128 + 128 * ((t + 1) & 1), aQv, aP, idesc_kk, false);  // BD_{t+1}
         umma_commit(&bars->s);
+        if (t == 0) {  // V is first read after a whole softmax pass: load it
+          load_v(0);   // behind the first MMAs' operands
+          if (nt > 1) load_v(1);
+        }
         // the stage is free once these MMAs have read it
         ok = mbar_wait(&bars->s, t & 1, err, kDevTimeoutMma);
         if (!ok) break;
@@ -482,9 +521,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       warp_arrive(&bars->p);
     }
     // ---- epilogue: out = O / l over both key halves
-    if (ok && nt > 0) ok = warp_wait(&bars->o, (nt - 1) & 1, err, kDevTimeoutMma);
+    if (ok) ok = warp_wait(&bars->o, (nt - 1) & 1, err, kDevTimeoutMma);
     float inv = 0.f;
-    if (ok && nt > 0) {
+    if (ok) {
       tc_fence_after();
       xbuf[xphase * 256 + kh * 128 + il] = l;
       warp_arrive(&bars->x);
@@ -494,29 +533,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         inv = lt > 0.f ? 1.f / lt : 0.f;
       }
     }
+    // The normalised tile goes to shared memory in the TMA layout (the q+u
+    // tile's buffer: every MMA that read it completed before O did) and
+    // leaves in two bulk tensor stores; rows past q_hi fall outside the
+    // output map and are not written.
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
-      const int col = 64 * kh + 32 * c;
       uint32_t o[32];
-      if (ok && nt > 0) {
-        tmem_ld32(trow + 384 + col, o);
+      if (ok) {
+        tmem_ld32(trow + 384 + 64 * kh + 32 * c, o);
         tmem_ld_wait();
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = 0u;
       }
-      if (i < g.q_hi) {
-        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          pk[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(b) * g.out_bs +
-                                              static_cast<size_t>(i - g.out_base) * D +
-                                              h * kDh + col);
+      for (int v = 0; v < 4; ++v) {
+        uint32_t pk[4];
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        for (int e = 0; e < 4; ++e)
+          pk[e] = pack_bf16x2(__uint_as_float(o[8 * v + 2 * e]) * inv,
+                              __uint_as_float(o[8 * v + 2 * e + 1]) * inv);
+        *reinterpret_cast<uint4*>(sQu + kh * kHalf + sw128_offset(il, 4 * c + v)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1, kSoftmaxThreads);
+    if (threadIdx.x == 0) {
+      tma_store_3d(&map_out, sQu, h * kDh, i0 - g.out_base, b);
+      tma_store_3d(&map_out, sQu + kHalf, h * kDh + 64, i0 - g.out_base, b);
+      bulk_commit();
+      bulk_wait_all();
     }
     if (!ok) *abort_flag = 1;
   }
@@ -573,7 +621,6 @@ cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float*
                                     const float* v, const int32_t* key_len, AttnContextDev ctx,
                                     const AttnGeom& g, void* out, int B, int H, int* err,
                                     int num_sms, cudaStream_t stream) {
-  (void)num_sms;
   static std::atomic<uint64_t> attr{0};
   if (cudaError_t e = smem_attr_once(relpos_attn_kernel, static_cast<int>(kSmemBytes), attr))
     return e;
@@ -583,16 +630,20 @@ cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float*
   if (g.q_lo < g.base || g.q_hi > g.base + g.tbuf || g.k_lo < g.base ||
       g.k_hi > g.base + g.tbuf || g.k_lo < 0 || g.k_hi > g.Tg || g.q_lo < g.out_base)
     return cudaErrorInvalidValue;
-  CUtensorMap map_qkv, map_p;
+  CUtensorMap map_qkv, map_p, map_out;
   if (!make_tmap_3d(&map_qkv, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3ull * D, g.tbuf, B,
                     static_cast<uint64_t>(g.qkv_ts) * 2, static_cast<uint64_t>(g.qkv_bs) * 2, 64,
                     kTile, 1, true) ||
       !make_tmap_2d(&map_p, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, g.p_rows,
-                    static_cast<uint64_t>(D) * 2, 64, kTile, true))
+                    static_cast<uint64_t>(D) * 2, 64, kTile, true) ||
+      !make_tmap_3d(&map_out, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, g.q_hi - g.out_base,
+                    B, static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(g.out_bs) * 2, 64,
+                    kTile, 1, true))
     return cudaErrorInvalidValue;
   dim3 grid((g.q_hi - g.q_lo + kTile - 1) / kTile, H, B);
   relpos_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      map_qkv, map_p, u, v, key_len, ctx, g, static_cast<__nv_bfloat16*>(out), H, err);
+      map_qkv, map_p, u, v, map_out, key_len, ctx, g, static_cast<__nv_bfloat16*>(out), H,
+      num_sms > 0 ? num_sms : 148, err);
   return cudaGetLastError();
 }
 

@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <vector>
 
@@ -84,7 +85,8 @@ struct nrp_block {
   bool dirty = true;
   DevLinear dl[kNumLinears];
   nrp::DevBuf d_ng[kNumNorms], d_nb[kNumNorms];
-  nrp::DevBuf d_dw_w, d_dw_b, d_cn_scale, d_cn_shift, d_cn_g, d_cn_b;
+  nrp::DevBuf d_dw_w;  // taps-major [K][D]
+  nrp::DevBuf d_dw_b, d_cn_scale, d_cn_shift, d_cn_g, d_cn_b;
   nrp::DevBuf h, hid, glu, dw;  // workspace
 };
 
@@ -96,6 +98,11 @@ struct nrp_encoder {
   std::vector<nrp_block*> blocks;
   nrp::DevBuf x, pos;
   int pos_T = -1, pos_dtype = -1;
+  // bf16 copies of the quantised weights of two layers: layer i + 1's are
+  // dequantised on `dq` into slot (i + 1) % 2 while layer i runs
+  cudaStream_t dq = nullptr;
+  cudaEvent_t dq_start = nullptr, dq_ready[2] = {}, dq_done[2] = {};
+  nrp::DevBuf dq_slot[2];
 };
 
 namespace {
@@ -171,7 +178,13 @@ int sync_block(nrp_block* k) {
     TRY_CUDA(upload_f32(k->d_nb[i], rounded(k->nb[i])));
   }
   // depthwise weight: MLX [D, K, 1] == [D][K]
-  TRY_CUDA(upload_f32(k->d_dw_w, rounded(k->dw_w)));
+  {  // taps-major [K][D] on the device
+    std::vector<float> wt(static_cast<size_t>(k->K) * D);
+    for (int c = 0; c < D; ++c)
+      for (int j = 0; j < k->K; ++j)
+        wt[static_cast<size_t>(j) * D + c] = nrp::bf16_round(k->dw_w[static_cast<size_t>(c) * k->K + j]);
+    TRY_CUDA(upload_f32(k->d_dw_w, wt));
+  }
   if (!k->dw_b.empty()) TRY_CUDA(upload_f32(k->d_dw_b, rounded(k->dw_b)));
   if (k->conv_norm == 0) {
     std::vector<float> scale(D), shift(D);
@@ -190,6 +203,33 @@ int sync_block(nrp_block* k) {
   }
   k->dirty = false;
   return NRP_OK;
+}
+
+// A quantised weight of a layer: codes, scales, zero points, [N, K].
+struct QuantWeight {
+  const void* wq;
+  const void* qs;
+  const void* qb;
+  int N, K;
+};
+
+// Rows (batch x frames) from which the encoder dequantises a layer's weights
+// ahead of it: the linears dequantise whole weights from 256 rows on.
+constexpr int64_t kPrefetchMinRows = 256;
+
+// The quantised weights of a synced block, its attention's included.
+void quant_weights(const nrp_block* k, std::vector<QuantWeight>& out) {
+  for (int i = 0; i < kNumLinears; ++i) {
+    const DevLinear& d = k->dl[i];
+    if (!d.quant) continue;
+    int N, Kin;
+    linear_shape(k, i, N, Kin);
+    out.push_back({d.w.p, d.s.p, d.z.p, N, Kin});
+  }
+  const nrp_attn* a = k->attn;
+  if (a->qkv_quant) out.push_back({a->w_qkv.p, a->s_qkv.p, a->z_qkv.p, 3 * a->D, a->D});
+  if (a->pos_quant) out.push_back({a->w_pos.p, a->s_pos.p, a->z_pos.p, a->D, a->D});
+  if (a->out_quant) out.push_back({a->w_out.p, a->s_out.p, a->z_out.p, a->D, a->D});
 }
 
 int block_linear(nrp_block* k, cudaStream_t st, int which, const void* x, int M, void* y,
@@ -471,6 +511,12 @@ int nrp_encoder_create(nrp_context* ctx, int n_layers, int d_model, int n_heads,
 
 int nrp_encoder_destroy(nrp_encoder* e) {
   if (!e) return NRP_OK;
+  if (e->dq) {
+    cudaStreamSynchronize(e->dq);
+    cudaStreamDestroy(e->dq);
+  }
+  for (cudaEvent_t ev : {e->dq_start, e->dq_ready[0], e->dq_ready[1], e->dq_done[0], e->dq_done[1]})
+    if (ev) cudaEventDestroy(ev);
   for (nrp_block* b : e->blocks) nrp_block_destroy(b);
   delete e;
   return NRP_OK;
@@ -521,8 +567,80 @@ int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void
     if (e->xscale != 1.f)
       TRY_CUDA(nrp::launch_scale(e->x.as<__nv_bfloat16>(), n, nrp::bf16_round(e->xscale), st));
   }
-  for (nrp_block* b : e->blocks) {
-    const int rc = nrp_block_forward(b, stream, e->x.p, B, T, e->pos.p, lengths, context, e->x.p);
+  // Quantised layers: the next layer's weights are dequantised on e->dq
+  // while the current layer runs (every forward still dequantises every
+  // weight; only the order of the work changes).  Not worth a stream below
+  // the rows from which the linears dequantise whole weights anyway.
+  const int L = static_cast<int>(e->blocks.size());
+  std::vector<std::vector<QuantWeight>> qw(L);
+  size_t slot_bytes = 0;
+  if (n / D >= kPrefetchMinRows) {
+    for (int i = 0; i < L; ++i) {
+      int rc = sync_block(e->blocks[i]);
+      if (!rc) rc = nrp::attn_sync(e->blocks[i]->attn);
+      if (rc) return rc;
+      size_t bytes = 0;
+      quant_weights(e->blocks[i], qw[i]);
+      for (const QuantWeight& q : qw[i]) bytes += static_cast<size_t>(q.N) * q.K * 2;
+      slot_bytes = std::max(slot_bytes, bytes);
+    }
+  }
+  const bool pre = slot_bytes > 0;
+  if (pre) {
+    if (!e->dq) {
+      TRY_CUDA(cudaStreamCreateWithFlags(&e->dq, cudaStreamNonBlocking));
+      for (cudaEvent_t* ev : {&e->dq_start, &e->dq_ready[0], &e->dq_ready[1], &e->dq_done[0],
+                              &e->dq_done[1]})
+        TRY_CUDA(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+    }
+    TRY_CUDA(e->dq_slot[0].ensure(slot_bytes));
+    TRY_CUDA(e->dq_slot[1].ensure(slot_bytes));
+    // slots are free once the work queued so far on st (an earlier forward) is done
+    TRY_CUDA(cudaEventRecord(e->dq_start, st));
+    TRY_CUDA(cudaStreamWaitEvent(e->dq, e->dq_start, 0));
+  }
+  // jobs of layer i into its slot; the (codes -> copy) table the linears look up
+  auto slot_jobs = [&](int i, std::vector<nrp::DeqJob>& jobs,
+                       std::vector<std::pair<const void*, const void*>>& table) {
+    auto* dst = e->dq_slot[i & 1].as<__nv_bfloat16>();
+    for (const QuantWeight& q : qw[i]) {
+      jobs.push_back({static_cast<const uint8_t*>(q.wq), static_cast<const __nv_bfloat16*>(q.qs),
+                      static_cast<const __nv_bfloat16*>(q.qb), dst, q.N, q.K});
+      table.emplace_back(q.wq, dst);
+      dst += static_cast<size_t>(q.N) * q.K;
+    }
+  };
+  auto issue = [&](int i) -> int {
+    std::vector<nrp::DeqJob> jobs;
+    std::vector<std::pair<const void*, const void*>> table;
+    slot_jobs(i, jobs, table);
+    if (i >= 2) TRY_CUDA(cudaStreamWaitEvent(e->dq, e->dq_done[i & 1], 0));  // layer i-2 done
+    {
+      nrp::ProfScope ps(e->ctx, NRP_KERNEL_DEQUANT, e->dq);
+      TRY_CUDA(nrp::launch_dequant_q8_batch(jobs.data(), static_cast<int>(jobs.size()),
+                                            e->ctx->num_sms, e->dq));
+    }
+    TRY_CUDA(cudaEventRecord(e->dq_ready[i & 1], e->dq));
+    return NRP_OK;
+  };
+  if (pre) {
+    const int rc = issue(0);
+    if (rc) return rc;
+  }
+  for (int i = 0; i < L; ++i) {
+    if (pre) {
+      if (i + 1 < L) {
+        const int rc = issue(i + 1);
+        if (rc) return rc;
+      }
+      TRY_CUDA(cudaStreamWaitEvent(st, e->dq_ready[i & 1], 0));
+      std::vector<nrp::DeqJob> jobs;
+      slot_jobs(i, jobs, e->ctx->predeq);
+    }
+    const int rc = nrp_block_forward(e->blocks[i], stream, e->x.p, B, T, e->pos.p, lengths,
+                                     context, e->x.p);
+    e->ctx->predeq.clear();
+    if (pre) TRY_CUDA(cudaEventRecord(e->dq_done[i & 1], st));
     if (rc) return rc;
   }
   // 717: transpose to [B, D, T]

@@ -88,20 +88,105 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* x,
 // Depthwise Conv1d over time (groups = D, kernel K, zero padding `pad_left`
 // frames before and K-1-pad_left after: (K-1)/2 each side offline, K-1 on the
 // left when causal), + bias, then optionally the inference BatchNorm folded
-// to a per-channel affine and SiLU.  A CTA covers kTT output frames of one
-// utterance; its input rows (kTT + K - 1) are staged in shared memory and
-// each thread owns 8 channels, whose K taps it keeps in registers (kK > 0,
-// the kernel size fixed at compile time) or reads from shared memory
-// (kK == 0, any K).
-constexpr int kTT = 32;
+// to a per-channel affine and SiLU.  Taps are taps-major, wt[k * D + c].
+//
+// dwconv_rows_kernel (kernel size fixed at compile time, D % 128 == 0): no
+// shared memory.  A lane owns 4 channels (8-byte loads, a warp covers 128
+// channels of a row), a warp kDwF consecutive output frames: it loads the
+// kDwF + kK - 1 input rows those need straight into registers, all in flight
+// together, and accumulates with packed f32x2 FMAs, taps in registers.  The
+// halo rows a neighbouring warp also loads come from L1/L2, so HBM sees each
+// input row about once.  Accumulation runs over the taps in order k = 0..K-1.
+constexpr int kDwF = 8;      // output frames per warp
+constexpr int kDwWarps = 8;  // warps per CTA: kDwF * kDwWarps frames x 128 channels
 template <int kK>
-__global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __restrict__ x,
-                                                     const float* __restrict__ w,  // [D][K]
-                                                     const float* __restrict__ bias,
-                                                     const float* __restrict__ bn_scale,
-                                                     const float* __restrict__ bn_shift,
-                                                     __nv_bfloat16* __restrict__ y, int T, int D,
-                                                     int K, int pad_left, int act_silu) {
+__global__ void __launch_bounds__(kDwWarps * 32, 2)
+    dwconv_rows_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wt,
+                       const float* __restrict__ bias, const float* __restrict__ bn_scale,
+                       const float* __restrict__ bn_shift, __nv_bfloat16* __restrict__ y, int T,
+                       int D, int pad_left, int act_silu) {
+  constexpr int kRows = kDwF + kK - 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.y * 128 + lane * 4;
+  const int t0 = (blockIdx.x * kDwWarps + warp) * kDwF;
+  if (t0 >= T) return;  // warp-uniform
+  const int64_t boff = static_cast<int64_t>(blockIdx.z) * T * D + c0;
+  const __nv_bfloat16* xb = x + boff;
+  uint2 raw[kRows];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const int t = t0 - pad_left + r;
+    raw[r] = (t >= 0 && t < T) ? __ldg(reinterpret_cast<const uint2*>(xb + static_cast<int64_t>(t) * D))
+                               : make_uint2(0u, 0u);
+  }
+  float wr[kK][4];
+#pragma unroll
+  for (int k = 0; k < kK; ++k) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(wt + k * D + c0));
+    wr[k][0] = q.x;
+    wr[k][1] = q.y;
+    wr[k][2] = q.z;
+    wr[k][3] = q.w;
+  }
+  float acc[kDwF][4];
+#pragma unroll
+  for (int o = 0; o < kDwF; ++o)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[o][e] = 0.f;
+  // output o takes input row o + k with tap k; rows ascend, so for each
+  // output the taps arrive in order k = 0..K-1
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const float2 f01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[r].x));
+    const float2 f23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[r].y));
+#pragma unroll
+    for (int o = 0; o < kDwF; ++o) {
+      const int k = r - o;
+      if (k < 0 || k >= kK) continue;
+      fma2_acc(acc[o][0], acc[o][1], wr[k][0], wr[k][1], f01.x, f01.y);
+      fma2_acc(acc[o][2], acc[o][3], wr[k][2], wr[k][3], f23.x, f23.y);
+    }
+  }
+  float bi[4] = {0.f, 0.f, 0.f, 0.f}, sc[4] = {1.f, 1.f, 1.f, 1.f}, sh[4] = {0.f, 0.f, 0.f, 0.f};
+  if (bias) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(bias + c0));
+    bi[0] = q.x, bi[1] = q.y, bi[2] = q.z, bi[3] = q.w;
+  }
+  if (bn_scale) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(bn_scale + c0));
+    sc[0] = q.x, sc[1] = q.y, sc[2] = q.z, sc[3] = q.w;
+  }
+  if (bn_shift) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(bn_shift + c0));
+    sh[0] = q.x, sh[1] = q.y, sh[2] = q.z, sh[3] = q.w;
+  }
+  __nv_bfloat16* yb = y + boff;
+#pragma unroll
+  for (int o = 0; o < kDwF; ++o) {
+    if (t0 + o >= T) break;
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float t = (acc[o][e] + bi[e]) * sc[e] + sh[e];
+      v[e] = act_silu ? silu(t) : t;
+    }
+    *reinterpret_cast<uint2*>(yb + static_cast<int64_t>(t0 + o) * D) =
+        make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  }
+}
+
+// Any kernel size: a CTA covers kTT output frames of one utterance; its
+// input rows (kTT + K - 1) are staged in shared memory with cp.async and the
+// taps read from shared memory; each thread owns 8 channels.
+constexpr int kTT = 32;
+__global__ void __launch_bounds__(256) dwconv_smem_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const float* __restrict__ wt,
+                                                          const float* __restrict__ bias,
+                                                          const float* __restrict__ bn_scale,
+                                                          const float* __restrict__ bn_shift,
+                                                          __nv_bfloat16* __restrict__ y, int T,
+                                                          int D, int K, int pad_left,
+                                                          int act_silu) {
   extern __shared__ __align__(16) uint8_t dw_smem[];
   __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(dw_smem);  // [kTT + K - 1][D]
   float* wsm = reinterpret_cast<float*>(dw_smem + static_cast<size_t>(kTT + K - 1) * D * 2);
@@ -110,7 +195,6 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
   const int rows = kTT + K - 1;
   const int vecs = D / 8;
   const __nv_bfloat16* xb = x + static_cast<int64_t>(b) * T * D;
-  // the input rows go in with cp.async, all of them in flight at once
   for (int i = threadIdx.x; i < rows * vecs; i += blockDim.x) {
     const int r = i / vecs, cv = i - r * vecs;
     const int t = t0 - pad_left + r;
@@ -123,12 +207,8 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
       *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  for (int i = threadIdx.x; i < K * D; i += blockDim.x) wsm[i] = wt[i];
   asm volatile("cp.async.wait_all;\n" ::: "memory");
-  if (kK == 0)  // taps transposed to [K][D] for 16-byte reads
-    for (int i = threadIdx.x; i < K * D; i += blockDim.x) {
-      const int c = i / K, k = i - c * K;
-      wsm[k * D + c] = w[i];
-    }
   __syncthreads();
   __nv_bfloat16* yb = y + static_cast<int64_t>(b) * T * D;
   for (int cv = threadIdx.x; cv < vecs; cv += blockDim.x) {
@@ -140,35 +220,19 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const __nv_bfloat16* __rest
       sc[e] = bn_scale ? bn_scale[c0 + e] : 1.f;
       sh[e] = bn_shift ? bn_shift[c0 + e] : 0.f;
     }
-    float wr[kK > 0 ? kK : 1][8];
-    if (kK > 0)
-#pragma unroll
-      for (int k = 0; k < (kK > 0 ? kK : 1); ++k)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wr[k][e] = w[(c0 + e) * kK + k];
     const int tn = min(kTT, T - t0);
     for (int tt = 0; tt < tn; ++tt) {
       float acc[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-      if (kK > 0) {
+      for (int k = 0; k < K; ++k) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
+        const float4 w0 = *reinterpret_cast<const float4*>(wsm + k * D + c0);
+        const float4 w1 = *reinterpret_cast<const float4*>(wsm + k * D + c0 + 4);
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int k = 0; k < (kK > 0 ? kK : 1); ++k) {
-          float f[8];
-          unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] = fmaf(wr[k][e], f[e], acc[e]);
-        }
-      } else {
-        for (int k = 0; k < K; ++k) {
-          float f[8];
-          unpack8(*reinterpret_cast<const uint4*>(tile + (tt + k) * D + c0), f);
-          const float4 w0 = *reinterpret_cast<const float4*>(wsm + k * D + c0);
-          const float4 w1 = *reinterpret_cast<const float4*>(wsm + k * D + c0 + 4);
-          const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] = fmaf(ww[e], f[e], acc[e]);
-        }
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(ww[e], f[e], acc[e]);
       }
       float o[8];
 #pragma unroll
@@ -237,34 +301,28 @@ cudaError_t launch_layernorm(const __nv_bfloat16* x, const float* gamma, const f
   return cudaGetLastError();
 }
 
-size_t dwconv_smem_bytes(int D, int K, bool taps_in_smem) {
-  return static_cast<size_t>(kTT + K - 1) * D * 2 + (taps_in_smem ? static_cast<size_t>(K) * D * 4 : 0);
-}
-
-cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* w, const float* bias,
+cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* wt, const float* bias,
                           const float* bn_scale, const float* bn_shift, __nv_bfloat16* y, int B,
                           int T, int D, int K, bool causal, bool act_silu, cudaStream_t stream) {
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (D % 8 != 0 || K < 1 || B > 65535) return cudaErrorInvalidValue;
-  const bool fixed = K == 9;  // FastConformer's kernel size: taps in registers
-  const size_t smem = dwconv_smem_bytes(D, K, !fixed);
+  const int pad = causal ? K - 1 : (K - 1) / 2;
+  if (K == 9 && D % 128 == 0) {  // FastConformer's kernel size
+    const int frames = kDwF * kDwWarps;
+    const dim3 grid((T + frames - 1) / frames, D / 128, B);
+    dwconv_rows_kernel<9><<<grid, kDwWarps * 32, 0, stream>>>(x, wt, bias, bn_scale, bn_shift, y,
+                                                              T, D, pad, act_silu);
+    return cudaGetLastError();
+  }
+  const size_t smem = static_cast<size_t>(kTT + K - 1) * D * 2 + static_cast<size_t>(K) * D * 4;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr{0};
+  if (smem > 48 * 1024)
+    if (cudaError_t e = smem_attr_once(dwconv_smem_kernel, 227 * 1024, attr)) return e;
   const dim3 grid((T + kTT - 1) / kTT, B);
   const int threads = D / 8 < 256 ? D / 8 : 256;
-  const int pad = causal ? K - 1 : (K - 1) / 2;
-  if (fixed) {
-    static std::atomic<uint64_t> attr{0};
-    if (smem > 48 * 1024)
-      if (cudaError_t e = smem_attr_once(dwconv_kernel<9>, 227 * 1024, attr)) return e;
-    dwconv_kernel<9><<<grid, threads, smem, stream>>>(x, w, bias, bn_scale, bn_shift, y, T, D, K,
+  dwconv_smem_kernel<<<grid, threads, smem, stream>>>(x, wt, bias, bn_scale, bn_shift, y, T, D, K,
                                                       pad, act_silu);
-  } else {
-    static std::atomic<uint64_t> attr{0};
-    if (smem > 48 * 1024)
-      if (cudaError_t e = smem_attr_once(dwconv_kernel<0>, 227 * 1024, attr)) return e;
-    dwconv_kernel<0><<<grid, threads, smem, stream>>>(x, w, bias, bn_scale, bn_shift, y, T, D, K,
-                                                      pad, act_silu);
-  }
   return cudaGetLastError();
 }
 

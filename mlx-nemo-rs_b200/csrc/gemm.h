@@ -95,6 +95,21 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
 // once per 128-row tile.  Requires K % 64 == 0.
 cudaError_t launch_dequant_q8(const uint8_t* wq, const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                               __nv_bfloat16* w, int N, int K, int num_sms, cudaStream_t stream);
+// Several weights in one launch (at most kMaxDeqJobs).
+struct DeqJob {
+  const uint8_t* wq;
+  const __nv_bfloat16* qs;
+  const __nv_bfloat16* qb;
+  __nv_bfloat16* w;
+  int N, K;
+};
+constexpr int kMaxDeqJobs = 12;
+struct DeqBatch {
+  DeqJob job[kMaxDeqJobs];
+  int64_t begin16[kMaxDeqJobs + 1];  // first 16-weight unit of each job, then the total
+  int n;
+};
+cudaError_t launch_dequant_q8_batch(const DeqJob* jobs, int n, int num_sms, cudaStream_t stream);
 
 // ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
@@ -180,9 +195,9 @@ cudaError_t launch_relpos_attn_stream_simt(const T* q, int ldq, const T* knew, c
 cudaError_t launch_layernorm(const __nv_bfloat16* x, const float* gamma, const float* beta,
                              __nv_bfloat16* y, int64_t rows, int D, float eps, bool act_silu,
                              cudaStream_t stream);
-// Depthwise conv over time of [B, T, D] (w f32 [D][K], bias [D] or null),
+// Depthwise conv over time of [B, T, D] (taps wt f32 [K][D], bias [D] or null),
 // then y = act((conv + bias) * bn_scale + bn_shift) (scale/shift null = 1/0).
-cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* w, const float* bias,
+cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* wt, const float* bias,
                           const float* bn_scale, const float* bn_shift, __nv_bfloat16* y, int B,
                           int T, int D, int K, bool causal, bool act_silu, cudaStream_t stream);
 cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stream);

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <utility>
 #include <vector>
 
 #include "../../include/nemo_relpos.h"
@@ -69,6 +70,12 @@ struct nrp_context {
   // (stream-ordered: reused by every such call on the context)
   nrp::DevBuf wscratch;
   nrp::DevBuf wscratch_side;  // the same for work on `side`
+  // bf16 copies of quantised weights made ahead of time (the encoder
+  // dequantises the next layer while the current one runs): a quantised
+  // linear whose code pointer is listed uses the copy.  Set and cleared by
+  // the caller around the launches it covers, which must be stream-ordered
+  // after the copies were written.
+  std::vector<std::pair<const void*, const void*>> predeq;
   // a second stream for work that overlaps the caller's (forked and joined
   // with events, so the caller's stream order is kept)
   cudaStream_t side = nullptr;

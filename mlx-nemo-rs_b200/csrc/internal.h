@@ -74,6 +74,9 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
            const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
            void* y, int ldy, const RowTiling& rt, const Epilogue& ep);
 
+// Uploads the module's parameters in its dtype if they changed.
+int attn_sync(nrp_attn* a);
+
 // nrp_attn_forward with `out_ep` as the epilogue of linear_out.
 int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, const void* pos_emb,
                  const int32_t* lengths, const nrp_att_context* context, void* out,

@@ -203,43 +203,62 @@ namespace {
 // and rounded once to bf16 -- the values the in-register GEMM producer
 // writes into its B tiles.  One thread per 16 weights (a 16-byte load, two
 // 16-byte stores); HBM-bound.
-__global__ void dequant_q8_kernel(const uint8_t* __restrict__ wq, const __nv_bfloat16* __restrict__ qs,
-                                  const __nv_bfloat16* __restrict__ qb,
-                                  __nv_bfloat16* __restrict__ w, int64_t n16, int K) {
-  const int groups = K / 64;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+// Dequantises one or more 8-bit weights (w = scale * q + bias per 64-wide
+// group, MLX affine) into bf16 in one launch: the jobs' 16-weight units are
+// numbered consecutively and the grid strides over all of them.
+__global__ void dequant_q8_kernel(const __grid_constant__ DeqBatch jobs) {
+  const int64_t total = jobs.begin16[jobs.n];
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t e0 = i * 16;
-    const int64_t n = e0 / K;
-    const int k = static_cast<int>(e0 - n * K);
-    const float sc = __bfloat162float(qs[n * groups + k / 64]);
-    const float bi = __bfloat162float(qb[n * groups + k / 64]);
-    const uint4 q = reinterpret_cast<const uint4*>(wq)[i];
+    int j = 0;
+    while (i >= jobs.begin16[j + 1]) ++j;
+    const DeqJob& jb = jobs.job[j];
+    const int64_t u = i - jobs.begin16[j];
+    const int64_t e0 = u * 16;
+    const int64_t n = e0 / jb.K;
+    const int k = static_cast<int>(e0 - n * jb.K);
+    const int groups = jb.K / 64;
+    const float sc = __bfloat162float(jb.qs[n * groups + k / 64]);
+    const float bi = __bfloat162float(jb.qb[n * groups + k / 64]);
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(jb.wq) + u);
     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
     uint32_t o[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t v = words[j];
-      o[2 * j] = pack_bf16x2(fmaf(sc, static_cast<float>(v & 0xFF), bi),
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t v = words[t];
+      o[2 * t] = pack_bf16x2(fmaf(sc, static_cast<float>(v & 0xFF), bi),
                              fmaf(sc, static_cast<float>((v >> 8) & 0xFF), bi));
-      o[2 * j + 1] = pack_bf16x2(fmaf(sc, static_cast<float>((v >> 16) & 0xFF), bi),
+      o[2 * t + 1] = pack_bf16x2(fmaf(sc, static_cast<float>((v >> 16) & 0xFF), bi),
                                  fmaf(sc, static_cast<float>(v >> 24), bi));
     }
-    uint4* dst = reinterpret_cast<uint4*>(w + e0);
+    uint4* dst = reinterpret_cast<uint4*>(jb.w + e0);
     dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
     dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
 }
 }  // namespace
 
+cudaError_t launch_dequant_q8_batch(const DeqJob* jobs, int n, int num_sms, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  if (n > kMaxDeqJobs) return cudaErrorInvalidValue;
+  DeqBatch b{};
+  b.n = n;
+  b.begin16[0] = 0;
+  for (int j = 0; j < n; ++j) {
+    if (jobs[j].K % 64 != 0 || jobs[j].N <= 0) return cudaErrorInvalidValue;
+    b.job[j] = jobs[j];
+    b.begin16[j + 1] = b.begin16[j] + static_cast<int64_t>(jobs[j].N) * jobs[j].K / 16;
+  }
+  const int64_t want = (b.begin16[n] + 255) / 256;
+  const int grid = static_cast<int>(want < num_sms * 8 ? want : num_sms * 8);
+  dequant_q8_kernel<<<grid, 256, 0, stream>>>(b);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_dequant_q8(const uint8_t* wq, const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                               __nv_bfloat16* w, int N, int K, int num_sms, cudaStream_t stream) {
-  if (K % 64 != 0 || N <= 0) return cudaErrorInvalidValue;
-  const int64_t n16 = static_cast<int64_t>(N) * K / 16;
-  const int64_t want = (n16 + 255) / 256;
-  const int grid = static_cast<int>(want < num_sms * 8 ? want : num_sms * 8);
-  dequant_q8_kernel<<<grid, 256, 0, stream>>>(wq, qs, qb, w, n16, K);
-  return cudaGetLastError();
+  const DeqJob j{wq, qs, qb, w, N, K};
+  return launch_dequant_q8_batch(&j, 1, num_sms, stream);
 }
 
 cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,

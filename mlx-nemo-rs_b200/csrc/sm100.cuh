@@ -128,6 +128,19 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// Prefetch a tensor tile into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
+// Barrier `id` (1..15) over the first `threads` threads of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -307,6 +320,15 @@ __device__ __forceinline__ void fma_f32x2v(float& x0, float& x1, float a0, float
       " mov.b64 rc, {%5, %6};\n fma.rn.f32x2 rd, ra, rm, rc;\n mov.b64 {%0, %1}, rd;\n}"
       : "=f"(x0), "=f"(x1)
       : "f"(a0), "f"(a1), "f"(m), "f"(c0), "f"(c1));
+}
+
+// (c0, c1) += (a0 * b0, a1 * b1), one fused rounding each.
+__device__ __forceinline__ void fma2_acc(float& c0, float& c1, float a0, float a1, float b0,
+                                         float b1) {
+  asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mov.b64 rc, {%0, %1};\n fma.rn.f32x2 rc, ra, rb, rc;\n mov.b64 {%0, %1}, rc;\n}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
 // 1 / (1 + e^-x) from the hardware tanh approximation (one MUFU op):

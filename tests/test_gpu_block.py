@@ -41,6 +41,8 @@ def make_block(nrp, wd, D, H, ff, K, causal, conv_norm, quant):
     (2, 260, 256, 2, 1024, 9, False, "batch_norm", True, [260, 130], None),
     (2, 200, 256, 2, 512, 5, True, "layer_norm", False, None, (64, 0, False)),
     (1, 129, 512, 4, 2048, 31, False, "batch_norm", True, None, (70, 13, True)),
+    (2, 150, 512, 4, 1024, 9, True, "layer_norm", False, [150, 77], None),
+    (3, 70, 256, 2, 768, 9, False, "batch_norm", True, [70, 1, 33], None),
     (2, 500, 1024, 8, 4096, 9, False, "batch_norm", True, [500, 313], None),
     (3, 500, 1024, 8, 4096, 9, False, "batch_norm", True, [500, 250, 421], None),
 ])
@@ -88,11 +90,14 @@ def test_block_in_place_equals_out_of_place(nrp, orc):
 
 
 def test_encoder_forward_from_embeddings(nrp, orc):
-    """Two layers of forward_from_embeddings (conformer.rs:694-722): x *
-    sqrt(d_model), the blocks, the [B, D, T] transpose."""
+    """Three layers of forward_from_embeddings (conformer.rs:694-722): x *
+    sqrt(d_model), the blocks, the [B, D, T] transpose.  The quantised
+    weights of each next layer are dequantised on a second stream into one
+    of two slots, so three layers reuse a slot; a second forward reuses both
+    and must give the same bits."""
     import torch
     rng = np.random.default_rng(4)
-    B, T, D, H, ff, K, L = 2, 180, 256, 2, 1024, 9, 2
+    B, T, D, H, ff, K, L = 2, 180, 256, 2, 1024, 9, 3
     enc = nrp.ConformerEncoder(L, D, H, ff, K)
     bws, wd = [], {}
     for i in range(L):
@@ -103,8 +108,11 @@ def test_encoder_forward_from_embeddings(nrp, orc):
     enc.set_dtype(nrp.BF16)
     x = rng.standard_normal((B, T, D)).astype(np.float32)
     lengths = np.array([180, 97], np.int32)
-    out, out_len = enc.forward_from_embeddings(torch.from_numpy(x).cuda().bfloat16(), lengths)
+    xd = torch.from_numpy(x).cuda().bfloat16()
+    out, out_len = enc.forward_from_embeddings(xd, lengths)
+    again, _ = enc.forward_from_embeddings(xd, lengths)
     enc.ctx.check()
+    assert torch.equal(out, again)
     assert tuple(out.shape) == (B, D, T) and np.array_equal(out_len, lengths)
     got = out.float().cpu().numpy().transpose(0, 2, 1)
     h = orc.bf16_round(orc.bf16_round(x) * np.float32(np.sqrt(D)))
