@@ -226,6 +226,16 @@ int sync_params(nrp_attn* a) {
     }
   CUDA_TRY(upload(a->u_dev, u.data(), D, NRP_DTYPE_F32));
   CUDA_TRY(upload(a->v_dev, v.data(), D, NRP_DTYPE_F32));
+  a->uv_packed.assign(static_cast<size_t>(a->H) * 128, 0u);
+  for (int h = 0; h < a->H; ++h)
+    for (int k = 0; k < 64; ++k) {
+      const int c = h * a->dh + 2 * k;
+      if (c + 1 >= D) break;
+      a->uv_packed[h * 128 + k] =
+          bf16_bits(u[c]) | (static_cast<uint32_t>(bf16_bits(u[c + 1])) << 16);
+      a->uv_packed[h * 128 + 64 + k] =
+          bf16_bits(v[c]) | (static_cast<uint32_t>(bf16_bits(v[c + 1])) << 16);
+    }
   a->dirty = false;
   a->spos_len = -1;
   return ok();
@@ -477,12 +487,12 @@ int nrp_context_create(int device, nrp_context** out) {
   auto* c = new nrp_context;
   c->device = device;
   c->num_sms = prop.multiProcessorCount;
-  cudaError_t e = cudaMalloc(&c->d_err, sizeof(int));
+  cudaError_t e = cudaMalloc(&c->d_err, sizeof(int) * kCtxInts);
   if (e != cudaSuccess) {
     delete c;
     return fail(NRP_ERR_NOMEM, "cudaMalloc: %s", cudaGetErrorString(e));
   }
-  cudaMemset(c->d_err, 0, sizeof(int));
+  cudaMemset(c->d_err, 0, sizeof(int) * kCtxInts);
   e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
@@ -694,9 +704,9 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
     if (rc) return rc;
     CUDA_TRY(cudaStreamWaitEvent(st, ctx->join, 0));
     ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
-    CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->u_dev.as<float>(),
-                                          a->v_dev.as<float>(), lengths, cd, g, a->cbuf.p, B,
-                                          a->H, ctx->d_err, ctx->num_sms, st));
+    CUDA_TRY(nrp::launch_relpos_attn_bf16(a->qkv.p, a->pbuf.p, a->uv_packed.data(), lengths,
+                                          cd, g, a->cbuf.p, B, a->H, ctx->d_err,
+                                          nrp::sched_slot(ctx), ctx->num_sms, st));
   } else {
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
@@ -879,9 +889,9 @@ int nrp_attn_forward_seq_sharded(nrp_attn* a, nrp_halo* h, void* stream, const v
       qkv = buf + static_cast<size_t>(hl) * row;
     }
     ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
-    CUDA_TRY(nrp::launch_relpos_attn_bf16(qkv, a->pbuf.p, a->u_dev.as<float>(),
-                                          a->v_dev.as<float>(), lengths, cd, gi, a->cbuf.p, B,
-                                          a->H, ctx->d_err, ctx->num_sms, st));
+    CUDA_TRY(nrp::launch_relpos_attn_bf16(qkv, a->pbuf.p, a->uv_packed.data(), lengths, cd,
+                                          gi, a->cbuf.p, B, a->H, ctx->d_err,
+                                          nrp::sched_slot(ctx), ctx->num_sms, st));
     return ok();
   };
   if (!exchange || first >= last) {

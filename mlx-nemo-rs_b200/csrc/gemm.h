@@ -151,14 +151,24 @@ struct AttnContextDev {
 };
 void visible_offsets(const AttnContextDev& ctx, int T, int& dmin, int& dmax);
 
-// qkv per geom; p: projected positions per geom; u, v: [H, 128] f32
-// position biases (bf16-rounded values, added to q in bf16 inside the
-// kernel); key_len: [B] int32 (key j visible iff j < max(key_len[b], 1)) or
-// null; out: bf16, row of frame i of utterance b at b * out_bs + (i - out_base) * D.
-cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const float* u,
-                                    const float* v, const int32_t* key_len, AttnContextDev ctx,
+// q+u / q+v biases of every head as bf16 pairs (the attention kernel takes
+// them as parameters): head h's u at w[128h .. 128h+64), its v at
+// w[128h+64 .. 128h+128).
+constexpr int kMaxHeadsUV = 16;
+struct AttnUV {
+  uint32_t w[kMaxHeadsUV * 128];
+};
+
+// qkv per geom; p: projected positions per geom; uv_host: [H][128] bf16
+// pairs as in AttnUV (H <= kMaxHeadsUV); key_len: [B] int32 (key j visible
+// iff j < max(key_len[b], 1)) or null; out: bf16, row of frame i of utterance
+// b at b * out_bs + (i - out_base) * D.  sched: two ints, zero before the
+// launch and left zero after it (the kernel's item counter); launches that
+// share them must not run concurrently.
+cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const uint32_t* uv_host,
+                                    const int32_t* key_len, AttnContextDev ctx,
                                     const AttnGeom& g, void* out, int B, int H, int* err,
-                                    int num_sms, cudaStream_t stream);
+                                    int* sched, int num_sms, cudaStream_t stream);
 
 // ---- generic CUDA-core attention (fp32 module dtype, any head_dim <= 128) ----
 // q [B,Tq,D] (row stride ldq), k/v [B,Tk,D] (row strides ldk, ldv), p

@@ -57,10 +57,17 @@ int report_error(int code, const char* msg);
 
 }  // namespace nrp
 
+// d_err[0]: the sticky device error code; then kSchedSlots pairs of ints,
+// the item counters of persistent kernels (each left zero by its launch;
+// consecutive launches take consecutive pairs).
+constexpr int kSchedSlots = 32;
+constexpr int kCtxInts = 2 + 2 * kSchedSlots;
+
 struct nrp_context {
   int device = 0;
   int num_sms = 148;
   int* d_err = nullptr;
+  uint32_t sched_seq = 0;
   bool prof = false;
   std::vector<nrp::ProfRec> recs;
   std::vector<cudaEvent_t> pool;
@@ -90,6 +97,7 @@ struct nrp_attn {
   int cache_drop = 0;
   nrp::Linear lin[5];
   std::vector<float> u, v;
+  std::vector<uint32_t> uv_packed;  // [H][128] bf16 pairs of the rounded u, v (AttnUV)
   bool dirty = true;
   // device parameters in the module dtype
   bool qkv_quant = false;
@@ -130,6 +138,11 @@ struct nrp_halo {
 };
 
 namespace nrp {
+// The counter pair of the next persistent-kernel launch on this context.
+inline int* sched_slot(nrp_context* c) {
+  return c->d_err + 2 + 2 * static_cast<int>(c->sched_seq++ % kSchedSlots);
+}
+
 // Queues on halo->stream, after the work queued so far on `st`: for side s
 // (0: rank - 1, 1: rank + 1; skipped when that rank does not exist or both
 // byte counts are 0) send send_bytes[s] bytes from buf + send_off[s] and

@@ -158,8 +158,8 @@ extern "C" int nrp_attn_forward_noalloc(nrp_attn* a, void* stream, const void* x
                 g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr, pbuf,
                 D);
     if (rc) return rc;
-    TRY_CUDA(nrp::launch_relpos_attn_bf16(qkv, pbuf, a->u_dev.as<float>(), a->v_dev.as<float>(),
-                                          lengths, cd, g, cbuf, B, a->H, ctx->d_err,
+    TRY_CUDA(nrp::launch_relpos_attn_bf16(qkv, pbuf, a->uv_packed.data(), lengths, cd, g, cbuf,
+                                          B, a->H, ctx->d_err, nrp::sched_slot(ctx),
                                           ctx->num_sms, st));
   } else {
     rc = linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,

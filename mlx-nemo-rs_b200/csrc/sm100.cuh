@@ -322,6 +322,13 @@ __device__ __forceinline__ void fma_f32x2v(float& x0, float& x1, float a0, float
       : "f"(a0), "f"(a1), "f"(m), "f"(c0), "f"(c1));
 }
 
+// Two bf16 sums in one instruction, each rounded once to nearest even.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // (c0, c1) += (a0 * b0, a1 * b1), one fused rounding each.
 __device__ __forceinline__ void fma2_acc(float& c0, float& c1, float a0, float a1, float b0,
                                          float b1) {
