@@ -210,7 +210,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap map_p,    // [p_rows][D] bf16
                        const __grid_constant__ AttnUV uv,            // q biases, bf16 pairs
                        const __grid_constant__ CUtensorMap map_out,  // [B][rows][D] bf16
-                       const __nv_bfloat16* __restrict__ qkv,        // the same buffer
                        const int32_t* __restrict__ key_len, AttnContextDev ctx, AttnGeom g,
                        __nv_bfloat16* __restrict__ out, int B, int H, int* err, int* sched) {
   // Dynamic shared memory starts 1024-byte aligned when, as here, the kernel
@@ -327,10 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(dst, &map_qkv, bar, vcol, it.j0 + t * kTile - g.base, it.b);
           tma_load_3d(dst + kHalf, &map_qkv, bar, vcol + 64, it.j0 + t * kTile - g.base, it.b);
         };
-        // Every MMA of the previous item has completed (its last s was waited
-        // below): the helpers may write the q+u/q+v tiles (they hold Q in
-        // registers already), and the first {K, P} stage may load.
-        mbar_arrive(&bars->q);
+        // Q and the first {K, P} stage: every MMA of the previous item that
+        // read those buffers has completed (its s was waited below)
+        mbar_arrive_expect_tx(&bars->q, kTileBytes);
+        tma_load_3d(sQu, &map_qkv, &bars->q, it.h * kDh, it.i0 - g.base, it.b);
+        tma_load_3d(sQu + kHalf, &map_qkv, &bars->q, it.h * kDh + 64, it.i0 - g.base, it.b);
         load_stage(0);
         // P chunk 0 is only read by the first BD MMA: staged in the V slot of
         // the item's first tile (its last reader, tile gt-2, has completed:
@@ -406,48 +406,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 9) {
     // ------------------------------------------------ helpers
-    // ---- q+u and q+v tiles (bf16 adds, attention.rs:506-508).  The three
-    // helper warps share the 128 x 2 (row, 64-column half) units: a thread
-    // keeps one half and up to 3 rows.  Each loads its rows of the item's Q
-    // into registers as soon as it knows the item, then waits until the
-    // issuer reports the q+u/q+v buffers free (every MMA of the previous item
-    // completed) and writes the two tiles; u and v are kernel parameters
-    // (bf16 pairs).
-    const int t3 = (warp - 9) * 32 + lane;
-    const int half = t3 & 1;
-    uint4 qr[3][8];
-    auto load_q = [&](int b, int h, int i0) {
+    // ---- q+u and q+v tiles of head h (bf16 adds, attention.rs:506-508),
+    // once the issuer has loaded the item's Q tile (every MMA of the
+    // previous item that read the q+v buffer completed before that load was
+    // issued).  The three helper warps share the 128 x 2 (row, 64-column
+    // half) units; a thread keeps one half, so its 32 u and 32 v pairs (the
+    // kernel parameters) are loaded once.
+    auto build_q_tiles = [&](int h) {
+      const int t3 = (warp - 9) * 32 + lane;
+      const int half = t3 & 1;
+      const uint32_t* uh = uv.w + h * 128 + half * 32;
+      uint32_t uw[32], vw[32];
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const int row = (t3 >> 1) + 16 * kHelperWarps * k;
-        const int fr = i0 + row - g.base;  // >= 0: tiles start at q_lo >= base
-        const bool in = row < kTile && fr < g.tbuf;
-        const __nv_bfloat16* src = qkv + static_cast<int64_t>(b) * g.qkv_bs +
-                                   static_cast<int64_t>(in ? fr : 0) * g.qkv_ts + h * kDh +
-                                   half * 64;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          qr[k][ch] = in ? __ldg(reinterpret_cast<const uint4*>(src + ch * 8))
-                         : make_uint4(0u, 0u, 0u, 0u);
+      for (int k = 0; k < 32; ++k) {
+        uw[k] = uh[k];
+        vw[k] = uh[64 + k];
       }
-    };
-    auto store_q_tiles = [&](int h) {
-      const int ub = h * 128 + half * 32;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const int row = (t3 >> 1) + 16 * kHelperWarps * k;
-        if (row >= kTile) break;
+#pragma unroll 1
+      for (int row = t3 >> 1; row < kTile; row += 16 * kHelperWarps) {
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
           const uint32_t off = half * kHalf + sw128_offset(row, ch);
-          const uint4 q = qr[k][ch];
-          const int w = ub + 4 * ch;
+          const uint4 q = *reinterpret_cast<const uint4*>(sQu + off);
           *reinterpret_cast<uint4*>(sQu + off) =
-              make_uint4(add_bf16x2(q.x, uv.w[w]), add_bf16x2(q.y, uv.w[w + 1]),
-                         add_bf16x2(q.z, uv.w[w + 2]), add_bf16x2(q.w, uv.w[w + 3]));
+              make_uint4(add_bf16x2(q.x, uw[4 * ch]), add_bf16x2(q.y, uw[4 * ch + 1]),
+                         add_bf16x2(q.z, uw[4 * ch + 2]), add_bf16x2(q.w, uw[4 * ch + 3]));
           *reinterpret_cast<uint4*>(sQv + off) =
-              make_uint4(add_bf16x2(q.x, uv.w[w + 64]), add_bf16x2(q.y, uv.w[w + 65]),
-                         add_bf16x2(q.z, uv.w[w + 66]), add_bf16x2(q.w, uv.w[w + 67]));
+              make_uint4(add_bf16x2(q.x, vw[4 * ch]), add_bf16x2(q.y, vw[4 * ch + 1]),
+                         add_bf16x2(q.z, vw[4 * ch + 2]), add_bf16x2(q.w, vw[4 * ch + 3]));
         }
       }
       fence_proxy_async_smem();
@@ -457,14 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t dc = 0, ic = 0;
       while (true) {
         if (!warp_wait(&bars->dfull[dc & 1], (dc >> 1) & 1, err, kDevTimeoutEpi)) break;
-        const int b = bars->desc[dc & 1][0], h = bars->desc[dc & 1][1];
-        const int i0 = bars->desc[dc & 1][2], nt = bars->desc[dc & 1][4];
+        const int h = bars->desc[dc & 1][1], nt = bars->desc[dc & 1][4];
         warp_arrive(&bars->dempty[dc & 1]);
         ++dc;
         if (nt < 0) break;
-        load_q(b, h, i0);
         const bool ok = warp_wait(&bars->q, ic & 1, err, kDevTimeoutLoad);
-        if (ok) store_q_tiles(h);
+        if (ok) build_q_tiles(h);
         warp_arrive(&bars->prep);
         ++ic;
         if (!ok) {
@@ -563,9 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ++pc;
       if (it.nt < 0) break;
-      load_q(it.b, it.h, it.i0);
       ok = warp_wait(&bars->q, ic & 1, err, kDevTimeoutLoad);
-      if (ok) store_q_tiles(it.h);
+      if (ok) build_q_tiles(it.h);
       warp_arrive(&bars->prep);
       ++ic;
       if (!ok) {
@@ -905,8 +888,8 @@ cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const uint32
   const int sms = num_sms > 0 ? num_sms : 148;
   const int grid = static_cast<int>(n_items < sms ? n_items : sms);  // one CTA per SM
   relpos_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      map_qkv, map_p, uv, map_out, static_cast<const __nv_bfloat16*>(qkv), key_len, ctx, g,
-      static_cast<__nv_bfloat16*>(out), B, H, err, sched);
+      map_qkv, map_p, uv, map_out, key_len, ctx, g, static_cast<__nv_bfloat16*>(out), B, H, err,
+      sched);
   return cudaGetLastError();
 }
 
