@@ -252,9 +252,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->ofree, 1);
     mbar_init(&bars->dfull[0], 1);
     mbar_init(&bars->dfull[1], 1);
-    // read by the issuer, the softmax warps and the helpers other than warp 9
-    mbar_init(&bars->dempty[0], 1 + kSoftmaxWarps + kHelperWarps - 1);
-    mbar_init(&bars->dempty[1], 1 + kSoftmaxWarps + kHelperWarps - 1);
+    // read by the issuer, the softmax warps and the helpers
+    mbar_init(&bars->dempty[0], 1 + kSoftmaxWarps + kHelperWarps);
+    mbar_init(&bars->dempty[1], 1 + kSoftmaxWarps + kHelperWarps);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -438,31 +438,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
     };
-    if (warp > 9) {
-      // warps 10-11: follow the descriptor ring, build their share
-      uint32_t dc = 0, ic = 0;
-      while (true) {
-        if (!warp_wait(&bars->dfull[dc & 1], (dc >> 1) & 1, err, kDevTimeoutEpi)) break;
-        const int h = bars->desc[dc & 1][1], nt = bars->desc[dc & 1][4];
-        warp_arrive(&bars->dempty[dc & 1]);
-        ++dc;
-        if (nt < 0) break;
-        const bool ok = warp_wait(&bars->q, ic & 1, err, kDevTimeoutLoad);
-        if (ok) build_q_tiles(h);
-        warp_arrive(&bars->prep);
-        ++ic;
-        if (!ok) {
-          *abort_flag = 1;
-          break;
-        }
-      }
-    } else {
-    // ---- warp 9: the scheduler, and its share of the q+u/q+v tiles
-    // Utterances by decreasing length (ties by index): the warp ranks them
-    // from one load of the lengths.
+    // ---- warp 9 is the scheduler.  Utterances by decreasing length (ties
+    // by index): the warp ranks them from one load of the lengths.
     uint8_t* order = smem + kOffOrder;
     const bool sorted = key_len && B <= kMaxSortedBatch;
-    if (sorted) {
+    if (warp == 9 && sorted) {
       constexpr int kPer = kMaxSortedBatch / 32;
       int len[kPer], rank[kPer];
 #pragma unroll
@@ -492,70 +472,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-    uint32_t pc = 0, ic = 0;
+    uint32_t pc = 0, ic = 0, dc = 0;
     bool ok = true;
     const int per_b = X * H;
     while (true) {
-      // the next item with keys; padding tiles are written as zeros here
-      Item it;
-      while (true) {
-        int qn = 0;
-        if (lane == 0) qn = atomicAdd(sched, 1);
-        qn = __shfl_sync(0xffffffffu, qn, 0);
-        if (qn >= n_items || !ok) {
-          it.nt = -1;
-          break;
-        }
-        const int ub = qn / per_b, rem = qn - ub * per_b;
-        it = make_item((sorted ? order[ub] : ub) * per_b + rem, X, H, key_len, ctx, g);
-        if (it.nt > 0) break;
-        const int rows = min(kTile, g.q_hi - it.i0);
-        __nv_bfloat16* ob = out + static_cast<size_t>(it.b) * g.out_bs + it.h * kDh;
-        for (int k = lane; k < rows * 16; k += 32) {
-          const int rr = k >> 4, c = k & 15;
-          *reinterpret_cast<uint4*>(ob + static_cast<size_t>(it.i0 + rr - g.out_base) * D +
-                                    c * 8) = make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
-      if (__any_sync(0xffffffffu, *abort_flag)) {
-        ok = false;
-        it.nt = -1;
-      }
-      // publish; the slot is free once the issuer and the softmax warps have
-      // read the item two back
-      const uint32_t slot = pc & 1;
-      if (pc >= 2 && !warp_wait(&bars->dempty[slot], ((pc >> 1) - 1) & 1, err, kDevTimeoutEpi)) {
-        ok = false;
-        it.nt = -1;
-      }
-      if (lane == 0) {
-        int* d = bars->desc[slot];
-        d[0] = it.b;
-        d[1] = it.h;
-        d[2] = it.i0;
-        d[3] = it.j0;
-        d[4] = it.nt;
-        d[5] = it.rbase;
-        d[6] = it.kend;
-        mbar_arrive(&bars->dfull[slot]);
-        if (it.nt > 0)  // its first Q, K and V tiles into L2
-          for (int half = 0; half < 2; ++half) {
-            tma_prefetch_3d(&map_qkv, it.h * kDh + 64 * half, it.i0 - g.base, it.b);
-            tma_prefetch_3d(&map_qkv, D + it.h * kDh + 64 * half, it.j0 - g.base, it.b);
-            tma_prefetch_3d(&map_qkv, 2 * D + it.h * kDh + 64 * half, it.j0 - g.base, it.b);
+      if (warp == 9) {
+        // the next item with keys; padding tiles are written as zeros here
+        Item it;
+        while (true) {
+          int qn = 0;
+          if (lane == 0) qn = atomicAdd(sched, 1);
+          qn = __shfl_sync(0xffffffffu, qn, 0);
+          if (qn >= n_items || !ok) {
+            it.nt = -1;
+            break;
           }
+          const int ub = qn / per_b, rem = qn - ub * per_b;
+          it = make_item((sorted ? order[ub] : ub) * per_b + rem, X, H, key_len, ctx, g);
+          if (it.nt > 0) break;
+          const int rows = min(kTile, g.q_hi - it.i0);
+          __nv_bfloat16* ob = out + static_cast<size_t>(it.b) * g.out_bs + it.h * kDh;
+          for (int k = lane; k < rows * 16; k += 32) {
+            const int rr = k >> 4, c = k & 15;
+            *reinterpret_cast<uint4*>(ob + static_cast<size_t>(it.i0 + rr - g.out_base) * D +
+                                      c * 8) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        if (__any_sync(0xffffffffu, *abort_flag)) {
+          ok = false;
+          it.nt = -1;
+        }
+        // publish; the slot is free once the issuer and the softmax warps have
+        // read the item two back
+        const uint32_t slot = pc & 1;
+        if (pc >= 2 && !warp_wait(&bars->dempty[slot], ((pc >> 1) - 1) & 1, err, kDevTimeoutEpi)) {
+          ok = false;
+          it.nt = -1;
+        }
+        if (lane == 0) {
+          int* d = bars->desc[slot];
+          d[0] = it.b;
+          d[1] = it.h;
+          d[2] = it.i0;
+          d[3] = it.j0;
+          d[4] = it.nt;
+          d[5] = it.rbase;
+          d[6] = it.kend;
+          mbar_arrive(&bars->dfull[slot]);
+          if (it.nt > 0)  // its first Q, K and V tiles into L2
+            for (int half = 0; half < 2; ++half) {
+              tma_prefetch_3d(&map_qkv, it.h * kDh + 64 * half, it.i0 - g.base, it.b);
+              tma_prefetch_3d(&map_qkv, D + it.h * kDh + 64 * half, it.j0 - g.base, it.b);
+              tma_prefetch_3d(&map_qkv, 2 * D + it.h * kDh + 64 * half, it.j0 - g.base, it.b);
+            }
+        }
+        ++pc;
       }
-      ++pc;
-      if (it.nt < 0) break;
+      // ---- every helper: the next item from the ring, then its share of
+      // the item's q+u/q+v tiles
+      if (!warp_wait(&bars->dfull[dc & 1], (dc >> 1) & 1, err, kDevTimeoutEpi)) break;
+      const int h = bars->desc[dc & 1][1], nt = bars->desc[dc & 1][4];
+      warp_arrive(&bars->dempty[dc & 1]);
+      ++dc;
+      if (nt < 0) break;
       ok = warp_wait(&bars->q, ic & 1, err, kDevTimeoutLoad);
-      if (ok) build_q_tiles(it.h);
+      if (ok) build_q_tiles(h);
       warp_arrive(&bars->prep);
       ++ic;
       if (!ok) {
         *abort_flag = 1;
         break;
       }
-    }
     }
   } else {
     // ------------------------------------------------- softmax threads
@@ -658,13 +645,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         warp_arrive(&bars->dempty[dc & 1]);
         ++dc;
       }
-      if (it.nt < 0) break;
-      if (__any_sync(0xffffffffu, *abort_flag)) { ok = false; break; }
-      if (pending) {
+      if (pending) {  // the previous item's output (also after the last item)
         epilogue();
         pending = false;
         if (!ok) break;
       }
+      if (it.nt < 0) break;
+      if (__any_sync(0xffffffffu, *abort_flag)) { ok = false; break; }
       // ---- the item's key tiles
       const int i = it.i0 + il;
       int rlo, rhi;
@@ -804,7 +791,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       gt += it.nt;
       ++ic;
     }
-    if (ok && pending) epilogue();
     if (!ok) *abort_flag = 1;
   }
 
