@@ -556,12 +556,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (log2 units), i.e. 8 / scale_log2 in raw score units
     const float rescale_raw = 8.f / scale_log2;
     const int shift = 31 - lane;
-    const bool s8 = shift & 8, s2 = shift & 2, s1 = shift & 1;
-    // the 16 and 4 stages select on the FMA pipe, the others on the ALU
-    // pipe, so the shift is split between the two: b * f + a * (1 - f) with
-    // f in {0, 1} is exact for finite values (up to the sign of a zero)
-    const float f16 = (shift & 16) ? 1.f : 0.f, n16 = 1.f - f16;
-    const float f4 = (shift & 4) ? 1.f : 0.f, n4 = 1.f - f4;
+    // the shift's stages are selects (a selection on the FMA pipe, b*f +
+    // a*(1-f), measured slower: the loop is instruction-fetch bound, and it
+    // doubles the instructions of a stage)
+    const bool s16 = shift & 16, s8 = shift & 8, s4 = shift & 4, s2 = shift & 2, s1 = shift & 1;
     float* xbuf = reinterpret_cast<float*>(smem + kOffX);  // [parity][half][row] exchange
     uint32_t xphase = 0, gt = 0, ic = 0, ec = 0, dc = 0;
     bool ok = true;
@@ -691,11 +689,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // a[e] <- a[shift + e]: barrel shift by the lane's skew
 #pragma unroll
-          for (int x = 0; x < 47; ++x) a[x] = __fmaf_rn(a[x + 16], f16, __fmul_rn(a[x], n16));
+          for (int x = 0; x < 47; ++x) a[x] = s16 ? a[x + 16] : a[x];
 #pragma unroll
           for (int x = 0; x < 39; ++x) a[x] = s8 ? a[x + 8] : a[x];
 #pragma unroll
-          for (int x = 0; x < 35; ++x) a[x] = __fmaf_rn(a[x + 4], f4, __fmul_rn(a[x], n4));
+          for (int x = 0; x < 35; ++x) a[x] = s4 ? a[x + 4] : a[x];
 #pragma unroll
           for (int x = 0; x < 33; ++x) a[x] = s2 ? a[x + 2] : a[x];
 #pragma unroll
