@@ -21,8 +21,8 @@
 // at offset 127-il: a per-lane skew, done in registers with a 5-stage
 // predicated barrel shift over a 64-column window.
 //
-// Biases.  The CTA's query tile is staged once and turned into two bf16
-// tiles, q+u (A operand of the content product) and q+v (A operand of the
+// Biases.  Each query tile is staged once and turned into two bf16 tiles,
+// q+u (A operand of the content product) and q+v (A operand of the
 // positional product) -- the same bf16 adds as the reference's
 // q_with_bias_u / q_with_bias_v (attention.rs:506-508).
 //
@@ -43,12 +43,19 @@
 // next {K, P} stage loads as soon as the tile's MMAs have read it and V is
 // loaded a tile ahead.
 //
-// Warps 0-7 (softmax): warp w owns TMEM lane quadrant w&3 (one query row
-// per thread) and key half w>>2 (64 keys); the two threads of a row swap
-// their row maxima through shared memory.  Warp 8: TMEM owner; its lane 0
-// issues every TMA load and MMA.  Online softmax in the log2 domain; the
+// Grid.  Persistent, one CTA per SM (relpos_attn_kernel below): the work
+// items (query tile, head, utterance) come from a counter the grid shares,
+// so SMs stay balanced, and each item's loads and first MMAs run under the
+// previous item's last tile.
+//
+// Softmax (warps 0-7): warp w owns TMEM lane quadrant w&3 (one query row per
+// thread) and key half w>>2 (64 keys); the two threads of a row swap their
+// row maxima through shared memory.  Online softmax in the log2 domain; the
 // output is rescaled only when a row maximum grows by more than 2^8 (exact:
 // the final normalisation uses the same maximum).  Every wait is bounded.
+//
+// The softmax tile loop is bound by instruction fetch as much as by its
+// pipes, so code size counts: each role's per-item work is inlined once.
 #include <math.h>
 
 #include <cstring>
