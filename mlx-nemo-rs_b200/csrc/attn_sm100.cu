@@ -315,7 +315,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&bars->dempty[dc & 1]);
           ++dc;
         }
-        if (it.nt < 0) break;
         const int kcol = D + it.h * kDh, vcol = 2 * D + it.h * kDh;
         auto load_stage = [&](int t) {  // K_t and P chunk t+1
           mbar_arrive_expect_tx(&bars->kp, kStageTx);
@@ -333,27 +332,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(dst, &map_qkv, bar, vcol, it.j0 + t * kTile - g.base, it.b);
           tma_load_3d(dst + kHalf, &map_qkv, bar, vcol + 64, it.j0 + t * kTile - g.base, it.b);
         };
-        // Q and the first {K, P} stage: every MMA of the previous item that
-        // read those buffers has completed (its s was waited below)
-        mbar_arrive_expect_tx(&bars->q, kTileBytes);
-        tma_load_3d(sQu, &map_qkv, &bars->q, it.h * kDh, it.i0 - g.base, it.b);
-        tma_load_3d(sQu + kHalf, &map_qkv, &bars->q, it.h * kDh + 64, it.i0 - g.base, it.b);
-        load_stage(0);
         // P chunk 0 is only read by the first BD MMA: staged in the V slot of
         // the item's first tile (its last reader, tile gt-2, has completed:
         // the s commit waited for item k-1 covers every earlier MMA), where
         // V_0 follows once BD_0 has completed
         uint8_t* p0buf = sV + (gt & 1) * kTileBytes;
-        mbar_arrive_expect_tx(&bars->p0, kTileBytes);
-        tma_load_2d(p0buf, &map_p, &bars->p0, it.h * kDh, it.rbase);
-        tma_load_2d(p0buf + kHalf, &map_p, &bars->p0, it.h * kDh + 64, it.rbase);
-        if (pending) {  // the previous item's last P.V
+        if (it.nt > 0) {
+          // Q and the first {K, P} stage: every MMA of the previous item that
+          // read those buffers has completed (its s was waited below)
+          mbar_arrive_expect_tx(&bars->q, kTileBytes);
+          tma_load_3d(sQu, &map_qkv, &bars->q, it.h * kDh, it.i0 - g.base, it.b);
+          tma_load_3d(sQu + kHalf, &map_qkv, &bars->q, it.h * kDh + 64, it.i0 - g.base, it.b);
+          load_stage(0);
+          mbar_arrive_expect_tx(&bars->p0, kTileBytes);
+          tma_load_2d(p0buf, &map_p, &bars->p0, it.h * kDh, it.rbase);
+          tma_load_2d(p0buf + kHalf, &map_p, &bars->p0, it.h * kDh + 64, it.rbase);
+        }
+        if (pending) {  // the previous item's last P.V (also after the last item)
           ok = mbar_wait(&bars->p, g_last & 1, err, kDevTimeoutEpi) &&
                mbar_wait(&bars->v[g_last & 1], (g_last >> 1) & 1, err, kDevTimeoutLoad);
           if (!ok) break;
           pv(g_last, acc_last);
           pending = false;
         }
+        if (it.nt < 0) break;
         // BD_0 once the q+u / q+v tiles are ready and the previous item's
         // last pass 1 released the S and BD columns
         ok = mbar_wait(&bars->prep, ic & 1, err, kDevTimeoutEpi) &&
@@ -403,11 +405,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_last = it.nt > 1;
         gt += it.nt;
         ++ic;
-      }
-      if (ok && pending) {  // P.V of the last tile
-        ok = mbar_wait(&bars->p, g_last & 1, err, kDevTimeoutEpi) &&
-             mbar_wait(&bars->v[g_last & 1], (g_last >> 1) & 1, err, kDevTimeoutLoad);
-        if (ok) pv(g_last, acc_last);
       }
       if (!ok) *abort_flag = 1;
     }
