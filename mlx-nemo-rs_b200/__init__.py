@@ -682,6 +682,23 @@ class ConformerEncoder:
         for i, layer in enumerate(self.layers):
             layer.load_weights(weights, f"encoder.layers.{i}", quant)
 
+    def load_checkpoint(self, path: str) -> Optional[QuantizationConfig]:
+        """Weights from a .nemo archive (NemoCheckpoint), a model directory
+        (SafetensorsLoader.from_directory) or one .safetensors file; the
+        convolution weights are brought to MLX's layout first.  Returns the
+        quantization config applied (None: standard linears)."""
+        from .checkpoint import NemoCheckpoint, SafetensorsLoader, load_safetensors_weights
+        quant = None
+        if os.path.isdir(path):
+            loader = SafetensorsLoader.from_directory(path)
+            weights, quant = loader.load_weights(), loader.quantization
+        elif path.endswith(".safetensors"):
+            weights = load_safetensors_weights(path)
+        else:
+            weights = NemoCheckpoint.open(path).load_weights()
+        self.load_weights(weights, quant)
+        return quant
+
     def forward_from_embeddings(self, x, lengths, context: Optional[AttentionContext] = None,
                                 out=None):
         """conformer.rs:694-722: returns ([B, D, T] bf16, lengths)."""
@@ -942,3 +959,9 @@ def qlinear(x, wq, scales, biases, bias=None, group_size=64, bits=8,
                              scales.data_ptr(), biases.data_ptr(), N, group_size, bits,
                              _ptr(bias), out.data_ptr()))
     return out
+
+
+# weight ingestion (safetensors, .nemo archives, model directories)
+from .checkpoint import (CheckpointError, NemoCheckpoint, SafetensorsLoader,  # noqa: E402
+                         WeightFormat, load_safetensors_weights, read_safetensors,
+                         read_safetensors_metadata, transform_weights_to_mlx, write_safetensors)

@@ -121,3 +121,50 @@ def test_encoder_forward_from_embeddings(nrp, orc):
         h = orc.block_forward(h, bw, pe, H, ff, K, lengths=lengths, bf16=True)
     err = rel_err(got, h, lengths)
     assert err < TOL_BF16, err
+
+
+@pytest.mark.parametrize("form", ["mlx_dir", "nemo"])
+def test_encoder_from_checkpoint_equals_dict(nrp, orc, tmp_path, form):
+    """ConformerEncoder.load_checkpoint (weights.rs, checkpoint.rs): an MLX
+    8-bit model directory, or a .nemo archive with PyTorch-layout float
+    weights, gives the same bits as loading the same arrays from a dict."""
+    import json
+    import tarfile
+    import torch
+    from test_checkpoint import _pytorch_layout
+    rng = np.random.default_rng(11)
+    B, T, D, H, ff, K, L = 2, 140, 256, 2, 1024, 9, 2
+    quant = form == "mlx_dir"
+    wd = {}
+    for i in range(L):
+        _, w = rand_block(rng, D, H, ff, K, quant=quant, orc=orc, prefix=f"encoder.layers.{i}")
+        wd.update(w)
+    wd = {k: np.asarray(v) for k, v in wd.items()}
+    if form == "mlx_dir":
+        path = tmp_path / "model"
+        path.mkdir()
+        nrp.write_safetensors(str(path / "model.safetensors"), wd, metadata={"format": "mlx"})
+        (path / "config.json").write_text(json.dumps({"quantization": {"bits": 8,
+                                                                       "group_size": 64}}))
+    else:
+        st = tmp_path / "w.safetensors"
+        nrp.write_safetensors(str(st), _pytorch_layout(wd))
+        path = tmp_path / "m.nemo"
+        with tarfile.open(path, "w") as tar:
+            tar.add(str(st), arcname="model_weights.safetensors")
+            cfg = tmp_path / "model_config.yaml"
+            cfg.write_text("encoder: {}\n")
+            tar.add(str(cfg), arcname="model_config.yaml")
+    a = nrp.ConformerEncoder(L, D, H, ff, K)
+    a.load_weights(wd, nrp.QuantizationConfig(8, 64) if quant else None)
+    b = nrp.ConformerEncoder(L, D, H, ff, K)
+    q = b.load_checkpoint(str(path))
+    assert (q is not None) == quant
+    a.set_dtype(nrp.BF16)
+    b.set_dtype(nrp.BF16)
+    x = torch.from_numpy(rng.standard_normal((B, T, D)).astype(np.float32)).cuda().bfloat16()
+    lengths = np.array([140, 77], np.int32)
+    ya, _ = a.forward_from_embeddings(x, lengths)
+    yb, _ = b.forward_from_embeddings(x, lengths)
+    a.ctx.check()
+    assert torch.equal(ya, yb)
