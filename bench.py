@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -475,13 +476,16 @@ SGL_WORKLOAD = ("BASELINE config 0: one rel-pos MHA layer, fp32, B=1 T=125 d_mod
 
 
 def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, workload,
-             config, scaling, e2e, dtype, cpu=None, hbm_bytes=None, reset=None):
+             config, scaling, e2e, dtype, cpu=None, hbm_bytes=None, reset=None,
+             prof_step=None):
     """Common timing for the secondary workloads: W warm-up steps, K steps
     timed with CUDA events (L2 flushed between steps, outside the events),
     max over ranks; per-kernel device time from the library's events over K
     more steps; e2e = (h2d(slot), compute(slot), d2h(slot), bytes in, bytes
     out) run for K steps by run_pipelined (host copies inside); one JSON
-    line.  flops / hbm_bytes: per step, per kernel kind (algorithmic)."""
+    line.  flops / hbm_bytes: per step, per kernel kind (algorithmic).
+    prof_step: the same step run without CUDA graphs, for the pass that times
+    each launch (a graph replay runs no host code to record its events)."""
     import torch
     import torch.distributed as dist
     dev = torch.device("cuda", local)
@@ -525,7 +529,7 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
     ctx.profile_reset()
     for k in range(args.steps):
         flush.zero_()
-        step(k)
+        (prof_step or step)(k)
     torch.cuda.synchronize()
     prof = ctx.profile_read()
     ctx.profile(False)
@@ -732,7 +736,8 @@ def main_encoder(args):
 
 def main_stream(args):
     """Config 2: one chunk of 14 frames for 64 sessions through 24 layers of
-    forward_with_cache; weak scaling (each rank its own 64 sessions)."""
+    forward_with_cache, each chunk step replayed as a CUDA graph (one per fill
+    level and ring position); weak scaling (each rank its own 64 sessions)."""
     import torch
     import torch.distributed as dist
     from __graft_entry__ import load_package
@@ -759,6 +764,10 @@ def main_stream(args):
     xs = [torch.from_numpy(rng.standard_normal((STR_SESS, STR_CHUNK, D), dtype=np.float32))
           .to(dev, torch.bfloat16) for _ in range(4)]
     bufs = [torch.empty_like(xs[0]) for _ in range(2)]
+    # fixed input/output buffers per slot: the chunk step runs as CUDA graphs
+    # (StreamingStepGraphs), whose launches read and write fixed addresses
+    xin = [torch.empty_like(xs[0]) for _ in range(2)]
+    outs = [torch.empty_like(xs[0]) for _ in range(2)]
     state = {"chunk": 0}
 
     def reset():
@@ -766,27 +775,43 @@ def main_stream(args):
             c.reset()
         state["chunk"] = 0
 
-    def step(k, xin=None, out_last=None):
+    def layers_step(filled, slot):
+        h = xin[slot]
+        for i, a in enumerate(layers):
+            o = outs[slot] if i == len(layers) - 1 else bufs[i & 1]
+            a.forward_with_cache(h, pos, caches[i], filled, STR_CHUNK, actx, out=o)
+            h = o
+
+    graphs = nrp.StreamingStepGraphs(layers_step, caches)
+
+    def step(k, slot=None, eager=False):
         c = state["chunk"]
         if c == STR_CHUNKS:
             reset()
             c = 0
-        filled = min(c * STR_CHUNK, STR_CACHE)
-        h = xin if xin is not None else xs[k % len(xs)]
-        for i, a in enumerate(layers):
-            o = out_last if (out_last is not None and i == len(layers) - 1) else bufs[i & 1]
-            a.forward_with_cache(h, pos, caches[i], filled, STR_CHUNK, actx, out=o)
-            h = o
+        if slot is None:  # device-timed steps: the chunk comes from device memory
+            slot = 0
+            xin[0].copy_(xs[k % len(xs)], non_blocking=True)
+        (layers_step if eager else graphs)(min(c * STR_CHUNK, STR_CACHE), slot)
         state["chunk"] = c + 1
-        return h
+        return outs[slot]
+
+    # capture every (fill level, ring position, slot) graph before anything is
+    # timed: each key's first step runs eagerly, its second is captured
+    period = STR_CACHE // math.gcd(STR_CACHE, STR_CHUNK)
+    for slot in (0, 1):
+        for _ in range(2):
+            reset()
+            for k in range(STR_CACHE // STR_CHUNK + 1 + period):
+                step(k, slot)
+    torch.cuda.synchronize()
+    reset()
 
     x_host = torch.empty((STR_SESS, STR_CHUNK, D), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(xs[0].cpu())
     out_host = torch.empty_like(x_host).pin_memory()
-    xin = [torch.empty_like(xs[0]) for _ in range(2)]
-    outs = [torch.empty_like(xs[0]) for _ in range(2)]
     e2e = (lambda slot: xin[slot].copy_(x_host, non_blocking=True),
-           lambda slot: step(0, xin[slot], outs[slot]),
+           lambda slot: step(0, slot),
            lambda slot: out_host.copy_(outs[slot], non_blocking=True),
            x_host.numel() * 2, out_host.numel() * 2)
 
@@ -804,7 +829,7 @@ def main_stream(args):
               "layers": STR_LAYERS,
               "parallelism": f"session-parallel replicas x{world}"},
              "weak", e2e, "bf16", hbm_bytes=hbm,
-             reset=reset)
+             reset=reset, prof_step=lambda k: step(k, eager=True))
     if world > 1:
         dist.destroy_process_group()
     return 0

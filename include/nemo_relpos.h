@@ -206,6 +206,13 @@ int nrp_cache_create(nrp_attn* attn, int batch, int cache_len, nrp_cache** out);
 int nrp_cache_destroy(nrp_cache* cache);
 /* Zero the cache (EncoderCache::new state). */
 int nrp_cache_reset(nrp_cache* cache, void* stream);
+/* The ring slot of the oldest cached frame (host state, advanced by every
+ * nrp_attn_forward_with_cache).  A caller that replays the device work of a
+ * forward_with_cache call (a captured CUDA graph) without running the call
+ * sets it to the value that call left.  No counterpart in the reference,
+ * whose cache is a tensor that is rebuilt every chunk. */
+int nrp_cache_get_head(const nrp_cache* cache, int* head);
+int nrp_cache_set_head(nrp_cache* cache, int head);
 /* Copy in / out the cache in EncoderCache.last_channel order (oldest frame
  * first): device f32 [batch, cache_len, d_model].  Import re-projects K/V
  * with the module's current weights. */

@@ -105,6 +105,8 @@ def lib():
             "nrp_cache_create": ([vp, i, i, vp], i),
             "nrp_cache_destroy": ([vp], i),
             "nrp_cache_reset": ([vp, vp], i),
+            "nrp_cache_get_head": ([vp, vp], i),
+            "nrp_cache_set_head": ([vp, i], i),
             "nrp_cache_import_h": ([vp, vp, vp], i),
             "nrp_cache_export_h": ([vp, vp, vp], i),
             "nrp_attn_forward_with_cache": ([vp, vp, vp, i, i, vp, vp, i, i, vp, vp], i),
@@ -832,6 +834,17 @@ class AttentionCache:
     def reset(self):
         _check(lib().nrp_cache_reset(self.handle, _stream()))
 
+    @property
+    def head(self) -> int:
+        """Ring slot of the oldest cached frame (host state)."""
+        h = C.c_int()
+        _check(lib().nrp_cache_get_head(self.handle, C.byref(h)))
+        return h.value
+
+    @head.setter
+    def head(self, value: int):
+        _check(lib().nrp_cache_set_head(self.handle, int(value)))
+
     def export_h(self):
         import torch
         out = torch.empty((self.batch, self.cache_len, self.attn.d_model), dtype=torch.float32,
@@ -842,6 +855,52 @@ class AttentionCache:
     def import_h(self, h):
         h = h.float().contiguous().cuda()
         _check(lib().nrp_cache_import_h(self.handle, h.data_ptr(), _stream()))
+
+
+class StreamingStepGraphs:
+    """A streaming chunk step replayed as CUDA graphs, with no host work per
+    layer (the sync-free driver the reference's forward_streaming lacks:
+    conformer.rs:840-1047 rebuilds masks and caches on the host every chunk).
+
+    `step(filled, *args)` enqueues one chunk of work on the current stream: calls of
+    `forward_with_cache` on the `caches`, reading and writing device buffers
+    that stay the same from chunk to chunk (the caller copies each new chunk
+    into the step's input buffer; `args`, hashable, may pick among several
+    such buffers).  The launches of a step depend on the fill level and on
+    each cache's ring slot, so a graph is kept per (filled, ring slots, args)
+    key: once the cache is full the slots cycle with
+    period cache_len / gcd(cache_len, frames appended per chunk), so a few
+    graphs serve a whole stream.  The first step with a key runs as it is
+    (sizing every workspace), the second is captured and replayed, later ones
+    are replayed.  Capturing runs the calls' host logic without their device
+    work, so the ring slots that logic leaves are restored after each replay.
+    """
+
+    def __init__(self, step, caches):
+        self.step = step
+        self.caches = list(caches)
+        self.graphs = {}   # key -> (graph, ring slots after the step)
+        self.seen = set()
+
+    def __call__(self, filled: int, *args):
+        import torch
+        key = (int(filled), tuple(c.head for c in self.caches), args)
+        if key in self.graphs:
+            g, after = self.graphs[key]
+            g.replay()
+        elif key in self.seen:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.step(filled, *args)
+            after = tuple(c.head for c in self.caches)
+            self.graphs[key] = (g, after)
+            g.replay()
+        else:
+            self.seen.add(key)
+            self.step(filled, *args)
+            return
+        for c, h in zip(self.caches, after):
+            c.head = h
 
 
 class EncoderCache:

@@ -952,6 +952,19 @@ int nrp_cache_reset(nrp_cache* c, void* stream) {
   return ok();
 }
 
+int nrp_cache_get_head(const nrp_cache* c, int* head) {
+  if (!c || !head) return fail(NRP_ERR_INVALID, "null argument");
+  *head = c->head;
+  return ok();
+}
+
+int nrp_cache_set_head(nrp_cache* c, int head) {
+  if (!c) return fail(NRP_ERR_INVALID, "null cache");
+  if (head < 0 || head >= c->C) return fail(NRP_ERR_INVALID, "ring slot %d of %d", head, c->C);
+  c->head = head;
+  return ok();
+}
+
 int nrp_cache_export_h(nrp_cache* c, float* h, void* stream) {
   if (!c || !h) return fail(NRP_ERR_INVALID, "null argument");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
