@@ -274,6 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort;
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 8) {
     // ------------------------------------------------ TMA + MMA issuer
@@ -875,10 +877,9 @@ cudaError_t launch_relpos_attn_bf16(const void* qkv, const void* p, const uint32
   if (n_items > INT32_MAX) return cudaErrorInvalidValue;
   const int sms = num_sms > 0 ? num_sms : 148;
   const int grid = static_cast<int>(n_items < sms ? n_items : sms);  // one CTA per SM
-  relpos_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      map_qkv, map_p, uv, map_out, key_len, ctx, g, static_cast<__nv_bfloat16*>(out), B, H, err,
-      sched);
-  return cudaGetLastError();
+  return launch_pdl(relpos_attn_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, map_qkv,
+                    map_p, uv, map_out, key_len, ctx, g, static_cast<__nv_bfloat16*>(out), B, H,
+                    err, sched);
 }
 
 }  // namespace nrp

@@ -131,6 +131,8 @@ __global__ void __launch_bounds__(kThreads)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int i0 = blockIdx.x * kQ, h = blockIdx.y, b = blockIdx.z;
+  pdl_launch_dependents();
+  pdl_wait();
   const int col = h * kDh;
   const int64_t ld3 = 3ll * D;
   const int r0 = T - kQ - i0;  // global P row of window row 0
@@ -324,10 +326,9 @@ cudaError_t launch_relpos_attn_stream_mma(const __nv_bfloat16* qkv, const __nv_b
   static std::atomic<uint64_t> attr{0};
   if (cudaError_t e = smem_attr_once(stream_attn_kernel, 227 * 1024, attr)) return e;
   const dim3 grid(nq, H, B);
-  stream_attn_kernel<<<grid, kThreads, smem, stream>>>(
-      qkv, kc, vc, const_cast<__nv_bfloat16*>(kc), const_cast<__nv_bfloat16*>(vc), hc, x, C, head,
-      n_app, src0, p, u, v, sm, out, T, D);
-  return cudaGetLastError();
+  return launch_pdl(stream_attn_kernel, grid, dim3(kThreads), smem, stream, qkv, kc, vc,
+                    const_cast<__nv_bfloat16*>(kc), const_cast<__nv_bfloat16*>(vc), hc, x, C, head,
+                    n_app, src0, p, u, v, sm, out, T, D);
 }
 
 }  // namespace nrp

@@ -40,7 +40,9 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* x,
                                                         int act_silu) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  pdl_launch_dependents();
   if (row >= rows) return;
+  pdl_wait();
   constexpr int D = 256 * kChunks;
   const __nv_bfloat16* xr = x + row * D;
   float v[kChunks][8];
@@ -109,7 +111,9 @@ __global__ void __launch_bounds__(kDwWarps * 32, 2)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c0 = blockIdx.y * 128 + lane * 4;
   const int t0 = (blockIdx.x * kDwWarps + warp) * kDwF;
+  pdl_launch_dependents();
   if (t0 >= T) return;  // warp-uniform
+  pdl_wait();
   const int64_t boff = static_cast<int64_t>(blockIdx.z) * T * D + c0;
   const __nv_bfloat16* xb = x + boff;
   uint2 raw[kRows];
@@ -194,6 +198,8 @@ __global__ void __launch_bounds__(256) dwconv_smem_kernel(const __nv_bfloat16* _
   const int t0 = blockIdx.x * kTT;
   const int rows = kTT + K - 1;
   const int vecs = D / 8;
+  pdl_launch_dependents();
+  pdl_wait();
   const __nv_bfloat16* xb = x + static_cast<int64_t>(b) * T * D;
   for (int i = threadIdx.x; i < rows * vecs; i += blockDim.x) {
     const int r = i / vecs, cv = i - r * vecs;
@@ -246,6 +252,8 @@ __global__ void __launch_bounds__(256) dwconv_smem_kernel(const __nv_bfloat16* _
 }
 
 __global__ void scale_kernel(__nv_bfloat16* x, int64_t n8, float s) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float f[8];
@@ -260,6 +268,8 @@ __global__ void scale_kernel(__nv_bfloat16* x, int64_t n8, float s) {
 __global__ void transpose_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                  int T, int D) {
   __shared__ __nv_bfloat16 tile[32][33];
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.z;
   const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
   const __nv_bfloat16* xb = x + static_cast<int64_t>(b) * T * D;
@@ -284,17 +294,17 @@ cudaError_t launch_layernorm(const __nv_bfloat16* x, const float* gamma, const f
   const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
   switch (D) {
     case 256:
-      layernorm_kernel<1><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
-      break;
+      return launch_pdl(layernorm_kernel<1>, grid, dim3(256), 0, stream, x, gamma, beta, y, rows,
+                        eps, act_silu);
     case 512:
-      layernorm_kernel<2><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
-      break;
+      return launch_pdl(layernorm_kernel<2>, grid, dim3(256), 0, stream, x, gamma, beta, y, rows,
+                        eps, act_silu);
     case 1024:
-      layernorm_kernel<4><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
-      break;
+      return launch_pdl(layernorm_kernel<4>, grid, dim3(256), 0, stream, x, gamma, beta, y, rows,
+                        eps, act_silu);
     case 2048:
-      layernorm_kernel<8><<<grid, 256, 0, stream>>>(x, gamma, beta, y, rows, eps, act_silu);
-      break;
+      return launch_pdl(layernorm_kernel<8>, grid, dim3(256), 0, stream, x, gamma, beta, y, rows,
+                        eps, act_silu);
     default:
       return cudaErrorInvalidValue;
   }
@@ -310,9 +320,8 @@ cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* wt, const float* 
   if (K == 9 && D % 128 == 0) {  // FastConformer's kernel size
     const int frames = kDwF * kDwWarps;
     const dim3 grid((T + frames - 1) / frames, D / 128, B);
-    dwconv_rows_kernel<9><<<grid, kDwWarps * 32, 0, stream>>>(x, wt, bias, bn_scale, bn_shift, y,
-                                                              T, D, pad, act_silu);
-    return cudaGetLastError();
+    return launch_pdl(dwconv_rows_kernel<9>, grid, dim3(kDwWarps * 32), 0, stream, x, wt, bias,
+                      bn_scale, bn_shift, y, T, D, pad, static_cast<int>(act_silu));
   }
   const size_t smem = static_cast<size_t>(kTT + K - 1) * D * 2 + static_cast<size_t>(K) * D * 4;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -321,15 +330,15 @@ cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* wt, const float* 
     if (cudaError_t e = smem_attr_once(dwconv_smem_kernel, 227 * 1024, attr)) return e;
   const dim3 grid((T + kTT - 1) / kTT, B);
   const int threads = D / 8 < 256 ? D / 8 : 256;
-  dwconv_smem_kernel<<<grid, threads, smem, stream>>>(x, wt, bias, bn_scale, bn_shift, y, T, D, K,
-                                                      pad, act_silu);
+  return launch_pdl(dwconv_smem_kernel, grid, dim3(threads), smem, stream, x, wt, bias, bn_scale,
+                    bn_shift, y, T, D, K, pad, static_cast<int>(act_silu));
   return cudaGetLastError();
 }
 
 cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   if (n % 8 != 0) return cudaErrorInvalidValue;
-  scale_kernel<<<592, 256, 0, stream>>>(x, n / 8, s);
+  return launch_pdl(scale_kernel, dim3(592), dim3(256), 0, stream, x, n / 8, s);
   return cudaGetLastError();
 }
 
@@ -338,7 +347,7 @@ cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B
   if (B <= 0 || T <= 0) return cudaSuccess;
   if (B > 65535) return cudaErrorInvalidValue;
   const dim3 grid((T + 31) / 32, (D + 31) / 32, B);
-  transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(x, y, T, D);
+  return launch_pdl(transpose_kernel, grid, dim3(32, 8), 0, stream, x, y, T, D);
   return cudaGetLastError();
 }
 

@@ -10,6 +10,25 @@
 
 namespace nrp {
 
+// Launches `kernel` with programmatic stream serialization: it may start
+// while the previous kernel in the stream finishes, and waits for that
+// kernel's grid (pdl_wait) before touching memory.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Raises a kernel's dynamic shared-memory limit once per device (function
 // attributes belong to each device's context; `done` holds one bit per
 // device ordinal).

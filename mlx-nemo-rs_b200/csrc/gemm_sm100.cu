@@ -187,6 +187,8 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   tc_fence_after();
   const uint32_t tmem = ss->tmem_base;
   volatile int* abort_flag = &ss->abort;
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
@@ -514,9 +516,9 @@ cudaError_t launch_tn(const CUtensorMap& map_x, const void* w, const uint8_t* wq
   if (!make_y_map(&map_y, y, ldy, M, ep.mode == kEpiGlu ? N / 2 : N, rt))
     return cudaErrorInvalidValue;
   const int grid = grid_size(M, N, kBN, rt, num_sms);
-  gemm_tn_kernel<kQuant, kBN><<<grid, kQuant ? 320 : 192, kSmem, stream>>>(
-      map_x, map_w, map_y, wq, qs, qb, bias, M, N, K, rt, ep, err);
-  return cudaGetLastError();
+  return launch_pdl(gemm_tn_kernel<kQuant, kBN>, dim3(grid), dim3(kQuant ? 320 : 192),
+                    static_cast<size_t>(kSmem), stream, map_x, map_w, map_y, wq, qs, qb, bias, M,
+                    N, K, rt, ep, err);
 }
 }  // namespace
 

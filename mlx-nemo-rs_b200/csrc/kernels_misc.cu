@@ -207,6 +207,8 @@ namespace {
 // group, MLX affine) into bf16 in one launch: the jobs' 16-weight units are
 // numbered consecutively and the grid strides over all of them.
 __global__ void dequant_q8_kernel(const __grid_constant__ DeqBatch jobs) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = jobs.begin16[jobs.n];
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -251,8 +253,7 @@ cudaError_t launch_dequant_q8_batch(const DeqJob* jobs, int n, int num_sms, cuda
   }
   const int64_t want = (b.begin16[n] + 255) / 256;
   const int grid = static_cast<int>(want < num_sms * 8 ? want : num_sms * 8);
-  dequant_q8_kernel<<<grid, 256, 0, stream>>>(b);
-  return cudaGetLastError();
+  return launch_pdl(dequant_q8_kernel, dim3(grid), dim3(256), 0, stream, b);
 }
 
 cudaError_t launch_dequant_q8(const uint8_t* wq, const __nv_bfloat16* qs, const __nv_bfloat16* qb,

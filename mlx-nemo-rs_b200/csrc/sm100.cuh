@@ -136,6 +136,17 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, 
                : "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel in
+// the stream (launched with programmatic stream serialization) start its
+// launch and set-up on SMs this grid frees; wait blocks until the previous
+// kernel's grid has completed and its memory is visible.  A kernel calls both
+// after its set-up and before its first global load or store.  Without the
+// launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Barrier `id` (1..15) over the first `threads` threads of the CTA.
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
