@@ -361,6 +361,7 @@ int nrp_block_forward(nrp_block* block, void* stream, const void* x, int batch, 
  * table of RelPositionalEncoding(d_model, max_len) for seq_len, every block,
  * then the transpose to [batch, d_model, seq_len]. */
 typedef struct nrp_encoder nrp_encoder;
+typedef struct nrp_subsampling nrp_subsampling; /* (below) */
 int nrp_encoder_create(nrp_context* ctx, int n_layers, int d_model, int n_heads, int ff_dim,
                        int conv_kernel, int causal_conv, int conv_norm, int use_bias,
                        int xscaling, int max_len, nrp_encoder** out);
@@ -372,6 +373,67 @@ int nrp_encoder_set_dtype(nrp_encoder* enc, int dtype);
 int nrp_encoder_forward_from_embeddings(nrp_encoder* enc, void* stream, const void* x, int batch,
                                         int seq_len, const int32_t* lengths,
                                         const nrp_att_context* context, void* out);
+/* The encoder's pre_encode (ConformerEncoder::new, conformer.rs:381-420):
+ * creates the subsampling the encoder owns and runs in nrp_encoder_forward;
+ * *sub is borrowed (load its weights with nrp_subsampling_load_*). */
+int nrp_encoder_add_subsampling(nrp_encoder* enc, int feat_in, int subsampling_factor,
+                                int conv_channels, int causal_downsampling,
+                                nrp_subsampling** sub);
+/* ConformerEncoder::forward (475-560): features device f32 [batch, feat_in,
+ * frames]; lengths host int32 [batch] mel frames, or NULL (all frames):
+ * frames past a length are zeroed, the subsampling, x * xscale, the blocks
+ * with the subsampled lengths, the transpose.  out device [batch, d_model,
+ * T'] bf16 (T' = nrp_subsampling_output_length(frames)); out_lengths host
+ * int32 [batch] (Subsampling::output_lengths, 1387-1411) or NULL. */
+int nrp_encoder_forward(nrp_encoder* enc, void* stream, const float* features, int batch,
+                        int frames, const int32_t* lengths, const nrp_att_context* context,
+                        void* out, int32_t* out_lengths);
+
+/* ------------------------------------------ dw_striding subsampling */
+/* Subsampling (src/asr/modules/encoders/conformer.rs:1058-1588), the
+ * encoder's pre_encode: mel frames [batch, frames, feat_in] -> NHWC
+ * [.., 1]; conv.0 (1 -> C, 3x3, stride 2) + ReLU; per further stride a
+ * depthwise 3x3 stride-2 conv (groups C), a pointwise 1x1 conv and ReLU;
+ * [B, T', F', C] flattened channel-major ([B, T', C * F']) into the `out`
+ * linear -> [batch, T', d_model].  strides = log2(subsampling_factor) for
+ * 2, 4, 8 (any other factor: 2, as Subsampling::new).  Non-causal convs pad
+ * 1 on both sides; causal_downsampling pads (2, 1) on time and frequency
+ * (causal_pad_2d, 66-80).  Runs in bf16; conv_channels a power of two in
+ * [64, 2048], d_model % 32 == 0. */
+typedef enum {
+  NRP_FEATURES_BFT = 0, /* [batch, feat_in, frames] (ConformerEncoder::forward's input) */
+  NRP_FEATURES_BTF = 1  /* [batch, frames, feat_in] (forward_subsampling_only's) */
+} nrp_features_layout;
+/* Subsampling::new (1111-1205).  ctx may be NULL for a handle that only
+ * answers sizes (feat_out, output_length); its forward then fails. */
+int nrp_subsampling_create(nrp_context* ctx, int feat_in, int d_model, int subsampling_factor,
+                           int conv_channels, int causal_downsampling, nrp_subsampling** out);
+int nrp_subsampling_destroy(nrp_subsampling* sub);
+int nrp_subsampling_set_dtype(nrp_subsampling* sub, int dtype);
+/* compute_freq_output_size (1220-1244): F', so `out` has C * F' inputs. */
+int nrp_subsampling_feat_out(const nrp_subsampling* sub, int* feat_out);
+/* Subsampling::output_length (1315-1327): frames after the conv stack (also
+ * the time size of the forward's output for an input of `frames`). */
+int nrp_subsampling_output_length(const nrp_subsampling* sub, int frames, int* out_frames);
+/* load_conv2d (src/core/loading.rs:227-232) for pre_encode.conv.{index}
+ * (Subsampling::load_weights, 1557-1588): 0 = conv.0 [C, 3, 3, 1]; 2 + 3i =
+ * depthwise i [C, 3, 3, 1]; 3 + 3i = pointwise i [C, 1, 1, C]; host f32 in
+ * MLX's layout; bias [C] or NULL (zeros). */
+int nrp_subsampling_load_conv(nrp_subsampling* sub, int index, const float* weight,
+                              const float* bias);
+/* Weights::fetch_linear for pre_encode.out: weight [d_model, C * F'] in the
+ * reference's (channel, frequency) column order, bias [d_model] or NULL;
+ * quantised: as nrp_attn_load_linear_quantized. */
+int nrp_subsampling_load_out(nrp_subsampling* sub, const float* weight, const float* bias);
+int nrp_subsampling_load_out_quantized(nrp_subsampling* sub, int bits, int group_size,
+                                       const uint32_t* wq, const float* scales,
+                                       const float* biases, const float* bias);
+/* Subsampling::forward_frames (1413-1555): features device f32 in `layout`;
+ * lengths device int32 [batch] or NULL: frames t >= lengths[b] read as zero
+ * (ConformerEncoder::forward's mel mask, 484-518); out device
+ * [batch, T', d_model] bf16, T' = nrp_subsampling_output_length(frames). */
+int nrp_subsampling_forward(nrp_subsampling* sub, void* stream, const float* features, int layout,
+                            int batch, int frames, const int32_t* lengths, void* out);
 
 /* --------------------------------------------------- linear primitives */
 /* LinearLayer::forward, Standard arm (quantization.rs:128-135) on device
@@ -406,7 +468,8 @@ typedef enum {
   NRP_KERNEL_DWCONV = 9,      /* depthwise conv + BatchNorm + SiLU */
   NRP_KERNEL_ELEMENTWISE = 10, /* input scaling, transposes, copies */
   NRP_KERNEL_DEQUANT = 11,    /* 8-bit weights to bf16 (large-M quantised GEMM) */
-  NRP_KERNEL_KINDS = 12
+  NRP_KERNEL_SUBSAMPLE = 12,  /* the subsampling's direct (non-GEMM) convolutions */
+  NRP_KERNEL_KINDS = 13
 } nrp_kernel_kind;
 int nrp_profile_enable(nrp_context* ctx, int enable);
 int nrp_profile_reset(nrp_context* ctx);

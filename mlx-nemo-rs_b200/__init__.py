@@ -134,6 +134,17 @@ def lib():
             "nrp_encoder_block": ([vp, i, vp], i),
             "nrp_encoder_set_dtype": ([vp, i], i),
             "nrp_encoder_forward_from_embeddings": ([vp, vp, vp, i, i, vp, vp, vp], i),
+            "nrp_encoder_add_subsampling": ([vp, i, i, i, i, vp], i),
+            "nrp_encoder_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
+            "nrp_subsampling_create": ([vp, i, i, i, i, i, vp], i),
+            "nrp_subsampling_destroy": ([vp], i),
+            "nrp_subsampling_set_dtype": ([vp, i], i),
+            "nrp_subsampling_feat_out": ([vp, vp], i),
+            "nrp_subsampling_output_length": ([vp, i, vp], i),
+            "nrp_subsampling_load_conv": ([vp, i, vp, vp], i),
+            "nrp_subsampling_load_out": ([vp, vp, vp], i),
+            "nrp_subsampling_load_out_quantized": ([vp, i, i, vp, vp, vp, vp], i),
+            "nrp_subsampling_forward": ([vp, vp, vp, i, i, i, vp, vp], i),
             "nrp_profile_enable": ([vp, i], i),
             "nrp_profile_reset": ([vp], i),
             "nrp_profile_read": ([vp, i, vp, vp], i),
@@ -196,7 +207,8 @@ class Context:
         _check(lib().nrp_context_check(self.handle, stream if stream is not None else _stream()))
 
     KERNELS = ("gemm_bf16", "gemm_q8", "qgemv", "gemm_f32", "attn_sm100", "attn_simt",
-               "attn_stream", "ring_append", "layernorm", "dwconv", "elementwise", "dequant")
+               "attn_stream", "ring_append", "layernorm", "dwconv", "elementwise", "dequant",
+               "subsample")
 
     def profile(self, enable: bool = True):
         _check(lib().nrp_profile_enable(self.handle, int(enable)))
@@ -644,14 +656,130 @@ class ConformerBlock:
         return out
 
 
+FEATURES_BFT = 0  # [batch, feat_in, frames]
+FEATURES_BTF = 1  # [batch, frames, feat_in]
+
+
+class Subsampling:
+    """The dw_striding Subsampling (src/asr/modules/encoders/conformer.rs:
+    1058-1588), the encoder's pre_encode: mel frames -> [B, T', d_model] in
+    bf16 on the device."""
+
+    def __init__(self, feat_in: int, d_model: int, subsampling_factor: int = 8,
+                 conv_channels: int = 256, causal_downsampling: bool = False,
+                 ctx: Optional[Context] = None, _handle=None, _owner=None,
+                 host_only: bool = False):
+        self.ctx = None if host_only else (ctx or Context.default())
+        self.feat_in, self.d_model = feat_in, d_model
+        self.factor, self.conv_channels = subsampling_factor, conv_channels
+        self.causal = bool(causal_downsampling)
+        if _handle is None:
+            h = C.c_void_p()
+            _check(lib().nrp_subsampling_create(self.ctx.handle if self.ctx else None,
+                                                feat_in, d_model,
+                                                subsampling_factor, conv_channels,
+                                                int(self.causal), C.byref(h)))
+            self.handle, self._owned = h, True
+        else:
+            self.handle, self._owned = _handle, False
+        self._owner = _owner
+        n = C.c_int()
+        _check(lib().nrp_subsampling_feat_out(self.handle, C.byref(n)))
+        self.feat_out = n.value
+        self.n_strides = {2: 1, 4: 2, 8: 3}.get(subsampling_factor, 2)
+
+    def __del__(self):
+        try:
+            if self._owned and self.handle:
+                lib().nrp_subsampling_destroy(self.handle)
+        except Exception:
+            pass
+
+    def set_dtype(self, dtype: int):
+        _check(lib().nrp_subsampling_set_dtype(self.handle, dtype))
+
+    def output_length(self, frames: int) -> int:
+        """Subsampling::output_length (conformer.rs:1315-1327)."""
+        n = C.c_int()
+        _check(lib().nrp_subsampling_output_length(self.handle, int(frames), C.byref(n)))
+        return n.value
+
+    def output_lengths(self, lengths) -> np.ndarray:
+        """Subsampling::output_lengths (conformer.rs:1387-1411)."""
+        return np.array([self.output_length(max(int(v), 0)) for v in np.asarray(lengths)],
+                        np.int32)
+
+    def set_conv(self, index: int, weight, bias=None):
+        """pre_encode.conv.{index} in MLX's layout [O, kH, kW, I]: 0 = conv.0,
+        2 + 3i the depthwise convs, 3 + 3i the pointwise ones."""
+        w = _np_f32(weight)
+        b = _np_f32(bias) if bias is not None else None
+        _check(lib().nrp_subsampling_load_conv(self.handle, index, w.ctypes.data,
+                                               b.ctypes.data if b is not None else None))
+
+    def set_out(self, layer: "LinearLayer"):
+        if layer.is_quantized():
+            wq = np.ascontiguousarray(layer.weight, np.uint32)
+            sc, bi = _np_f32(layer.scales), _np_f32(layer.biases)
+            b = _np_f32(layer.bias) if layer.bias is not None else None
+            _check(lib().nrp_subsampling_load_out_quantized(
+                self.handle, layer.bits, layer.group_size, wq.ctypes.data, sc.ctypes.data,
+                bi.ctypes.data, b.ctypes.data if b is not None else None))
+        else:
+            w = _np_f32(layer.weight)
+            b = _np_f32(layer.bias) if layer.bias is not None else None
+            _check(lib().nrp_subsampling_load_out(self.handle, w.ctypes.data,
+                                                  b.ctypes.data if b is not None else None))
+
+    def load_weights(self, weights: Dict[str, object], prefix: str = "encoder.pre_encode",
+                     quant: Optional[QuantizationConfig] = None):
+        """Subsampling::load_weights (conformer.rs:1557-1588)."""
+        idx = [0] + [j for i in range(self.n_strides - 1) for j in (2 + 3 * i, 3 + 3 * i)]
+        for k in idx:
+            w = weights.get(f"{prefix}.conv.{k}.weight")
+            if w is not None:
+                self.set_conv(k, w, weights.get(f"{prefix}.conv.{k}.bias"))
+        layer = load_linear_layer(weights, f"{prefix}.out", quant)
+        if layer is not None:
+            self.set_out(layer)
+
+    def forward(self, features, lengths=None, layout: int = FEATURES_BTF, out=None):
+        """forward_frames (conformer.rs:1413-1555) on device f32 features
+        ([B, T, F] by default, or [B, F, T]); lengths: host or device int32
+        [B] or None; frames past a length read as zero (the encoder's mel
+        mask).  Returns ([B, T', d_model] bf16, output lengths or None)."""
+        import torch
+        if layout == FEATURES_BTF:
+            B, T, F = features.shape
+        else:
+            B, F, T = features.shape
+        assert F == self.feat_in and features.dtype == torch.float32 and features.is_contiguous()
+        Tp = self.output_length(T)
+        if out is None:
+            out = torch.empty((B, Tp, self.d_model), dtype=torch.bfloat16,
+                              device=features.device)
+        dl, out_len = None, None
+        if lengths is not None:
+            dl = torch.as_tensor(np.asarray(lengths.cpu() if hasattr(lengths, "cpu") else lengths,
+                                            np.int32)).to(features.device)
+            out_len = self.output_lengths(dl.cpu().numpy())
+        _check(lib().nrp_subsampling_forward(self.handle, _stream(), features.data_ptr(), layout,
+                                             B, T, dl.data_ptr() if dl is not None else None,
+                                             out.data_ptr()))
+        return out, out_len
+
+
 class ConformerEncoder:
-    """The conformer stack of ConformerEncoder (conformer.rs:381-722):
-    forward_from_embeddings on post-subsampling embeddings."""
+    """ConformerEncoder (conformer.rs:381-722): the conformer stack, with
+    forward_from_embeddings on post-subsampling embeddings, and, given
+    feat_in, the dw_striding pre_encode and forward on mel features."""
 
     def __init__(self, n_layers: int, d_model: int, n_heads: int, ff_dim: int,
                  conv_kernel: int = 9, causal_conv: bool = False,
                  conv_norm: str = "batch_norm", use_bias: bool = True, xscaling: bool = True,
-                 max_len: int = 5000, ctx: Optional[Context] = None):
+                 max_len: int = 5000, ctx: Optional[Context] = None,
+                 feat_in: Optional[int] = None, subsampling_factor: int = 8,
+                 subsampling_conv_channels: int = 256, causal_downsampling: bool = False):
         self.ctx = ctx or Context.default()
         self.d_model = d_model
         h = C.c_void_p()
@@ -667,6 +795,15 @@ class ConformerEncoder:
             self.layers.append(ConformerBlock(d_model, n_heads, ff_dim, conv_kernel, causal_conv,
                                               conv_norm, use_bias, self.ctx, _handle=b,
                                               _owner=self))
+        self.subsampling = None
+        if feat_in is not None:
+            sh = C.c_void_p()
+            _check(lib().nrp_encoder_add_subsampling(h, feat_in, subsampling_factor,
+                                                     subsampling_conv_channels,
+                                                     int(causal_downsampling), C.byref(sh)))
+            self.subsampling = Subsampling(feat_in, d_model, subsampling_factor,
+                                           subsampling_conv_channels, causal_downsampling,
+                                           self.ctx, _handle=sh, _owner=self)
 
     def __del__(self):
         try:
@@ -680,7 +817,10 @@ class ConformerEncoder:
 
     def load_weights(self, weights: Dict[str, object],
                      quant: Optional[QuantizationConfig] = None):
-        """conformer.rs:590-605: layer i from encoder.layers.{i}."""
+        """conformer.rs:590-605: pre_encode from encoder.pre_encode, layer i
+        from encoder.layers.{i}."""
+        if self.subsampling is not None:
+            self.subsampling.load_weights(weights, "encoder.pre_encode", quant)
         for i, layer in enumerate(self.layers):
             layer.load_weights(weights, f"encoder.layers.{i}", quant)
 
@@ -715,6 +855,29 @@ class ConformerEncoder:
             mask.lengths.data_ptr() if mask is not None else None,
             C.byref(c) if c is not None else None, out.data_ptr()))
         return out, lengths
+
+    def forward(self, features, lengths=None, context: Optional[AttentionContext] = None,
+                out=None):
+        """ConformerEncoder::forward (conformer.rs:475-560): features device
+        f32 [B, feat_in, frames], lengths host int32 [B] (mel frames) or None.
+        Returns ([B, D, T'] bf16, subsampled lengths int32 [B])."""
+        import torch
+        if self.subsampling is None:
+            raise NrpError(NRP_ERR_INVALID, "the encoder was built without feat_in")
+        B, F, T = features.shape
+        assert features.dtype == torch.float32 and features.is_contiguous()
+        Tp = self.subsampling.output_length(T)
+        if out is None:
+            out = torch.empty((B, self.d_model, Tp), dtype=torch.bfloat16,
+                              device=features.device)
+        ln = np.ascontiguousarray(lengths, np.int32) if lengths is not None else None
+        out_len = np.empty(B, np.int32)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_encoder_forward(
+            self.handle, _stream(), features.data_ptr(), B, T,
+            ln.ctypes.data if ln is not None else None, C.byref(c) if c is not None else None,
+            out.data_ptr(), out_len.ctypes.data))
+        return out, out_len
 
 
 # ------------------------------------------- sequence split (several GPUs)

@@ -129,6 +129,14 @@ void dequant_host(const Linear& L, int N, int K, std::vector<float>& w) {
     }
 }
 
+}  // namespace
+
+void nrp::dequant_linear_host(const Linear& L, int N, int K, std::vector<float>& w) {
+  dequant_host(L, N, K, w);
+}
+
+namespace {
+
 // Device copies of the parameters in the module dtype.  Q, K and V are
 // concatenated into one [3D, D] projection so the three run as one GEMM.
 int sync_params(nrp_attn* a) {

@@ -103,6 +103,11 @@ struct nrp_encoder {
   cudaStream_t dq = nullptr;
   cudaEvent_t dq_start = nullptr, dq_ready[2] = {}, dq_done[2] = {};
   nrp::DevBuf dq_slot[2];
+  // pre_encode (nrp_encoder_add_subsampling) and the device copy of one
+  // forward's mel lengths and subsampled lengths [2][B]
+  nrp_subsampling* sub = nullptr;
+  nrp::DevBuf lens;
+  std::vector<int32_t> lens_host;
 };
 
 namespace {
@@ -518,6 +523,7 @@ int nrp_encoder_destroy(nrp_encoder* e) {
   for (cudaEvent_t ev : {e->dq_start, e->dq_ready[0], e->dq_ready[1], e->dq_done[0], e->dq_done[1]})
     if (ev) cudaEventDestroy(ev);
   for (nrp_block* b : e->blocks) nrp_block_destroy(b);
+  nrp_subsampling_destroy(e->sub);
   delete e;
   return NRP_OK;
 }
@@ -536,22 +542,43 @@ int nrp_encoder_set_dtype(nrp_encoder* e, int dtype) {
     const int rc = nrp_block_set_dtype(b, dtype);
     if (rc) return rc;
   }
+  if (e->sub) {
+    const int rc = nrp_subsampling_set_dtype(e->sub, dtype);
+    if (rc) return rc;
+  }
   e->dtype = dtype;
   return NRP_OK;
 }
 
-int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void* x, int B, int T,
-                                        const int32_t* lengths, const nrp_att_context* context,
-                                        void* out) {
-  if (!e || !x || !out) return failf(NRP_ERR_INVALID, "null argument");
-  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
-  if (e->dtype != NRP_DTYPE_BF16)
-    return failf(NRP_ERR_UNSUPPORTED, "the encoder runs in bf16 (nrp_encoder_set_dtype)");
-  if (nrp::select_device(e->ctx)) return NRP_ERR_CUDA;
+int nrp_encoder_add_subsampling(nrp_encoder* e, int feat_in, int subsampling_factor,
+                                int conv_channels, int causal_downsampling,
+                                nrp_subsampling** sub) {
+  if (!e) return failf(NRP_ERR_INVALID, "null encoder");
+  if (e->sub) return failf(NRP_ERR_INVALID, "the encoder already has a subsampling");
+  nrp_subsampling* s = nullptr;
+  int rc = nrp_subsampling_create(e->ctx, feat_in, e->D, subsampling_factor, conv_channels,
+                                  causal_downsampling, &s);
+  if (!rc) rc = nrp_subsampling_set_dtype(s, e->dtype);
+  if (rc) {
+    nrp_subsampling_destroy(s);
+    return rc;
+  }
+  e->sub = s;
+  if (sub) *sub = s;
+  return NRP_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// x * xscale, the blocks and the transpose to [B, D, T] over the embeddings
+// in e->x (conformer.rs:530-557 and 694-722).
+int encoder_layers(nrp_encoder* e, void* stream, int B, int T, const int32_t* lengths,
+                   const nrp_att_context* context, void* out) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int D = e->D;
   const int64_t n = static_cast<int64_t>(B) * T * D;
-  TRY_CUDA(e->x.ensure(n * 2));
   // 707-708: the positional table for this length (built once per length;
   // nrp_pe_encoding stages it through the host)
   if (e->pos_T != T) {
@@ -560,12 +587,10 @@ int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void
     if (rc) return rc;
     e->pos_T = T;
   }
-  {
+  // 701-704: x * xscale
+  if (e->xscale != 1.f) {
     nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
-    TRY_CUDA(cudaMemcpyAsync(e->x.p, x, n * 2, cudaMemcpyDeviceToDevice, st));
-    // 701-704: x * xscale
-    if (e->xscale != 1.f)
-      TRY_CUDA(nrp::launch_scale(e->x.as<__nv_bfloat16>(), n, nrp::bf16_round(e->xscale), st));
+    TRY_CUDA(nrp::launch_scale(e->x.as<__nv_bfloat16>(), n, nrp::bf16_round(e->xscale), st));
   }
   // Quantised layers: the next layer's weights are dequantised on e->dq
   // while the current layer runs (every forward still dequantises every
@@ -647,6 +672,71 @@ int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void
   nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
   TRY_CUDA(nrp::launch_transpose_btd(e->x.as<__nv_bfloat16>(), static_cast<__nv_bfloat16*>(out), B,
                                      T, D, st));
+  return NRP_OK;
+}
+
+int encoder_checks(nrp_encoder* e, int B, int T) {
+  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  if (e->dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_UNSUPPORTED, "the encoder runs in bf16 (nrp_encoder_set_dtype)");
+  if (nrp::select_device(e->ctx)) return NRP_ERR_CUDA;
+  return NRP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void* x, int B, int T,
+                                        const int32_t* lengths, const nrp_att_context* context,
+                                        void* out) {
+  if (!e || !x || !out) return failf(NRP_ERR_INVALID, "null argument");
+  int rc = encoder_checks(e, B, T);
+  if (rc) return rc;
+  const int64_t n = static_cast<int64_t>(B) * T * e->D;
+  TRY_CUDA(e->x.ensure(n * 2));
+  {
+    nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, static_cast<cudaStream_t>(stream));
+    TRY_CUDA(cudaMemcpyAsync(e->x.p, x, n * 2, cudaMemcpyDeviceToDevice,
+                             static_cast<cudaStream_t>(stream)));
+  }
+  return encoder_layers(e, stream, B, T, lengths, context, out);
+}
+
+int nrp_encoder_forward(nrp_encoder* e, void* stream, const float* features, int B, int frames,
+                        const int32_t* lengths, const nrp_att_context* context, void* out,
+                        int32_t* out_lengths) {
+  if (!e || !features || !out) return failf(NRP_ERR_INVALID, "null argument");
+  if (!e->sub) return failf(NRP_ERR_INVALID, "the encoder has no subsampling");
+  if (B <= 0 || frames <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, frames);
+  const int T = nrp::subsampling_output_frames(e->sub, frames);
+  int rc = encoder_checks(e, B, T);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // 484-518: mel frames past each length read as zero; 1387-1411: the
+  // subsampled lengths, which mask the blocks (PaddingMask::new, 1603-1614:
+  // none when no frame is padding)
+  e->lens_host.resize(2 * static_cast<size_t>(B));
+  bool padded = false;
+  for (int b = 0; b < B; ++b) {
+    const int len = lengths ? lengths[b] : frames;
+    e->lens_host[b] = len;
+    e->lens_host[B + b] = nrp::subsampling_output_frames(e->sub, std::max(len, 0));
+    padded = padded || e->lens_host[B + b] < T;
+  }
+  TRY_CUDA(e->lens.ensure(2 * static_cast<size_t>(B) * 4));
+  TRY_CUDA(cudaMemcpyAsync(e->lens.p, e->lens_host.data(), 2 * static_cast<size_t>(B) * 4,
+                           cudaMemcpyHostToDevice, st));
+  const int32_t* d_len = e->lens.as<int32_t>();
+  TRY_CUDA(e->x.ensure(static_cast<size_t>(B) * T * e->D * 2));
+  const int64_t F = nrp::subsampling_feat_in(e->sub);
+  rc = nrp::subsampling_run(e->sub, st, features, F * frames, 1, frames, B, frames,
+                            lengths ? d_len : nullptr, e->x.p);
+  if (rc) return rc;
+  rc = encoder_layers(e, stream, B, T, padded ? d_len + B : nullptr, context, out);
+  if (rc) return rc;
+  if (out_lengths)
+    for (int b = 0; b < B; ++b) out_lengths[b] = e->lens_host[B + b];
   return NRP_OK;
 }
 

@@ -82,7 +82,9 @@ struct RowTiling {
 //                 = value * sigmoid(gate), so y has N/2 columns; with len,
 //                 rows t >= len[b] are written as zeros (ConvolutionModule's
 //                 GLU and padded-frame zeroing)
-enum EpiMode { kEpiBias = 0, kEpiSilu = 1, kEpiResidual = 2, kEpiGlu = 3 };
+//   kEpiRelu      y = max(round(acc) + bias, 0): a pointwise conv whose output
+//                 is rounded before its bias add, then ReLU (the subsampling)
+enum EpiMode { kEpiBias = 0, kEpiSilu = 1, kEpiResidual = 2, kEpiGlu = 3, kEpiRelu = 4 };
 struct Epilogue {
   int mode = kEpiBias;
   const __nv_bfloat16* res = nullptr;
@@ -232,6 +234,30 @@ cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* wt, const float* 
 cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stream);
 cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D,
                                  cudaStream_t stream);
+
+// ---- dw_striding subsampling convolutions (subsampling_kernels.cu) ----
+// conv.0 (1 -> C, 3x3, stride 2, + bias, ReLU) of f32 mel frames, optionally
+// fused with the first depthwise 3x3 stride-2 conv (+ bias).  Mel element
+// (b, t, f) is mel[b * mel_bs + t * mel_ts + f * mel_fs]; frames t >= len[b]
+// read as zero (len null: none).  pad = 1, or 2 for causal padding (left 2,
+// right 1).  out NHWC bf16: [B][T2][F2][C] fused, else [B][T1][F1][C].
+// Weights f32 [C][9] taps (bf16-rounded values), biases f32 [C].
+// Requires C % 32 == 0.
+struct SubConvArgs {
+  const float* mel = nullptr;
+  int64_t mel_bs = 0, mel_ts = 0, mel_fs = 0;
+  const int32_t* len = nullptr;
+  int T = 0, F = 0, T1 = 0, F1 = 0, T2 = 0, F2 = 0, C = 0, pad = 1;
+  const float *w0 = nullptr, *b0 = nullptr, *w1 = nullptr, *b1 = nullptr;
+  __nv_bfloat16* out = nullptr;
+};
+size_t subsample_conv0_smem(int F1, bool fuse);
+cudaError_t launch_subsample_conv0(const SubConvArgs& a, int B, bool fuse, cudaStream_t stream);
+// y [B][To][Fo][C] = depthwise 3x3 stride 2 + bias of x [B][Ti][Fi][C]
+// (both bf16 NHWC); C a power of two in [8, 2048].
+cudaError_t launch_subsample_dw(const __nv_bfloat16* x, int B, int Ti, int Fi, int C, int pad,
+                                const float* w, const float* b, __nv_bfloat16* y, int To, int Fo,
+                                int num_sms, cudaStream_t stream);
 
 // ---- streaming attention on tensor cores (attn_stream.cu), bf16 ----
 // q|k|v [B, T, 3D] of the chunk, rings kc/vc/hc [B, C, D] (oldest frame at

@@ -337,10 +337,17 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 64; ++e) v[e] = __uint_as_float(r[e]);
+            if (ep.mode == kEpiRelu) {  // the conv's own rounding, before its bias add
+#pragma unroll
+              for (int e = 0; e < 64; ++e) v[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
+            }
             if (bias) add_bias64(v, bias, n0 + c, N, bias_vec);
             if (ep.mode == kEpiSilu) {
 #pragma unroll
               for (int e = 0; e < 64; ++e) v[e] = v[e] * sigmoid_approx(v[e]);
+            } else if (ep.mode == kEpiRelu) {
+#pragma unroll
+              for (int e = 0; e < 64; ++e) v[e] = fmaxf(v[e], 0.f);
             } else if (resid) {
 #pragma unroll
               for (int ch = 0; ch < 8; ++ch) {
@@ -479,7 +486,7 @@ bool epilogue_ok(const Epilogue& ep, int N) {
     return ep.res && ep.ldr % 8 == 0 && ep.res_bs % 8 == 0 && N % 8 == 0 &&
            (reinterpret_cast<uintptr_t>(ep.res) & 15) == 0;
   if (ep.mode == kEpiGlu) return N % 256 == 0;
-  return ep.mode == kEpiBias || ep.mode == kEpiSilu;
+  return ep.mode == kEpiBias || ep.mode == kEpiSilu || ep.mode == kEpiRelu;
 }
 int tiles_m_of(int M, const RowTiling& rt) {
   return rt.T > 0 ? rt.B * ((rt.T + kBM - 1) / kBM) : (M + kBM - 1) / kBM;

@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "gemm.h"
 #include "handles.h"
@@ -84,5 +85,15 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
 
 // Makes the context's device current.
 int select_device(nrp_context* ctx);
+
+// MLX affine dequantisation of a quantised Linear on the host (f32 [N, K]).
+void dequant_linear_host(const Linear& L, int N, int K, std::vector<float>& w);
+
+// The subsampling (subsampling.cpp): mel element (b, t, f) at mel[b * bs +
+// t * ts + f * fs]; lengths device int32 [B] or null (mel mask).
+int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64_t bs, int64_t ts,
+                    int64_t fs, int B, int T, const int32_t* lengths, void* out);
+int subsampling_output_frames(const nrp_subsampling* s, int frames);
+int subsampling_feat_in(const nrp_subsampling* s);
 
 }  // namespace nrp

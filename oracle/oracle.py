@@ -92,6 +92,9 @@ def lib():
             C.POINTER(_BlockWeights), _f32p, C.c_void_p, C.c_void_p, C.c_int, _f32p]
         L.orc_block_forward.restype = C.c_int
         L.orc_bf16_round_array.argtypes = [_f32p, C.c_int64]
+        L.orc_subsampling_forward.argtypes = [_f32p] + [C.c_int] * 7 + [C.c_void_p, C.c_int,
+                                                                         _f32p]
+        L.orc_subsampling_forward.restype = C.c_int
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _LIB = L
@@ -315,5 +318,58 @@ def block_forward(x, bw, pos_emb, n_heads, ff_dim, kernel, causal=False, conv_no
         x, B, T, D, n_heads, ff_dim, kernel, int(bool(causal)), int(conv_norm), C.byref(st),
         _f32(pos_emb), ln.ctypes.data if ln is not None else None,
         C.cast(C.pointer(cs), C.c_void_p) if cs is not None else None, int(bool(bf16)), out)
+    assert rc == 0
+    return out
+
+
+class _SubWeights(C.Structure):
+    _fields_ = [("conv0_w", C.c_void_p), ("conv0_b", C.c_void_p),
+                ("dw_w", C.c_void_p * 2), ("dw_b", C.c_void_p * 2),
+                ("pw_w", C.c_void_p * 2), ("pw_b", C.c_void_p * 2),
+                ("out_w", C.c_void_p), ("out_b", C.c_void_p)]
+
+
+def subsampling_strides(factor):
+    return lib().orc_subsampling_strides(int(factor))
+
+
+def subsampling_out_len(length, factor, causal):
+    """Subsampling::output_length (conformer.rs:1315-1327)."""
+    return lib().orc_subsampling_out_len(int(length), int(factor), int(bool(causal)))
+
+
+def subsampling_feat_out(feat_in, factor, causal):
+    """compute_freq_output_size (conformer.rs:1220-1244)."""
+    return lib().orc_subsampling_feat_out(int(feat_in), int(factor), int(bool(causal)))
+
+
+def subsampling_forward(x, sw, d_model, factor=8, causal=False, bf16=True):
+    """Subsampling::forward_frames (conformer.rs:1413-1555) on x [B, T, F].
+
+    sw: {"conv0": (w [C, 3, 3, 1], b), "dw": [(w [C, 3, 3, 1], b), ...],
+    "pw": [(w [C, 1, 1, C], b), ...], "out": (w [d_model, C * F'], b)}
+    (MLX layouts; biases may be None)."""
+    x = _f32(x)
+    B, T, F = x.shape
+    Cc = np.asarray(sw["conv0"][0]).shape[0]
+    keep = []
+
+    def ptr(a):
+        if a is None:
+            return None
+        a = _f32(a)
+        keep.append(a)
+        return a.ctypes.data
+
+    st = _SubWeights()
+    st.conv0_w, st.conv0_b = ptr(sw["conv0"][0]), ptr(sw["conv0"][1])
+    for i, ((dw, db), (pw, pb)) in enumerate(zip(sw.get("dw", []), sw.get("pw", []))):
+        st.dw_w[i], st.dw_b[i] = ptr(dw), ptr(db)
+        st.pw_w[i], st.pw_b[i] = ptr(pw), ptr(pb)
+    st.out_w, st.out_b = ptr(sw["out"][0]), ptr(sw["out"][1])
+    Tp = subsampling_out_len(T, factor, causal)
+    out = np.empty((B, Tp, d_model), np.float32)
+    rc = lib().orc_subsampling_forward(x, B, T, F, Cc, int(factor), int(bool(causal)),
+                                       int(d_model), C.byref(st), int(bool(bf16)), out)
     assert rc == 0
     return out

@@ -800,3 +800,137 @@ int orc_block_forward(const float *x, int B, int T, int D, int H, int ff, int K,
   free(dw_w); free(dw_b); free(cn_g); free(cn_b); free(cn_m); free(cn_v);
   return 0;
 }
+
+/* ------------------------------------------ dw_striding subsampling */
+
+/* Subsampling::new (conformer.rs:1118-1123): strides = log2(factor) for
+ * 2, 4, 8; any other factor gets 2. */
+int orc_subsampling_strides(int factor) {
+  return factor == 2 ? 1 : factor == 4 ? 2 : factor == 8 ? 3 : 2;
+}
+
+/* One stride-2, kernel-3 conv along an axis (conformer.rs:1306-1326 and the
+ * conv output size): causal pads (k-1, s-1) = (2, 1), floor(n/2) + 1;
+ * otherwise padding 1 on both sides, floor((n-1)/2) + 1 (floor division,
+ * so 0 -> 0). */
+static int sub_conv_len(int n, int causal) {
+  if (causal) {
+    const int p = n;  /* n + (k-1) + (s-1) - k */
+    return (p >= 0 ? p / 2 : -((-p + 1) / 2)) + 1;
+  }
+  const int p = n - 1;
+  return (p >= 0 ? p / 2 : -((-p + 1) / 2)) + 1;
+}
+
+/* Subsampling::output_length (1315-1327). */
+int orc_subsampling_out_len(int len, int factor, int causal) {
+  const int s = orc_subsampling_strides(factor);
+  for (int i = 0; i < s; ++i) len = sub_conv_len(len, causal);
+  return len > 0 ? len : 0;
+}
+
+/* compute_freq_output_size (1220-1244). */
+int orc_subsampling_feat_out(int feat_in, int factor, int causal) {
+  const int s = orc_subsampling_strides(factor);
+  int f = feat_in;
+  for (int i = 0; i < s; ++i) f = causal ? f / 2 + 1 : (f + 2 - 3) / 2 + 1;
+  return f;
+}
+
+/* A 3x3 stride-2 conv over NHWC x [B, Ti, Fi, cin] -> y [B, To, Fo, C]:
+ * cin == 1 is the first conv (every output channel reads channel 0),
+ * cin == C the depthwise one (groups = C); w [C, 3, 3, 1] (MLX layout),
+ * input (2*to + kt - pad, 2*fo + kf - pad), zero outside the input.  The
+ * conv output is rounded, then the bias add (nn::Conv2d::forward), then the
+ * optional ReLU. */
+static void sub_conv3x3_s2(const float *x, int B, int Ti, int Fi, int cin, int C,
+                           int pad, const float *w, const float *bias, int relu,
+                           int bf16, float *y, int To, int Fo) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int b = 0; b < B; ++b)
+    for (int to = 0; to < To; ++to)
+      for (int fo = 0; fo < Fo; ++fo)
+        for (int c = 0; c < C; ++c) {
+          const int ci = cin == 1 ? 0 : c;
+          float acc = 0.0f;
+          for (int kt = 0; kt < 3; ++kt) {
+            const int ti = 2 * to + kt - pad;
+            if (ti < 0 || ti >= Ti) continue;
+            for (int kf = 0; kf < 3; ++kf) {
+              const int fi = 2 * fo + kf - pad;
+              if (fi < 0 || fi >= Fi) continue;
+              acc += x[(((size_t)b * Ti + ti) * Fi + fi) * cin + ci] * w[c * 9 + kt * 3 + kf];
+            }
+          }
+          float v = rnd(acc, bf16);
+          if (bias) v = rnd(v + bias[c], bf16);
+          if (relu && v < 0.0f) v = 0.0f;
+          y[(((size_t)b * To + to) * Fo + fo) * C + c] = v;
+        }
+}
+
+/* Subsampling::forward_frames (conformer.rs:1413-1555), dw_striding:
+ *   x [B, T, F] -> NHWC [B, T, F, 1]; (causal_pad_2d, 66-80: (2, 1) on time
+ *   and frequency, then padding 0; otherwise padding 1)
+ *   conv.0 (1 -> C, 3x3, stride 2) + ReLU
+ *   per further stride: depthwise 3x3 stride 2 (groups C), pointwise 1x1
+ *   (C -> C), ReLU
+ *   [B, T', F', C] -> [B, T', C, F'] -> [B, T', C*F'] -> out linear.
+ * With bf16 every parameter and the input are rounded (set_dtype, 1098-1108,
+ * and the encoder's as_dtype, 519) and every op's output too.
+ * out [B, T', d_model], T' = orc_subsampling_out_len(T). */
+int orc_subsampling_forward(const float *x, int B, int T, int F, int C, int factor,
+                            int causal, int d_model, const orc_subsampling_weights *w,
+                            int bf16, float *out) {
+  if (B <= 0 || T <= 0 || F <= 0 || C <= 0 || d_model <= 0) return -1;
+  const int S = orc_subsampling_strides(factor);
+  const int pad = causal ? 2 : 1;
+  int Ti = T, Fi = F;
+  float *cur = dup_round(x, (size_t)B * T * F, bf16);
+  int cin = 1;
+  for (int s = 0; s < S; ++s) {
+    const int To = sub_conv_len(Ti, causal), Fo = sub_conv_len(Fi, causal);
+    const size_t n = (size_t)B * To * Fo * C;
+    float *y = (float *)malloc(sizeof(float) * n);
+    float *cw = dup_round(s == 0 ? w->conv0_w : w->dw_w[s - 1], (size_t)C * 9, bf16);
+    float *cb = dup_round(s == 0 ? w->conv0_b : w->dw_b[s - 1], (size_t)C, bf16);
+    sub_conv3x3_s2(cur, B, Ti, Fi, cin, C, pad, cw, cb, s == 0, bf16, y, To, Fo);
+    free(cw);
+    free(cb);
+    free(cur);
+    cur = y;
+    if (s > 0) {
+      /* pointwise conv: w [C, 1, 1, C] is a [C, C] linear, then ReLU */
+      float *pw = dup_round(w->pw_w[s - 1], (size_t)C * C, bf16);
+      float *pb = dup_round(w->pw_b[s - 1], (size_t)C, bf16);
+      float *z = (float *)malloc(sizeof(float) * n);
+      linear_r(cur, (int)(n / C), C, pw, C, pb, bf16, z);
+#pragma omp parallel for schedule(static)
+      for (int64_t e = 0; e < (int64_t)n; ++e)
+        if (z[e] < 0.0f) z[e] = 0.0f;
+      free(pw);
+      free(pb);
+      free(cur);
+      cur = z;
+    }
+    Ti = To;
+    Fi = Fo;
+    cin = C;
+  }
+  /* 1519-1536: [B, T', F', C] -> [B, T', C, F'] flattened */
+  const int K = C * Fi;
+  float *flat = (float *)malloc(sizeof(float) * (size_t)B * Ti * K);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int r = 0; r < B * Ti; ++r)
+    for (int f = 0; f < Fi; ++f)
+      for (int c = 0; c < C; ++c)
+        flat[(size_t)r * K + (size_t)c * Fi + f] = cur[((size_t)r * Fi + f) * C + c];
+  free(cur);
+  float *ow = dup_round(w->out_w, (size_t)d_model * K, bf16);
+  float *ob = dup_round(w->out_b, (size_t)d_model, bf16);
+  linear_r(flat, B * Ti, K, ow, d_model, ob, bf16, out);
+  free(ow);
+  free(ob);
+  free(flat);
+  return 0;
+}

@@ -161,6 +161,27 @@ int orc_block_forward(const float *x, int B, int T, int D, int H, int ff, int K,
                       const float *pos_emb, const int32_t *lengths,
                       const orc_context *ctx, int bf16, float *out);
 
+/* ---- dw_striding subsampling (conformer.rs:1058-1555) ---- */
+#define ORC_SUB_MAX_PAIRS 2
+typedef struct {
+  const float *conv0_w, *conv0_b;                 /* [C, 3, 3, 1], [C] */
+  const float *dw_w[ORC_SUB_MAX_PAIRS], *dw_b[ORC_SUB_MAX_PAIRS]; /* [C, 3, 3, 1] */
+  const float *pw_w[ORC_SUB_MAX_PAIRS], *pw_b[ORC_SUB_MAX_PAIRS]; /* [C, 1, 1, C] */
+  const float *out_w, *out_b;                     /* [d_model, C * F'], [d_model] */
+} orc_subsampling_weights;
+
+/* strides = log2(factor) for 2, 4, 8, else 2 (conformer.rs:1118-1123). */
+int orc_subsampling_strides(int factor);
+/* Subsampling::output_length (1315-1327). */
+int orc_subsampling_out_len(int len, int factor, int causal);
+/* compute_freq_output_size (1220-1244): F'. */
+int orc_subsampling_feat_out(int feat_in, int factor, int causal);
+/* Subsampling::forward_frames (1413-1555): x [B, T, F] (already masked by
+ * the caller when it should be), out [B, T', d_model].  Biases may be NULL. */
+int orc_subsampling_forward(const float *x, int B, int T, int F, int C, int factor,
+                            int causal, int d_model, const orc_subsampling_weights *w,
+                            int bf16, float *out);
+
 /* bfloat16 round-to-nearest-even of a float (what an MLX astype does). */
 float orc_bf16_round(float x);
 void orc_bf16_round_array(float *x, int64_t n);

@@ -134,3 +134,21 @@ def test_no_gpu_calls_fail_loudly(nrp):
         pytest.skip("a GPU is present")
     with pytest.raises(nrp.NrpError):
         nrp.Context(0)
+
+
+def test_subsampling_sizes_match_oracle(nrp, orc):
+    """Subsampling::output_length and compute_freq_output_size through the C
+    ABI (a handle without a device context) against the oracle's."""
+    from oracle import oracle
+    for factor in (2, 4, 8, 16):
+        for causal in (False, True):
+            for feat in (16, 80, 128):
+                s = nrp.Subsampling(feat, 64, factor, 64, causal, host_only=True)
+                assert s.feat_out == oracle.subsampling_feat_out(feat, factor, causal)
+                for n in list(range(0, 40)) + [4000, 4001, 120000]:
+                    assert s.output_length(n) == oracle.subsampling_out_len(n, factor, causal)
+    s = nrp.Subsampling(80, 64, 8, 64, False, host_only=True)
+    with pytest.raises(nrp.NrpError):
+        s.set_conv(1, np.zeros((64, 3, 3, 1), np.float32))  # conv.1 is the ReLU
+    with pytest.raises(nrp.NrpError):
+        nrp.Subsampling(80, 64, 8, 96, False, host_only=True)  # channels not a power of two
