@@ -256,10 +256,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="offline",
-                    choices=["offline", "long", "encoder", "stream", "single"],
+                    choices=["offline", "long", "encoder", "stream", "single", "subsampling"],
                     help="offline: BASELINE config 1 (the headline line); long: config 4, "
                          "the sequence split across the ranks; encoder: config 3; stream: "
-                         "config 2; single: config 0")
+                         "config 2; single: config 0; subsampling: the pre_encode of "
+                         "config 3's batch from mel frames")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -271,6 +272,8 @@ def main():
         return main_stream(args)
     if args.workload == "single":
         return main_single(args)
+    if args.workload == "subsampling":
+        return main_subsampling(args)
 
     import torch
     import torch.distributed as dist
@@ -469,6 +472,13 @@ STR_WORKLOAD = ("BASELINE config 2: cache-aware streaming rel-pos attention, 24 
                 "64 sessions, chunk 14 (13 lookahead + 1), 70-frame left K/V cache, "
                 "chunked_limited [70,13], bf16; a step is one chunk through the 24 layers, the "
                 "caches restart empty every 50 chunks")
+# The encoder's pre_encode on config 3's batch as mel input (feat_in 128, as
+# the parakeet FastConformers): 500 encoder frames = 4000 mel frames
+SUB_B, SUB_T, SUB_F, SUB_C, SUB_FACTOR = 32, 4000, 128, 256, 8
+SUB_LEN_LO, SUB_LEN_HI = 2000, 4000
+SUB_WORKLOAD = ("dw_striding subsampling (pre_encode): 8x, conv channels 256, feat_in 128, "
+                "d_model 1024, non-causal, bf16; mel [B=32, 128, 4000] f32 with lengths "
+                "U[2000,4000] masked (config 3's batch before subsampling)")
 # one fp32 layer, batch 1, T=125
 SGL_T = 125
 SGL_WORKLOAD = ("BASELINE config 0: one rel-pos MHA layer, fp32, B=1 T=125 d_model=1024 "
@@ -729,6 +739,84 @@ def main_encoder(args):
               "parallelism": f"utterance-parallel replicas x{world}"},
              "weak", e2e, "bf16", cpu=cpu,
              hbm_bytes=bytes_)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main_subsampling(args):
+    """Subsampling::forward_frames of config 3's batch from mel frames; one
+    step = one forward; frames counted = encoder frames out (B * T')."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(77 + rank)
+    sub = nrp.Subsampling(SUB_F, D, SUB_FACTOR, SUB_C, False, ctx=ctx)
+    f = lambda sd, *sh: (rng.standard_normal(sh, dtype=np.float32) * sd)
+    Fp, C = sub.feat_out, SUB_C
+    wts = {"conv0": (f(0.3, C, 3, 3, 1), f(0.1, C)),
+           "dw": [(f(0.3, C, 3, 3, 1), f(0.1, C)) for _ in range(2)],
+           "pw": [(f(1 / 16, C, 1, 1, C), f(0.1, C)) for _ in range(2)],
+           "out": (f(1 / math.sqrt(C * Fp), D, C * Fp), f(0.1, D))}
+    sub.set_conv(0, *wts["conv0"])
+    for i in range(2):
+        sub.set_conv(2 + 3 * i, *wts["dw"][i])
+        sub.set_conv(3 + 3 * i, *wts["pw"][i])
+    sub.set_out(nrp.LinearLayer.standard(*wts["out"]))
+    sub.set_dtype(nrp.BF16)
+    dev = torch.device("cuda", local)
+    x = rng.standard_normal((SUB_B, SUB_F, SUB_T), dtype=np.float32)
+    lengths = rng.integers(SUB_LEN_LO, SUB_LEN_HI + 1, SUB_B).astype(np.int32)
+    xd = torch.from_numpy(x).to(dev)
+    ld = torch.from_numpy(lengths).to(dev)
+    Tp = sub.output_length(SUB_T)
+    out = torch.empty((SUB_B, Tp, D), dtype=torch.bfloat16, device=dev)
+
+    def step(k, xin=xd, o=out):
+        sub.forward(xin, ld, layout=nrp.FEATURES_BFT, out=o)
+
+    x_host = torch.from_numpy(x).pin_memory()
+    out_host = torch.empty_like(out, device="cpu").pin_memory()
+    xs = [torch.empty_like(xd) for _ in range(2)]
+    outs = [torch.empty_like(out) for _ in range(2)]
+    e2e = (lambda slot: xs[slot].copy_(x_host, non_blocking=True),
+           lambda slot: step(0, xs[slot], outs[slot]),
+           lambda slot: out_host.copy_(outs[slot], non_blocking=True),
+           x_host.numel() * 4, out_host.numel() * 2)
+    T1, F1 = (SUB_T - 1) // 2 + 1, (SUB_F - 1) // 2 + 1
+    T2, F2 = (T1 - 1) // 2 + 1, (F1 - 1) // 2 + 1
+    T3, F3 = (T2 - 1) // 2 + 1, (F2 - 1) // 2 + 1
+    frames = SUB_B * Tp
+    # tensor work: the two pointwise convs and `out`; HBM work of the direct
+    # convs: the mel read + the first depthwise output written, and the
+    # second depthwise conv's input read + output written
+    flops = {"gemm_bf16": 2 * SUB_B * (T2 * F2 + T3 * F3) * C * C + 2 * SUB_B * T3 * C * F3 * D}
+    bytes_ = {"subsample": SUB_B * SUB_F * SUB_T * 4 + SUB_B * T2 * F2 * C * 2 * 2
+              + SUB_B * T3 * F3 * C * 2}
+
+    def cpu():
+        """The oracle on utterance 0 (its masked mel), all host threads."""
+        from oracle import oracle as orc
+        threads = os.cpu_count() or 1
+        orc.set_threads(threads)
+        L0 = int(lengths[0])
+        xu = np.ascontiguousarray(x[:1].transpose(0, 2, 1))
+        xu[:, L0:] = 0.0
+        t0 = time.perf_counter()
+        orc.subsampling_forward(xu, wts, D, SUB_FACTOR, False, bf16=True)
+        dt = time.perf_counter() - t0
+        return {"value": Tp / dt, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": f"utterance 0 ({SUB_T} mel frames -> {Tp} encoder frames); CPU "
+                          f"restatement (oracle subsampling_forward, bf16 rounding), host "
+                          f"CPU: {cpu_model()}"}
+    _harness(args, world, rank, local, ctx, step, frames, flops, None, SUB_WORKLOAD,
+             {"batch_per_gpu": SUB_B, "mel_frames": SUB_T, "feat_in": SUB_F,
+              "encoder_frames": Tp, "conv_channels": C, "d_model": D,
+              "parallelism": f"utterance-parallel replicas x{world}"},
+             "weak", e2e, "bf16", cpu=cpu, hbm_bytes=bytes_)
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -745,9 +745,10 @@ class Subsampling:
 
     def forward(self, features, lengths=None, layout: int = FEATURES_BTF, out=None):
         """forward_frames (conformer.rs:1413-1555) on device f32 features
-        ([B, T, F] by default, or [B, F, T]); lengths: host or device int32
-        [B] or None; frames past a length read as zero (the encoder's mel
-        mask).  Returns ([B, T', d_model] bf16, output lengths or None)."""
+        ([B, T, F] by default, or [B, F, T]); lengths: host int32 [B], a
+        device int32 tensor, or None; frames past a length read as zero (the
+        encoder's mel mask).  Returns ([B, T', d_model] bf16, the output
+        lengths for host lengths, else None)."""
         import torch
         if layout == FEATURES_BTF:
             B, T, F = features.shape
@@ -759,10 +760,13 @@ class Subsampling:
             out = torch.empty((B, Tp, self.d_model), dtype=torch.bfloat16,
                               device=features.device)
         dl, out_len = None, None
-        if lengths is not None:
-            dl = torch.as_tensor(np.asarray(lengths.cpu() if hasattr(lengths, "cpu") else lengths,
-                                            np.int32)).to(features.device)
-            out_len = self.output_lengths(dl.cpu().numpy())
+        if isinstance(lengths, torch.Tensor) and lengths.is_cuda:
+            assert lengths.dtype == torch.int32 and lengths.numel() == B
+            dl = lengths  # (output lengths: self.output_lengths of the host copy)
+        elif lengths is not None:
+            ln = np.ascontiguousarray(lengths, np.int32)
+            dl = torch.from_numpy(ln).to(features.device)
+            out_len = self.output_lengths(ln)
         _check(lib().nrp_subsampling_forward(self.handle, _stream(), features.data_ptr(), layout,
                                              B, T, dl.data_ptr() if dl is not None else None,
                                              out.data_ptr()))

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <vector>
 
 namespace nrp {
 
@@ -241,22 +242,34 @@ cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B
 // (b, t, f) is mel[b * mel_bs + t * mel_ts + f * mel_fs]; frames t >= len[b]
 // read as zero (len null: none).  pad = 1, or 2 for causal padding (left 2,
 // right 1).  out NHWC bf16: [B][T2][F2][C] fused, else [B][T1][F1][C].
-// Weights f32 [C][9] taps (bf16-rounded values), biases f32 [C].
-// Requires C % 32 == 0.
+// Weights and biases come as MMA B fragments (subsample_conv0_frags,
+// subsample_dw_frags).  Requires C % 32 == 0 and F1 <= 80.
 struct SubConvArgs {
   const float* mel = nullptr;
   int64_t mel_bs = 0, mel_ts = 0, mel_fs = 0;
   const int32_t* len = nullptr;
   int T = 0, F = 0, T1 = 0, F1 = 0, T2 = 0, F2 = 0, C = 0, pad = 1;
-  const float *w0 = nullptr, *b0 = nullptr, *w1 = nullptr, *b1 = nullptr;
+  const uint32_t *f0 = nullptr, *f1 = nullptr;  // conv.0 and depthwise fragments
   __nv_bfloat16* out = nullptr;
 };
+// Fragment words per (group, lane): 12 (three 16-byte loads).
+constexpr int kSubFragWords = 12;
+// The host-side fragment layouts (bf16 pairs, low half first), for C
+// channels: conv.0 w [C][9], b [C] -> [C/32][32 lanes][12]: for n-tile nt
+// of the 32-channel group, words 3nt, 3nt+1 = (w[c][2t], w[c][2t+1]),
+// (t == 0 ? w[c][8] : 0, 0) with c = 8 nt + g, word 3nt+2 = (b[8nt+2t],
+// b[8nt+2t+1]) (g = lane / 4, t = lane % 4).  Depthwise w [C][9], b [C]
+// -> [C/8][32 lanes][12]: words 2j, 2j+1 = tap 2j, 2j+1 of channel c on the
+// diagonal (lane's pair (g == 2t ? v : 0, g == 2t+1 ? v : 0)), word 10 =
+// the bias pair of channels 2t, 2t+1, word 11 = 0.
+void subsample_conv0_frags(const float* w, const float* b, int C, std::vector<uint32_t>& out);
+void subsample_dw_frags(const float* w, const float* b, int C, std::vector<uint32_t>& out);
 size_t subsample_conv0_smem(int F1, bool fuse);
 cudaError_t launch_subsample_conv0(const SubConvArgs& a, int B, bool fuse, cudaStream_t stream);
 // y [B][To][Fo][C] = depthwise 3x3 stride 2 + bias of x [B][Ti][Fi][C]
-// (both bf16 NHWC); C a power of two in [8, 2048].
+// (both bf16 NHWC); C % 32 == 0.
 cudaError_t launch_subsample_dw(const __nv_bfloat16* x, int B, int Ti, int Fi, int C, int pad,
-                                const float* w, const float* b, __nv_bfloat16* y, int To, int Fo,
+                                const uint32_t* frag, __nv_bfloat16* y, int To, int Fo,
                                 int num_sms, cudaStream_t stream);
 
 // ---- streaming attention on tensor cores (attn_stream.cu), bf16 ----

@@ -68,7 +68,7 @@ struct nrp_subsampling {
   HostConv pw[kMaxStrides - 1];
   nrp::Linear out;
   bool dirty = true;
-  nrp::DevBuf d_conv_w[kMaxStrides], d_conv_b[kMaxStrides];  // f32 [C][9], [C]
+  nrp::DevBuf d_frag[kMaxStrides];  // conv.0, then depthwise, MMA B fragments
   nrp::DevBuf d_pw_w[kMaxStrides - 1], d_pw_b[kMaxStrides - 1];  // bf16 [C][C], [C]
   nrp::DevBuf d_out_w, d_out_b;  // bf16 [D][F' * C] (columns f' * C + c), [D]
   bool has_out_b = false;
@@ -85,11 +85,9 @@ cudaError_t upload_bf16v(nrp::DevBuf& dst, const std::vector<float>& v) {
   return e;
 }
 
-cudaError_t upload_rounded_f32(nrp::DevBuf& dst, const std::vector<float>& v) {
-  std::vector<float> h(v.size());
-  for (size_t i = 0; i < v.size(); ++i) h[i] = nrp::bf16_round(v[i]);
-  cudaError_t e = dst.ensure(h.size() * 4);
-  if (e == cudaSuccess) e = cudaMemcpy(dst.p, h.data(), h.size() * 4, cudaMemcpyHostToDevice);
+cudaError_t upload_u32(nrp::DevBuf& dst, const std::vector<uint32_t>& v) {
+  cudaError_t e = dst.ensure(v.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(dst.p, v.data(), v.size() * 4, cudaMemcpyHostToDevice);
   return e;
 }
 
@@ -103,8 +101,12 @@ int sync_sub(nrp_subsampling* s) {
       return failf(NRP_ERR_INVALID, "subsampling conv weights not loaded (stage %d)", i);
   if (!s->out.loaded) return failf(NRP_ERR_INVALID, "subsampling out weights not loaded");
   for (int i = 0; i < s->S; ++i) {
-    TRY_CUDA(upload_rounded_f32(s->d_conv_w[i], s->conv[i].w));
-    TRY_CUDA(upload_rounded_f32(s->d_conv_b[i], s->conv[i].b));
+    std::vector<uint32_t> frag;
+    if (i == 0)
+      nrp::subsample_conv0_frags(s->conv[i].w.data(), s->conv[i].b.data(), C, frag);
+    else
+      nrp::subsample_dw_frags(s->conv[i].w.data(), s->conv[i].b.data(), C, frag);
+    TRY_CUDA(upload_u32(s->d_frag[i], frag));
   }
   for (int i = 0; i + 1 < s->S; ++i) {
     TRY_CUDA(upload_bf16v(s->d_pw_w[i], s->pw[i].w));
@@ -133,6 +135,44 @@ int sync_sub(nrp_subsampling* s) {
 
 namespace nrp {
 
+namespace {
+uint32_t pack_pair(float lo, float hi) {
+  return static_cast<uint32_t>(bf16_bits(lo)) | (static_cast<uint32_t>(bf16_bits(hi)) << 16);
+}
+}  // namespace
+
+void subsample_conv0_frags(const float* w, const float* b, int C, std::vector<uint32_t>& out) {
+  out.assign(static_cast<size_t>(C / 32) * 32 * kSubFragWords, 0u);
+  for (int cg = 0; cg < C / 32; ++cg)
+    for (int lane = 0; lane < 32; ++lane) {
+      const int g = lane >> 2, t = lane & 3;
+      uint32_t* o = out.data() + (static_cast<size_t>(cg) * 32 + lane) * kSubFragWords;
+      for (int nt = 0; nt < 4; ++nt) {
+        const float* wc = w + (cg * 32 + 8 * nt + g) * 9;
+        const int cb = cg * 32 + 8 * nt + 2 * t;
+        o[3 * nt] = pack_pair(wc[2 * t], wc[2 * t + 1]);
+        o[3 * nt + 1] = t == 0 ? pack_pair(wc[8], 0.f) : 0u;
+        o[3 * nt + 2] = pack_pair(b[cb], b[cb + 1]);
+      }
+    }
+}
+
+void subsample_dw_frags(const float* w, const float* b, int C, std::vector<uint32_t>& out) {
+  out.assign(static_cast<size_t>(C / 8) * 32 * kSubFragWords, 0u);
+  for (int q = 0; q < C / 8; ++q)
+    for (int lane = 0; lane < 32; ++lane) {
+      const int g = lane >> 2, t = lane & 3;
+      uint32_t* o = out.data() + (static_cast<size_t>(q) * 32 + lane) * kSubFragWords;
+      const float* wc = w + (q * 8 + g) * 9;
+      for (int j = 0; j < 5; ++j) {
+        const float lo = wc[2 * j], hi = j < 4 ? wc[2 * j + 1] : 0.f;
+        o[2 * j] = pack_pair(g == 2 * t ? lo : 0.f, g == 2 * t + 1 ? lo : 0.f);
+        o[2 * j + 1] = pack_pair(g == 2 * t ? hi : 0.f, g == 2 * t + 1 ? hi : 0.f);
+      }
+      o[10] = pack_pair(b[q * 8 + 2 * t], b[q * 8 + 2 * t + 1]);
+    }
+}
+
 int subsampling_output_frames(const nrp_subsampling* s, int frames) {
   for (int i = 0; i < s->S; ++i) frames = conv_len(frames, s->causal);
   return std::max(frames, 0);
@@ -158,8 +198,9 @@ int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64
     Fi[i + 1] = conv_len(Fi[i], s->causal);
   }
   const int fused = s->S >= 2 ? 2 : 1;  // stages the first kernel covers
-  if (subsample_conv0_smem(Fi[1], fused == 2) > 227u * 1024u)
-    return failf(NRP_ERR_UNSUPPORTED, "feat_in %d too large for the conv.0 tile", s->F);
+  if (Fi[1] > 80)
+    return failf(NRP_ERR_UNSUPPORTED, "feat_in %d: the conv.0 kernel takes at most 80 conv.0 "
+                 "columns (feat_in <= 158)", s->F);
   size_t act_elems = static_cast<size_t>(B) * Ti[fused] * Fi[fused] * C;
   TRY_CUDA(s->act[0].ensure(act_elems * 2));
   TRY_CUDA(s->act[1].ensure(act_elems * 2));
@@ -180,12 +221,8 @@ int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64
     a.F2 = fused == 2 ? Fi[2] : 0;
     a.C = C;
     a.pad = pad;
-    a.w0 = s->d_conv_w[0].as<float>();
-    a.b0 = s->d_conv_b[0].as<float>();
-    if (fused == 2) {
-      a.w1 = s->d_conv_w[1].as<float>();
-      a.b1 = s->d_conv_b[1].as<float>();
-    }
+    a.f0 = s->d_frag[0].as<uint32_t>();
+    if (fused == 2) a.f1 = s->d_frag[1].as<uint32_t>();
     a.out = buf[0];
     ProfScope ps(s->ctx, NRP_KERNEL_SUBSAMPLE, st);
     TRY_CUDA(launch_subsample_conv0(a, B, fused == 2, st));
@@ -194,8 +231,8 @@ int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64
   for (int i = 1; i < s->S; ++i) {
     if (i >= 2) {  // a further depthwise conv
       ProfScope ps(s->ctx, NRP_KERNEL_SUBSAMPLE, st);
-      TRY_CUDA(launch_subsample_dw(buf[cur], B, Ti[i], Fi[i], C, pad, s->d_conv_w[i].as<float>(),
-                                   s->d_conv_b[i].as<float>(), buf[cur ^ 1], Ti[i + 1],
+      TRY_CUDA(launch_subsample_dw(buf[cur], B, Ti[i], Fi[i], C, pad,
+                                   s->d_frag[i].as<uint32_t>(), buf[cur ^ 1], Ti[i + 1],
                                    Fi[i + 1], s->ctx->num_sms, st));
       cur ^= 1;
     }
