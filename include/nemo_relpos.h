@@ -356,6 +356,22 @@ int nrp_block_forward(nrp_block* block, void* stream, const void* x, int batch, 
                       const void* pos_emb, const int32_t* lengths,
                       const nrp_att_context* context, void* out);
 
+/* ConformerBlock::forward_with_cache (conformer.rs:1877-1967) with
+ * ConvolutionModule::forward_with_cache (2332-2400), as forward_streaming
+ * drives it (883-1000): x, out device [batch, seq_len, d_model] bf16 (out
+ * may be x); pos_emb device [2*(C+seq_len)-1, d_model]; attn_cache the
+ * block attention's cache (nrp_cache_create on nrp_block_attn, C frames);
+ * conv_cache device bf16 [batch, conv_kernel-1, d_model] (time-major; the
+ * reference's cache_last_time[layer] is [batch, d_model, conv_kernel-1]):
+ * read, then replaced by the last conv_kernel-1 frames of [cache | GLU
+ * output]; filled, valid, context as nrp_attn_forward_with_cache; frames
+ * t >= valid are zeroed before the depthwise conv (the pad mask, 929-941).
+ * The depthwise conv runs without padding over [cache | chunk]. */
+int nrp_block_forward_with_cache(nrp_block* block, void* stream, const void* x, int batch,
+                                 int seq_len, const void* pos_emb, nrp_cache* attn_cache,
+                                 void* conv_cache, int filled, int valid,
+                                 const nrp_att_context* context, void* out);
+
 /* ConformerEncoder::forward_from_embeddings (conformer.rs:694-722) over
  * n_layers blocks: x * xscale (sqrt(d_model) when xscaling), the positional
  * table of RelPositionalEncoding(d_model, max_len) for seq_len, every block,

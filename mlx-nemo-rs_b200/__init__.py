@@ -129,6 +129,7 @@ def lib():
             "nrp_block_load_depthwise": ([vp, vp, vp], i),
             "nrp_block_load_conv_norm": ([vp, vp, vp, vp, vp], i),
             "nrp_block_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
+            "nrp_block_forward_with_cache": ([vp, vp, vp, i, i, vp, vp, vp, i, i, vp, vp], i),
             "nrp_encoder_create": ([vp] + [i] * 10 + [vp], i),
             "nrp_encoder_destroy": ([vp], i),
             "nrp_encoder_block": ([vp, i, vp], i),
@@ -406,12 +407,14 @@ class RelPositionMultiHeadAttention:
         self.att_context_size: Optional[Tuple[int, int]] = None
 
     @classmethod
-    def _view(cls, handle, d_model: int, n_heads: int, ctx: Context):
-        """A module owned by a ConformerBlock (not freed by this object)."""
+    def _view(cls, handle, d_model: int, n_heads: int, ctx: Context, owner=None):
+        """A module owned by a ConformerBlock (not freed by this object; it
+        keeps the block alive while the view, or a cache made from it, is)."""
         self = cls.__new__(cls)
         self.ctx = ctx
         self.handle = handle
         self._owned = False
+        self._owner = owner
         self.d_model = d_model
         self._n_heads = n_heads
         self.dtype = F32
@@ -567,7 +570,8 @@ class ConformerBlock:
             self.handle, self._owned = _handle, False
         a = C.c_void_p()
         _check(lib().nrp_block_attn(self.handle, C.byref(a)))
-        self.self_attn = RelPositionMultiHeadAttention._view(a, d_model, n_heads, self.ctx)
+        self.self_attn = RelPositionMultiHeadAttention._view(a, d_model, n_heads, self.ctx,
+                                                             owner=self)
 
     def __del__(self):
         try:
@@ -654,6 +658,36 @@ class ConformerBlock:
                                        _ptr(lengths), C.byref(c) if c is not None else None,
                                        out.data_ptr()))
         return out
+
+    def forward_with_cache(self, x, pos_emb, cache: "AttentionCache", conv_cache,
+                           cache_filled_len: int, valid_len: int,
+                           context: Optional[AttentionContext] = None, out=None):
+        """ConformerBlock::forward_with_cache (conformer.rs:1877-1967) as
+        forward_streaming drives it (883-1000).  x [B, T, D] bf16; pos_emb the
+        table for C + T frames; cache the block attention's AttentionCache;
+        conv_cache device bf16 [B, conv_kernel - 1, D] (new_conv_cache()),
+        replaced in place by the last conv_kernel - 1 GLU frames; frames >=
+        valid_len are zeroed before the depthwise conv."""
+        import torch
+        B, T, D = x.shape
+        assert tuple(conv_cache.shape) == (B, self.conv_kernel - 1, D)
+        assert conv_cache.dtype == torch.bfloat16 and conv_cache.is_contiguous()
+        pe = pos_emb.reshape(-1, D)
+        if out is None:
+            out = torch.empty_like(x)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_block_forward_with_cache(
+            self.handle, _stream(), x.data_ptr(), B, T, pe.data_ptr(), cache.handle,
+            conv_cache.data_ptr(), int(cache_filled_len), int(valid_len),
+            C.byref(c) if c is not None else None, out.data_ptr()))
+        return out
+
+    def new_conv_cache(self, batch: int, device=None):
+        """A zero conv cache [batch, conv_kernel - 1, d_model] bf16 (NeMo starts
+        streams with zeros: conformer.rs:960-963)."""
+        import torch
+        return torch.zeros((batch, self.conv_kernel - 1, self.d_model), dtype=torch.bfloat16,
+                           device=device or torch.device("cuda", self.ctx.device))
 
 
 FEATURES_BFT = 0  # [batch, feat_in, frames]

@@ -70,11 +70,15 @@ int failf(int code, const char* fmt, ...) {
 
 namespace {
 
+// A failed call's error is also taken out of the runtime's last-error slot,
+// where the launch checks (cudaGetLastError) of later calls would find it.
 #define CUDA_TRY(expr)                                                                    \
   do {                                                                                   \
     cudaError_t e_ = (expr);                                                             \
-    if (e_ != cudaSuccess)                                                               \
+    if (e_ != cudaSuccess) {                                                             \
+      (void)cudaGetLastError();                                                          \
       return fail(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));        \
+    }                                                                                    \
   } while (0)
 
 using nrp::bf16_bits;
@@ -271,8 +275,10 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   }
   if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)
     return fail(NRP_ERR_UNSUPPORTED, "bf16 linear needs K %% 64 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
-  // (the GEMV writes flat rows: not for an output with its own batch stride)
-  if (quant && M <= 16 && rt.y_bstride == 0 && ep.mode == nrp::kEpiBias) {
+  // (the GEMV writes flat rows: not for an output with its own batch stride;
+  // it takes K % 512 == 0, other K go to the 8-bit GEMM below)
+  if (quant && M <= 16 && K % 512 == 0 && rt.y_bstride == 0 && rt.x_bstride == 0 &&
+      ep.mode == nrp::kEpiBias) {
     ProfScope ps(ctx, NRP_KERNEL_QGEMV, st);
     CUDA_TRY(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
                                static_cast<const uint8_t*>(w),
@@ -311,7 +317,9 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   const bool xmap_ok =
       rt.T > 0 ? nrp::make_tmap_3d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, rt.T, rt.B,
                                    static_cast<uint64_t>(K) * 2,
-                                   static_cast<uint64_t>(K) * 2 * rt.T, 64, 128, 1, true)
+                                   static_cast<uint64_t>(rt.x_bstride ? rt.x_bstride
+                                                                      : static_cast<int64_t>(K) * rt.T) * 2,
+                                   64, 128, 1, true)
                : nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
                                    static_cast<uint64_t>(K) * 2, 64, 128, true);
   if (!xmap_ok) return fail(NRP_ERR_CUDA, "TMA descriptor for x rejected");
@@ -514,7 +522,7 @@ int nrp_context_create(int device, nrp_context** out) {
 
 int nrp_context_destroy(nrp_context* ctx) {
   if (!ctx) return ok();
-  cudaSetDevice(ctx->device);
+  cudaSetDevice(ctx->device);  // (errors of this teardown are dropped below)
   prof_collect(ctx);
   for (cudaEvent_t e : ctx->pool) cudaEventDestroy(e);
   if (ctx->side) {
@@ -525,6 +533,7 @@ int nrp_context_destroy(nrp_context* ctx) {
   if (ctx->join) cudaEventDestroy(ctx->join);
   cudaFree(ctx->d_err);
   delete ctx;
+  (void)cudaGetLastError();
   return ok();
 }
 
@@ -570,6 +579,7 @@ int nrp_attn_create(nrp_context* ctx, int d_model, int n_heads, int use_bias, nr
     return fail(NRP_ERR_UNSUPPORTED, "head_dim %d > 128", d_model / n_heads);
   auto* a = new nrp_attn;
   a->ctx = ctx;
+  a->device = ctx->device;
   a->D = d_model;
   a->H = n_heads;
   a->dh = d_model / n_heads;
@@ -588,8 +598,10 @@ int nrp_attn_create(nrp_context* ctx, int d_model, int n_heads, int use_bias, nr
 
 int nrp_attn_destroy(nrp_attn* attn) {
   if (attn) {
-    cudaSetDevice(attn->ctx->device);
+    // (its context may be gone already: only the device number is used)
+    cudaSetDevice(attn->device);
     delete attn;
+    (void)cudaGetLastError();
   }
   return ok();
 }
@@ -926,6 +938,7 @@ int nrp_cache_create(nrp_attn* attn, int batch, int cache_len, nrp_cache** out) 
   if (check_device(attn->ctx)) return NRP_ERR_CUDA;
   auto* c = new nrp_cache;
   c->attn = attn;
+  c->device = attn->ctx->device;
   c->B = batch;
   c->C = cache_len;
   c->D = attn->D;
@@ -944,8 +957,10 @@ int nrp_cache_create(nrp_attn* attn, int batch, int cache_len, nrp_cache** out) 
 
 int nrp_cache_destroy(nrp_cache* cache) {
   if (cache) {
-    cudaSetDevice(cache->attn->ctx->device);
+    // (its module may have been destroyed first: only the device number is used)
+    cudaSetDevice(cache->device);
     delete cache;
+    (void)cudaGetLastError();
   }
   return ok();
 }
@@ -1031,6 +1046,16 @@ int nrp_cache_import_h(nrp_cache* c, const float* h, void* stream) {
 int nrp_attn_forward_with_cache(nrp_attn* a, void* stream, const void* x, int B, int T,
                                 const void* pos_emb, nrp_cache* c, int filled, int valid,
                                 const nrp_att_context* context, void* out) {
+  return nrp::attn_forward_with_cache(a, static_cast<cudaStream_t>(stream), x, B, T, pos_emb, c,
+                                      filled, valid, context, out, nrp::Epilogue());
+}
+
+}  // extern "C"
+
+int nrp::attn_forward_with_cache(nrp_attn* a, cudaStream_t st, const void* x, int B, int T,
+                                 const void* pos_emb, nrp_cache* c, int filled, int valid,
+                                 const nrp_att_context* context, void* out,
+                                 const nrp::Epilogue& out_ep) {
   if (!a || !x || !pos_emb || !c || !out) return fail(NRP_ERR_INVALID, "null argument");
   if (c->attn != a) return fail(NRP_ERR_INVALID, "cache belongs to another module");
   if (B != c->B || T <= 0) return fail(NRP_ERR_INVALID, "batch %d / seq_len %d do not match the cache", B, T);
@@ -1039,7 +1064,6 @@ int nrp_attn_forward_with_cache(nrp_attn* a, void* stream, const void* x, int B,
   if (check_device(ctx)) return NRP_ERR_CUDA;
   int rc = sync_params(a);
   if (rc) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int D = a->D, C = c->C, Tk = C + T, P = 2 * Tk - 1;
   const size_t es = esize(a->dtype);
   const size_t BT = static_cast<size_t>(B) * T;
@@ -1114,8 +1138,10 @@ int nrp_attn_forward_with_cache(nrp_attn* a, void* stream, const void* x, int B,
   if (n_app > 0) c->head = (c->head + n_app) % C;
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
-                    out, D);
+                    out, D, nrp::RowTiling(), out_ep);
 }
+
+extern "C" {
 
 // ------------------------------------------------------------ profiling
 int nrp_profile_enable(nrp_context* ctx, int enable) {

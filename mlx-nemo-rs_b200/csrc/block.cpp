@@ -32,11 +32,13 @@ namespace {
 
 using nrp::failf;
 
-#define TRY_CUDA(expr)                                                                \
-  do {                                                                                \
-    const cudaError_t e_ = (expr);                                                    \
-    if (e_ != cudaSuccess)                                                            \
-      return failf(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_));     \
+#define TRY_CUDA(expr)                                                        \
+  do {                                                                        \
+    const cudaError_t e_ = (expr);                                            \
+    if (e_ != cudaSuccess) {                                                  \
+      (void)cudaGetLastError(); /* not left for later launch checks */        \
+      return failf(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_)); \
+    }                                                                         \
   } while (0)
 
 constexpr int kNumLinears = 6;
@@ -88,6 +90,7 @@ struct nrp_block {
   nrp::DevBuf d_dw_w;  // taps-major [K][D]
   nrp::DevBuf d_dw_b, d_cn_scale, d_cn_shift, d_cn_g, d_cn_b;
   nrp::DevBuf h, hid, glu, dw;  // workspace
+  nrp::DevBuf vbuf;             // [B] copies of a streaming step's valid length
 };
 
 struct nrp_encoder {
@@ -487,6 +490,127 @@ int nrp_block_forward(nrp_block* k, void* stream, const void* x, int B, int T,
   return layer_norm(k, st, NRP_BLOCK_NORM_OUT, out, out, M);
 }
 
+int nrp_block_forward_with_cache(nrp_block* k, void* stream, const void* x, int B, int T,
+                                 const void* pos_emb, nrp_cache* attn_cache, void* conv_cache,
+                                 int filled, int valid, const nrp_att_context* context,
+                                 void* out) {
+  if (!k || !x || !pos_emb || !attn_cache || !out) return failf(NRP_ERR_INVALID, "null argument");
+  if (k->K > 1 && !conv_cache) return failf(NRP_ERR_INVALID, "null conv cache");
+  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  if (k->dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_UNSUPPORTED, "the conformer block runs in bf16 (nrp_block_set_dtype)");
+  const int D = k->D, K = k->K;
+  if (D != 256 && D != 512 && D != 1024 && D != 2048)
+    return failf(NRP_ERR_UNSUPPORTED, "d_model %d (the block needs 256, 512, 1024 or 2048)", D);
+  if (k->ff % 64) return failf(NRP_ERR_UNSUPPORTED, "ff_dim %d not a multiple of 64", k->ff);
+  if (B > 256) return failf(NRP_ERR_UNSUPPORTED, "the streaming block supports batch <= 256");
+  if (nrp::select_device(k->ctx)) return NRP_ERR_CUDA;
+  int rc = sync_block(k);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t M = static_cast<int64_t>(B) * T;
+  const int Tc = K - 1 + T;  // the conv cache, then the chunk
+  const int64_t Mc = static_cast<int64_t>(B) * Tc;
+  if (Mc > INT32_MAX / 4) return failf(NRP_ERR_UNSUPPORTED, "batch x seq_len too large");
+  const int Mi = static_cast<int>(M);
+  valid = std::min(std::max(valid, 0), T);
+  TRY_CUDA(k->h.ensure(M * D * 2));
+  TRY_CUDA(k->hid.ensure(M * k->ff * 2));
+  TRY_CUDA(k->glu.ensure(Mc * D * 2));
+  TRY_CUDA(k->dw.ensure(Mc * D * 2));
+  TRY_CUDA(k->vbuf.ensure(static_cast<size_t>(B) * 4));
+  if (out != x) {
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(cudaMemcpyAsync(out, x, M * D * 2, cudaMemcpyDeviceToDevice, st));
+  }
+  auto residual = [&](float alpha) {
+    nrp::Epilogue e;
+    e.mode = nrp::kEpiResidual;
+    e.res = static_cast<const __nv_bfloat16*>(out);
+    e.ldr = D;
+    e.alpha = alpha;
+    return e;
+  };
+  nrp::Epilogue silu;
+  silu.mode = nrp::kEpiSilu;
+  const nrp::RowTiling flat;
+  auto feed_forward = [&](int norm, int l1, int l2) -> int {
+    int r = layer_norm(k, st, norm, out, k->h.p, M);
+    if (!r) r = block_linear(k, st, l1, k->h.p, Mi, k->hid.p, k->ff, flat, silu);
+    if (!r) r = block_linear(k, st, l2, k->hid.p, Mi, out, D, flat, residual(0.5f));
+    return r;
+  };
+  // 1916-1923: x += 0.5 * FF1(LN x)
+  rc = feed_forward(NRP_BLOCK_NORM_FF1, NRP_BLOCK_FF1_LINEAR1, NRP_BLOCK_FF1_LINEAR2);
+  if (rc) return rc;
+  // 1925-1935: x += MHA(LN x) against the attention cache
+  rc = layer_norm(k, st, NRP_BLOCK_NORM_ATT, out, k->h.p, M);
+  if (rc) return rc;
+  rc = nrp::attn_forward_with_cache(k->attn, st, k->h.p, B, T, pos_emb, attn_cache, filled, valid,
+                                    context, out, residual(1.f));
+  if (rc) return rc;
+  // 1943-1948, 2332-2400: x += Conv(LN x) with the conv cache.  The GLU
+  // output of the chunk goes after each utterance's K-1 cached frames
+  // (frames >= valid zeroed: the pad mask, 929-941); the depthwise conv runs
+  // over [cache | chunk] and its last T outputs feed pointwise_conv2; the
+  // new cache is the last K-1 frames of [cache | chunk].
+  rc = layer_norm(k, st, NRP_BLOCK_NORM_CONV, out, k->h.p, M);
+  if (rc) return rc;
+  auto* glu = k->glu.as<__nv_bfloat16>();
+  {
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(nrp::launch_fill_i32(k->vbuf.as<int32_t>(), valid, B, st));
+  }
+  nrp::RowTiling grows;
+  grows.len = k->vbuf.as<int32_t>();
+  grows.T = T;
+  grows.B = B;
+  grows.y_bstride = static_cast<int64_t>(Tc) * D;
+  nrp::Epilogue gl;
+  gl.mode = nrp::kEpiGlu;
+  gl.len = grows.len;
+  rc = block_linear(k, st, NRP_BLOCK_CONV_PW1, k->h.p, Mi, glu + static_cast<size_t>(K - 1) * D, D,
+                    grows, gl);
+  if (rc) return rc;
+  if (K > 1) {
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    const size_t row = static_cast<size_t>(D) * 2;
+    TRY_CUDA(cudaMemcpy2DAsync(glu, Tc * row, conv_cache, (K - 1) * row, (K - 1) * row, B,
+                               cudaMemcpyDeviceToDevice, st));
+    TRY_CUDA(cudaMemcpy2DAsync(conv_cache, (K - 1) * row, glu + static_cast<size_t>(T) * D, Tc * row,
+                               (K - 1) * row, B, cudaMemcpyDeviceToDevice, st));
+  }
+  {
+    const bool bn = k->conv_norm == 0;
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_DWCONV, st);
+    // causal over the Tc rows: output row K-1+t reads rows t .. t+K-1 only
+    TRY_CUDA(nrp::launch_dwconv(glu, k->d_dw_w.as<float>(),
+                                k->dw_b.empty() ? nullptr : k->d_dw_b.as<float>(),
+                                bn ? k->d_cn_scale.as<float>() : nullptr,
+                                bn ? k->d_cn_shift.as<float>() : nullptr,
+                                k->dw.as<__nv_bfloat16>(), B, Tc, D, K, true, bn, st));
+  }
+  if (k->conv_norm == 1) {
+    nrp::ProfScope ps(k->ctx, NRP_KERNEL_LAYERNORM, st);
+    TRY_CUDA(nrp::launch_layernorm(k->dw.as<__nv_bfloat16>(), k->d_cn_g.as<float>(),
+                                   k->d_cn_b.as<float>(), k->dw.as<__nv_bfloat16>(), Mc, D, 1e-5f,
+                                   true, st));
+  }
+  nrp::RowTiling drows;
+  drows.T = T;
+  drows.B = B;
+  drows.x_bstride = static_cast<int64_t>(Tc) * D;
+  rc = block_linear(k, st, NRP_BLOCK_CONV_PW2,
+                    k->dw.as<__nv_bfloat16>() + static_cast<size_t>(K - 1) * D, Mi, out, D, drows,
+                    residual(1.f));
+  if (rc) return rc;
+  // 1952-1958: x += 0.5 * FF2(LN x)
+  rc = feed_forward(NRP_BLOCK_NORM_FF2, NRP_BLOCK_FF2_LINEAR1, NRP_BLOCK_FF2_LINEAR2);
+  if (rc) return rc;
+  // 1961: final LayerNorm
+  return layer_norm(k, st, NRP_BLOCK_NORM_OUT, out, out, M);
+}
+
 // ---------------------------------------------------------------- encoder
 int nrp_encoder_create(nrp_context* ctx, int n_layers, int d_model, int n_heads, int ff_dim,
                        int conv_kernel, int causal_conv, int conv_norm, int use_bias,
@@ -525,6 +649,7 @@ int nrp_encoder_destroy(nrp_encoder* e) {
   for (nrp_block* b : e->blocks) nrp_block_destroy(b);
   nrp_subsampling_destroy(e->sub);
   delete e;
+  (void)cudaGetLastError();
   return NRP_OK;
 }
 

@@ -342,6 +342,20 @@ cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stre
   return cudaGetLastError();
 }
 
+namespace {
+__global__ void fill_i32_kernel(int32_t* p, int v, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+}  // namespace
+
+cudaError_t launch_fill_i32(int32_t* p, int v, int n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  return launch_pdl(fill_i32_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, p, v, n);
+}
+
 cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D,
                                  cudaStream_t stream) {
   if (B <= 0 || T <= 0) return cudaSuccess;

@@ -71,6 +71,9 @@ struct RowTiling {
   // means T * ldy (utterances stacked).  A time-major output [T][B][N] is
   // ldy = B * N, y_bstride = N.  Rows t >= T are never written.
   int64_t y_bstride = 0;
+  // Input rows of utterance b start at x + b * x_bstride (elements, a
+  // multiple of 8); 0 means T * K.
+  int64_t x_bstride = 0;
 };
 
 // What the GEMM epilogue does with v = acc + bias (f32) before the single
@@ -235,6 +238,8 @@ cudaError_t launch_dwconv(const __nv_bfloat16* x, const float* wt, const float* 
 cudaError_t launch_scale(__nv_bfloat16* x, int64_t n, float s, cudaStream_t stream);
 cudaError_t launch_transpose_btd(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D,
                                  cudaStream_t stream);
+// p[0 .. n) = v
+cudaError_t launch_fill_i32(int32_t* p, int v, int n, cudaStream_t stream);
 
 // ---- dw_striding subsampling convolutions (subsampling_kernels.cu) ----
 // conv.0 (1 -> C, 3x3, stride 2, + bias, ReLU) of f32 mel frames, optionally

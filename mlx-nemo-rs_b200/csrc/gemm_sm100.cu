@@ -118,20 +118,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = K / kBK;
   int* live_pre = reinterpret_cast<int*>(sE + kEpiBytes + sizeof(GemmSmem));  // [B+1]
-  int live_m = tiles_m;
-  if (batched && rt.len) {
-    if (threadIdx.x == 0) {
-      int acc = 0;
-      for (int b = 0; b < rt.B; ++b) {
-        live_pre[b] = acc;
-        const int L = rt.len[b];
-        acc += L <= 0 ? 0 : min(tpb, (L + kBM - 1) / kBM);
-      }
-      live_pre[rt.B] = acc;
-    }
-    __syncthreads();
-    live_m = live_pre[rt.B];
-  }
+  int live_m = tiles_m;  // (set from the lengths after pdl_wait below)
   // list index -> (first row of the tile, its utterance); true = zero-fill tile
   auto tile_rows = [&](int tile, int& r0, int& bb) -> bool {
     const int tm = tile / tiles_n;
@@ -189,6 +176,21 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   volatile int* abort_flag = &ss->abort;
   pdl_launch_dependents();
   pdl_wait();
+  // the lengths may come from the previous kernel in the stream: read them
+  // only after its grid is complete
+  if (batched && rt.len) {
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int b = 0; b < rt.B; ++b) {
+        live_pre[b] = acc;
+        const int L = rt.len[b];
+        acc += L <= 0 ? 0 : min(tpb, (L + kBM - 1) / kBM);
+      }
+      live_pre[rt.B] = acc;
+    }
+    __syncthreads();
+    live_m = live_pre[rt.B];
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer

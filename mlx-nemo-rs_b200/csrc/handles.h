@@ -91,6 +91,7 @@ struct nrp_context {
 
 struct nrp_attn {
   nrp_context* ctx = nullptr;
+  int device = 0;  // ctx->device, kept for teardown
   int D = 0, H = 0, dh = 0;
   int use_bias = 1;
   int dtype = NRP_DTYPE_F32;
@@ -117,6 +118,7 @@ struct nrp_attn {
 
 struct nrp_cache {
   nrp_attn* attn = nullptr;
+  int device = 0;  // attn's device, kept for teardown
   int B = 0, C = 0, D = 0, dtype = 0;
   int head = 0;  // ring slot of the oldest frame
   nrp::DevBuf kc, vc, hc;

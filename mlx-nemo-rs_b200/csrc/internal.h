@@ -83,6 +83,11 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
                  const int32_t* lengths, const nrp_att_context* context, void* out,
                  const Epilogue& out_ep);
 
+// nrp_attn_forward_with_cache with `out_ep` as the epilogue of linear_out.
+int attn_forward_with_cache(nrp_attn* a, cudaStream_t st, const void* x, int B, int T,
+                            const void* pos_emb, nrp_cache* c, int filled, int valid,
+                            const nrp_att_context* context, void* out, const Epilogue& out_ep);
+
 // Makes the context's device current.
 int select_device(nrp_context* ctx);
 

@@ -64,7 +64,10 @@ int scratch_address(int device, void** out) {
 #define TRY_CUDA(expr)                                                         \
   do {                                                                         \
     const cudaError_t e_ = (expr);                                             \
-    if (e_ != cudaSuccess) return nrp::report_error(NRP_ERR_CUDA, cudaGetErrorString(e_)); \
+    if (e_ != cudaSuccess) {                                                   \
+      (void)cudaGetLastError();                                                \
+      return nrp::report_error(NRP_ERR_CUDA, cudaGetErrorString(e_));          \
+    }                                                                          \
   } while (0)
 
 // y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias), as nrp_attn_forward runs
@@ -79,7 +82,7 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
                                   st));
     return NRP_OK;
   }
-  if (quant && M <= 16) {
+  if (quant && M <= 16 && K % 512 == 0) {
     TRY_CUDA(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
                                static_cast<const uint8_t*>(w),
                                static_cast<const __nv_bfloat16*>(qs),

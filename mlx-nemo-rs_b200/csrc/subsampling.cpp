@@ -32,11 +32,13 @@ namespace {
 
 using nrp::failf;
 
-#define TRY_CUDA(expr)                                                            \
-  do {                                                                            \
-    const cudaError_t e_ = (expr);                                                \
-    if (e_ != cudaSuccess)                                                        \
+#define TRY_CUDA(expr)                                                        \
+  do {                                                                        \
+    const cudaError_t e_ = (expr);                                            \
+    if (e_ != cudaSuccess) {                                                  \
+      (void)cudaGetLastError(); /* not left for later launch checks */        \
       return failf(NRP_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_)); \
+    }                                                                         \
   } while (0)
 
 constexpr int kMaxStrides = 3;

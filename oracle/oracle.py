@@ -95,6 +95,10 @@ def lib():
         L.orc_subsampling_forward.argtypes = [_f32p] + [C.c_int] * 7 + [C.c_void_p, C.c_int,
                                                                          _f32p]
         L.orc_subsampling_forward.restype = C.c_int
+        L.orc_stream_block_step.argtypes = (
+            [_f32p] + [C.c_int] * 7 + [C.c_void_p, _f32p, _f32p, C.c_int, _f32p] +
+            [C.c_int] * 7 + [_f32p])
+        L.orc_stream_block_step.restype = C.c_int
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _LIB = L
@@ -280,19 +284,7 @@ BLOCK_LINEARS = ("ff1_1", "ff1_2", "pw1", "pw2", "ff2_1", "ff2_2")
 BLOCK_NORMS = ("ff1", "att", "conv", "ff2", "out")
 
 
-def block_forward(x, bw, pos_emb, n_heads, ff_dim, kernel, causal=False, conv_norm=0,
-                  lengths=None, context=None, bf16=True):
-    """ConformerBlock::forward (conformer.rs:1693-1870).
-
-    bw: {"ff1_1": (w, b), ... (BLOCK_LINEARS, f32 weights [out, in]; a
-    quantised layer gives its dequantised weights), "dw": (w [D, K], b),
-    "conv_norm": (gamma, beta, mean, var) (mean/var None for a layer norm),
-    "norms": {name: (gamma, beta)} for BLOCK_NORMS, "attn": the mha_forward
-    weight dict}."""
-    x = _f32(x)
-    B, T, D = x.shape
-    keep = []
-
+def _block_struct(bw, D, kernel, keep):
     def ptr(a):
         if a is None:
             return None
@@ -311,6 +303,44 @@ def block_forward(x, bw, pos_emb, n_heads, ff_dim, kernel, causal=False, conv_no
         st.norm_g[i] = ptr(bw["norms"][name][0])
         st.norm_b[i] = ptr(bw["norms"][name][1])
     st.attn = _weights_struct(bw["attn"], keep)
+    return st
+
+
+def stream_block_step(x, bw, pos_emb, n_heads, ff_dim, kernel, h_cache, conv_cache, filled,
+                      valid, left=-1, right=-1, chunked=False, cache_drop_size=0, conv_norm=0,
+                      bf16=True):
+    """ConformerBlock::forward_with_cache (conformer.rs:1877-1967) as
+    forward_streaming drives it.  h_cache [B,C,D] and conv_cache [B,K-1,D]
+    (f32, C-contiguous) are updated in place; returns (out, next_filled)."""
+    x = _f32(x)
+    B, T, D = x.shape
+    assert h_cache.dtype == np.float32 and h_cache.flags["C_CONTIGUOUS"]
+    assert conv_cache.dtype == np.float32 and conv_cache.flags["C_CONTIGUOUS"]
+    assert conv_cache.shape == (B, kernel - 1, D)
+    keep = []
+    st = _block_struct(bw, D, kernel, keep)
+    out = np.empty_like(x)
+    nxt = lib().orc_stream_block_step(
+        x, B, T, D, n_heads, ff_dim, kernel, int(conv_norm), C.byref(st), _f32(pos_emb),
+        h_cache, h_cache.shape[1], conv_cache, filled, valid, left, right, int(bool(chunked)),
+        cache_drop_size, int(bool(bf16)), out)
+    assert nxt >= 0
+    return out, nxt
+
+
+def block_forward(x, bw, pos_emb, n_heads, ff_dim, kernel, causal=False, conv_norm=0,
+                  lengths=None, context=None, bf16=True):
+    """ConformerBlock::forward (conformer.rs:1693-1870).
+
+    bw: {"ff1_1": (w, b), ... (BLOCK_LINEARS, f32 weights [out, in]; a
+    quantised layer gives its dequantised weights), "dw": (w [D, K], b),
+    "conv_norm": (gamma, beta, mean, var) (mean/var None for a layer norm),
+    "norms": {name: (gamma, beta)} for BLOCK_NORMS, "attn": the mha_forward
+    weight dict}."""
+    x = _f32(x)
+    B, T, D = x.shape
+    keep = []
+    st = _block_struct(bw, D, kernel, keep)
     ln = np.ascontiguousarray(lengths, np.int32) if lengths is not None else None
     cs = _ctx_struct(context)
     out = np.empty_like(x)

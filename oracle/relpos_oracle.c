@@ -934,3 +934,111 @@ int orc_subsampling_forward(const float *x, int B, int T, int F, int C, int fact
   free(flat);
   return 0;
 }
+
+/* ------------------------------------------- streaming Conformer block */
+
+/* ConformerBlock::forward_with_cache (conformer.rs:1877-1967) as
+ * ConformerEncoder::forward_streaming drives it (883-1000): FF1 half step;
+ * the attention on LN(x) through orc_stream_layer_step (mask from the
+ * first stream's fill level and valid length, ring slide and re-pad of
+ * h_cache [B,C,D] in place); ConvolutionModule::forward_with_cache
+ * (2332-2400): pointwise_conv1 + GLU, frames t >= valid zeroed (the pad mask,
+ * 929-941), concatenated after conv_cache [B,K-1,D] (time-major here; the
+ * reference keeps [B,D,K-1]), the new conv cache = the last K-1 frames of
+ * the concatenation, the depthwise conv over it without padding (T outputs),
+ * the conv norm, SiLU, pointwise_conv2; FF2 half step; final LayerNorm.
+ * Rounding as orc_block_forward.  Returns the next fill level. */
+int orc_stream_block_step(const float *x, int B, int T, int D, int H, int ff, int K,
+                          int conv_norm, const orc_block_weights *w, const float *pos_emb,
+                          float *h_cache, int C, float *conv_cache, int filled, int valid,
+                          int left, int right, int chunked, int cache_drop_size, int bf16,
+                          float *out) {
+  if (B <= 0 || T <= 0 || D <= 0 || H <= 0 || D % H || ff <= 0 || K <= 0) return -1;
+  const int64_t M = (int64_t)B * T;
+  const size_t n = (size_t)M * D;
+  float *ng[5], *nb[5];
+  for (int i = 0; i < 5; ++i) {
+    ng[i] = dup_round(w->norm_g[i], D, bf16);
+    nb[i] = dup_round(w->norm_b[i], D, bf16);
+  }
+  const orc_lin *src[6] = {&w->ff1_1, &w->ff1_2, &w->pw1, &w->pw2, &w->ff2_1, &w->ff2_2};
+  const int lin_n[6] = {ff, D, 2 * D, D, ff, D}, lin_k[6] = {D, ff, D, D, D, ff};
+  orc_lin L[6];
+  for (int i = 0; i < 6; ++i) {
+    L[i].w = dup_round(src[i]->w, (size_t)lin_n[i] * lin_k[i], bf16);
+    L[i].b = dup_round(src[i]->b, (size_t)lin_n[i], bf16);
+  }
+  float *dw_w = dup_round(w->dw_w, (size_t)D * K, bf16);
+  float *dw_b = dup_round(w->dw_b, D, bf16);
+  float *cn_g = dup_round(w->cn_g, D, bf16), *cn_b = dup_round(w->cn_b, D, bf16);
+  float *cn_m = conv_norm == 0 ? dup_round(w->cn_m, D, bf16) : NULL;
+  float *cn_v = conv_norm == 0 ? dup_round(w->cn_v, D, bf16) : NULL;
+  const float eps = rnd(1e-5f, bf16);
+  if (valid > T) valid = T;
+  if (valid < 0) valid = 0;
+
+  float *xx = dup_round(x, n, bf16);
+  float *h = (float *)malloc(sizeof(float) * n);
+  float *tmp = (float *)malloc(sizeof(float) * n);
+  float *hid = (float *)malloc(sizeof(float) * (size_t)M * (ff > 2 * D ? ff : 2 * D));
+  const int Tc = K - 1 + T;
+  float *cat = (float *)malloc(sizeof(float) * (size_t)B * Tc * D);
+
+  ff_residual(xx, M, D, ff, &L[0], &L[1], ng[0], nb[0], bf16, h, hid, tmp);
+  /* x += MHA(LN x) with the cache */
+  layer_norm_r(xx, M, D, ng[1], nb[1], bf16, h);
+  const int next = orc_stream_layer_step(h, B, T, D, H, &w->attn, pos_emb, h_cache, C, filled,
+                                         valid, left, right, chunked, cache_drop_size, bf16, tmp);
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < (int64_t)n; ++e) xx[e] = rnd(xx[e] + tmp[e], bf16);
+  /* x += Conv(LN x) with the cache */
+  layer_norm_r(xx, M, D, ng[2], nb[2], bf16, h);
+  linear_r(h, (int)M, D, L[2].w, 2 * D, L[2].b, bf16, hid);
+  for (int b = 0; b < B; ++b) {
+    memcpy(cat + (size_t)b * Tc * D, conv_cache + (size_t)b * (K - 1) * D,
+           sizeof(float) * (size_t)(K - 1) * D);
+    for (int t = 0; t < T; ++t)
+      for (int c = 0; c < D; ++c) {
+        const int64_t r = (int64_t)b * T + t;
+        const float a = hid[r * 2 * D + c], g = hid[r * 2 * D + D + c];
+        const float v = rnd(a * rnd(sigm(g), bf16), bf16);
+        cat[((size_t)b * Tc + K - 1 + t) * D + c] = t < valid ? v : 0.0f;
+      }
+    memcpy(conv_cache + (size_t)b * (K - 1) * D, cat + ((size_t)b * Tc + T) * D,
+           sizeof(float) * (size_t)(K - 1) * D);
+  }
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int b = 0; b < B; ++b)
+    for (int t = 0; t < T; ++t)
+      for (int c = 0; c < D; ++c) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k)
+          acc += dw_w[(size_t)c * K + k] * cat[((size_t)b * Tc + t + k) * D + c];
+        if (dw_b) acc = rnd(acc, bf16) + dw_b[c];
+        h[((size_t)b * T + t) * D + c] = rnd(acc, bf16);
+      }
+  if (conv_norm == 0) {
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < (int64_t)n; ++e) {
+      const int c = (int)(e % D);
+      const float xm = rnd(h[e] - cn_m[c], bf16);
+      const float inv = rnd(1.0f / sqrtf(rnd(cn_v[c] + eps, bf16)), bf16);
+      const float nv = rnd(xm * inv, bf16);
+      h[e] = rnd(rnd(nv * cn_g[c], bf16) + cn_b[c], bf16);
+    }
+  } else {
+    layer_norm_r(h, M, D, cn_g, cn_b, bf16, h);
+  }
+  silu_r(h, (int64_t)n, bf16);
+  linear_r(h, (int)M, D, L[3].w, D, L[3].b, bf16, tmp);
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < (int64_t)n; ++e) xx[e] = rnd(xx[e] + tmp[e], bf16);
+  ff_residual(xx, M, D, ff, &L[4], &L[5], ng[3], nb[3], bf16, h, hid, tmp);
+  layer_norm_r(xx, M, D, ng[4], nb[4], bf16, out);
+
+  free(xx); free(h); free(tmp); free(hid); free(cat);
+  for (int i = 0; i < 5; ++i) { free(ng[i]); free(nb[i]); }
+  for (int i = 0; i < 6; ++i) { free((void *)L[i].w); free((void *)L[i].b); }
+  free(dw_w); free(dw_b); free(cn_g); free(cn_b); free(cn_m); free(cn_v);
+  return next;
+}

@@ -182,6 +182,19 @@ int orc_subsampling_forward(const float *x, int B, int T, int F, int C, int fact
                             int causal, int d_model, const orc_subsampling_weights *w,
                             int bf16, float *out);
 
+/* One streaming step of a ConformerBlock (forward_with_cache, conformer.rs:
+ * 1877-1967, with ConvolutionModule::forward_with_cache 2332-2400) as
+ * forward_streaming drives it: h_cache [B,C,D] (the attention input ring,
+ * as orc_stream_layer_step) and conv_cache [B,K-1,D] (time-major; the last
+ * K-1 GLU frames) are updated in place; frames t >= valid are zeroed before
+ * the depthwise conv.  x, out [B,T,D]; pos_emb [2(C+T)-1, D].  Returns the
+ * next fill level. */
+int orc_stream_block_step(const float *x, int B, int T, int D, int H, int ff, int K,
+                          int conv_norm, const orc_block_weights *w, const float *pos_emb,
+                          float *h_cache, int C, float *conv_cache, int filled, int valid,
+                          int left, int right, int chunked, int cache_drop_size, int bf16,
+                          float *out);
+
 /* bfloat16 round-to-nearest-even of a float (what an MLX astype does). */
 float orc_bf16_round(float x);
 void orc_bf16_round_array(float *x, int64_t n);
