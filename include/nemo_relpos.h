@@ -372,6 +372,14 @@ int nrp_block_forward_with_cache(nrp_block* block, void* stream, const void* x, 
                                  void* conv_cache, int filled, int valid,
                                  const nrp_att_context* context, void* out);
 
+/* EncoderCache on the device (streaming/core.rs:117-185) for an encoder's
+ * forward_streaming: per layer the attention's K/V/h ring of cache_len
+ * frames (last_channel) and the conv cache [batch, conv_kernel-1, d_model]
+ * bf16 (last_time, time-major), and the fill level the streams share
+ * (last_channel_len: forward_streaming reads the first stream's,
+ * conformer.rs:853-857).  Make it after nrp_encoder_set_dtype(BF16). */
+typedef struct nrp_encoder_cache nrp_encoder_cache;
+
 /* ConformerEncoder::forward_from_embeddings (conformer.rs:694-722) over
  * n_layers blocks: x * xscale (sqrt(d_model) when xscaling), the positional
  * table of RelPositionalEncoding(d_model, max_len) for seq_len, every block,
@@ -404,6 +412,38 @@ int nrp_encoder_add_subsampling(nrp_encoder* enc, int feat_in, int subsampling_f
 int nrp_encoder_forward(nrp_encoder* enc, void* stream, const float* features, int batch,
                         int frames, const int32_t* lengths, const nrp_att_context* context,
                         void* out, int32_t* out_lengths);
+int nrp_encoder_cache_create(nrp_encoder* enc, int batch, int cache_len,
+                             nrp_encoder_cache** out);
+int nrp_encoder_cache_destroy(nrp_encoder_cache* cache);
+/* zeros every cache (NeMo starts a stream with zeros), fill level 0 */
+int nrp_encoder_cache_reset(nrp_encoder_cache* cache, void* stream);
+int nrp_encoder_cache_get_filled(const nrp_encoder_cache* cache, int* filled);
+int nrp_encoder_cache_set_filled(nrp_encoder_cache* cache, int filled);
+/* layer's attention ring (export/import its h with nrp_cache_export_h /
+ * nrp_cache_import_h) and its conv cache (device pointer); either out
+ * pointer may be NULL */
+int nrp_encoder_cache_layer(nrp_encoder_cache* cache, int layer, nrp_cache** attn_cache,
+                            void** conv_cache);
+/* copies a layer's conv cache to (to_cache = 0) or from (1) device data
+ * bf16 [batch, conv_kernel-1, d_model] */
+int nrp_encoder_cache_copy_conv(nrp_encoder_cache* cache, int layer, void* data, int to_cache,
+                                void* stream);
+/* ConformerEncoder::forward_streaming (conformer.rs:840-1047): features
+ * device f32 [batch, feat_in, frames] (a chunk with its pre-encode cache
+ * frames in front, as the caller builds it); the subsampling (no mel mask
+ * on this path), the first drop_extra_pre_encoded output frames dropped,
+ * x * xscale, every block's forward_with_cache against `cache` with the
+ * first stream's fill level and valid length (subsampled lengths[0] less
+ * the drop; lengths host int32 [batch] mel frames, or NULL: all frames),
+ * the transpose; the fill level advances by the frames kept.  out device
+ * [batch, d_model, T] bf16 with T = nrp_subsampling_output_length(frames)
+ * - drop_extra_pre_encoded; out_lengths host int32 [batch] (subsampled
+ * lengths less the drop) and out_frames (T) may be NULL. */
+int nrp_encoder_forward_streaming(nrp_encoder* enc, void* stream, const float* features,
+                                  int batch, int frames, const int32_t* lengths,
+                                  nrp_encoder_cache* cache, int drop_extra_pre_encoded,
+                                  const nrp_att_context* context, void* out,
+                                  int32_t* out_lengths, int* out_frames);
 
 /* ------------------------------------------ dw_striding subsampling */
 /* Subsampling (src/asr/modules/encoders/conformer.rs:1058-1588), the

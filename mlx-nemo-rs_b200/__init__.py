@@ -129,13 +129,21 @@ def lib():
             "nrp_block_load_depthwise": ([vp, vp, vp], i),
             "nrp_block_load_conv_norm": ([vp, vp, vp, vp, vp], i),
             "nrp_block_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
-            "nrp_block_forward_with_cache": ([vp, vp, vp, i, i, vp, vp, vp, i, i, vp, vp], i),
             "nrp_encoder_create": ([vp] + [i] * 10 + [vp], i),
             "nrp_encoder_destroy": ([vp], i),
             "nrp_encoder_block": ([vp, i, vp], i),
             "nrp_encoder_set_dtype": ([vp, i], i),
             "nrp_encoder_forward_from_embeddings": ([vp, vp, vp, i, i, vp, vp, vp], i),
             "nrp_encoder_add_subsampling": ([vp, i, i, i, i, vp], i),
+            "nrp_block_forward_with_cache": ([vp, vp, vp, i, i, vp, vp, vp, i, i, vp, vp], i),
+            "nrp_encoder_cache_create": ([vp, i, i, vp], i),
+            "nrp_encoder_cache_destroy": ([vp], i),
+            "nrp_encoder_cache_reset": ([vp, vp], i),
+            "nrp_encoder_cache_get_filled": ([vp, vp], i),
+            "nrp_encoder_cache_set_filled": ([vp, i], i),
+            "nrp_encoder_cache_layer": ([vp, i, vp, vp], i),
+            "nrp_encoder_cache_copy_conv": ([vp, i, vp, i, vp], i),
+            "nrp_encoder_forward_streaming": ([vp, vp, vp, i, i, vp, vp, i, vp, vp, vp, vp], i),
             "nrp_encoder_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
             "nrp_subsampling_create": ([vp, i, i, i, i, i, vp], i),
             "nrp_subsampling_destroy": ([vp], i),
@@ -894,6 +902,37 @@ class ConformerEncoder:
             C.byref(c) if c is not None else None, out.data_ptr()))
         return out, lengths
 
+    def new_stream_cache(self, batch: int, cache_len: int) -> EncoderStreamCache:
+        """Device caches for forward_streaming (after set_dtype(BF16))."""
+        return EncoderStreamCache(self, batch, cache_len)
+
+    def forward_streaming(self, features, lengths, cache: EncoderStreamCache,
+                          drop_extra_pre_encoded: int = 0,
+                          context: Optional[AttentionContext] = None, out=None):
+        """ConformerEncoder::forward_streaming (conformer.rs:840-1047):
+        features device f32 [B, feat_in, frames] (the chunk with its
+        pre-encode cache frames in front); lengths host int32 [B] or None.
+        Returns ([B, D, T] bf16, output lengths int32 [B]); cache.filled
+        advances."""
+        import torch
+        if self.subsampling is None:
+            raise NrpError(NRP_ERR_INVALID, "the encoder was built without feat_in")
+        B, F, T = features.shape
+        assert features.dtype == torch.float32 and features.is_contiguous()
+        Tp = self.subsampling.output_length(T) - drop_extra_pre_encoded
+        if out is None:
+            out = torch.empty((B, self.d_model, Tp), dtype=torch.bfloat16,
+                              device=features.device)
+        ln = np.ascontiguousarray(lengths, np.int32) if lengths is not None else None
+        out_len = np.empty(B, np.int32)
+        c = context._c() if context is not None else None
+        _check(lib().nrp_encoder_forward_streaming(
+            self.handle, _stream(), features.data_ptr(), B, T,
+            ln.ctypes.data if ln is not None else None, cache.handle,
+            int(drop_extra_pre_encoded), C.byref(c) if c is not None else None, out.data_ptr(),
+            out_len.ctypes.data, None))
+        return out, out_len
+
     def forward(self, features, lengths=None, context: Optional[AttentionContext] = None,
                 out=None):
         """ConformerEncoder::forward (conformer.rs:475-560): features device
@@ -916,6 +955,73 @@ class ConformerEncoder:
             ln.ctypes.data if ln is not None else None, C.byref(c) if c is not None else None,
             out.data_ptr(), out_len.ctypes.data))
         return out, out_len
+
+
+class EncoderStreamCache:
+    """An encoder's streaming caches on the device (EncoderCache,
+    streaming/core.rs:117-185): per layer the attention ring and the conv
+    cache, and the shared fill level (last_channel_len)."""
+
+    def __init__(self, encoder: "ConformerEncoder", batch: int, cache_len: int):
+        h = C.c_void_p()
+        _check(lib().nrp_encoder_cache_create(encoder.handle, batch, cache_len, C.byref(h)))
+        self.handle = h
+        self.encoder = encoder
+        self.batch, self.cache_len = batch, cache_len
+        self.conv_kernel = encoder.layers[0].conv_kernel if encoder.layers else 1
+
+    def __del__(self):
+        try:
+            if self.handle:
+                lib().nrp_encoder_cache_destroy(self.handle)
+        except Exception:
+            pass
+
+    def reset(self):
+        _check(lib().nrp_encoder_cache_reset(self.handle, _stream()))
+
+    @property
+    def filled(self) -> int:
+        n = C.c_int()
+        _check(lib().nrp_encoder_cache_get_filled(self.handle, C.byref(n)))
+        return n.value
+
+    @filled.setter
+    def filled(self, v: int):
+        _check(lib().nrp_encoder_cache_set_filled(self.handle, int(v)))
+
+    def last_channel(self):
+        """[layers, B, C, D] f32 (oldest frame first), as EncoderCache.last_channel."""
+        import torch
+        outs = []
+        for i in range(len(self.encoder.layers)):
+            a = C.c_void_p()
+            _check(lib().nrp_encoder_cache_layer(self.handle, i, C.byref(a), None))
+            out = torch.empty((self.batch, self.cache_len, self.encoder.d_model),
+                              dtype=torch.float32, device="cuda")
+            _check(lib().nrp_cache_export_h(a, out.data_ptr(), _stream()))
+            outs.append(out)
+        return torch.stack(outs)
+
+    def last_time(self):
+        """[layers, B, D, conv_kernel - 1] f32, as EncoderCache.last_time."""
+        import torch
+        outs = []
+        for i in range(len(self.encoder.layers)):
+            buf = torch.empty((self.batch, self.conv_kernel - 1, self.encoder.d_model),
+                              dtype=torch.bfloat16, device="cuda")
+            _check(lib().nrp_encoder_cache_copy_conv(self.handle, i, buf.data_ptr(), 0,
+                                                     _stream()))
+            outs.append(buf.float().transpose(1, 2))
+        return torch.stack(outs)
+
+    def set_last_time(self, t):
+        """Load [layers, B, D, conv_kernel - 1] (EncoderCache.last_time)."""
+        import torch
+        for i in range(len(self.encoder.layers)):
+            buf = t[i].permute(0, 2, 1).to(torch.bfloat16).contiguous().cuda()
+            _check(lib().nrp_encoder_cache_copy_conv(self.handle, i, buf.data_ptr(), 1,
+                                                     _stream()))
 
 
 # ------------------------------------------- sequence split (several GPUs)

@@ -751,6 +751,8 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
 
 int attn_sync(nrp_attn* a) { return sync_params(a); }
 
+int attn_cache_drop(const nrp_attn* a) { return a->cache_drop; }
+
 int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
            const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
            void* y, int ldy, const RowTiling& rt, const Epilogue& ep) {

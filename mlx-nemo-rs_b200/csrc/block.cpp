@@ -111,6 +111,22 @@ struct nrp_encoder {
   nrp_subsampling* sub = nullptr;
   nrp::DevBuf lens;
   std::vector<int32_t> lens_host;
+  // forward_streaming: the subsampled chunk before the pre-encode frames
+  // are dropped, and the positional table of cache + chunk frames
+  nrp::DevBuf sx, spos;
+  int spos_T = -1;
+};
+
+// EncoderCache on the device (streaming/core.rs:117-185): per layer the
+// attention's ring (last_channel) and the conv cache [B][K-1][D] bf16
+// (last_time, time-major), and the fill level the streams share
+// (forward_streaming reads the first stream's, conformer.rs:853-857, 892).
+struct nrp_encoder_cache {
+  nrp_encoder* enc = nullptr;
+  int B = 0, C = 0, K = 0, D = 0;
+  int filled = 0;
+  std::vector<nrp_cache*> attn;
+  nrp::DevBuf conv;  // [layer][B][K-1][D]
 };
 
 namespace {
@@ -653,6 +669,95 @@ int nrp_encoder_destroy(nrp_encoder* e) {
   return NRP_OK;
 }
 
+int nrp_encoder_cache_create(nrp_encoder* e, int batch, int cache_len, nrp_encoder_cache** out) {
+  if (!e || !out) return failf(NRP_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (batch <= 0 || cache_len <= 0) return failf(NRP_ERR_INVALID, "invalid cache arguments");
+  if (e->dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_UNSUPPORTED, "set the encoder's dtype (bf16) before making its cache");
+  if (nrp::select_device(e->ctx)) return NRP_ERR_CUDA;
+  auto* c = new nrp_encoder_cache;
+  c->enc = e;
+  c->B = batch;
+  c->C = cache_len;
+  c->K = e->blocks.empty() ? 1 : e->blocks[0]->K;
+  c->D = e->D;
+  for (nrp_block* b : e->blocks) {
+    nrp_cache* ac = nullptr;
+    const int rc = nrp_cache_create(b->attn, batch, cache_len, &ac);
+    if (rc) {
+      nrp_encoder_cache_destroy(c);
+      return rc;
+    }
+    c->attn.push_back(ac);
+  }
+  const size_t bytes = e->blocks.size() * static_cast<size_t>(batch) * (c->K - 1) * c->D * 2;
+  if (c->conv.ensure(bytes) != cudaSuccess || cudaMemset(c->conv.p, 0, bytes ? bytes : 16)) {
+    (void)cudaGetLastError();
+    nrp_encoder_cache_destroy(c);
+    return failf(NRP_ERR_NOMEM, "encoder cache allocation failed");
+  }
+  *out = c;
+  return NRP_OK;
+}
+
+int nrp_encoder_cache_destroy(nrp_encoder_cache* c) {
+  if (!c) return NRP_OK;
+  for (nrp_cache* a : c->attn) nrp_cache_destroy(a);
+  delete c;
+  (void)cudaGetLastError();
+  return NRP_OK;
+}
+
+int nrp_encoder_cache_reset(nrp_encoder_cache* c, void* stream) {
+  if (!c) return failf(NRP_ERR_INVALID, "null cache");
+  for (nrp_cache* a : c->attn) {
+    const int rc = nrp_cache_reset(a, stream);
+    if (rc) return rc;
+  }
+  if (c->conv.bytes)
+    TRY_CUDA(cudaMemsetAsync(c->conv.p, 0, c->conv.bytes, static_cast<cudaStream_t>(stream)));
+  c->filled = 0;
+  return NRP_OK;
+}
+
+int nrp_encoder_cache_get_filled(const nrp_encoder_cache* c, int* filled) {
+  if (!c || !filled) return failf(NRP_ERR_INVALID, "null argument");
+  *filled = c->filled;
+  return NRP_OK;
+}
+
+int nrp_encoder_cache_set_filled(nrp_encoder_cache* c, int filled) {
+  if (!c) return failf(NRP_ERR_INVALID, "null cache");
+  c->filled = std::min(std::max(filled, 0), c->C);
+  return NRP_OK;
+}
+
+int nrp_encoder_cache_layer(nrp_encoder_cache* c, int layer, nrp_cache** attn_cache,
+                            void** conv_cache) {
+  if (!c) return failf(NRP_ERR_INVALID, "null cache");
+  if (layer < 0 || layer >= static_cast<int>(c->attn.size()))
+    return failf(NRP_ERR_INVALID, "layer %d of %d", layer, static_cast<int>(c->attn.size()));
+  if (attn_cache) *attn_cache = c->attn[layer];
+  if (conv_cache)
+    *conv_cache = c->conv.as<__nv_bfloat16>() +
+                  static_cast<size_t>(layer) * c->B * (c->K - 1) * c->D;
+  return NRP_OK;
+}
+
+int nrp_encoder_cache_copy_conv(nrp_encoder_cache* c, int layer, void* data, int to_cache,
+                                void* stream) {
+  if (!c || !data) return failf(NRP_ERR_INVALID, "null argument");
+  void* conv = nullptr;
+  const int rc = nrp_encoder_cache_layer(c, layer, nullptr, &conv);
+  if (rc) return rc;
+  const size_t bytes = static_cast<size_t>(c->B) * (c->K - 1) * c->D * 2;
+  if (bytes)
+    TRY_CUDA(cudaMemcpyAsync(to_cache ? conv : data, to_cache ? data : conv, bytes,
+                             cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+  return NRP_OK;
+}
+
 int nrp_encoder_block(nrp_encoder* e, int layer, nrp_block** block) {
   if (!e || !block) return failf(NRP_ERR_INVALID, "null argument");
   if (layer < 0 || layer >= static_cast<int>(e->blocks.size()))
@@ -826,6 +931,88 @@ int nrp_encoder_forward_from_embeddings(nrp_encoder* e, void* stream, const void
                              static_cast<cudaStream_t>(stream)));
   }
   return encoder_layers(e, stream, B, T, lengths, context, out);
+}
+
+int nrp_encoder_forward_streaming(nrp_encoder* e, void* stream, const float* features, int B,
+                                  int frames, const int32_t* lengths, nrp_encoder_cache* cache,
+                                  int drop_extra_pre_encoded, const nrp_att_context* context,
+                                  void* out, int32_t* out_lengths, int* out_frames) {
+  if (!e || !features || !cache || !out) return failf(NRP_ERR_INVALID, "null argument");
+  if (!e->sub) return failf(NRP_ERR_INVALID, "the encoder has no subsampling");
+  if (cache->enc != e) return failf(NRP_ERR_INVALID, "cache belongs to another encoder");
+  if (B != cache->B) return failf(NRP_ERR_INVALID, "batch %d does not match the cache", B);
+  if (B <= 0 || frames <= 0 || drop_extra_pre_encoded < 0)
+    return failf(NRP_ERR_INVALID, "empty input [%d, %d] or negative drop", B, frames);
+  const int Ts = nrp::subsampling_output_frames(e->sub, frames);
+  const int T = Ts - drop_extra_pre_encoded;  // 864-868
+  int rc = encoder_checks(e, B, T);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int D = e->D, C = cache->C;
+  const size_t row = static_cast<size_t>(D) * 2;
+  // 860-862: the conv stack over the chunk (no mel mask on this path)
+  void* sub_out = e->x.p;
+  TRY_CUDA(e->x.ensure(static_cast<size_t>(B) * T * row));
+  if (drop_extra_pre_encoded > 0) {
+    TRY_CUDA(e->sx.ensure(static_cast<size_t>(B) * Ts * row));
+    sub_out = e->sx.p;
+  } else {
+    sub_out = e->x.p;
+  }
+  const int64_t F = nrp::subsampling_feat_in(e->sub);
+  rc = nrp::subsampling_run(e->sub, st, features, F * frames, 1, frames, B, frames, nullptr,
+                            sub_out);
+  if (rc) return rc;
+  if (drop_extra_pre_encoded > 0) {
+    nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(cudaMemcpy2DAsync(e->x.p, T * row,
+                               static_cast<uint8_t*>(e->sx.p) + drop_extra_pre_encoded * row,
+                               Ts * row, T * row, B, cudaMemcpyDeviceToDevice, st));
+  }
+  // 869-876: subsampled lengths less the dropped frames
+  std::vector<int32_t> olen(B);
+  for (int b = 0; b < B; ++b) {
+    const int len = lengths ? std::max(lengths[b], 0) : frames;
+    olen[b] = std::max(nrp::subsampling_output_frames(e->sub, len) - drop_extra_pre_encoded, 0);
+  }
+  // 878-882: x * xscale
+  const int64_t n = static_cast<int64_t>(B) * T * D;
+  if (e->xscale != 1.f) {
+    nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(nrp::launch_scale(e->x.as<__nv_bfloat16>(), n, nrp::bf16_round(e->xscale), st));
+  }
+  // 884-892: the first stream's valid length and fill level; the positional
+  // table of cache + chunk frames
+  const int valid = std::min(olen[0], T);
+  const int filled = std::min(std::max(cache->filled, 0), C);
+  if (e->spos_T != C + T) {
+    TRY_CUDA(e->spos.ensure(static_cast<size_t>(2 * (C + T) - 1) * row));
+    rc = nrp_pe_encoding(e->ctx, D, e->max_len, C + T, NRP_DTYPE_BF16, e->spos.p, stream);
+    if (rc) return rc;
+    e->spos_T = C + T;
+  }
+  // 943-1000: every block with its caches
+  for (size_t i = 0; i < e->blocks.size(); ++i) {
+    void* conv = nullptr;
+    rc = nrp_encoder_cache_layer(cache, static_cast<int>(i), nullptr, &conv);
+    if (!rc)
+      rc = nrp_block_forward_with_cache(e->blocks[i], stream, e->x.p, B, T, e->spos.p,
+                                        cache->attn[i], conv, filled, valid, context, e->x.p);
+    if (rc) return rc;
+  }
+  // 1003-1004: [B, D, T]
+  {
+    nrp::ProfScope ps(e->ctx, NRP_KERNEL_ELEMENTWISE, st);
+    TRY_CUDA(nrp::launch_transpose_btd(e->x.as<__nv_bfloat16>(), static_cast<__nv_bfloat16*>(out),
+                                       B, T, D, st));
+  }
+  // 1020-1030: fill level += frames kept (T - cache_drop_size)
+  const int drop = e->blocks.empty() ? 0 : nrp::attn_cache_drop(e->blocks[0]->attn);
+  cache->filled = std::min(filled + std::max(T - drop, 0), C);
+  if (out_lengths)
+    for (int b = 0; b < B; ++b) out_lengths[b] = olen[b];
+  if (out_frames) *out_frames = T;
+  return NRP_OK;
 }
 
 int nrp_encoder_forward(nrp_encoder* e, void* stream, const float* features, int B, int frames,

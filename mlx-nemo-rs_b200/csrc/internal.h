@@ -88,6 +88,9 @@ int attn_forward_with_cache(nrp_attn* a, cudaStream_t st, const void* x, int B, 
                             const void* pos_emb, nrp_cache* c, int filled, int valid,
                             const nrp_att_context* context, void* out, const Epilogue& out_ep);
 
+// The module's cache_drop_size (nrp_attn_set_cache_drop_size).
+int attn_cache_drop(const nrp_attn* a);
+
 // Makes the context's device current.
 int select_device(nrp_context* ctx);
 
