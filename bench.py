@@ -256,11 +256,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="offline",
-                    choices=["offline", "long", "encoder", "stream", "single", "subsampling"],
+                    choices=["offline", "long", "encoder", "stream", "single", "subsampling",
+                             "stream_encoder"],
                     help="offline: BASELINE config 1 (the headline line); long: config 4, "
                          "the sequence split across the ranks; encoder: config 3; stream: "
                          "config 2; single: config 0; subsampling: the pre_encode of "
-                         "config 3's batch from mel frames")
+                         "config 3's batch from mel frames; stream_encoder: the whole "
+                         "streaming encoder step from mel chunks")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -274,6 +276,8 @@ def main():
         return main_single(args)
     if args.workload == "subsampling":
         return main_subsampling(args)
+    if args.workload == "stream_encoder":
+        return main_stream_encoder(args)
 
     import torch
     import torch.distributed as dist
@@ -479,6 +483,11 @@ SUB_LEN_LO, SUB_LEN_HI = 2000, 4000
 SUB_WORKLOAD = ("dw_striding subsampling (pre_encode): 8x, conv channels 256, feat_in 128, "
                 "d_model 1024, non-causal, bf16; mel [B=32, 128, 4000] f32 with lengths "
                 "U[2000,4000] masked (config 3's batch before subsampling)")
+STRENC_WORKLOAD = ("cache-aware streaming encoder step (forward_streaming): 64 sessions, "
+                   "112 mel frames per chunk (128 bins) -> causal 8x subsampling, 1 pre-encoded "
+                   "frame dropped -> 14 frames through 24 streaming blocks (config 3's layer, "
+                   "causal conv with its cache, 8-bit weights), attention cache 70, "
+                   "chunked_limited [70,13]; caches restart every 50 chunks")
 # one fp32 layer, batch 1, T=125
 SGL_T = 125
 SGL_WORKLOAD = ("BASELINE config 0: one rel-pos MHA layer, fp32, B=1 T=125 d_model=1024 "
@@ -616,18 +625,11 @@ def _dist_init(args):
     return world, rank, local
 
 
-def main_encoder(args):
-    """Config 3: forward_from_embeddings over 24 quantised blocks; weak
-    scaling (each rank its own 32-utterance batch)."""
-    import torch
-    import torch.distributed as dist
-    from __graft_entry__ import load_package
-    from oracle import oracle as orc  # quantiser of the synthetic checkpoint only
-    world, rank, local = _dist_init(args)
-    nrp = load_package()
-    ctx = nrp.Context(local)
-    rng = np.random.default_rng(5150 + rank)
-    enc = nrp.ConformerEncoder(ENC_LAYERS, D, H, ENC_FF, ENC_K, ctx=ctx)
+def _load_quant_layers(nrp, orc, enc, rng):
+    """Config 3's layer weights into every block of `enc`: all linears MLX
+    8-bit g64 from N(0, 0.02^2) masters with fp16 scales and biases, norms
+    1 + N(0, 0.02^2) / N(0, 0.02^2), BatchNorm affine, depthwise k = 9.
+    Returns the first two layers' (prefix, weights) for the CPU sample."""
     f = lambda *sh: (rng.standard_normal(sh, dtype=np.float32) * 0.02)
     shapes = {"feed_forward1.linear1": (ENC_FF, D), "feed_forward1.linear2": (D, ENC_FF),
               "conv.pointwise_conv1": (2 * D, D), "conv.pointwise_conv2": (D, D),
@@ -635,7 +637,7 @@ def main_encoder(args):
               "self_attn.linear_q": (D, D), "self_attn.linear_k": (D, D),
               "self_attn.linear_v": (D, D), "self_attn.linear_out": (D, D),
               "self_attn.linear_pos": (D, D)}
-    sample_layers = []  # the oracle's CPU sample: the first two layers' weights
+    sample_layers = []
     for i, blk in enumerate(enc.layers):
         wd = {}
         p = f"encoder.layers.{i}"
@@ -659,6 +661,22 @@ def main_encoder(args):
         blk.load_weights(wd, p, nrp.QuantizationConfig(8, 64))
         if i < 2:
             sample_layers.append((p, wd))
+    return sample_layers
+
+
+def main_encoder(args):
+    """Config 3: forward_from_embeddings over 24 quantised blocks; weak
+    scaling (each rank its own 32-utterance batch)."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    from oracle import oracle as orc  # quantiser of the synthetic checkpoint only
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(5150 + rank)
+    enc = nrp.ConformerEncoder(ENC_LAYERS, D, H, ENC_FF, ENC_K, ctx=ctx)
+    sample_layers = _load_quant_layers(nrp, orc, enc, rng)
     enc.set_dtype(nrp.BF16)
     dev = torch.device("cuda", local)
     x = rng.standard_normal((ENC_B, ENC_T, D), dtype=np.float32)
@@ -817,6 +835,122 @@ def main_subsampling(args):
               "encoder_frames": Tp, "conv_channels": C, "d_model": D,
               "parallelism": f"utterance-parallel replicas x{world}"},
              "weak", e2e, "bf16", cpu=cpu, hbm_bytes=bytes_)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main_stream_encoder(args):
+    """The whole cache-aware streaming encoder step (forward_streaming): 64
+    sessions, a chunk of 112 mel frames (14 encoder frames after causal 8x
+    subsampling and the one pre-encoded frame dropped) through the
+    subsampling and 24 streaming blocks (8-bit weights, conv caches, 70-frame
+    attention caches, chunked_limited [70, 13]); the caches restart every 50
+    chunks; weak scaling (each rank its own sessions)."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    from oracle import oracle as orc  # quantiser of the synthetic checkpoint only
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    rng = np.random.default_rng(4242 + rank)
+    enc = nrp.ConformerEncoder(ENC_LAYERS, D, H, ENC_FF, ENC_K, causal_conv=True, ctx=ctx,
+                               feat_in=SUB_F, subsampling_factor=8,
+                               subsampling_conv_channels=SUB_C, causal_downsampling=True)
+    sample_layers = _load_quant_layers(nrp, orc, enc, rng)
+    f = lambda sd, *sh: (rng.standard_normal(sh, dtype=np.float32) * sd)
+    sub = enc.subsampling
+    Fp = sub.feat_out
+    sub.set_conv(0, f(0.3, SUB_C, 3, 3, 1), f(0.1, SUB_C))
+    for i in range(2):
+        sub.set_conv(2 + 3 * i, f(0.3, SUB_C, 3, 3, 1), f(0.1, SUB_C))
+        sub.set_conv(3 + 3 * i, f(1 / 16, SUB_C, 1, 1, SUB_C), f(0.1, SUB_C))
+    sub.set_out(nrp.LinearLayer.standard(f(1 / math.sqrt(SUB_C * Fp), D, SUB_C * Fp), f(0.1, D)))
+    enc.set_dtype(nrp.BF16)
+    cache = enc.new_stream_cache(STR_SESS, STR_CACHE)
+    actx = nrp.AttentionContext.new((STR_CACHE, STR_CHUNK - 1), "chunked_limited")
+    dev = torch.device("cuda", local)
+    mel_frames, drop = 8 * STR_CHUNK, 1
+    mels = [torch.from_numpy(rng.standard_normal((STR_SESS, SUB_F, mel_frames), dtype=np.float32))
+            .to(dev) for _ in range(4)]
+    xin = [torch.empty_like(mels[0]) for _ in range(2)]
+    outs = [torch.empty((STR_SESS, D, STR_CHUNK), dtype=torch.bfloat16, device=dev)
+            for _ in range(2)]
+    state = {"chunk": 0}
+
+    def reset():
+        cache.reset()
+        state["chunk"] = 0
+
+    def step(k, slot=None):
+        if state["chunk"] == STR_CHUNKS:
+            reset()
+        feats = mels[k % len(mels)] if slot is None else xin[slot]
+        enc.forward_streaming(feats, None, cache, drop, actx, out=outs[slot or 0])
+        state["chunk"] += 1
+        return outs[slot or 0]
+
+    x_host = mels[0].cpu().pin_memory()
+    out_host = torch.empty_like(outs[0], device="cpu").pin_memory()
+    e2e = (lambda slot: xin[slot].copy_(x_host, non_blocking=True),
+           lambda slot: step(0, slot),
+           lambda slot: out_host.copy_(outs[slot], non_blocking=True),
+           x_host.numel() * 4, out_host.numel() * 2)
+    frames = STR_SESS * STR_CHUNK
+    per_frame = 2 * 2 * (2 * D * ENC_FF) + 4 * 2 * D * D + 2 * D * 2 * D + 2 * D * D
+    flops = {"gemm_bf16": ENC_LAYERS * per_frame * frames}
+
+    def cpu():
+        """The oracle on session 0: its subsampled chunk through the first two
+        streaming layers, time scaled to 24 layers (the layers cost the same;
+        the subsampling is timed once per chunk)."""
+        threads = os.cpu_count() or 1
+        orc.set_threads(threads)
+        deq = lambda wd, k: orc.dequantize(wd[k + ".weight"], orc.bf16_round(wd[k + ".scales"]),
+                                           orc.bf16_round(wd[k + ".biases"]), 64, 8)
+        x = orc.bf16_round(rng.standard_normal((1, STR_CHUNK, D)).astype(np.float32))
+        pe_h = orc.get_encoding(D, 5000, STR_CACHE + STR_CHUNK)
+        t0 = time.perf_counter()
+        for p, wd in sample_layers:
+            lin = lambda n: (deq(wd, f"{p}.{n}"), wd.get(f"{p}.{n}.bias"))
+            bw = {"ff1_1": lin("feed_forward1.linear1"), "ff1_2": lin("feed_forward1.linear2"),
+                  "pw1": lin("conv.pointwise_conv1"), "pw2": lin("conv.pointwise_conv2"),
+                  "ff2_1": lin("feed_forward2.linear1"), "ff2_2": lin("feed_forward2.linear2"),
+                  "dw": (wd[f"{p}.conv.depthwise_conv.weight"].reshape(D, ENC_K),
+                         wd[f"{p}.conv.depthwise_conv.bias"]),
+                  "conv_norm": tuple(wd[f"{p}.conv.batch_norm.{n}"] for n in
+                                     ("weight", "bias", "running_mean", "running_var")),
+                  "norms": {o: (wd[f"{p}.{n}.weight"], wd[f"{p}.{n}.bias"])
+                            for o, n in zip(orc.BLOCK_NORMS, nrp.BLOCK_NORMS)},
+                  "attn": {"wq": deq(wd, f"{p}.self_attn.linear_q"),
+                           "bq": wd[f"{p}.self_attn.linear_q.bias"],
+                           "wk": deq(wd, f"{p}.self_attn.linear_k"),
+                           "bk": wd[f"{p}.self_attn.linear_k.bias"],
+                           "wv": deq(wd, f"{p}.self_attn.linear_v"),
+                           "bv": wd[f"{p}.self_attn.linear_v.bias"],
+                           "wo": deq(wd, f"{p}.self_attn.linear_out"),
+                           "bo": wd[f"{p}.self_attn.linear_out.bias"],
+                           "wp": deq(wd, f"{p}.self_attn.linear_pos"),
+                           "pos_bias_u": wd[f"{p}.self_attn.pos_bias_u"],
+                           "pos_bias_v": wd[f"{p}.self_attn.pos_bias_v"]}}
+            hc = np.zeros((1, STR_CACHE, D), np.float32)
+            cc = np.zeros((1, ENC_K - 1, D), np.float32)
+            x, _ = orc.stream_block_step(x, bw, pe_h, H, ENC_FF, ENC_K, hc, cc, STR_CACHE,
+                                         STR_CHUNK, STR_CACHE, STR_CHUNK - 1, True)
+        dt = (time.perf_counter() - t0) * ENC_LAYERS / len(sample_layers)
+        return {"value": STR_CHUNK / dt, "unit": "frames/s", "cores": threads, "kind": "port",
+                "sample": f"one session's chunk ({STR_CHUNK} frames, full caches) through the "
+                          f"first {len(sample_layers)} of {ENC_LAYERS} streaming layers, time "
+                          f"scaled to {ENC_LAYERS} layers (subsampling not timed); CPU "
+                          f"restatement (oracle stream_block_step, bf16 rounding), host CPU: "
+                          f"{cpu_model()}"}
+    _harness(args, world, rank, local, ctx, step, frames, flops, None, STRENC_WORKLOAD,
+             {"sessions_per_gpu": STR_SESS, "chunk": STR_CHUNK, "cache": STR_CACHE,
+              "layers": ENC_LAYERS, "mel_frames_per_chunk": mel_frames, "feat_in": SUB_F,
+              "weights": "MLX 8-bit g64, fp16 scales",
+              "parallelism": f"session-parallel replicas x{world}"},
+             "weak", e2e, "bf16", cpu=cpu, reset=reset)
     if world > 1:
         dist.destroy_process_group()
     return 0

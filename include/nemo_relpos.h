@@ -126,6 +126,13 @@ int nrp_context_destroy(nrp_context* ctx);
 /* Synchronises `stream`, then reads and clears the device error word:
  * NRP_ERR_DEVICE if a kernel gave up on a bounded wait since the last check. */
 int nrp_context_check(nrp_context* ctx, void* stream);
+/* Quantised linears with 256 or more rows run as bf16 GEMMs over their
+ * weight's dequantised copy.  With the weight cache on (the default), each
+ * weight's copy is made on its first such use and kept until its module
+ * re-uploads or frees the weight (2 bytes per parameter of device memory:
+ * 0.6 GB for a 24-layer d_model-1024 encoder); off, the copy is remade in a
+ * scratch buffer on every call (the reference's memory footprint). */
+int nrp_context_set_weight_cache(nrp_context* ctx, int enable);
 
 /* get_encoding on the device in the given dtype (f32 table cast like
  * RelPositionalEncoding::set_dtype, attention.rs:180-183): dev_out

@@ -154,6 +154,7 @@ def lib():
             "nrp_subsampling_load_out": ([vp, vp, vp], i),
             "nrp_subsampling_load_out_quantized": ([vp, i, i, vp, vp, vp, vp], i),
             "nrp_subsampling_forward": ([vp, vp, vp, i, i, i, vp, vp], i),
+            "nrp_context_set_weight_cache": ([vp, i], i),
             "nrp_profile_enable": ([vp, i], i),
             "nrp_profile_reset": ([vp], i),
             "nrp_profile_read": ([vp, i, vp, vp], i),
@@ -209,6 +210,11 @@ class Context:
         if device not in cls._default:
             cls._default[device] = Context(device)
         return cls._default[device]
+
+    def set_weight_cache(self, enable: bool = True):
+        """Keep each quantised weight's bf16 copy for linears of >= 256 rows
+        (default on), or remake it every call."""
+        _check(lib().nrp_context_set_weight_cache(self.handle, int(bool(enable))))
 
     def check(self, stream=None):
         """Synchronise and raise NrpError(NRP_ERR_DEVICE) if a kernel gave up

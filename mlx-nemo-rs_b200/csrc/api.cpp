@@ -182,6 +182,8 @@ int sync_params(nrp_attn* a) {
     return upload(zp, z.data(), z.size(), NRP_DTYPE_BF16);
   };
 
+  // codes about to be replaced: their kept bf16 copies go too
+  for (const DevBuf* q : {&a->w_qkv, &a->w_out, &a->w_pos}) nrp::deq_forget(a->ctx, q->p);
   // --- fused Q|K|V
   if (a->qkv_quant) {
     for (int i = 0; i < 3; ++i)
@@ -259,10 +261,14 @@ constexpr int kDequantOnceMinRows = 256;
 
 // y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias) in the module dtype; W is
 // either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
+// keep: the weight belongs to a module (its codes' address stays theirs
+// until the module re-uploads or frees them), so a quantised weight's bf16
+// copy may be kept (nrp_context::deq_cache); caller-owned buffers
+// (nrp_qlinear) are never kept.
 int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
                const void* w, bool quant, const void* qs, const void* qb, int N,
                const void* bias, void* y, int ldy, const nrp::RowTiling& rt = nrp::RowTiling(),
-               const nrp::Epilogue& ep = nrp::Epilogue()) {
+               const nrp::Epilogue& ep = nrp::Epilogue(), bool keep = false) {
   if (M <= 0) return ok();
   if (dtype == NRP_DTYPE_F32) {
     if (ep.mode != nrp::kEpiBias)
@@ -295,9 +301,30 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
         quant = false;
         break;
       }
-  // Quantised weights with many rows: dequantise the weight once into the
-  // context's scratch and run the bf16 GEMM (the in-register producer would
-  // redo the dequantisation for every 128-row tile).
+  // Quantised weights with many rows: the weight's bf16 copy, made on its
+  // first such use and kept (the in-register producer would redo the
+  // dequantisation for every 128-row tile)
+  if (quant && M >= kDequantOnceMinRows && keep && ctx->deq_cache_on) {
+    auto it = ctx->deq_cache.find(w);
+    if (it == ctx->deq_cache.end()) {
+      auto copy = std::make_unique<nrp::DevBuf>();
+      CUDA_TRY(copy->ensure(static_cast<size_t>(N) * K * 2));
+      {
+        ProfScope ps(ctx, NRP_KERNEL_DEQUANT, st);
+        CUDA_TRY(nrp::launch_dequant_q8(static_cast<const uint8_t*>(w),
+                                        static_cast<const __nv_bfloat16*>(qs),
+                                        static_cast<const __nv_bfloat16*>(qb),
+                                        copy->as<__nv_bfloat16>(), N, K, ctx->num_sms, st));
+      }
+      // once: later calls may come on any stream
+      CUDA_TRY(cudaStreamSynchronize(st));
+      it = ctx->deq_cache.emplace(w, std::move(copy)).first;
+    }
+    w = it->second->p;
+    quant = false;
+  }
+  // Without the kept copies: dequantise the weight once per call into the
+  // context's scratch.
   if (quant && M >= kDequantOnceMinRows) {
     // one scratch per stream the library uses, so overlapping calls on the
     // caller's stream and the side stream never share it
@@ -537,6 +564,17 @@ int nrp_context_destroy(nrp_context* ctx) {
   return ok();
 }
 
+int nrp_context_set_weight_cache(nrp_context* ctx, int enable) {
+  if (!ctx) return fail(NRP_ERR_INVALID, "null context");
+  ctx->deq_cache_on = enable != 0;
+  if (!ctx->deq_cache_on) {
+    if (check_device(ctx)) return NRP_ERR_CUDA;
+    CUDA_TRY(cudaDeviceSynchronize());  // (copies still read by queued work)
+    ctx->deq_cache.clear();
+  }
+  return ok();
+}
+
 int nrp_context_check(nrp_context* ctx, void* stream) {
   if (!ctx) return fail(NRP_ERR_INVALID, "null context");
   if (check_device(ctx)) return NRP_ERR_CUDA;
@@ -580,6 +618,7 @@ int nrp_attn_create(nrp_context* ctx, int d_model, int n_heads, int use_bias, nr
   auto* a = new nrp_attn;
   a->ctx = ctx;
   a->device = ctx->device;
+  a->ctx_alive = ctx->alive;
   a->D = d_model;
   a->H = n_heads;
   a->dh = d_model / n_heads;
@@ -600,6 +639,9 @@ int nrp_attn_destroy(nrp_attn* attn) {
   if (attn) {
     // (its context may be gone already: only the device number is used)
     cudaSetDevice(attn->device);
+    if (!attn->ctx_alive.expired())
+      for (const DevBuf* q : {&attn->w_qkv, &attn->w_out, &attn->w_pos})
+        nrp::deq_forget(attn->ctx, q->p);
     delete attn;
     (void)cudaGetLastError();
   }
@@ -715,12 +757,12 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
     rc = run_linear(ctx, ctx->side, a->dtype,
                     static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * es,
                     g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr,
-                    a->pbuf.p, D);
+                    a->pbuf.p, D, nrp::RowTiling(), nrp::Epilogue(), true);
     if (rc) return rc;
     CUDA_TRY(cudaEventRecord(ctx->join, ctx->side));
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
-                    3 * D, rows);
+                    3 * D, rows, nrp::Epilogue(), true);
     if (rc) return rc;
     CUDA_TRY(cudaStreamWaitEvent(st, ctx->join, 0));
     ProfScope ps(ctx, NRP_KERNEL_ATTN_SM100, st);
@@ -730,10 +772,10 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
   } else {
     rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
                     a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p,
-                    3 * D);
+                    3 * D, nrp::RowTiling(), nrp::Epilogue(), true);
     if (rc) return rc;
     rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
-                    a->z_pos.p, D, nullptr, a->pbuf.p, D);
+                    a->z_pos.p, D, nullptr, a->pbuf.p, D, nrp::RowTiling(), nrp::Epilogue(), true);
     if (rc) return rc;
     const float* q = a->qkv.as<float>();
     nrp::StreamMaskDev none{};
@@ -746,17 +788,21 @@ int attn_forward(nrp_attn* a, cudaStream_t st, const void* x, int B, int T, cons
   // 565: linear_out (the caller's epilogue: a block adds its residual here)
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
-                    out, D, rows, out_ep);
+                    out, D, rows, out_ep, true);
 }
 
 int attn_sync(nrp_attn* a) { return sync_params(a); }
 
 int attn_cache_drop(const nrp_attn* a) { return a->cache_drop; }
 
+void deq_forget(nrp_context* ctx, const void* codes) {
+  if (ctx && codes) ctx->deq_cache.erase(codes);
+}
+
 int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
            const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
-           void* y, int ldy, const RowTiling& rt, const Epilogue& ep) {
-  return run_linear(ctx, st, dtype, x, M, K, w, quant, qs, qb, N, bias, y, ldy, rt, ep);
+           void* y, int ldy, const RowTiling& rt, const Epilogue& ep, bool keep) {
+  return run_linear(ctx, st, dtype, x, M, K, w, quant, qs, qb, N, bias, y, ldy, rt, ep, keep);
 }
 
 int select_device(nrp_context* ctx) { return check_device(ctx); }
@@ -863,7 +909,7 @@ int nrp_attn_forward_seq_sharded(nrp_attn* a, nrp_halo* h, void* stream, const v
   rc = run_linear(ctx, st, a->dtype,
                   static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * 2,
                   g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr,
-                  a->pbuf.p, D);
+                  a->pbuf.p, D, nrp::RowTiling(), nrp::Epilogue(), true);
   if (rc) return rc;
   // q|k|v of the local frames into the buffer's middle rows (478-480)
   nrp::RowTiling rt;
@@ -873,7 +919,7 @@ int nrp_attn_forward_seq_sharded(nrp_attn* a, nrp_halo* h, void* stream, const v
   uint8_t* buf = static_cast<uint8_t*>(h->buf.p);
   rc = run_linear(ctx, st, a->dtype, x, B * len, D, a->w_qkv.p, a->qkv_quant, a->s_qkv.p,
                   a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr,
-                  buf + static_cast<size_t>(hl) * row, B * 3 * D, rt);
+                  buf + static_cast<size_t>(hl) * row, B * 3 * D, rt, nrp::Epilogue(), true);
   if (rc) return rc;
   const bool exchange = hl + hr + send_prev + send_next > 0;
   if (exchange) {
@@ -931,7 +977,7 @@ int nrp_attn_forward_seq_sharded(nrp_attn* a, nrp_halo* h, void* stream, const v
   }
   // linear_out (565)
   return run_linear(ctx, st, a->dtype, a->cbuf.p, B * len, D, a->w_out.p, a->out_quant,
-                    a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr, out, D);
+                    a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr, out, D, nrp::RowTiling(), nrp::Epilogue(), true);
 }
 
 // -------------------------------------------------------------- caches
@@ -1038,6 +1084,8 @@ int nrp_cache_import_h(nrp_cache* c, const float* h, void* stream) {
     const void* s = a->qkv_quant ? static_cast<const uint8_t*>(a->s_qkv.p) + which * static_cast<size_t>(D) * (D / 64) * 2 : nullptr;
     const void* z = a->qkv_quant ? static_cast<const uint8_t*>(a->z_qkv.p) + which * static_cast<size_t>(D) * (D / 64) * 2 : nullptr;
     const void* bias = a->has_b_qkv ? static_cast<const uint8_t*>(a->b_qkv.p) + which * D * es : nullptr;
+    // (an address inside the fused codes: not kept, the module forgets only
+    // the buffer's own address)
     rc = run_linear(a->ctx, st, c->dtype, c->hc.p, M, D, w, a->qkv_quant, s, z, D, bias,
                     which == 1 ? c->kc.p : c->vc.p, D);
     if (rc) return rc;
@@ -1072,12 +1120,12 @@ int nrp::attn_forward_with_cache(nrp_attn* a, cudaStream_t st, const void* x, in
   CUDA_TRY(a->qkv.ensure(BT * 3 * D * es));
   CUDA_TRY(a->cbuf.ensure(BT * D * es));
   rc = run_linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
-                  a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p, 3 * D);
+                  a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, a->qkv.p, 3 * D, nrp::RowTiling(), nrp::Epilogue(), true);
   if (rc) return rc;
   if (a->spos_len != P) {  // 749-761: projected positions reused per pos_len
     CUDA_TRY(a->spos.ensure(static_cast<size_t>(P) * D * es));
     rc = run_linear(ctx, st, a->dtype, pos_emb, P, D, a->w_pos.p, a->pos_quant, a->s_pos.p,
-                    a->z_pos.p, D, nullptr, a->spos.p, D);
+                    a->z_pos.p, D, nullptr, a->spos.p, D, nrp::RowTiling(), nrp::Epilogue(), true);
     if (rc) return rc;
     a->spos_len = P;
   }
@@ -1140,7 +1188,7 @@ int nrp::attn_forward_with_cache(nrp_attn* a, cudaStream_t st, const void* x, in
   if (n_app > 0) c->head = (c->head + n_app) % C;
   return run_linear(ctx, st, a->dtype, a->cbuf.p, static_cast<int>(BT), D, a->w_out.p,
                     a->out_quant, a->s_out.p, a->z_out.p, D, a->has_b_out ? a->b_out.p : nullptr,
-                    out, D, nrp::RowTiling(), out_ep);
+                    out, D, nrp::RowTiling(), out_ep, true);
 }
 
 extern "C" {

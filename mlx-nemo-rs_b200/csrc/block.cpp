@@ -74,6 +74,7 @@ int glu_source_row(int n, int D) {
 
 struct nrp_block {
   nrp_context* ctx = nullptr;
+  std::weak_ptr<bool> ctx_alive;  // (see nrp_context::alive)
   int D = 0, H = 0, ff = 0, K = 0;
   bool causal = false;
   int conv_norm = 0;  // 0 batch norm, 1 layer norm
@@ -158,6 +159,7 @@ int sync_block(nrp_block* k) {
     const bool glu = i == NRP_BLOCK_CONV_PW1;
     auto src_row = [&](int n) { return glu ? glu_source_row(n, D) : n; };
     DevLinear& d = k->dl[i];
+    nrp::deq_forget(k->ctx, d.w.p);  // the codes are replaced
     d.quant = L.quant;
     if (L.quant) {
       if (L.bits != 8 || L.group != 64)
@@ -262,7 +264,7 @@ int block_linear(nrp_block* k, cudaStream_t st, int which, const void* x, int M,
   linear_shape(k, which, N, Kin);
   const DevLinear& d = k->dl[which];
   return nrp::linear(k->ctx, st, NRP_DTYPE_BF16, x, M, Kin, d.w.p, d.quant, d.s.p, d.z.p, N,
-                     d.has_b ? d.b.p : nullptr, y, ldy, rt, ep);
+                     d.has_b ? d.b.p : nullptr, y, ldy, rt, ep, true);
 }
 
 int layer_norm(nrp_block* k, cudaStream_t st, int which, const void* x, void* y, int64_t rows) {
@@ -289,6 +291,7 @@ int nrp_block_create(nrp_context* ctx, int d_model, int n_heads, int ff_dim, int
     return failf(NRP_ERR_UNSUPPORTED, "non-causal conv needs an odd kernel (%d)", conv_kernel);
   auto* k = new nrp_block;
   k->ctx = ctx;
+  k->ctx_alive = ctx->alive;
   k->D = d_model;
   k->H = n_heads;
   k->ff = ff_dim;
@@ -329,6 +332,8 @@ int nrp_block_create(nrp_context* ctx, int d_model, int n_heads, int ff_dim, int
 
 int nrp_block_destroy(nrp_block* k) {
   if (!k) return NRP_OK;
+  if (!k->ctx_alive.expired())
+    for (const DevLinear& d : k->dl) nrp::deq_forget(k->ctx, d.w.p);
   nrp_attn_destroy(k->attn);
   delete k;
   return NRP_OK;
@@ -829,7 +834,9 @@ int encoder_layers(nrp_encoder* e, void* stream, int B, int T, const int32_t* le
   const int L = static_cast<int>(e->blocks.size());
   std::vector<std::vector<QuantWeight>> qw(L);
   size_t slot_bytes = 0;
-  if (n / D >= kPrefetchMinRows) {
+  // (with the context's kept bf16 copies, the linears dequantise nothing after
+  // the first forward: nothing to prefetch)
+  if (n / D >= kPrefetchMinRows && !e->ctx->deq_cache_on) {
     for (int i = 0; i < L; ++i) {
       int rc = sync_block(e->blocks[i]);
       if (!rc) rc = nrp::attn_sync(e->blocks[i]->attn);

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
+#include <unordered_map>
 #include <utility>
 #include <vector>
 
@@ -83,6 +85,15 @@ struct nrp_context {
   // the caller around the launches it covers, which must be stream-ordered
   // after the copies were written.
   std::vector<std::pair<const void*, const void*>> predeq;
+  // bf16 copies of quantised weights kept for the weights' lifetime, keyed
+  // by the device address of their codes: a quantised linear with many rows
+  // uses its copy instead of dequantising the whole weight again every
+  // call.  A module drops its entries when it re-uploads or frees the codes
+  // (deq_forget), so a reused address never matches a stale copy.
+  bool deq_cache_on = true;
+  std::unordered_map<const void*, std::unique_ptr<nrp::DevBuf>> deq_cache;
+  // expires with the context: modules destroyed after it leave its table alone
+  std::shared_ptr<bool> alive = std::make_shared<bool>(true);
   // a second stream for work that overlaps the caller's (forked and joined
   // with events, so the caller's stream order is kept)
   cudaStream_t side = nullptr;
@@ -92,6 +103,7 @@ struct nrp_context {
 struct nrp_attn {
   nrp_context* ctx = nullptr;
   int device = 0;  // ctx->device, kept for teardown
+  std::weak_ptr<bool> ctx_alive;
   int D = 0, H = 0, dh = 0;
   int use_bias = 1;
   int dtype = NRP_DTYPE_F32;

@@ -71,9 +71,15 @@ struct ProfScope {
 // y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias) with the epilogue `ep`,
 // dispatched as nrp_linear / the module projections are (bf16 tcgen05 GEMM,
 // 8-bit GEMM, small-M GEMV, f32 CUDA-core GEMM).
+// keep: the weight is module-owned, so its bf16 copy may be kept
+// (nrp_context::deq_cache).
 int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
            const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
-           void* y, int ldy, const RowTiling& rt, const Epilogue& ep);
+           void* y, int ldy, const RowTiling& rt, const Epilogue& ep, bool keep = false);
+
+// Drops the persistent bf16 copy of the quantised weight whose codes are at
+// `codes` (before the codes are re-uploaded or freed).
+void deq_forget(nrp_context* ctx, const void* codes);
 
 // Uploads the module's parameters in its dtype if they changed.
 int attn_sync(nrp_attn* a);

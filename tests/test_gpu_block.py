@@ -168,3 +168,36 @@ def test_encoder_from_checkpoint_equals_dict(nrp, orc, tmp_path, form):
     yb, _ = b.forward_from_embeddings(x, lengths)
     a.ctx.check()
     assert torch.equal(ya, yb)
+
+
+def test_weight_cache_equals_per_call_dequant_and_follows_reloads(nrp, orc):
+    """The kept bf16 copies of quantised weights give the same bits as the
+    per-call dequantisation, and re-loading a block's weights replaces its
+    copies (the output follows the new weights, checked against the
+    oracle)."""
+    import torch
+    rng = np.random.default_rng(31)
+    B, T, D, H, ff, K = 2, 300, 256, 2, 1024, 9
+    ctx = nrp.Context(0)
+    bw1, wd1 = rand_block(rng, D, H, ff, K, quant=True, orc=orc)
+    bw2, wd2 = rand_block(rng, D, H, ff, K, quant=True, orc=orc)
+    blk = nrp.ConformerBlock(D, H, ff, K, ctx=ctx)
+    blk.load_weights(wd1, "b", nrp.QuantizationConfig(8, 64))
+    blk.set_dtype(nrp.BF16)
+    pe = nrp.RelPositionalEncoding(D, 5000, True)
+    pe.set_dtype(nrp.BF16)
+    x = rng.standard_normal((B, T, D)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda().bfloat16()
+    a = blk.forward(xd, pe.get_encoding(T))  # makes the copies
+    b = blk.forward(xd, pe.get_encoding(T))  # uses them
+    ctx.set_weight_cache(False)
+    c = blk.forward(xd, pe.get_encoding(T))  # scratch per call
+    ctx.set_weight_cache(True)
+    ctx.check()
+    assert torch.equal(a, b) and torch.equal(a, c)
+    blk.load_weights(wd2, "b", nrp.QuantizationConfig(8, 64))
+    blk.set_dtype(nrp.BF16)
+    y = blk.forward(xd, pe.get_encoding(T)).float().cpu().numpy()
+    ctx.check()
+    ref = orc.block_forward(x, bw2, pe.get_encoding_host(T)[0], H, ff, K, bf16=True)
+    assert rel_err(y, ref, [T] * B) < TOL_BF16
