@@ -996,6 +996,32 @@ class EncoderStreamCache:
     def filled(self, v: int):
         _check(lib().nrp_encoder_cache_set_filled(self.handle, int(v)))
 
+    class _Ring:
+        """A layer's attention ring: its slot of the oldest frame (`head`)."""
+
+        def __init__(self, handle):
+            self.handle = handle
+
+        @property
+        def head(self) -> int:
+            h = C.c_int()
+            _check(lib().nrp_cache_get_head(self.handle, C.byref(h)))
+            return h.value
+
+        @head.setter
+        def head(self, v: int):
+            _check(lib().nrp_cache_set_head(self.handle, int(v)))
+
+    def rings(self):
+        """The layers' attention rings, for StreamingStepGraphs (whose keys
+        and restores follow their slots)."""
+        out = []
+        for i in range(len(self.encoder.layers)):
+            a = C.c_void_p()
+            _check(lib().nrp_encoder_cache_layer(self.handle, i, C.byref(a), None))
+            out.append(EncoderStreamCache._Ring(a))
+        return out
+
     def last_channel(self):
         """[layers, B, C, D] f32 (oldest frame first), as EncoderCache.last_channel."""
         import torch

@@ -73,3 +73,43 @@ def test_graph_driven_stream_equals_eager(nrp):
         assert torch.equal(a, b), k
     for a, b in zip(h_eager, h_graph):
         assert torch.equal(a, b)
+
+
+def test_graph_driven_encoder_stream_equals_eager(nrp, orc):
+    """ConformerEncoder.forward_streaming (subsampling, conv caches,
+    attention rings, fill level) driven through StreamingStepGraphs over the
+    encoder cache's rings equals eager calls bit for bit, caches included."""
+    import torch
+    from test_gpu_stream_encoder import build
+    rng = np.random.default_rng(8)
+    L, D, H, ff, K, F = 2, 256, 2, 1024, 9, 80
+    B, T, C, chunks = 2, 7, 21, 12
+    enc, _, _ = build(nrp, orc, rng, L, D, H, ff, K, F, True)
+    actx = nrp.AttentionContext.new((C, T - 1), "chunked_limited")
+    mels = [torch.from_numpy(rng.standard_normal((B, F, 8 * T)).astype(np.float32)).cuda()
+            for _ in range(chunks)]
+
+    def run(use_graphs):
+        cache = enc.new_stream_cache(B, C)
+        x = torch.empty_like(mels[0])
+        out = torch.empty((B, D, T), dtype=torch.bfloat16, device="cuda")
+
+        def step(filled):
+            cache.filled = filled
+            enc.forward_streaming(x, None, cache, 1, actx, out=out)
+
+        drive = nrp.StreamingStepGraphs(step, cache.rings()) if use_graphs else step
+        outs = []
+        for k in range(chunks):
+            x.copy_(mels[k])
+            drive(min(k * T, C))
+            outs.append(out.clone())
+        enc.ctx.check()
+        return outs, cache.last_channel(), cache.last_time(), drive
+
+    eager, ch_e, t_e, _ = run(False)
+    graphed, ch_g, t_g, drive = run(True)
+    assert len(drive.graphs) >= 1
+    for k, (a, b) in enumerate(zip(eager, graphed)):
+        assert torch.equal(a, b), k
+    assert torch.equal(ch_e, ch_g) and torch.equal(t_e, t_g)
