@@ -252,6 +252,15 @@ typedef struct nrp_halo nrp_halo;
 /* Segment of `rank`: [start, start + len) of seq_len frames cut into nranks
  * pieces of ceil(seq_len / nranks) (the last one ragged; len may be 0). */
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len);
+/* Utterance-parallel replicas (one GPU per rank, no collective on the data
+ * path): splits a batch of n utterances over nranks so that their work is
+ * balanced.  An utterance of L frames costs L^2 + (4 d_model / 3) L (its
+ * attention, 6 d L^2, against its projections, 8 d^2 L).  Longest first,
+ * each to the least loaded rank (ties: the lower rank), which is within
+ * 4/3 of the best split.  rank_of [n]: the rank of each utterance;
+ * rank_cost [nranks] (may be NULL): each rank's total cost. */
+int nrp_partition_utterances(const int32_t* lengths, int n, int nranks, int d_model,
+                             int32_t* rank_of, double* rank_cost);
 
 /* The halo plan of `rank` under `context` (NULL: full context): its
  * segment, the frames it receives from rank-1 (halo_left) and rank+1

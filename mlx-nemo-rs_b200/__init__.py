@@ -113,6 +113,7 @@ def lib():
             "nrp_linear": ([vp, vp, i, vp, i, i, vp, i, vp, vp], i),
             "nrp_qlinear": ([vp, vp, vp, i, i, vp, vp, vp, i, i, i, vp, vp], i),
             "nrp_seq_shard": ([i, i, i, vp, vp], i),
+            "nrp_partition_utterances": ([vp, i, i, i, vp, vp], i),
             "nrp_seq_shard_plan": ([i, i, i, vp, vp], i),
             "nrp_halo_unique_id": ([vp], i),
             "nrp_halo_comm_create": ([vp, vp, i, i, i, vp], i),
@@ -1067,6 +1068,18 @@ class SeqPlan:
     halo_right: int
     send_prev: int
     send_next: int
+
+
+def partition_utterances(lengths, nranks: int, d_model: int = 1024):
+    """Utterance-parallel split of a batch over nranks GPUs
+    (nrp_partition_utterances): returns (per-rank index arrays in batch
+    order, per-rank cost)."""
+    ln = np.ascontiguousarray(lengths, np.int32)
+    rank_of = np.empty(len(ln), np.int32)
+    cost = np.empty(nranks, np.float64)
+    _check(lib().nrp_partition_utterances(ln.ctypes.data, len(ln), nranks, d_model,
+                                          rank_of.ctypes.data, cost.ctypes.data))
+    return [np.nonzero(rank_of == r)[0] for r in range(nranks)], cost
 
 
 def seq_shard(seq_len: int, nranks: int, rank: int) -> Tuple[int, int]:

@@ -812,6 +812,36 @@ int select_device(nrp_context* ctx) { return check_device(ctx); }
 extern "C" {
 
 // ------------------------------------------------------ sequence split
+int nrp_partition_utterances(const int32_t* lengths, int n, int nranks, int d_model,
+                             int32_t* rank_of, double* rank_cost) {
+  if (!lengths || !rank_of || n < 0 || nranks <= 0 || d_model <= 0)
+    return fail(NRP_ERR_INVALID, "invalid partition arguments");
+  // cost of an utterance of L frames: attention 6 d L^2 and projections
+  // 8 d^2 L (q, k, v, out), in units of 6 d
+  const double g = 4.0 * d_model / 3.0;
+  std::vector<double> cost(n);
+  std::vector<int> order(n);
+  for (int i = 0; i < n; ++i) {
+    const double L = std::max(lengths[i], 0);
+    cost[i] = L * L + g * L;
+    order[i] = i;
+  }
+  // longest processing time first: each utterance to the least loaded rank
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return cost[a] > cost[b]; });
+  std::vector<double> load(nranks, 0.0);
+  for (int i : order) {
+    int r = 0;
+    for (int k = 1; k < nranks; ++k)
+      if (load[k] < load[r]) r = k;
+    rank_of[i] = r;
+    load[r] += cost[i];
+  }
+  if (rank_cost)
+    for (int k = 0; k < nranks; ++k) rank_cost[k] = load[k];
+  return ok();
+}
+
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len) {
   if (!start || !len) return fail(NRP_ERR_INVALID, "null output");
   if (seq_len <= 0 || nranks < 1 || rank < 0 || rank >= nranks)
