@@ -230,6 +230,8 @@ def test_bf16_quantized_projections(nrp, orc):
     ("bf16", 1024, 8, 70, 14, (70, 13, True), 0),
     ("bf16", 256, 2, 40, 20, (40, 3, False), 3),
     ("bf16", 256, 2, 100, 12, None, 2),
+    ("bf16", 256, 2, 240, 16, None, 0),
+    ("bf16", 256, 2, 200, 33, (200, 10, False), 0),
 ])
 def test_streaming_chunks(nrp, orc, dtype_name, D, H, C, T, ctx, drop):
     """forward_with_cache over consecutive chunks (attention.rs:606-816,
