@@ -175,6 +175,14 @@ class ClockSampler:
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes ~0.1-1 s to print its first line: wait for it
+        # (bounded), so a short timed region still sees the sampler running
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *a):
@@ -359,8 +367,10 @@ def main():
     launches = sum(n for n, _ in prof.values())
 
     # ---- end to end through the public API with host buffers: each step
-    # copies its x and lengths in from pinned host memory and reads its
-    # output back (run_pipelined: copies overlap the neighbouring steps)
+    # copies its utterances' valid frames and the lengths in from pinned
+    # host memory and reads the valid output frames back (copy_frames;
+    # padded rows are unspecified, conformer.rs:1590-1593); run_pipelined
+    # overlaps the copies with the neighbouring steps' compute
     x_host = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
     len_host = torch.from_numpy(lengths.copy()).pin_memory()
@@ -369,14 +379,14 @@ def main():
     masks = [nrp.key_padding_mask(lengths, T) for _ in range(2)]
 
     def h2d_fn(slot):
-        xs[slot].copy_(x_host, non_blocking=True)
+        nrp.copy_frames(xs[slot], x_host, lengths)
         masks[slot].lengths.copy_(len_host, non_blocking=True)
 
     def compute_fn(slot):
         attn.forward(xs[slot], pos, None, masks[slot], out=outs[slot])
 
     def d2h_fn(slot):
-        out_host.copy_(outs[slot], non_blocking=True)
+        nrp.copy_frames(out_host, outs[slot], lengths)
 
     run_pipelined(4, h2d_fn, compute_fn, d2h_fn)  # warm-up
     barrier()
@@ -387,8 +397,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
     e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
-    h2d = x_host.numel() * 2 + len_host.numel() * 4
-    d2h = out_host.numel() * 2
+    h2d = frames * D * 2 + len_host.numel() * 4
+    d2h = frames * D * 2
 
     # ---- roofline of the dominant kernel
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")

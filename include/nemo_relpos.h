@@ -249,6 +249,17 @@ int nrp_attn_forward_with_cache(nrp_attn* attn, void* stream, const void* x, int
 typedef struct nrp_halo nrp_halo;
 #define NRP_HALO_ID_BYTES 128
 
+/* Copies the valid frames of each utterance of a [B, T, row] tensor:
+ * dst[b, :lengths[b]] = src[b, :lengths[b]] (lengths clipped to [0, T], host
+ * memory), one cudaMemcpyAsync per utterance on `stream` (cudaMemcpyDefault:
+ * pinned host <-> device or device <-> device).  Padded frames are left as
+ * they are: a forward's padded rows are unspecified (conformer.rs:1590-1593)
+ * and padded input rows reach no valid output row.  *bytes (may be NULL):
+ * the bytes queued.  This is the host side of a serving loop that moves only
+ * valid frames across PCIe. */
+int nrp_copy_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
+                    int64_t row_bytes, void* stream, int64_t* bytes);
+
 /* Segment of `rank`: [start, start + len) of seq_len frames cut into nranks
  * pieces of ceil(seq_len / nranks) (the last one ragged; len may be 0). */
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len);

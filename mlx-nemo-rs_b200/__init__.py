@@ -114,6 +114,7 @@ def lib():
             "nrp_qlinear": ([vp, vp, vp, i, i, vp, vp, vp, i, i, i, vp, vp], i),
             "nrp_seq_shard": ([i, i, i, vp, vp], i),
             "nrp_partition_utterances": ([vp, i, i, i, vp, vp], i),
+            "nrp_copy_frames": ([vp, vp, vp, i, i, C.c_int64, vp, vp], i),
             "nrp_seq_shard_plan": ([i, i, i, vp, vp], i),
             "nrp_halo_unique_id": ([vp], i),
             "nrp_halo_comm_create": ([vp, vp, i, i, i, vp], i),
@@ -1068,6 +1069,42 @@ class SeqPlan:
     halo_right: int
     send_prev: int
     send_next: int
+
+
+def copy_frames(dst, src, lengths, non_blocking: bool = True) -> int:
+    """dst[b, :lengths[b]] = src[b, :lengths[b]] for every utterance b: one
+    copy per utterance (its valid frames are contiguous in a [B, T, ...]
+    tensor) on the current stream, e.g. pinned host <-> device around a
+    forward.  Padded frames are left as they are: the reference leaves a
+    forward's padded rows unspecified (conformer.rs:1590-1593) and padded
+    input rows reach no valid output row.  Returns the bytes copied."""
+    if dst.shape != src.shape or dst.dtype != src.dtype or dst.dim() < 2:
+        raise ValueError("copy_frames: dst and src need the same [B, T, ...] shape and dtype")
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("copy_frames: contiguous tensors only")
+    B, T = dst.shape[0], dst.shape[1]
+    ln = np.ascontiguousarray(
+        lengths.detach().cpu().numpy() if hasattr(lengths, "detach") else lengths, np.int32)
+    if ln.shape != (B,):
+        raise ValueError("copy_frames: one length per utterance")
+    row = dst[0, 0].numel() * dst.element_size() if T else 0
+    if not (dst.is_cuda or src.is_cuda):  # host to host: no device involved
+        total = 0
+        for b, L in enumerate(ln.tolist()):
+            L = min(max(L, 0), T)
+            if L:
+                dst[b, :L].copy_(src[b, :L])
+                total += L * row
+        return total
+    if B == 0 or T == 0:
+        return 0
+    nbytes = C.c_int64(0)
+    _check(lib().nrp_copy_frames(dst.data_ptr(), src.data_ptr(),
+                                 ln.ctypes.data, B, T, row, _stream(), C.byref(nbytes)))
+    if not non_blocking:
+        import torch
+        torch.cuda.current_stream().synchronize()
+    return int(nbytes.value)
 
 
 def partition_utterances(lengths, nranks: int, d_model: int = 1024):

@@ -842,6 +842,30 @@ int nrp_partition_utterances(const int32_t* lengths, int n, int nranks, int d_mo
   return ok();
 }
 
+int nrp_copy_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
+                    int64_t row_bytes, void* stream, int64_t* bytes) {
+  if (!dst || !src || !lengths || B < 0 || T < 0 || row_bytes <= 0)
+    return fail(NRP_ERR_INVALID, "invalid copy_frames arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t bstride = static_cast<int64_t>(T) * row_bytes;
+  int64_t total = 0;
+  for (int b = 0; b < B; ++b) {
+    const int L = std::min(std::max(lengths[b], 0), T);
+    if (!L) continue;
+    const int64_t off = b * bstride;
+    const cudaError_t e =
+        cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, static_cast<const uint8_t*>(src) + off,
+                        static_cast<size_t>(L) * row_bytes, cudaMemcpyDefault, st);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(NRP_ERR_CUDA, cudaGetErrorString(e));
+    }
+    total += L * row_bytes;
+  }
+  if (bytes) *bytes = total;
+  return ok();
+}
+
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len) {
   if (!start || !len) return fail(NRP_ERR_INVALID, "null output");
   if (seq_len <= 0 || nranks < 1 || rank < 0 || rank >= nranks)
