@@ -268,7 +268,8 @@ constexpr int kDequantOnceMinRows = 256;
 int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
                const void* w, bool quant, const void* qs, const void* qb, int N,
                const void* bias, void* y, int ldy, const nrp::RowTiling& rt = nrp::RowTiling(),
-               const nrp::Epilogue& ep = nrp::Epilogue(), bool keep = false) {
+               const nrp::Epilogue& ep = nrp::Epilogue(), bool keep = false,
+               bool w_owned = true) {
   if (M <= 0) return ok();
   if (dtype == NRP_DTYPE_F32) {
     if (ep.mode != nrp::kEpiBias)
@@ -325,7 +326,9 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   }
   // Without the kept copies: dequantise the weight once per call into the
   // context's scratch.
+  bool w_from_scratch = false;
   if (quant && M >= kDequantOnceMinRows) {
+    w_from_scratch = true;
     // one scratch per stream the library uses, so overlapping calls on the
     // caller's stream and the side stream never share it
     nrp::DevBuf& scratch = st == ctx->side ? ctx->wscratch_side : ctx->wscratch;
@@ -360,9 +363,13 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
                                  ctx->d_err, st, rt, ep));
   } else {
     ProfScope ps(ctx, NRP_KERNEL_GEMM_BF16, st);
+    // Module weights were uploaded or dequantised ahead (kept copies after a
+    // sync, prefetched copies behind an event); weights dequantised into the
+    // scratch just now, and caller-owned ones, may come from the previous
+    // kernel
     CUDA_TRY(nrp::launch_gemm_bf16(mx, w, static_cast<const __nv_bfloat16*>(bias),
                                    static_cast<__nv_bfloat16*>(y), ldy, M, N, K, ctx->num_sms,
-                                   ctx->d_err, st, rt, ep));
+                                   ctx->d_err, st, rt, ep, w_owned && !w_from_scratch));
   }
   return ok();
 }
@@ -1280,7 +1287,7 @@ int nrp_linear(nrp_context* ctx, void* stream, int dtype, const void* x, int M, 
   if (dtype != NRP_DTYPE_F32 && dtype != NRP_DTYPE_BF16) return fail(NRP_ERR_UNSUPPORTED, "dtype %d", dtype);
   if (check_device(ctx)) return NRP_ERR_CUDA;
   return run_linear(ctx, static_cast<cudaStream_t>(stream), dtype, x, M, K, w, false, nullptr,
-                    nullptr, N, bias, y, N);
+                    nullptr, N, bias, y, N, nrp::RowTiling(), nrp::Epilogue(), false, false);
 }
 
 int nrp_qlinear(nrp_context* ctx, void* stream, const void* x, int M, int K, const uint32_t* wq,
@@ -1292,7 +1299,7 @@ int nrp_qlinear(nrp_context* ctx, void* stream, const void* x, int M, int K, con
     return fail(NRP_ERR_UNSUPPORTED, "quantized linear: bits %d group %d (supported: 8, 64)", bits, group_size);
   if (check_device(ctx)) return NRP_ERR_CUDA;
   return run_linear(ctx, static_cast<cudaStream_t>(stream), NRP_DTYPE_BF16, x, M, K, wq, true,
-                    scales, biases, N, bias, y, N);
+                    scales, biases, N, bias, y, N, nrp::RowTiling(), nrp::Epilogue(), false, false);
 }
 
 }  // extern "C"

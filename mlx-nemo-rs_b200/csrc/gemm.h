@@ -101,12 +101,15 @@ struct Epilogue {
 // ---- tcgen05 GEMM: y[M,N] = x[M,K] . W[N,K]^T (+ bias) ----
 // x map: bf16 [M, K], box (64, 128), swizzle 128.  w: bf16 [N, K] row-major
 // (the launcher makes its map for the tile width it picks).  Requires
-// K % 64 == 0 and N % 32 == 0.
+// K % 64 == 0 and N % 32 == 0.  w_early: no kernel still running on the
+// stream writes w (weights uploaded or dequantised ahead), so the kernel may
+// load its first W stages before waiting on the previous kernel.
 int gemm_smem_bytes();
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
                              int K, int num_sms, int* err, cudaStream_t stream,
-                             RowTiling rt = RowTiling(), const Epilogue& ep = Epilogue());
+                             RowTiling rt = RowTiling(), const Epilogue& ep = Epilogue(),
+                             bool w_early = false);
 // Quantised W: MLX affine 8-bit, group 64: wq [N, K] bytes (the packed u32
 // words read as little-endian bytes), scales/biases bf16 [N, K/64].
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                    const __nv_bfloat16* __restrict__ qs,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ bias, // [N] or null
-                   int M, int N, int K, RowTiling rt, Epilogue ep, int* err) {
+                   int M, int N, int K, RowTiling rt, Epilogue ep, int w_early, int* err) {
   constexpr int kStages = TileCfg<kBN>::kStages;
   constexpr uint32_t kBBytes = TileCfg<kBN>::kBBytes;
   extern __shared__ uint8_t smem_raw[];
@@ -174,6 +174,20 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   tc_fence_after();
   const uint32_t tmem = ss->tmem_base;
   volatile int* abort_flag = &ss->abort;
+  // The weights were not written by the kernels before this one (w_early):
+  // the first tile's first W stages load before the wait on the previous
+  // kernel, so their HBM latency hides under its tail.  Only when the tile
+  // list does not depend on device lengths (the first tile is live).
+  int pre = 0;
+  if (!kQuant && w_early && !(batched && rt.len) && warp == 0 && lane == 0 &&
+      static_cast<int>(blockIdx.x) < num_tiles) {
+    const int n0 = (static_cast<int>(blockIdx.x) % tiles_n) * kBN;
+    pre = num_kb < kStages ? num_kb : kStages;
+    for (int s = 0; s < pre; ++s) {
+      mbar_arrive_expect_tx(&ss->full[s], kABytes + kBBytes);
+      tma_load_2d(sB + s * kBBytes, &map_w, &ss->full[s], s * kBK, n0);
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();
   // the lengths may come from the previous kernel in the stream: read them
@@ -203,6 +217,13 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t round = it / kStages;
+          if (static_cast<int>(it) < pre) {  // W already on its way: X only
+            if (batched)
+              tma_load_3d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0, bb);
+            else
+              tma_load_2d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0);
+            continue;
+          }
           if (!mbar_wait(&ss->empty[s], (round & 1) ^ 1, err, kDevTimeoutLoad)) {
             *abort_flag = 1;
             break;
@@ -513,7 +534,7 @@ cudaError_t launch_tn(const CUtensorMap& map_x, const void* w, const uint8_t* wq
                       const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                       const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N, int K,
                       int num_sms, int* err, cudaStream_t stream, const RowTiling& rt,
-                      const Epilogue& ep) {
+                      const Epilogue& ep, bool w_early) {
   static std::atomic<uint64_t> attr{0};
   constexpr int kSmem = static_cast<int>(smem_bytes<kBN>());
   if (cudaError_t e = smem_attr_once(gemm_tn_kernel<kQuant, kBN>, kSmem, attr)) return e;
@@ -527,21 +548,21 @@ cudaError_t launch_tn(const CUtensorMap& map_x, const void* w, const uint8_t* wq
   const int grid = grid_size(M, N, kBN, rt, num_sms);
   return launch_pdl(gemm_tn_kernel<kQuant, kBN>, dim3(grid), dim3(kQuant ? 320 : 192),
                     static_cast<size_t>(kSmem), stream, map_x, map_w, map_y, wq, qs, qb, bias, M,
-                    N, K, rt, ep, err);
+                    N, K, rt, ep, w_early ? 1 : 0, err);
 }
 }  // namespace
 
 cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
                              const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N,
                              int K, int num_sms, int* err, cudaStream_t stream, RowTiling rt,
-                             const Epilogue& ep) {
+                             const Epilogue& ep, bool w_early) {
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
   if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
   if (pick_bn(M, N, rt, ep, num_sms) == 128)
     return launch_tn<false, 128>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
-                                 num_sms, err, stream, rt, ep);
+                                 num_sms, err, stream, rt, ep, w_early);
   return launch_tn<false, 256>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
-                               num_sms, err, stream, rt, ep);
+                               num_sms, err, stream, rt, ep, w_early);
 }
 
 cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __nv_bfloat16* qs,
@@ -552,9 +573,9 @@ cudaError_t launch_gemm_q8(const CUtensorMap& map_x, const uint8_t* wq, const __
   if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
   if (pick_bn(M, N, rt, ep, num_sms) == 128)
     return launch_tn<true, 128>(map_x, nullptr, wq, qs, qb, bias, y, ldy, M, N, K, num_sms, err,
-                                stream, rt, ep);
+                                stream, rt, ep, false);
   return launch_tn<true, 256>(map_x, nullptr, wq, qs, qb, bias, y, ldy, M, N, K, num_sms, err,
-                              stream, rt, ep);
+                              stream, rt, ep, false);
 }
 
 }  // namespace nrp
