@@ -23,6 +23,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -163,7 +164,9 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        # raw samples (the JSON line carries their summary)
+        self.path = os.path.join(os.environ.get("NRP_CLOCKS_DIR", tempfile.gettempdir()),
+                                 f"nrp_clocks_gpu{gpu_index}_{os.getpid()}.csv")
 
     def __enter__(self):
         try:
