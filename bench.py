@@ -40,6 +40,8 @@ L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (read + write) per launch from one ncu capture of this workload,
 # per kernel kind (profiles/relpos_attn_kernel_config1.md); None = not captured.
 TRAFFIC_BYTES = {"attn_sm100": 62.479e6 + 4.606e6, "gemm_bf16": None}
+# config 4's attention launch on one GPU: DRAM read + write of one ncu capture
+LONG_ATTN_TRAFFIC = 309.311e6 + 82.413e6
 
 
 def workload(seed: int):
@@ -1302,6 +1304,8 @@ def main_long(args):
             a = share[name] * args.steps / (ms / 1e3) / 1e12
             rk[name] = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s",
                         "algorithmic_flop_per_launch": share[name] * args.steps / n}
+    if world == 1 and "attn_sm100" in rk:
+        rk["attn_sm100"]["traffic"] = LONG_ATTN_TRAFFIC
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
     roof = None
     if dominant in rk:
