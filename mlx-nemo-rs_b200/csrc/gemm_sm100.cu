@@ -6,8 +6,9 @@
 // where producer warps dequantise u8 weights straight into the swizzled
 // shared-memory B tile, so the dequantised matrix never exists in HBM.
 //
-// Tiling: 128 x 256 output tile per CTA step, K in 64-element stages (one
-// 128-byte swizzle atom per row; also exactly one quantisation group), a
+// Tiling: 128 x 256 output tile per CTA step (128 x 128 or 128 x 192 when
+// that fills the persistent grid's one wave better), K in 64-element stages
+// (one 128-byte swizzle atom per row; also exactly one quantisation group), a
 // 4-deep TMA/mbarrier pipeline, and two 256-column TMEM accumulators so the
 // epilogue of tile t overlaps the MMAs of tile t+1.  The grid is persistent
 // (one CTA per SM, tiles strided by gridDim.x).
@@ -26,14 +27,15 @@ namespace nrp {
 namespace {
 
 constexpr int kBM = 128;
-// Output tiles are 128 x kBN with kBN = 256 (large problems) or 128 (problems
-// with few tiles: twice the CTAs, and 6 pipeline stages in the same budget).
+// Output tiles are 128 x kBN with kBN = 256 (large problems), 128 (problems
+// with few tiles: twice the CTAs, and 6 pipeline stages in the same budget)
+// or 192 (bf16 W: when 128-wide tiles overflow one wave and 192-wide fit it).
 constexpr int kBK = 64;
 constexpr int kMaxStages = 6;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 template <int kBN>
 struct TileCfg {
-  static constexpr int kStages = kBN == 256 ? 4 : 6;
+  static constexpr int kStages = kBN == 128 ? 6 : 4;
   static constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 / 16 KB
 };
 constexpr int kEpiWarp0 = 2;
@@ -56,7 +58,9 @@ constexpr size_t smem_bytes() {
   return 1024 /*align slack*/ + TileCfg<kBN>::kStages * (kABytes + TileCfg<kBN>::kBBytes) +
          kEpiBytes + 256 + 4 * (kMaxBatch + 1);
 }
-static_assert(smem_bytes<256>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory budget");
+static_assert(smem_bytes<256>() <= 232448 && smem_bytes<192>() <= 232448 &&
+                  smem_bytes<128>() <= 232448,
+              "shared memory budget");
 
 // v[e] += bias[n + e] for e < 32 (zero past N); 16-byte loads when `vec`.
 __device__ __forceinline__ void add_bias32(float* v, const __nv_bfloat16* bias, int n, int N,
@@ -558,7 +562,16 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
                              const Epilogue& ep, bool w_early) {
   if (rt.T > 0 && (rt.B < 1 || rt.B > kMaxBatch)) return cudaErrorInvalidValue;
   if (!epilogue_ok(ep, N)) return cudaErrorInvalidValue;
-  if (pick_bn(M, N, rt, ep, num_sms) == 128)
+  const int bn = pick_bn(M, N, rt, ep, num_sms);
+  // 192-wide tiles when 128-wide ones would spill past one wave and
+  // 192-wide ones fit it (the Q|K|V projection of a streaming chunk step,
+  // M = 896, N = 3072: 168 tiles -> 112, so no SM runs a second tile)
+  const int tm = tiles_m_of(M, rt);
+  if (bn == 128 && ep.mode != kEpiGlu && N % 192 == 0 && tm * (N / 128) > num_sms &&
+      tm * (N / 192) <= num_sms)
+    return launch_tn<false, 192>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
+                                 num_sms, err, stream, rt, ep, w_early);
+  if (bn == 128)
     return launch_tn<false, 128>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
                                  num_sms, err, stream, rt, ep, w_early);
   return launch_tn<false, 256>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,

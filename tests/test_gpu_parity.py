@@ -71,8 +71,10 @@ def run_forward(nrp, attn, x, T, lengths, context, dtype):
 
 
 # ---------------------------------------------------------------- linears
+# (896, 1024, 3072) and (1000, 1024, 3072) take the 192-wide tiles (128-wide
+# ones would overflow one wave of 148 SMs)
 @pytest.mark.parametrize("M,K,N", [(300, 1024, 3072), (1499, 1024, 1024), (7, 512, 256),
-                                   (128, 64, 32)])
+                                   (128, 64, 32), (896, 1024, 3072), (1000, 1024, 3072)])
 def test_linear_bf16_tcgen05(nrp, orc, M, K, N):
     import torch
     rng = np.random.default_rng(M + N)
