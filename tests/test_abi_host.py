@@ -36,6 +36,16 @@ def test_exports_every_declared_symbol(nrp):
     assert nrp.lib().nrp_abi_version() == 1
 
 
+def test_rust_binding_declares_every_function():
+    """The Rust FFI block in the integration notes names every function the
+    header declares, and no other: a maintainer can paste it as is."""
+    names = set(_declared_functions())
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    bound = set(re.findall(r"\bpub fn (nrp_[a-z0-9_]+)\(", doc))
+    assert names - bound == set(), sorted(names - bound)
+    assert bound - names == set(), sorted(bound - names)
+
+
 def test_pe_matches_oracle_and_kats(nrp, orc):
     for d, max_len, seq in [(4, 3, 3), (512, 100, 50), (16, 10, 25), (1024, 5000, 750),
                             (1024, 5000, 84)]:
