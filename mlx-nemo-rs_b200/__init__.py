@@ -102,6 +102,7 @@ def lib():
             "nrp_attn_load_linear_quantized": ([vp, i, i, i, vp, vp, vp, vp], i),
             "nrp_attn_load_pos_bias": ([vp, vp, vp], i),
             "nrp_attn_forward": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
+            "nrp_attn_forward_noalloc": ([vp, vp, vp, i, i, vp, vp, vp, vp], i),
             "nrp_cache_create": ([vp, i, i, vp], i),
             "nrp_cache_destroy": ([vp], i),
             "nrp_cache_reset": ([vp, vp], i),

@@ -46,6 +46,15 @@ def test_rust_binding_declares_every_function():
     assert bound - names == set(), sorted(bound - names)
 
 
+def test_python_mirror_declares_every_function():
+    """The Python mirror gives ctypes argument and return types for every
+    function the header declares."""
+    names = set(_declared_functions())
+    src = open(os.path.join(ROOT, "mlx-nemo-rs_b200", "__init__.py")).read()
+    table = set(re.findall(r'"(nrp_[a-z0-9_]+)":\s*\(', src))
+    assert names - table == set(), sorted(names - table)
+
+
 def test_pe_matches_oracle_and_kats(nrp, orc):
     for d, max_len, seq in [(4, 3, 3), (512, 100, 50), (16, 10, 25), (1024, 5000, 750),
                             (1024, 5000, 84)]:
