@@ -65,37 +65,69 @@ bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, 
 }
 
 // ------------------------------------------------------ fp32 SIMT GEMM
+// 64x64 output tile per CTA (256 threads, 4x4 outputs each), 32-wide k
+// tiles.  The next k tile is loaded into registers (float4 rows when K and
+// the pointers allow) while the current one is multiplied from shared
+// memory, so each step's load latency hides under the previous step's
+// FMAs.  Each output sums its products in ascending k with fmaf, as a plain
+// loop does.
 namespace {
-constexpr int kFT = 64, kFK = 16;
+constexpr int kFT = 64, kFK = 32;
 
+template <bool kVec>
 __global__ void __launch_bounds__(256)
     gemm_f32_kernel(const float* __restrict__ x, int M, int K, const float* __restrict__ w, int N,
                     const float* __restrict__ bias, float* __restrict__ y, int ldy) {
-  __shared__ float sx[kFK][kFT + 4];
-  __shared__ float sw[kFK][kFT + 4];
+  __shared__ __align__(16) float sx[kFK][kFT + 4];
+  __shared__ __align__(16) float sw[kFK][kFT + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * kFT, n0 = blockIdx.x * kFT;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += kFK) {
-    for (int e = threadIdx.x; e < kFT * kFK; e += 256) {
-      const int r = e / kFK, c = e % kFK;
-      const int m = m0 + r, n = n0 + r, k = k0 + c;
-      sx[c][r] = (m < M && k < K) ? x[static_cast<size_t>(m) * K + k] : 0.f;
-      sw[c][r] = (n < N && k < K) ? w[static_cast<size_t>(n) * K + k] : 0.f;
+  // loader: rows lr and lr + 32 of the x and w tiles, k columns lc .. lc+3
+  const int lr = threadIdx.x >> 3, lc = (threadIdx.x & 7) * 4;
+  float px[2][4], pw[2][4];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = lr + 32 * h, m = m0 + r, n = n0 + r, k = k0 + lc;
+      if (kVec) {
+        const float4 a = (m < M && k < K)
+                             ? *reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 b = (n < N && k < K)
+                             ? *reinterpret_cast<const float4*>(w + static_cast<size_t>(n) * K + k)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        px[h][0] = a.x, px[h][1] = a.y, px[h][2] = a.z, px[h][3] = a.w;
+        pw[h][0] = b.x, pw[h][1] = b.y, pw[h][2] = b.z, pw[h][3] = b.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          px[h][j] = (m < M && k + j < K) ? x[static_cast<size_t>(m) * K + k + j] : 0.f;
+          pw[h][j] = (n < N && k + j < K) ? w[static_cast<size_t>(n) * K + k + j] : 0.f;
+        }
+      }
     }
+  };
+  float acc[4][4] = {};
+  load(0);
+  for (int k0 = 0; k0 < K; k0 += kFK) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sx[lc + j][lr + 32 * h] = px[h][j];
+        sw[lc + j][lr + 32 * h] = pw[h][j];
+      }
     __syncthreads();
+    if (k0 + kFK < K) load(k0 + kFK);  // in flight under the FMAs below
 #pragma unroll
     for (int c = 0; c < kFK; ++c) {
-      float a[4], bb[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        a[u] = sx[c][ty * 4 + u];
-        bb[u] = sw[c][tx * 4 + u];
-      }
+      const float4 a = *reinterpret_cast<const float4*>(&sx[c][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&sw[c][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(a[u], bb[v], acc[u][v]);
+        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
     }
     __syncthreads();
   }
@@ -115,7 +147,12 @@ __global__ void __launch_bounds__(256)
 cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
                             const float* bias, float* y, int ldy, cudaStream_t stream) {
   dim3 grid((N + kFT - 1) / kFT, (M + kFT - 1) / kFT);
-  gemm_f32_kernel<<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+  const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  if (vec)
+    gemm_f32_kernel<true><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+  else
+    gemm_f32_kernel<false><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
   return cudaGetLastError();
 }
 
