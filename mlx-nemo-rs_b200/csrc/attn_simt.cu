@@ -31,6 +31,22 @@ __device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p) {
   return __bfloat162float(*p);
 }
 
+// Four consecutive elements as f32 (one 16- or 8-byte load); p aligned.
+template <typename T>
+__device__ __forceinline__ void ld4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void ld4<float>(const float* p, float (&v)[4]) {
+  const float4 f = *reinterpret_cast<const float4*>(p);
+  v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+}
+template <>
+__device__ __forceinline__ void ld4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+}
+
 template <typename T>
 __device__ __forceinline__ void st(T* p, float v);
 template <>
@@ -80,9 +96,26 @@ __global__ void __launch_bounds__(kWarps * 32)
                             : knew + (static_cast<size_t>(b) * Tn + (j - C)) * ldk + h * dh;
         const T* pr = p + static_cast<size_t>(Tq - 1 - i + j) * D + h * dh;
         float a = 0.f, c = 0.f;
-        for (int d = 0; d < dh; ++d) {
-          a = fmaf(s_qu[warp][d], ld(kj + d), a);
-          c = fmaf(s_qv[warp][d], ld(pr + d), c);
+        // each lane walks its own key row: 4 elements per load when the rows
+        // allow (one L1 request per lane instead of four), the same
+        // ascending-d fmaf chain either way
+        constexpr uintptr_t kAl = sizeof(T) * 4 - 1;
+        if ((dh & 3) == 0 && ((reinterpret_cast<uintptr_t>(kj) | reinterpret_cast<uintptr_t>(pr)) & kAl) == 0) {
+          for (int d = 0; d < dh; d += 4) {
+            float kv[4], pv4[4];
+            ld4(kj + d, kv);
+            ld4(pr + d, pv4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              a = fmaf(s_qu[warp][d + e], kv[e], a);
+              c = fmaf(s_qv[warp][d + e], pv4[e], c);
+            }
+          }
+        } else {
+          for (int d = 0; d < dh; ++d) {
+            a = fmaf(s_qu[warp][d], ld(kj + d), a);
+            c = fmaf(s_qv[warp][d], ld(pr + d), c);
+          }
         }
         sc = (a + c) * scale;
       }

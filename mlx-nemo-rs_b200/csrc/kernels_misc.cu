@@ -65,14 +65,14 @@ bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, 
 }
 
 // ------------------------------------------------------ fp32 SIMT GEMM
-// 64x64 output tile per CTA (256 threads, 4x4 outputs each), 32-wide k
+// 64x64 output tile per CTA (256 threads, 4x4 outputs each), 64-wide k
 // tiles.  The next k tile is loaded into registers (float4 rows when K and
 // the pointers allow) while the current one is multiplied from shared
 // memory, so each step's load latency hides under the previous step's
 // FMAs.  Each output sums its products in ascending k with fmaf, as a plain
 // loop does.
 namespace {
-constexpr int kFT = 64, kFK = 32;
+constexpr int kFT = 64, kFK = 64;
 
 template <bool kVec>
 __global__ void __launch_bounds__(256)
@@ -82,13 +82,13 @@ __global__ void __launch_bounds__(256)
   __shared__ __align__(16) float sw[kFK][kFT + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * kFT, n0 = blockIdx.x * kFT;
-  // loader: rows lr and lr + 32 of the x and w tiles, k columns lc .. lc+3
-  const int lr = threadIdx.x >> 3, lc = (threadIdx.x & 7) * 4;
-  float px[2][4], pw[2][4];
+  // loader: rows lr + 16h (h < 4) of the x and w tiles, k columns lc .. lc+3
+  const int lr = threadIdx.x >> 4, lc = (threadIdx.x & 15) * 4;
+  float px[4][4], pw[4][4];
   auto load = [&](int k0) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = lr + 32 * h, m = m0 + r, n = n0 + r, k = k0 + lc;
+    for (int h = 0; h < 4; ++h) {
+      const int r = lr + 16 * h, m = m0 + r, n = n0 + r, k = k0 + lc;
       if (kVec) {
         const float4 a = (m < M && k < K)
                              ? *reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k)
@@ -111,11 +111,11 @@ __global__ void __launch_bounds__(256)
   load(0);
   for (int k0 = 0; k0 < K; k0 += kFK) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < 4; ++h)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        sx[lc + j][lr + 32 * h] = px[h][j];
-        sw[lc + j][lr + 32 * h] = pw[h][j];
+        sx[lc + j][lr + 16 * h] = px[h][j];
+        sw[lc + j][lr + 16 * h] = pw[h][j];
       }
     __syncthreads();
     if (k0 + kFK < K) load(k0 + kFK);  // in flight under the FMAs below
