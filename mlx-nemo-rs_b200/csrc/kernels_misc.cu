@@ -65,75 +65,80 @@ bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, 
 }
 
 // ------------------------------------------------------ fp32 SIMT GEMM
-// 64x64 output tile per CTA (256 threads, 4x4 outputs each), 64-wide k
+// kTM x 64 output tile per CTA (256 threads, kTM/16 x 4 outputs each; kTM =
+// 32 when the 64-row grid would not give every SM two CTAs), 64-wide k
 // tiles.  The next k tile is loaded into registers (float4 rows when K and
 // the pointers allow) while the current one is multiplied from shared
 // memory, so each step's load latency hides under the previous step's
 // FMAs.  Each output sums its products in ascending k with fmaf, as a plain
 // loop does.
 namespace {
-constexpr int kFT = 64, kFK = 64;
+constexpr int kFN = 64, kFK = 64;
 
-template <bool kVec>
+template <bool kVec, int kTM>
 __global__ void __launch_bounds__(256)
     gemm_f32_kernel(const float* __restrict__ x, int M, int K, const float* __restrict__ w, int N,
                     const float* __restrict__ bias, float* __restrict__ y, int ldy) {
-  __shared__ __align__(16) float sx[kFK][kFT + 4];
-  __shared__ __align__(16) float sw[kFK][kFT + 4];
+  constexpr int kRU = kTM / 16;  // output rows per thread
+  __shared__ __align__(16) float sx[kFK][kTM + 4];
+  __shared__ __align__(16) float sw[kFK][kFN + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int m0 = blockIdx.y * kFT, n0 = blockIdx.x * kFT;
-  // loader: rows lr + 16h (h < 4) of the x and w tiles, k columns lc .. lc+3
+  const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kFN;
+  // loader: rows lr + 16h of the x (h < kRU) and w (h < 4) tiles, k columns lc .. lc+3
   const int lr = threadIdx.x >> 4, lc = (threadIdx.x & 15) * 4;
-  float px[4][4], pw[4][4];
-  auto load = [&](int k0) {
+  float px[kRU][4], pw[4][4];
+  auto load_row = [&](const float* src, int row, int rows, int k, float (&v)[4]) {
+    if (kVec) {
+      const float4 a = (row < rows && k < K)
+                           ? *reinterpret_cast<const float4*>(src + static_cast<size_t>(row) * K + k)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+    } else {
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const int r = lr + 16 * h, m = m0 + r, n = n0 + r, k = k0 + lc;
-      if (kVec) {
-        const float4 a = (m < M && k < K)
-                             ? *reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K + k)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 b = (n < N && k < K)
-                             ? *reinterpret_cast<const float4*>(w + static_cast<size_t>(n) * K + k)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        px[h][0] = a.x, px[h][1] = a.y, px[h][2] = a.z, px[h][3] = a.w;
-        pw[h][0] = b.x, pw[h][1] = b.y, pw[h][2] = b.z, pw[h][3] = b.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          px[h][j] = (m < M && k + j < K) ? x[static_cast<size_t>(m) * K + k + j] : 0.f;
-          pw[h][j] = (n < N && k + j < K) ? w[static_cast<size_t>(n) * K + k + j] : 0.f;
-        }
-      }
+      for (int j = 0; j < 4; ++j)
+        v[j] = (row < rows && k + j < K) ? src[static_cast<size_t>(row) * K + k + j] : 0.f;
     }
   };
-  float acc[4][4] = {};
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int h = 0; h < kRU; ++h) load_row(x, m0 + lr + 16 * h, M, k0 + lc, px[h]);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) load_row(w, n0 + lr + 16 * h, N, k0 + lc, pw[h]);
+  };
+  float acc[kRU][4] = {};
   load(0);
   for (int k0 = 0; k0 < K; k0 += kFK) {
 #pragma unroll
-    for (int h = 0; h < 4; ++h)
+    for (int j = 0; j < 4; ++j) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        sx[lc + j][lr + 16 * h] = px[h][j];
-        sw[lc + j][lr + 16 * h] = pw[h][j];
-      }
+      for (int h = 0; h < kRU; ++h) sx[lc + j][lr + 16 * h] = px[h][j];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) sw[lc + j][lr + 16 * h] = pw[h][j];
+    }
     __syncthreads();
     if (k0 + kFK < K) load(k0 + kFK);  // in flight under the FMAs below
 #pragma unroll
     for (int c = 0; c < kFK; ++c) {
-      const float4 a = *reinterpret_cast<const float4*>(&sx[c][ty * 4]);
+      float av[kRU];
+      if constexpr (kRU == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(&sx[c][ty * 4]);
+        av[0] = a.x, av[1] = a.y, av[2] = a.z, av[3] = a.w;
+      } else {
+        const float2 a = *reinterpret_cast<const float2*>(&sx[c][ty * 2]);
+        av[0] = a.x, av[1] = a.y;
+      }
       const float4 b = *reinterpret_cast<const float4*>(&sw[c][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+      const float bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < kRU; ++u)
 #pragma unroll
         for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int m = m0 + ty * 4 + u;
+  for (int u = 0; u < kRU; ++u) {
+    const int m = m0 + ty * kRU + u;
     if (m >= M) continue;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
@@ -142,17 +147,27 @@ __global__ void __launch_bounds__(256)
     }
   }
 }
+
+template <int kTM>
+void launch_f32(bool vec, const float* x, int M, int K, const float* w, int N, const float* bias,
+                float* y, int ldy, cudaStream_t stream) {
+  const dim3 grid((N + kFN - 1) / kFN, (M + kTM - 1) / kTM);
+  if (vec)
+    gemm_f32_kernel<true, kTM><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+  else
+    gemm_f32_kernel<false, kTM><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+}
 }  // namespace
 
 cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
                             const float* bias, float* y, int ldy, cudaStream_t stream) {
-  dim3 grid((N + kFT - 1) / kFT, (M + kFT - 1) / kFT);
   const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(w) & 15) == 0;
-  if (vec)
-    gemm_f32_kernel<true><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+  const long tiles64 = static_cast<long>((M + 63) / 64) * ((N + kFN - 1) / kFN);
+  if (tiles64 < 2 * 148)
+    launch_f32<32>(vec, x, M, K, w, N, bias, y, ldy, stream);
   else
-    gemm_f32_kernel<false><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+    launch_f32<64>(vec, x, M, K, w, N, bias, y, ldy, stream);
   return cudaGetLastError();
 }
 
