@@ -595,6 +595,18 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
             g = hbm_bytes[name] * args.steps / (ms / 1e3) / 1e9
             rk[name] = {"achieved": g, "frac": g / hbm_peak, "unit": "GB/s",
                         "algorithmic_bytes_per_launch": hbm_bytes[name] * args.steps / n}
+    if dtype == "f32":
+        # f32 kernels run on the FFMA pipes, not the tensor cores: also give
+        # their fraction of the nominal FFMA peak (SMs x 128 FMA/clock x 2
+        # FLOP x the maximum SM clock seen)
+        import torch
+        n_sm = torch.cuda.get_device_properties(local).multi_processor_count
+        mhz = clocks.summary().get("sm_max_mhz") or 1965.0
+        ffma_peak = n_sm * 128 * 2 * mhz * 1e6 / 1e12
+        for r in rk.values():
+            if r["unit"] == "TFLOP/s":
+                r["ffma_peak"] = ffma_peak
+                r["ffma_frac"] = r["achieved"] / ffma_peak
     dominant = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
     roof = None
     if dominant in rk:
@@ -604,6 +616,9 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
                 "peak": hbm_peak if hbm else tflops_peak, "unit": rk[dominant]["unit"],
                 "frac": rk[dominant]["frac"], "traffic": None,
                 "peak_source": hbm_src if hbm else peak_src}
+        if "ffma_frac" in rk[dominant]:
+            roof["ffma_peak"] = rk[dominant]["ffma_peak"]
+            roof["ffma_frac"] = rk[dominant]["ffma_frac"]
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
