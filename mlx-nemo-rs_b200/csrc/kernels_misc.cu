@@ -65,28 +65,31 @@ bool make_tmap_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, 
 }
 
 // ------------------------------------------------------ fp32 SIMT GEMM
-// kTM x 64 output tile per CTA (256 threads, kTM/16 x 4 outputs each; kTM =
-// 32 when the 64-row grid would not give every SM two CTAs), 64-wide k
-// tiles.  The next k tile is loaded into registers (float4 rows when K and
-// the pointers allow) while the current one is multiplied from shared
-// memory, so each step's load latency hides under the previous step's
-// FMAs.  Each output sums its products in ascending k with fmaf, as a plain
-// loop does.
+// kTM x 64 output tile per CTA, 4 x 4 outputs per thread: 256 threads for
+// 64 rows, or 128 threads for 32 rows when the 64-row grid would not give
+// every SM two CTAs.  64-wide k tiles.  The next k tile is loaded into
+// registers (float4 rows when K and the pointers allow) while the current
+// one is multiplied from shared memory, so each step's load latency hides
+// under the previous step's FMAs.  Each output sums its products in
+// ascending k with fmaf, as a plain loop does.
 namespace {
 constexpr int kFN = 64, kFK = 64;
 
 template <bool kVec, int kTM>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kTM * 4)
     gemm_f32_kernel(const float* __restrict__ x, int M, int K, const float* __restrict__ w, int N,
                     const float* __restrict__ bias, float* __restrict__ y, int ldy) {
-  constexpr int kRU = kTM / 16;  // output rows per thread
+  constexpr int kThreads = kTM * 4;
+  constexpr int kTY = kThreads / 16;  // thread rows (4 output rows each)
   __shared__ __align__(16) float sx[kFK][kTM + 4];
   __shared__ __align__(16) float sw[kFK][kFN + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kFN;
-  // loader: rows lr + 16h of the x (h < kRU) and w (h < 4) tiles, k columns lc .. lc+3
+  // loader: rows lr + kTY*h of the x (h < 4) and w (h < 64 / kTY) tiles,
+  // k columns lc .. lc+3
+  constexpr int kWH = kFN / kTY;
   const int lr = threadIdx.x >> 4, lc = (threadIdx.x & 15) * 4;
-  float px[kRU][4], pw[4][4];
+  float px[4][4], pw[kWH][4];
   auto load_row = [&](const float* src, int row, int rows, int k, float (&v)[4]) {
     if (kVec) {
       const float4 a = (row < rows && k < K)
@@ -101,44 +104,37 @@ __global__ void __launch_bounds__(256)
   };
   auto load = [&](int k0) {
 #pragma unroll
-    for (int h = 0; h < kRU; ++h) load_row(x, m0 + lr + 16 * h, M, k0 + lc, px[h]);
+    for (int h = 0; h < 4; ++h) load_row(x, m0 + lr + kTY * h, M, k0 + lc, px[h]);
 #pragma unroll
-    for (int h = 0; h < 4; ++h) load_row(w, n0 + lr + 16 * h, N, k0 + lc, pw[h]);
+    for (int h = 0; h < kWH; ++h) load_row(w, n0 + lr + kTY * h, N, k0 + lc, pw[h]);
   };
-  float acc[kRU][4] = {};
+  float acc[4][4] = {};
   load(0);
   for (int k0 = 0; k0 < K; k0 += kFK) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
 #pragma unroll
-      for (int h = 0; h < kRU; ++h) sx[lc + j][lr + 16 * h] = px[h][j];
+      for (int h = 0; h < 4; ++h) sx[lc + j][lr + kTY * h] = px[h][j];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) sw[lc + j][lr + 16 * h] = pw[h][j];
+      for (int h = 0; h < kWH; ++h) sw[lc + j][lr + kTY * h] = pw[h][j];
     }
     __syncthreads();
     if (k0 + kFK < K) load(k0 + kFK);  // in flight under the FMAs below
 #pragma unroll
     for (int c = 0; c < kFK; ++c) {
-      float av[kRU];
-      if constexpr (kRU == 4) {
-        const float4 a = *reinterpret_cast<const float4*>(&sx[c][ty * 4]);
-        av[0] = a.x, av[1] = a.y, av[2] = a.z, av[3] = a.w;
-      } else {
-        const float2 a = *reinterpret_cast<const float2*>(&sx[c][ty * 2]);
-        av[0] = a.x, av[1] = a.y;
-      }
+      const float4 a = *reinterpret_cast<const float4*>(&sx[c][ty * 4]);
       const float4 b = *reinterpret_cast<const float4*>(&sw[c][tx * 4]);
-      const float bv[4] = {b.x, b.y, b.z, b.w};
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int u = 0; u < kRU; ++u)
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int u = 0; u < kRU; ++u) {
-    const int m = m0 + ty * kRU + u;
+  for (int u = 0; u < 4; ++u) {
+    const int m = m0 + ty * 4 + u;
     if (m >= M) continue;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
@@ -153,9 +149,9 @@ void launch_f32(bool vec, const float* x, int M, int K, const float* w, int N, c
                 float* y, int ldy, cudaStream_t stream) {
   const dim3 grid((N + kFN - 1) / kFN, (M + kTM - 1) / kTM);
   if (vec)
-    gemm_f32_kernel<true, kTM><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+    gemm_f32_kernel<true, kTM><<<grid, kTM * 4, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
   else
-    gemm_f32_kernel<false, kTM><<<grid, 256, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
+    gemm_f32_kernel<false, kTM><<<grid, kTM * 4, 0, stream>>>(x, M, K, w, N, bias, y, ldy);
 }
 }  // namespace
 
