@@ -37,11 +37,17 @@ LEN_LO, LEN_HI = 375, 750
 WORKLOAD = ("BASELINE config 1: offline batched full-context rel-pos MHA layer, bf16, "
             "B=16 T=750 d_model=1024 8x128 heads, lengths U[375,750] with key padding mask")
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) per launch from one ncu capture of this workload,
-# per kernel kind (profiles/relpos_attn_kernel_config1.md); None = not captured.
-TRAFFIC_BYTES = {"attn_sm100": 62.479e6 + 4.606e6, "gemm_bf16": None}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each
+# of the forward's four launches, from one ncu capture of this workload's
+# bench command; None = not captured.
+TRAFFIC_BYTES = {"linear_pos": None, "qkv_gemm": 26.103e6 + 19.167e6,
+                 "attention": 62.479e6 + 4.606e6, "linear_out": None}
 # config 4's attention launch on one GPU: DRAM read + write of one ncu capture
 LONG_ATTN_TRAFFIC = 309.311e6 + 82.413e6
+# The forward's launches in the order the host issues them (linear_pos on
+# the context's second stream, beside the q|k|v GEMM)
+FORWARD_LAUNCHES = (("linear_pos", "gemm_bf16"), ("qkv_gemm", "gemm_bf16"),
+                    ("attention", "attn_sm100"), ("linear_out", "gemm_bf16"))
 
 
 def workload(seed: int):
@@ -227,10 +233,10 @@ def run_reference(args):
         return 0
     w, x, lengths = workload(1234)
     threads = os.cpu_count() or 1
-    n_utts = 2
+    n_utts = B
     for _ in range(args.warmup):
         oracle_sample(w, x, lengths, n_utts, threads)
-    # each step is a bounded sample; the run stops early once 90 s of CPU
+    # each step is the whole batch; the run stops early once 90 s of CPU
     # time have been measured, so the arm ends within a few minutes
     times, frames = [], 0
     for _ in range(args.steps):
@@ -249,7 +255,7 @@ def run_reference(args):
         "data": "synthetic", "config": {"workload": WORKLOAD, "sample_utterances": n_utts,
                                         "steps_measured": len(times)},
         "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "port",
-                         "sample": f"{n_utts} of the 16 utterances per step (valid frames "
+                         "sample": f"all {n_utts} utterances per step (valid frames "
                                    f"{frames}), CPU restatement of the reference algorithm "
                                    f"(ORC_REFERENCE_ALGO), host CPU: {cpu_model()}"},
         "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0,
@@ -261,6 +267,342 @@ def run_reference(args):
     return 0
 
 
+def _max_ranks(v, world, dev):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def host_link(world, dev, h2d_bytes, d2h_bytes, barrier, reps=20):
+    """Pinned host <-> device copy time of one step's bytes on this rank
+    while every rank copies at the same time: host to device alone, device
+    to host alone, and both directions at once on two streams (as the e2e
+    loop runs them).  Device-timed, max over ranks.  Together with the
+    device step time this bounds the e2e rate."""
+    import torch
+    hi = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    ho = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory()
+    di = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    do = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+
+    def run(do_in, do_out):
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        barrier()
+        start.record(cur)
+        s_in.wait_event(start)
+        s_out.wait_event(start)
+        for _ in range(reps):
+            if do_in:
+                with torch.cuda.stream(s_in):
+                    di.copy_(hi, non_blocking=True)
+            if do_out:
+                with torch.cuda.stream(s_out):
+                    ho.copy_(do, non_blocking=True)
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
+        stop.record(cur)
+        torch.cuda.synchronize(dev)
+        return _max_ranks(start.elapsed_time(stop) / reps, world, dev)
+
+    run(True, True)  # warm-up
+    t_in, t_out, t_both = run(True, False), run(False, True), run(True, True)
+    return {"h2d_gbs": h2d_bytes / t_in / 1e6, "d2h_gbs": d2h_bytes / t_out / 1e6,
+            "bidir_ms_per_step": t_both,
+            "bidir_gbs": (h2d_bytes + d2h_bytes) / t_both / 1e6,
+            "ranks_copying_at_once": world,
+            "how": f"{reps} copies of one step's bytes each way from/to pinned host memory, "
+                   f"every rank at once, CUDA events, slowest rank"}
+
+
+def _timed_steps(step, n, dev, world, barrier, flush):
+    """n steps timed with CUDA events (L2 flushed between them, outside the
+    events), summed; max over ranks."""
+    import torch
+    stream = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    torch.cuda.synchronize(dev)
+    barrier()
+    for k in range(n):
+        flush.zero_()
+        starts[k].record(stream)
+        step()
+        ends[k].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    return _max_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)), world, dev)
+
+
+def strong_split_attention(nrp, ctx, attn, pos, w, x, lengths, world, rank, dev, barrier, args):
+    """Config 1's one batch of 16 utterances split over the ranks by
+    nrp_partition_utterances (longest first onto the least loaded rank);
+    every rank runs the layer on its share; strong scaling: all 16
+    utterances' valid frames / the slowest rank's step time."""
+    import torch
+    parts, cost = nrp.partition_utterances(lengths, world, D)
+    idx = parts[rank]
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    if len(idx):
+        xr = torch.from_numpy(np.ascontiguousarray(x[idx])).to(dev, torch.bfloat16)
+        out = torch.empty_like(xr)
+        mask = nrp.key_padding_mask(lengths[idx], T)
+
+        def step():
+            attn.forward(xr, pos, None, mask, out=out)
+    else:
+        def step():
+            pass
+    for _ in range(3):
+        step()
+    ctx.check()
+    n = min(args.steps, 500)
+    ms = _timed_steps(step, n, dev, world, barrier, flush)
+    ctx.check()
+    frames = int(lengths.sum())
+    return {"value": frames * n / (ms / 1e3), "unit": "frames/s", "ms_per_step": ms / n,
+            "n_gpus": world, "steps": n, "scaling": "strong",
+            "utterances_per_rank": [int(len(p)) for p in parts],
+            "cost_per_rank": [float(c) for c in cost],
+            "workload": "config 1's one batch (16 utterances, B=16 T=750) split over the ranks "
+                        "by nrp_partition_utterances; no collective"}
+
+
+def _long_module(nrp, ctx, local):
+    """Config 4's layer: seeded N(0, 0.02^2) weights, the (128, 128) window,
+    the positional table for T = 12500, and the input sequence."""
+    rng = np.random.default_rng(4321)
+    f = lambda *sh: (rng.standard_normal(sh) * 0.02).astype(np.float32)
+    w = {"wq": f(D, D), "bq": f(D), "wk": f(D, D), "bk": f(D), "wv": f(D, D), "bv": f(D),
+         "wo": f(D, D), "bo": f(D), "wp": f(D, D), "pos_bias_u": f(H, D // H),
+         "pos_bias_v": f(H, D // H)}
+    attn = nrp.RelPositionMultiHeadAttention(D, H, True, ctx=ctx)
+    for which, (wk, bk) in enumerate((("wq", "bq"), ("wk", "bk"), ("wv", "bv"), ("wo", "bo"),
+                                      ("wp", None))):
+        attn.set_linear(which, nrp.LinearLayer.standard(w[wk], w[bk] if bk else None))
+    attn.set_pos_bias(w["pos_bias_u"], w["pos_bias_v"])
+    attn.set_dtype(nrp.BF16)
+    actx = nrp.AttentionContext.new(LONG_WINDOW, "regular")
+    pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
+    pe.set_dtype(nrp.BF16)
+    pos = pe.get_encoding(LONG_T)
+    # every rank draws the whole sequence (same seed) and keeps its segment
+    x = np.random.default_rng(8765).standard_normal((LONG_B, LONG_T, D)).astype(np.float32)
+    return w, attn, actx, pos, x
+
+
+def seq_split_config4(nrp, ctx, world, rank, local, dev, barrier, args):
+    """Config 4 ([4, 12500, 1024], window (128, 128)) with the sequence split
+    over the ranks (nrp_attn_forward_seq_sharded: 128-frame K/V halo over
+    NCCL); one GPU runs the plain windowed forward.  Strong scaling."""
+    import torch
+    _, attn, actx, pos, x = _long_module(nrp, ctx, local)
+    halo = None
+    if world > 1:
+        halo = nrp.HaloComm.from_process_group(ctx=ctx, timeout_ms=120000)
+        plan = halo.plan(LONG_T, actx)
+        s0, n0 = plan.start, plan.len
+    else:
+        s0, n0 = 0, LONG_T
+    xd = torch.from_numpy(np.ascontiguousarray(x[:, s0:s0 + n0])).to(dev, torch.bfloat16)
+    out = torch.empty_like(xd)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        if halo is None:
+            attn.forward(xd, pos, actx, None, out=out)
+        else:
+            attn.forward_seq_sharded(xd, pos, LONG_T, halo, actx, None, out=out)
+
+    for _ in range(3):
+        step()
+    if halo is not None:
+        halo.check()
+    ctx.check()
+    n = min(args.steps, 300)
+    ms = _timed_steps(step, n, dev, world, barrier, flush)
+    if halo is not None:
+        halo.check()
+        halo.close()
+    ctx.check()
+    return {"value": LONG_B * LONG_T * n / (ms / 1e3), "unit": "frames/s", "ms_per_step": ms / n,
+            "n_gpus": world, "steps": n, "scaling": "strong", "frames_per_rank": LONG_B * n0,
+            "workload": LONG_WORKLOAD if world > 1 else
+            "BASELINE config 4 on one GPU (plain windowed forward)"}
+
+
+def strong_split_encoder(nrp, ctx, world, rank, dev, barrier, args):
+    """Config 3's one batch (32 utterances, 24 layers, 8-bit linears read as
+    codes every forward: the weight cache is off) split over the ranks by
+    nrp_partition_utterances.  Strong scaling."""
+    import torch
+    from oracle import oracle as orc  # quantiser of the synthetic checkpoint only
+    rng = np.random.default_rng(5150)
+    enc = nrp.ConformerEncoder(ENC_LAYERS, D, H, ENC_FF, ENC_K, ctx=ctx)
+    _load_quant_layers(nrp, orc, enc, rng)
+    enc.set_dtype(nrp.BF16)
+    x = rng.standard_normal((ENC_B, ENC_T, D), dtype=np.float32)
+    lengths = rng.integers(ENC_LEN_LO, ENC_LEN_HI + 1, ENC_B).astype(np.int32)
+    parts, cost = nrp.partition_utterances(lengths, world, D)
+    idx = parts[rank]
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    ctx.set_weight_cache(False)
+    if len(idx):
+        xr = torch.from_numpy(np.ascontiguousarray(x[idx])).to(dev, torch.bfloat16)
+        out = torch.empty((len(idx), D, ENC_T), dtype=torch.bfloat16, device=dev)
+        lr = lengths[idx]
+
+        def step():
+            enc.forward_from_embeddings(xr, lr, None, out=out)
+    else:
+        def step():
+            pass
+    for _ in range(2):
+        step()
+    ctx.check()
+    n = min(args.steps, 20)
+    ms = _timed_steps(step, n, dev, world, barrier, flush)
+    ctx.check()
+    ctx.set_weight_cache(True)
+    frames = int(lengths.sum())
+    del enc
+    return {"value": frames * n / (ms / 1e3), "unit": "frames/s", "ms_per_step": ms / n,
+            "n_gpus": world, "steps": n, "scaling": "strong",
+            "utterances_per_rank": [int(len(p)) for p in parts],
+            "cost_per_rank": [float(c) for c in cost],
+            "workload": "config 3's one batch (B=32 T=500, 24 layers, MLX 8-bit linears read as "
+                        "u8 codes each forward) split over the ranks by "
+                        "nrp_partition_utterances; no collective"}
+
+
+# config 3's block linears (N, K): FF1 1024->4096->1024, pointwise convs,
+# q, k, v, out, pos; 24 layers
+QL_SHAPES = [(ENC_FF, D), (D, ENC_FF), (2 * D, D), (D, D), (ENC_FF, D), (D, ENC_FF),
+             (D, D), (D, D), (D, D), (D, D), (D, D)]
+QL_WORKLOAD = ("config 3's MLX 8-bit linears (group 64, bf16 scales and biases): the 11 linears "
+               "of each of 24 layers, one after another on one stream, at M rows (M = 14: one "
+               "streaming session's 14-frame chunk; M = 128)")
+
+
+def main_qlinear(args):
+    """North-star kernel (3), LinearLayer::forward's quantised arm
+    (quantization.rs:137-160) through nrp_qlinear: one step runs all 264
+    linears of config 3's 24 layers on M rows, replayed as a CUDA graph (the
+    launches are microseconds each).  M = 14 takes the GEMV (HBM-bound:
+    codes, scales and biases read once); M = 128 the tcgen05 GEMM that
+    dequantises the codes in its B producer.  Algorithmic bytes per linear:
+    N*K codes + 4*N*K/64 scale/bias + 2*M*K in + 2*M*N out; FLOP 2*M*N*K."""
+    import torch
+    from __graft_entry__ import load_package
+    world, rank, local = _dist_init(args)
+    nrp = load_package()
+    ctx = nrp.Context(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    layers = []
+    for _ in range(ENC_LAYERS):
+        for n, k in QL_SHAPES:
+            wq = torch.randint(-2**31, 2**31 - 1, (n, k // 4), dtype=torch.int32, device=dev,
+                               generator=g)
+            sc = (torch.rand((n, k // 64), device=dev, generator=g) * 4e-4 + 1e-4).bfloat16()
+            zp = (torch.rand((n, k // 64), device=dev, generator=g) * -0.1).bfloat16()
+            b = (torch.randn(n, device=dev, generator=g) * 0.02).bfloat16()
+            layers.append((wq, sc, zp, b, n, k))
+    stream = torch.cuda.Stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    hbm_peak = peaks.get("hbm_gbs") or 6650.0
+    burst, _, peak_src = _peaks()
+    barrier = (lambda: torch.distributed.barrier()) if world > 1 else (lambda: None)
+
+    def measure(M, n_steps):
+        xs = {k: torch.randn((M, k), device=dev, generator=g).bfloat16()
+              for k in {k for _, k in QL_SHAPES}}
+        ys = [torch.empty((M, n), dtype=torch.bfloat16, device=dev) for *_, n, _ in layers]
+
+        def run():
+            for (wq, sc, zp, b, n, k), y in zip(layers, ys):
+                nrp.qlinear(xs[k], wq, sc, zp, b, ctx=ctx, out=y)
+
+        with torch.cuda.stream(stream):
+            run()  # warm-up outside capture
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            run()
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        ctx.check()
+        ms = _timed_steps(graph.replay, n_steps, dev, world, barrier, flush)
+        ctx.check()
+        nbytes = sum(n * k + 4 * n * k // 64 + 2 * M * k + 2 * M * n + 2 * n
+                     for *_, n, k in layers)
+        flop = sum(2 * M * n * k for *_, n, k in layers)
+        t = ms / n_steps / 1e3
+        del graph
+        return {"rows": M, "ms_per_step": ms / n_steps, "steps": n_steps,
+                "linears_per_step": len(layers), "bytes_per_step": nbytes,
+                "flop_per_step": flop, "gbs": nbytes / t / 1e9, "tflops": flop / t / 1e12,
+                "hbm_frac": nbytes / t / 1e9 / hbm_peak, "tensor_frac": flop / t / 1e12 / burst}
+
+    n_steps = min(args.steps, 500)
+    with ClockSampler(local) as clocks:
+        small = measure(14, n_steps)
+        big = measure(128, n_steps)
+    # e2e through the public API: the 14 rows in from pinned host memory,
+    # the last linear's output back, per step (eager launches)
+    x_host = torch.randn((14, D)).bfloat16().pin_memory()
+    y_host = torch.empty((14, D), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty((14, D), dtype=torch.bfloat16, device=dev)
+    xk = torch.empty((14, ENC_FF), dtype=torch.bfloat16, device=dev)
+    ys = [torch.empty((14, n), dtype=torch.bfloat16, device=dev) for *_, n, _ in layers]
+
+    def compute(slot):
+        for (wq, sc, zp, b, n, k), y in zip(layers, ys):
+            nrp.qlinear(xd if k == D else xk, wq, sc, zp, b, ctx=ctx, out=y)
+
+    e2e_ms = run_pipelined(n_steps, lambda s: xd.copy_(x_host, non_blocking=True), compute,
+                           lambda s: y_host.copy_(ys[-1], non_blocking=True))
+    e2e_ms = _max_ranks(e2e_ms, world, dev)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": world * 14 * n_steps / (small["ms_per_step"] * n_steps / 1e3),
+            "unit": "frames/s", "n_gpus": world, "steps": n_steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": small["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 activations, u8 weights", "data": "synthetic",
+            "config": {"workload": QL_WORKLOAD, "rows": 14, "layers": ENC_LAYERS,
+                       "l2": "flushed between timed steps (256 MiB write, outside the events); "
+                             "the weights (643 MB) exceed L2 anyway"},
+            "e2e": {"value": world * 14 * n_steps / (e2e_ms / 1e3), "unit": "frames/s",
+                    "h2d_bytes_per_step": x_host.numel() * 2,
+                    "d2h_bytes_per_step": y_host.numel() * 2},
+            "gpu_launches": len(layers) * n_steps,
+            "roofline": {"bound": "hbm", "kernel": "qgemv (M = 14)", "achieved": small["gbs"],
+                         "peak": hbm_peak, "unit": "GB/s", "frac": small["hbm_frac"],
+                         "traffic": None, "peak_source": "measured (hbm_gbs, MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_step": small["bytes_per_step"]},
+            "rows_14": small,
+            "rows_128": dict(big, roofline={"bound": "tensor", "kernel": "gemm_q8 (M = 128)",
+                                            "achieved": big["tflops"], "peak": burst,
+                                            "unit": "TFLOP/s", "frac": big["tensor_frac"],
+                                            "peak_source": peak_src}),
+            "clocks": clocks.summary(),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -268,14 +610,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="config 1 only: skip the strong-scaling and sequence-split keys")
     ap.add_argument("--workload", default="offline",
                     choices=["offline", "long", "encoder", "stream", "single", "subsampling",
-                             "stream_encoder"],
+                             "stream_encoder", "qlinear"],
                     help="offline: BASELINE config 1 (the headline line); long: config 4, "
                          "the sequence split across the ranks; encoder: config 3; stream: "
                          "config 2; single: config 0; subsampling: the pre_encode of "
                          "config 3's batch from mel frames; stream_encoder: the whole "
-                         "streaming encoder step from mel chunks")
+                         "streaming encoder step from mel chunks; qlinear: config 3's 8-bit "
+                         "linears at 14 and 128 rows (the GEMV and the dequantising GEMM)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -291,6 +636,8 @@ def main():
         return main_subsampling(args)
     if args.workload == "stream_encoder":
         return main_stream_encoder(args)
+    if args.workload == "qlinear":
+        return main_qlinear(args)
 
     import torch
     import torch.distributed as dist
@@ -360,16 +707,23 @@ def main():
     frames = int(lengths.sum())
     value = world * frames * args.steps / (total_ms / 1e3)
 
-    # ---- per-kernel device times (CUDA events around each launch), same steps
+    # ---- per-launch device times (CUDA events the library records around
+    # each launch on its launching stream), same steps
     ctx.profile(True)
     ctx.profile_reset()
     for k in range(args.steps):
         flush.zero_()
         step()
     torch.cuda.synchronize()
-    prof = ctx.profile_read()
+    log = ctx.profile_launches()
     ctx.profile(False)
-    launches = sum(n for n, _ in prof.values())
+    launches = len(log)
+    nl = len(FORWARD_LAUNCHES)
+    if launches != nl * args.steps or any(
+            kind != FORWARD_LAUNCHES[i % nl][1] for i, (kind, _) in enumerate(log)):
+        raise RuntimeError(f"unexpected launch sequence: {log[:2 * nl]}")
+    per_launch = {name: [ms for i, (_, ms) in enumerate(log) if i % nl == j]
+                  for j, (name, _) in enumerate(FORWARD_LAUNCHES)}
 
     # ---- end to end through the public API with host buffers: each step
     # copies its utterances' valid frames and the lengths in from pinned
@@ -404,54 +758,62 @@ def main():
     e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
     h2d = frames * D * 2 + len_host.numel() * 4
     d2h = frames * D * 2
+    link = host_link(world, dev, h2d, d2h, barrier)
+    floor_ms = max(link["bidir_ms_per_step"], total_ms / args.steps)
+    link["e2e_ceiling_frames_per_s"] = world * frames / (floor_ms / 1e3)
+    link["e2e_frac_of_ceiling"] = e2e_value / link["e2e_ceiling_frames_per_s"]
 
-    # ---- roofline of the dominant kernel
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
-    tflops_peak = peaks.get("bf16_tflops_sustained")
-    peak_src = "measured (bf16_tflops_sustained, MEASURED_PEAKS.json)"
-    if not tflops_peak:
-        tflops_peak, peak_src = 1400.0, "fallback 1.4 PFLOP/s sustained"
+    # ---- roofline of each launch; the dominant one is `roofline`
+    burst, sustained, peak_src = _peaks()
     proj, pos_f, attn_f = algorithmic_flops(lengths)
-    per_kind_flops = {"gemm_bf16": proj + pos_f, "attn_sm100": attn_f}
+    flop = {"linear_pos": pos_f, "qkv_gemm": proj * 3 // 4, "attention": attn_f,
+            "linear_out": proj // 4}
+    total_launch_ms = sum(sum(v) for v in per_launch.values())
+    rk = {}
+    for name, ms_list in per_launch.items():
+        ms = sum(ms_list) / len(ms_list)
+        a = flop[name] / (ms / 1e3) / 1e12
+        rk[name] = {"launches": len(ms_list), "ms_per_launch": ms,
+                    "share": sum(ms_list) / total_launch_ms,
+                    "algorithmic_flop_per_launch": flop[name], "achieved": a,
+                    "unit": "TFLOP/s", "frac": a / burst, "frac_of_sustained": a / sustained,
+                    "traffic": TRAFFIC_BYTES.get(name)}
+    dominant = max(rk, key=lambda n: rk[n]["share"])
+    d = rk[dominant]
+    roof = {"bound": "tensor", "kernel": dominant, "achieved": d["achieved"], "peak": burst,
+            "unit": "TFLOP/s", "frac": d["frac"], "traffic": d["traffic"],
+            "peak_source": peak_src + "; burst: each step is 0.2 ms, not a seconds-long loop",
+            "algorithmic_flop_per_launch": d["algorithmic_flop_per_launch"]}
+    whole = (proj + pos_f + attn_f) * args.steps / (total_ms / 1e3) / 1e12
     kern = {}
-    for name, (n, ms) in prof.items():
-        kern[name] = {"launches": n, "ms_total": ms, "share": ms / max(sum(m for _, m in prof.values()), 1e-9)}
-    dominant = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
-    roof = None
-    if dominant in per_kind_flops:
-        n, ms = prof[dominant]
-        flop_per_launch = per_kind_flops[dominant] * args.steps / n
-        achieved = flop_per_launch / (ms / n / 1e3) / 1e12
-        roof = {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": tflops_peak,
-                "unit": "TFLOP/s", "frac": achieved / tflops_peak,
-                "traffic": TRAFFIC_BYTES.get(dominant),
-                "peak_source": peak_src,
-                "algorithmic_flop_per_launch": flop_per_launch}
-    attn_roof = None
-    if "attn_sm100" in prof:
-        n, ms = prof["attn_sm100"]
-        a = attn_f * args.steps / n / (ms / n / 1e3) / 1e12
-        attn_roof = {"achieved": a, "frac": a / tflops_peak, "unit": "TFLOP/s",
-                     "traffic": TRAFFIC_BYTES["attn_sm100"],
-                     "algorithmic_flop_per_launch": attn_f * args.steps / n}
-    gemm_roof = None
-    if "gemm_bf16" in prof:
-        n, ms = prof["gemm_bf16"]
-        g = (proj + pos_f) * args.steps / (ms / 1e3) / 1e12
-        gemm_roof = {"achieved": g, "frac": g / tflops_peak, "unit": "TFLOP/s"}
+    for name, kind in FORWARD_LAUNCHES:
+        k = kern.setdefault(kind, {"launches": 0, "ms_total": 0.0})
+        k["launches"] += len(per_launch[name])
+        k["ms_total"] += sum(per_launch[name])
+    for k in kern.values():
+        k["share"] = k["ms_total"] / total_launch_ms
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        oracle_sample(w, x, lengths, 1, threads)  # warm-up
-        runs = [oracle_sample(w, x, lengths, 2, threads) for _ in range(3)]
+        oracle_sample(w, x, lengths, 2, threads)  # warm-up
+        runs = [oracle_sample(w, x, lengths, B, threads) for _ in range(3)]
         fr = runs[0][0]
         med = statistics.median(r[1] for r in runs)
         cpu = {"value": fr / med, "unit": "frames/s", "cores": threads, "kind": "port",
-               "sample": f"2 of 16 utterances ({fr} valid frames), median of 3 after a warm-up; "
-                         f"CPU restatement of the reference algorithm (ORC_REFERENCE_ALGO, bf16 "
-                         f"rounding), host CPU: {cpu_model()}"}
+               "sample": f"the whole batch ({B} utterances, {fr} valid frames), median of 3 "
+                         f"after a warm-up; CPU restatement of the reference algorithm "
+                         f"(ORC_REFERENCE_ALGO, bf16 rounding), host CPU: {cpu_model()}"}
+
+    # ---- multi-GPU designs beside the weak-scaled replicas (every rank)
+    extras = {}
+    if not args.no_extras:
+        extras["strong_scaling_config1"] = strong_split_attention(
+            nrp, ctx, attn, pos, w, x, lengths, world, rank, dev, barrier, args)
+        extras["seq_split_config4"] = seq_split_config4(nrp, ctx, world, rank, local, dev,
+                                                        barrier, args)
+        extras["strong_scaling_config3"] = strong_split_encoder(nrp, ctx, world, rank, dev,
+                                                                barrier, args)
 
     if rank == 0:
         line = {
@@ -467,11 +829,17 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "roofline": roof,
-            "roofline_kernels": {"attn_sm100": attn_roof, "gemm_bf16": gemm_roof},
+            "roofline_kernels": rk,
+            "kernel_times_note": "per-launch CUDA events on each launch's stream; linear_pos "
+                                 "runs on a second stream beside the q|k|v GEMM, so the "
+                                 "launch times overlap and their sum exceeds ms_per_step",
+            "whole_step_tflops": whole,
             "kernels": kern,
+            "host_link": link,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -511,7 +879,7 @@ SGL_WORKLOAD = ("BASELINE config 0: one rel-pos MHA layer, fp32, B=1 T=125 d_mod
 
 def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, workload,
              config, scaling, e2e, dtype, cpu=None, hbm_bytes=None, reset=None,
-             prof_step=None):
+             prof_step=None, long_step=False, extra=None):
     """Common timing for the secondary workloads: W warm-up steps, K steps
     timed with CUDA events (L2 flushed between steps, outside the events),
     max over ranks; per-kernel device time from the library's events over K
@@ -577,7 +945,7 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
     barrier()
     e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
 
-    tflops_peak, peak_src = _peak()
+    tflops_peak, peak_src = _peak(long_step)
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
     hbm_peak = peaks.get("hbm_gbs") or 6650.0
@@ -638,6 +1006,7 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
             "cpu_baseline": cpu() if (cpu and rank == 0 and world == 1 and
                                       not args.no_cpu_baseline) else None,
         }
+        line.update(extra or {})
         print(json.dumps(line), flush=True)
 
 
@@ -696,7 +1065,9 @@ def _load_quant_layers(nrp, orc, enc, rng):
 
 def main_encoder(args):
     """Config 3: forward_from_embeddings over 24 quantised blocks; weak
-    scaling (each rank its own 32-utterance batch)."""
+    scaling (each rank its own 32-utterance batch).  The line measures the
+    8-bit weights read as codes every forward; bf16_weight_copies gives the
+    same forward over kept bf16 copies of the weights."""
     import torch
     import torch.distributed as dist
     from __graft_entry__ import load_package
@@ -781,12 +1152,30 @@ def main_encoder(args):
                           f"{ENC_LAYERS} layers, time scaled to {ENC_LAYERS} layers; CPU "
                           f"restatement (oracle block_forward, bf16 rounding), host CPU: "
                           f"{cpu_model()}"}
+    # the variant with the weight cache on: each quantised weight's bf16 copy
+    # is kept after its first use, so the timed steps read bf16 weights
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    for k in range(3):
+        step(k)
+    n_kept = min(args.steps, 50)
+    kept_ms = _timed_steps(lambda: step(0), n_kept, dev, world, barrier, flush)
+    kept = {"value": world * valid * n_kept / (kept_ms / 1e3), "unit": "frames/s",
+            "ms_per_step": kept_ms / n_kept, "steps": n_kept,
+            "weights": "bf16 copies of the 8-bit weights, kept after their first use "
+                       "(nrp_context_set_weight_cache on; 0.6 GB of device memory)"}
+    # the measured line: every forward reads the u8 codes (weight cache off):
+    # each layer's weights are dequantised once per forward, on a side stream
+    # one layer ahead, into two bf16 slots
+    ctx.set_weight_cache(False)
     _harness(args, world, rank, local, ctx, step, valid, flops, None, ENC_WORKLOAD,
              {"batch_per_gpu": ENC_B, "seq_len": ENC_T, "layers": ENC_LAYERS,
-              "valid_frames_per_gpu": valid, "weights": "MLX 8-bit g64, fp16 scales",
+              "valid_frames_per_gpu": valid,
+              "weights": "MLX 8-bit g64, fp16 scales; the u8 codes are read every forward "
+                         "(weight cache off)",
               "parallelism": f"utterance-parallel replicas x{world}"},
              "weak", e2e, "bf16", cpu=cpu,
-             hbm_bytes=bytes_)
+             hbm_bytes=bytes_, long_step=True, extra={"bf16_weight_copies": kept})
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -1174,13 +1563,25 @@ def main_single(args):
     return 0
 
 
-def _peak():
+def _peaks():
+    """(burst, sustained) bf16 TFLOP/s and where they come from."""
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
-    p = peaks.get("bf16_tflops_sustained")
-    if p:
-        return p, "measured (bf16_tflops_sustained, MEASURED_PEAKS.json)"
-    return 1400.0, "fallback 1.4 PFLOP/s sustained"
+    b, s_ = peaks.get("bf16_tflops"), peaks.get("bf16_tflops_sustained")
+    if b and s_:
+        return b, s_, "measured (bf16_tflops, MEASURED_PEAKS.json)"
+    return 1590.0, 1400.0, "fallback 1.59 PFLOP/s burst"
+
+
+def _peak(long_step=False):
+    """The denominator of a workload's tensor roofline: the burst peak for
+    steps of a few ms or less, the sustained one for steps long enough to
+    settle under the power cap."""
+    b, s_, src = _peaks()
+    if long_step:
+        return s_, src.replace("bf16_tflops,", "bf16_tflops_sustained,").replace(
+            "1.59 PFLOP/s burst", "1.4 PFLOP/s sustained") + "; sustained: long steps"
+    return b, src
 
 
 def main_long(args):
@@ -1203,24 +1604,8 @@ def main_long(args):
                                 device_id=torch.device("cuda", local))
     nrp = load_package()
     ctx = nrp.Context(local)
-    rng = np.random.default_rng(4321)
-    f = lambda *sh: (rng.standard_normal(sh) * 0.02).astype(np.float32)
-    w = {"wq": f(D, D), "bq": f(D), "wk": f(D, D), "bk": f(D), "wv": f(D, D), "bv": f(D),
-         "wo": f(D, D), "bo": f(D), "wp": f(D, D), "pos_bias_u": f(H, D // H),
-         "pos_bias_v": f(H, D // H)}
-    attn = nrp.RelPositionMultiHeadAttention(D, H, True, ctx=ctx)
-    for which, (wk, bk) in enumerate((("wq", "bq"), ("wk", "bk"), ("wv", "bv"), ("wo", "bo"),
-                                      ("wp", None))):
-        attn.set_linear(which, nrp.LinearLayer.standard(w[wk], w[bk] if bk else None))
-    attn.set_pos_bias(w["pos_bias_u"], w["pos_bias_v"])
-    attn.set_dtype(nrp.BF16)
-    actx = nrp.AttentionContext.new(LONG_WINDOW, "regular")
-    pe = nrp.RelPositionalEncoding(D, 5000, True, device=local)
-    pe.set_dtype(nrp.BF16)
-    pos = pe.get_encoding(LONG_T)
+    w, attn, actx, pos, x = _long_module(nrp, ctx, local)
     dev = torch.device("cuda", local)
-    # every rank draws the whole sequence (same seed) and keeps its segment
-    x = np.random.default_rng(8765).standard_normal((LONG_B, LONG_T, D)).astype(np.float32)
     halo = None
     if world > 1:
         halo = nrp.HaloComm.from_process_group(ctx=ctx, timeout_ms=120000)

@@ -12,7 +12,17 @@
  *   - tensors are row-major; "device" pointers are caller-owned CUDA memory
  *     on the context's device; "host" pointers are read during the call;
  *   - device work is queued on the caller's cudaStream_t (passed as void*,
- *     NULL = legacy default stream) with no hidden device synchronisation;
+ *     NULL = legacy default stream).  A call synchronises nothing once the
+ *     library's workspace has grown to the shapes it sees: a call with a
+ *     larger shape than any before grows the module's intermediate buffers
+ *     with cudaMalloc (which synchronises the device), and a quantised
+ *     weight's first use at 256 or more rows makes its kept bf16 copy
+ *     (cudaMalloc, then one cudaStreamSynchronize of the caller's stream;
+ *     see nrp_context_set_weight_cache).  Warm a module up once at its
+ *     largest shape before latency-critical use or stream capture, or use
+ *     nrp_attn_forward_noalloc;
+ *   - every call that launches work makes its context's device current on
+ *     the calling thread (nrp_attn_forward_noalloc restores the caller's);
  *   - a handle is used by one host thread at a time (the reference's
  *     `&mut self` methods); one device per context.
  */
@@ -191,15 +201,21 @@ int nrp_attn_forward(nrp_attn* attn, void* stream, const void* x, int batch, int
  * which cannot wait on cudaMalloc's device synchronisation, or a process
  * whose device memory is handed out by another runtime's allocator.  Its
  * intermediate tensors live in a fixed 32 MiB array in the library's device
- * memory (held by every GPU that loads the library, until exit), so it
- * allocates nothing; sizes whose intermediates need more
- * (about 8 KB per frame plus 2 KB per position at d_model 1024, bf16) are
- * rejected with NRP_ERR_INVALID.  The module's parameters must already be on
- * the device (one nrp_attn_forward or nrp_attn_forward_with_cache call
- * uploads them); otherwise NRP_ERR_INVALID.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress), so make that
- * first call before any stream capture.  All calls share the array: calls
- * whose work overlaps on the GPU race and must be serialised by the caller. */
+ * memory, so it allocates nothing.  The array is committed, and its device
+ * address looked up, when the first context on a device is created
+ * (nrp_context_create); the device holds it from then until the process
+ * exits.  The limit is batch * seq_len * 8 KB + positions * 2 KB <= 32 MiB
+ * at d_model 1024 in bf16 (positions = 2 * seq_len - 1, or the rows a
+ * context window reaches: 257 for (128, 128)), i.e. about 2.8k frames for
+ * one utterance with full context; larger sizes are rejected with
+ * NRP_ERR_INVALID.  The module's parameters must already be on the device
+ * (one nrp_attn_forward or nrp_attn_forward_with_cache call uploads them);
+ * otherwise NRP_ERR_INVALID.  Quantised weights use the bf16 copies that
+ * call kept when it ran on 256 or more rows (the context's weight cache);
+ * without them the 8-bit GEMM dequantises in its producer, which is slower.
+ * The caller's current device is restored on return.  All calls share the
+ * array: calls whose work overlaps on the GPU race and must be serialised
+ * by the caller. */
 int nrp_attn_forward_noalloc(nrp_attn* attn, void* stream, const void* x, int batch, int seq_len,
                              const void* pos_emb, const int32_t* lengths,
                              const nrp_att_context* context, void* out);
@@ -558,6 +574,11 @@ int nrp_profile_enable(nrp_context* ctx, int enable);
 int nrp_profile_reset(nrp_context* ctx);
 /* Synchronises on the recorded events; writes launches and total ms of `kind`. */
 int nrp_profile_read(nrp_context* ctx, int kind, int64_t* launches, double* total_ms);
+/* The recorded launches since the last reset in the order the host issued
+ * them: kinds[i] (nrp_kernel_kind) and ms[i] for i < min(*count, capacity);
+ * *count = the number recorded.  Synchronises on the recorded events. */
+int nrp_profile_launches(nrp_context* ctx, int* kinds, float* ms, int64_t capacity,
+                         int64_t* count);
 
 #ifdef __cplusplus
 }

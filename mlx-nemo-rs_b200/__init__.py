@@ -161,6 +161,7 @@ def lib():
             "nrp_profile_enable": ([vp, i], i),
             "nrp_profile_reset": ([vp], i),
             "nrp_profile_read": ([vp, i, vp, vp], i),
+            "nrp_profile_launches": ([vp, vp, vp, C.c_int64, vp], i),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -233,6 +234,16 @@ class Context:
 
     def profile_reset(self):
         _check(lib().nrp_profile_reset(self.handle))
+
+    def profile_launches(self):
+        """[(kernel, ms)] of every recorded launch since the last reset, in
+        the order the host issued them."""
+        n = C.c_int64()
+        _check(lib().nrp_profile_launches(self.handle, None, None, 0, C.byref(n)))
+        kinds = (C.c_int * max(n.value, 1))()
+        ms = (C.c_float * max(n.value, 1))()
+        _check(lib().nrp_profile_launches(self.handle, kinds, ms, n.value, C.byref(n)))
+        return [(self.KERNELS[kinds[i]], float(ms[i])) for i in range(n.value)]
 
     def profile_read(self) -> Dict[str, Tuple[int, float]]:
         """{kernel: (launches, total ms)} for kernels that ran."""

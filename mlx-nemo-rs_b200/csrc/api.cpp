@@ -97,6 +97,7 @@ int prof_collect(nrp_context* c) {
     cudaEventElapsedTime(&ms, r.start, r.stop);
     c->prof_ms[r.kind] += ms;
     c->prof_n[r.kind] += 1;
+    c->prof_log.emplace_back(r.kind, ms);
     c->pool.push_back(r.start);
     c->pool.push_back(r.stop);
   }
@@ -534,6 +535,9 @@ int nrp_context_create(int device, nrp_context** out) {
   if (prop.major != 10)
     return fail(NRP_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                 device, prop.major, prop.minor);
+  // the no-allocation forward's static array: its module is loaded (and the
+  // array's device memory committed) here, not by a noalloc call
+  if (int rc = nrp::noalloc_scratch_prepare(device)) return rc;
   auto* c = new nrp_context;
   c->device = device;
   c->num_sms = prop.multiProcessorCount;
@@ -1268,7 +1272,23 @@ int nrp_profile_reset(nrp_context* ctx) {
     ctx->prof_ms[k] = 0.0;
     ctx->prof_n[k] = 0;
   }
+  ctx->prof_log.clear();
   return rc;
+}
+
+int nrp_profile_launches(nrp_context* ctx, int* kinds, float* ms, int64_t capacity,
+                         int64_t* count) {
+  if (!ctx || !count || capacity < 0 || (capacity > 0 && (!kinds || !ms)))
+    return fail(NRP_ERR_INVALID, "invalid profile log arguments");
+  int rc = prof_collect(ctx);
+  if (rc) return rc;
+  const int64_t n = static_cast<int64_t>(ctx->prof_log.size());
+  for (int64_t i = 0; i < n && i < capacity; ++i) {
+    kinds[i] = ctx->prof_log[i].first;
+    ms[i] = ctx->prof_log[i].second;
+  }
+  *count = n;
+  return ok();
 }
 
 int nrp_profile_read(nrp_context* ctx, int kind, int64_t* launches, double* total_ms) {

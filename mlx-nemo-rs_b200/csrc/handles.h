@@ -57,6 +57,13 @@ struct ProfRec {
 // Sets this thread's nrp_last_error() message and returns `code`.
 int report_error(int code, const char* msg);
 
+// Looks up, on `device` (the current device), the device address of the
+// static array nrp_attn_forward_noalloc keeps its intermediates in
+// (noalloc.cu).  The array lives in a module of its own, which the CUDA
+// runtime loads -- committing the array's device memory -- on this first
+// use; nrp_context_create calls it so that no noalloc call ever does.
+int noalloc_scratch_prepare(int device);
+
 }  // namespace nrp
 
 // d_err[0]: the sticky device error code; then kSchedSlots pairs of ints,
@@ -75,6 +82,7 @@ struct nrp_context {
   std::vector<cudaEvent_t> pool;
   double prof_ms[NRP_KERNEL_KINDS] = {};
   int64_t prof_n[NRP_KERNEL_KINDS] = {};
+  std::vector<std::pair<int, float>> prof_log;  // (kind, ms) per launch, issue order
   // bf16 copy of one quantised weight for the large-M quantised GEMM
   // (stream-ordered: reused by every such call on the context)
   nrp::DevBuf wscratch;

@@ -11,12 +11,16 @@
 // places its intermediates in g_static_scratch, a fixed array in the
 // library's own device memory, so the call allocates nothing.
 //
-// The array is kStaticScratchBytes (32 MiB).  Every GPU that loads this
-// library holds it until the process exits, and every call shares it: a call
-// overwrites what the previous call left there (it clears nothing because
-// every byte it reads is written earlier in the same call), and two calls
-// whose work overlaps on the GPU (different streams, or different modules on
-// one device) race on it.  Callers serialise such calls themselves.
+// The array is kStaticScratchBytes (32 MiB).  It sits in a module of its own
+// (this file has no kernels), which the CUDA runtime loads on the first use
+// of the array: nrp_context_create makes that use (it looks the array's
+// device address up), so every GPU with a context holds the array from then
+// until the process exits, and no noalloc call loads anything.  Every call
+// shares the array: a call overwrites what the previous call left there (it
+// clears nothing because every byte it reads is written earlier in the same
+// call), and two calls whose work overlaps on the GPU (different streams, or
+// different modules on one device) race on it.  Callers serialise such calls
+// themselves.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -43,23 +47,31 @@ int report(int code, const char* fmt, long long a = 0, long long b = 0) {
   return nrp::report_error(code, buf);
 }
 
-// Device address of g_static_scratch on `device` (the current device).  The
-// host-side name of the array is not a device address, so it is looked up
-// once per device with cudaGetSymbolAddress and cached.
-int scratch_address(int device, void** out) {
-  if (device < 0 || device >= kMaxDevices)
-    return report(NRP_ERR_UNSUPPORTED, "device %lld beyond the scratch table", device);
+// Device address of g_static_scratch on `device`, looked up by
+// nrp::noalloc_scratch_prepare when the device's first context was created.
+void* scratch_address(int device) {
+  if (device < 0 || device >= kMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[device]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess || !p)
-      return nrp::report_error(NRP_ERR_CUDA, cudaGetErrorString(e));
-    g_scratch_addr[device] = p;
-  }
-  *out = g_scratch_addr[device];
-  return NRP_OK;
+  return g_scratch_addr[device];
 }
+
+// Makes `device` current for the call and gives the caller's current device
+// back when the call returns.
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t enter(int device) {
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return e;
+    if (prev == device) {
+      prev = -1;
+      return cudaSuccess;
+    }
+    return cudaSetDevice(device);
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 
 #define TRY_CUDA(expr)                                                         \
   do {                                                                         \
@@ -70,8 +82,12 @@ int scratch_address(int device, void** out) {
     }                                                                          \
   } while (0)
 
-// y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias), as nrp_attn_forward runs
-// its projections, with nothing allocated.
+// y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias), with nothing allocated.
+// The kernels are those nrp_attn_forward runs.  A quantised weight with many
+// rows uses the bf16 copy an earlier allocating forward kept (the context's
+// weight cache), as nrp_attn_forward does; without one, the 8-bit tcgen05
+// GEMM dequantises it in its producer (correct, but it redoes the
+// dequantisation per 128-row tile: about a fifth of the bf16 GEMM's rate).
 int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, int K,
            const void* w, bool quant, const void* qs, const void* qb, int N, const void* bias,
            void* y, int ldy) {
@@ -90,6 +106,13 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
                                static_cast<const __nv_bfloat16*>(bias),
                                static_cast<__nv_bfloat16*>(y), ldy, N, st));
     return NRP_OK;
+  }
+  if (quant && M >= 256) {
+    const auto it = ctx->deq_cache.find(w);
+    if (it != ctx->deq_cache.end()) {
+      w = it->second->p;
+      quant = false;
+    }
   }
   CUtensorMap mx;
   if (!nrp::make_tmap_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M,
@@ -112,6 +135,26 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
 
 }  // namespace
 
+namespace nrp {
+
+int noalloc_scratch_prepare(int device) {
+  if (device < 0 || device >= kMaxDevices)
+    return report(NRP_ERR_UNSUPPORTED, "device %lld beyond the static scratch table", device);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[device]) return NRP_OK;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess || !p) {
+    (void)cudaGetLastError();
+    return report_error(NRP_ERR_CUDA, e != cudaSuccess ? cudaGetErrorString(e)
+                                                       : "no device address for the static scratch");
+  }
+  g_scratch_addr[device] = p;
+  return NRP_OK;
+}
+
+}  // namespace nrp
+
 extern "C" int nrp_attn_forward_noalloc(nrp_attn* a, void* stream, const void* x, int B, int T,
                                         const void* pos_emb, const int32_t* lengths,
                                         const nrp_att_context* context, void* out) {
@@ -122,40 +165,45 @@ extern "C" int nrp_attn_forward_noalloc(nrp_attn* a, void* stream, const void* x
                   "the module's parameters are not on the device yet: one nrp_attn_forward or "
                   "nrp_attn_forward_with_cache call (which allocates them) must come first");
   nrp_context* ctx = a->ctx;
-  int cur = -1;
-  TRY_CUDA(cudaGetDevice(&cur));
-  if (cur != ctx->device) TRY_CUDA(cudaSetDevice(ctx->device));
+  DeviceScope scope;
+  TRY_CUDA(scope.enter(ctx->device));
   const int D = a->D, P = 2 * T - 1;
   const size_t es = a->dtype == NRP_DTYPE_BF16 ? 2 : 4;
   const size_t BT = static_cast<size_t>(B) * T;
+  nrp::AttnContextDev cd{0, -1, -1, 0};
+  if (context) cd = {1, context->left, context->right, context->chunked};
+  // bf16 projects only the P rows the context's relative positions reach
+  // (257 for a (128, 128) window), as nrp_attn_forward; f32 all 2T-1
+  nrp::AttnGeom g = nrp::full_geom(T, D);
+  if (a->dtype == NRP_DTYPE_BF16) {
+    int dmin, dmax;
+    nrp::visible_offsets(cd, T, dmin, dmax);
+    g.p_base = T - 1 + dmin;
+    g.p_rows = dmax - dmin + 1;
+  }
   const size_t qkv_bytes = round256(BT * 3 * D * es);
   const size_t ctx_bytes = round256(BT * D * es);
-  const size_t pos_bytes = round256(static_cast<size_t>(P) * D * es);
+  const size_t pos_bytes =
+      round256(static_cast<size_t>(a->dtype == NRP_DTYPE_BF16 ? g.p_rows : P) * D * es);
   const size_t need = qkv_bytes + ctx_bytes + pos_bytes;
   if (need > kStaticScratchBytes)
     return report(NRP_ERR_INVALID,
                   "batch x seq_len needs %lld bytes of intermediates, more than the %lld-byte "
                   "static scratch of nrp_attn_forward_noalloc (use nrp_attn_forward)",
                   static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes));
-  void* base = nullptr;
-  int rc = scratch_address(ctx->device, &base);
-  if (rc) return rc;
+  void* base = scratch_address(ctx->device);
+  if (!base)
+    return report(NRP_ERR_INVALID,
+                  "no static scratch address for device %lld (no context was created on it)",
+                  ctx->device);
   uint8_t* qkv = static_cast<uint8_t*>(base);
   uint8_t* cbuf = qkv + qkv_bytes;
   uint8_t* pbuf = cbuf + ctx_bytes;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant, a->s_qkv.p,
-              a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, qkv, 3 * D);
+  int rc = linear(ctx, st, a->dtype, x, static_cast<int>(BT), D, a->w_qkv.p, a->qkv_quant,
+                  a->s_qkv.p, a->z_qkv.p, 3 * D, a->has_b_qkv ? a->b_qkv.p : nullptr, qkv, 3 * D);
   if (rc) return rc;
-  nrp::AttnContextDev cd{0, -1, -1, 0};
-  if (context) cd = {1, context->left, context->right, context->chunked};
   if (a->dtype == NRP_DTYPE_BF16) {
-    // linear_pos over the P rows the context reaches, as nrp_attn_forward
-    nrp::AttnGeom g = nrp::full_geom(T, D);
-    int dmin, dmax;
-    nrp::visible_offsets(cd, T, dmin, dmax);
-    g.p_base = T - 1 + dmin;
-    g.p_rows = dmax - dmin + 1;
     rc = linear(ctx, st, a->dtype,
                 static_cast<const uint8_t*>(pos_emb) + static_cast<size_t>(g.p_base) * D * es,
                 g.p_rows, D, a->w_pos.p, a->pos_quant, a->s_pos.p, a->z_pos.p, D, nullptr, pbuf,

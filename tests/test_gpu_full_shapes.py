@@ -1,0 +1,116 @@
+"""Device parity at BASELINE's full shapes, against the CPU oracle, through
+the C ABI (bf16 tolerance 2e-2 of the output scale, plus a per-element bound
+|got - ref| <= 2e-2 * (rms(ref) + |ref|), over valid rows).
+
+- Config 4: one windowed layer at [4, 12500, 1024], window (128, 128), on one
+  GPU.  With a window, an output row depends on the input frames within 128
+  of it only, and the projected positions depend on the relative position
+  only (attention.rs:59-103, 232-272), so the oracle checks the device's
+  full-length forward on 512-frame segments: both ends of every utterance
+  and one interior stretch (rows whose whole window lies in the segment).
+- Config 2: cache-aware streaming attention (attention.rs:606-816,
+  conformer.rs:883-1000) with 64 sessions, chunk 14, cache 70,
+  chunked_limited [70, 13], over 10 chunks: the fill-up and the full cache.
+- Config 3: the 24-layer encoder with MLX 8-bit linears from N(0, 0.02^2)
+  masters (forward_from_embeddings, conformer.rs:542-550, 694-722) on two
+  short utterances.
+"""
+import numpy as np
+import pytest
+
+from conftest import rand_block, rand_weights
+from __graft_entry__ import load_package
+from test_gpu_parity import check_close, make_module
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 2e-2
+
+
+@pytest.fixture(scope="module")
+def nrp():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return load_package()
+
+
+def test_config4_windowed_layer_full_length(nrp, orc):
+    import torch
+    B, T, D, H, W, SEG = 4, 12500, 1024, 8, 128, 512
+    rng = np.random.default_rng(4)
+    w = rand_weights(rng, D, H)
+    attn = make_module(nrp, w, D, H, nrp.BF16)
+    x = orc.bf16_round(rng.standard_normal((B, T, D)).astype(np.float32))
+    pe = nrp.RelPositionalEncoding(D, 5000, False)
+    pe.set_dtype(nrp.BF16)
+    ctx = nrp.AttentionContext.new((W, W), "regular")
+    got = attn.forward(torch.from_numpy(x).to("cuda", torch.bfloat16), pe.get_encoding(T), ctx)
+    attn.ctx.check()
+    got = got.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    # segments [start, start + SEG) and the rows of each whose window
+    # [i - W, i + W] lies inside the segment (or is cut by the sequence end)
+    segs = [(0, 0, SEG - W), (6000, 6000 + W, 6000 + SEG - W), (T - SEG, T - SEG + W, T)]
+    xs = np.concatenate([x[:, s:s + SEG] for s, _, _ in segs])
+    ref = orc.mha_forward(xs, w, pe.get_encoding_host(SEG)[0], H, context=(W, W, False),
+                          bf16=True)
+    for k, (s, lo, hi) in enumerate(segs):
+        r = ref[k * B:(k + 1) * B, lo - s:hi - s]
+        check_close(got[:, lo:hi], r, None, TOL_BF16)
+
+
+def test_config2_streaming_64_sessions(nrp, orc):
+    import torch
+    B, D, H, C, T, ctx = 64, 1024, 8, 70, 14, (70, 13, True)
+    rng = np.random.default_rng(2)
+    w = rand_weights(rng, D, H)
+    attn = make_module(nrp, w, D, H, nrp.BF16)
+    cache = nrp.AttentionCache(attn, B, C)
+    pe = nrp.RelPositionalEncoding(D, 5000, False)
+    pe.set_dtype(nrp.BF16)
+    pos = pe.get_encoding(C + T)
+    pos_h = pe.get_encoding_host(C + T)[0]
+    context = nrp.AttentionContext.new(ctx[:2], "chunked_limited")
+    h_ref = np.zeros((B, C, D), np.float32)
+    filled = 0
+    for step in range(10):
+        x = orc.bf16_round(rng.standard_normal((B, T, D)).astype(np.float32))
+        out = attn.forward_with_cache(torch.from_numpy(x).to("cuda", torch.bfloat16), pos, cache,
+                                      filled, T, context)
+        attn.ctx.check()
+        got = out.float().cpu().numpy()
+        ref, nxt = orc.stream_layer_step(x, w, pos_h, H, h_ref, filled, T, ctx[0], ctx[1], True,
+                                         0, bf16=True)
+        check_close(got, ref, None, TOL_BF16)
+        assert np.abs(cache.export_h().cpu().numpy() - h_ref).max() <= 1e-6, step
+        filled = nxt
+    assert filled == C
+
+
+def test_config3_encoder_24_layers_8bit(nrp, orc):
+    import torch
+    L, D, H, ff, K = 24, 1024, 8, 4096, 9
+    B, T = 2, 100
+    lengths = np.array([100, 61], np.int32)
+    seeds = [3000 + i for i in range(L)]
+    enc = nrp.ConformerEncoder(L, D, H, ff, K)
+    wd = {}
+    for i, sd in enumerate(seeds):
+        _, w = rand_block(np.random.default_rng(sd), D, H, ff, K, quant=True, orc=orc,
+                          prefix=f"encoder.layers.{i}", scale=0.02)
+        wd.update(w)
+    enc.load_weights(wd, nrp.QuantizationConfig(8, 64))
+    del wd
+    enc.set_dtype(nrp.BF16)
+    x = np.random.default_rng(7).standard_normal((B, T, D)).astype(np.float32)
+    out, _ = enc.forward_from_embeddings(torch.from_numpy(x).cuda().bfloat16(), lengths)
+    enc.ctx.check()
+    got = out.float().cpu().numpy().transpose(0, 2, 1)
+    h = orc.bf16_round(orc.bf16_round(x) * np.float32(np.sqrt(D)))
+    pe = orc.get_encoding(D, 5000, T)
+    for sd in seeds:  # the same layers again, one at a time
+        bw, _ = rand_block(np.random.default_rng(sd), D, H, ff, K, quant=True, orc=orc,
+                           prefix="b", scale=0.02)
+        h = orc.block_forward(h, bw, pe, H, ff, K, lengths=lengths, bf16=True)
+    check_close(got, h, lengths, TOL_BF16)

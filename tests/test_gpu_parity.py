@@ -3,8 +3,10 @@
 Tolerances: f32 modules 1e-4, bf16 modules 2e-2, as
 max-abs error relative to the output's scale: rel = max|got - ref| /
 max|ref| over the valid query rows (padded rows are unspecified in the reference,
-src/asr/modules/encoders/conformer.rs:1590-1593).  The bf16 oracle rounds to
-bf16 where the reference's bf16 graph does.
+src/asr/modules/encoders/conformer.rs:1590-1593), and per element
+|got - ref| <= tol * (rms(ref) + |ref|), so that a wrong small element
+cannot hide behind the largest one.  The bf16 oracle rounds to bf16 where the
+reference's bf16 graph does.
 """
 import numpy as np
 import pytest
@@ -49,6 +51,23 @@ def rel_err(got, ref, lengths=None):
     return a, a / max(float(np.abs(r).max()), 1e-12)
 
 
+def check_close(got, ref, lengths, tol):
+    """Asserts both bounds of the module docstring over the valid rows
+    (lengths None: all rows) and returns (max abs err, max-normalised err,
+    worst per-element ratio)."""
+    if lengths is None:
+        lengths = [got.shape[1]] * got.shape[0]
+    g = np.concatenate([got[b, :L].ravel() for b, L in enumerate(lengths)]).astype(np.float64)
+    r = np.concatenate([ref[b, :L].ravel() for b, L in enumerate(lengths)]).astype(np.float64)
+    d = np.abs(g - r)
+    a = float(d.max())
+    rel = a / max(float(np.abs(r).max()), 1e-12)
+    rms = float(np.sqrt(np.mean(r * r)))
+    worst = float((d / (tol * (rms + np.abs(r)) + 1e-30)).max())
+    assert rel < tol and worst <= 1.0, (a, rel, worst)
+    return a, rel, worst
+
+
 def make_module(nrp, w, D, H, dtype, use_bias=True):
     attn = nrp.RelPositionMultiHeadAttention(D, H, use_bias)
     attn.load_weights(weight_dict(w), "l")
@@ -84,8 +103,7 @@ def test_linear_bf16_tcgen05(nrp, orc, M, K, N):
     dev = lambda a: torch.from_numpy(a).to("cuda", torch.bfloat16)
     y = nrp.linear(dev(x), dev(w), dev(b)).float().cpu().numpy()
     ref = orc.linear(x, w, b)
-    a, r = rel_err(y[None], ref[None])
-    assert r < 1e-2, (a, r)  # bf16 output rounding only
+    check_close(y[None], ref[None], None, 1e-2)  # bf16 output rounding only
 
 
 def test_linear_f32(nrp, orc):
@@ -96,16 +114,17 @@ def test_linear_f32(nrp, orc):
     b = (rng.standard_normal(1024) * 0.02).astype(np.float32)
     y = nrp.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(),
                    torch.from_numpy(b).cuda()).cpu().numpy()
-    a, r = rel_err(y[None], orc.linear(x, w, b)[None])
-    assert a < TOL_F32 and r < TOL_F32, (a, r)
+    a, _, _ = check_close(y[None], orc.linear(x, w, b)[None], None, TOL_F32)
+    assert a < TOL_F32
 
 
-@pytest.mark.parametrize("M", [1, 14, 16, 17, 300, 896, 1024, 2500])
+@pytest.mark.parametrize("M", [1, 14, 16, 17, 64, 128, 200, 255, 256, 300, 896, 1024, 2500])
 @pytest.mark.parametrize("K,N", [(1024, 1024), (1024, 4096), (4096, 1024)])
 def test_qlinear_mlx_affine_8bit(nrp, orc, M, K, N):
-    """M <= 16: the GEMV; up to 1023 rows: the tcgen05 GEMM with the
-    dequantising producer; from 1024 rows: the weight dequantised once, then
-    the bf16 GEMM."""
+    """M <= 16: the GEMV; 17 to 255 rows: the tcgen05 GEMM with the
+    dequantising producer (17, 64, 128, 200, 255: one and two row tiles,
+    full and ragged); from 256 rows: the weight dequantised once per call
+    (caller-owned weights are never kept), then the bf16 GEMM."""
     import torch
     rng = np.random.default_rng(M * 7 + N)
     wm = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
@@ -117,8 +136,7 @@ def test_qlinear_mlx_affine_8bit(nrp, orc, M, K, N):
     y = nrp.qlinear(dev(x), torch.from_numpy(wq.view(np.int32)).cuda(), dev(s), dev(z),
                     dev(bias)).float().cpu().numpy()
     ref = orc.linear(x, orc.dequantize(wq, s, z, 64, 8), bias)
-    a, r = rel_err(y[None], ref[None])
-    assert r < 1e-2, (a, r)
+    check_close(y[None], ref[None], None, 1e-2)
 
 
 # ------------------------------------------------------- offline, f32
@@ -137,8 +155,7 @@ def test_f32_reference_test_shapes(nrp, orc, context):
     got, pe = run_forward(nrp, attn, x, T, lengths, context, nrp.F32)
     ref = orc.mha_forward(x, w, pe, H, lengths=lengths, context=context,
                           mode=orc.ORC_REFERENCE_ALGO)
-    a, r = rel_err(got, ref, lengths)
-    assert r < TOL_F32, (a, r)
+    check_close(got, ref, lengths, TOL_F32)
 
 
 def test_f32_config0(nrp, orc):
@@ -150,8 +167,8 @@ def test_f32_config0(nrp, orc):
     attn = make_module(nrp, w, D, H, nrp.F32)
     got, pe = run_forward(nrp, attn, x, T, None, None, nrp.F32)
     ref = orc.mha_forward(x, w, pe, H, mode=orc.ORC_REFERENCE_ALGO)
-    a, r = rel_err(got, ref)
-    assert a < TOL_F32 and r < TOL_F32, (a, r)  # outputs are O(0.1): both hold
+    a, _, _ = check_close(got, ref, None, TOL_F32)
+    assert a < TOL_F32  # outputs are O(0.1): the absolute bound holds too
 
 
 # ------------------------------------------------------ offline, bf16
@@ -177,13 +194,12 @@ def test_bf16_offline(nrp, orc, B, T, lengths, context):
     got, pe = run_forward(nrp, attn, x, T, ln, context, nrp.BF16)
     assert np.isfinite(got).all()
     ref = orc.mha_forward(x, w, pe, H, lengths=ln, context=context, bf16=True)
-    a, r = rel_err(got, ref, ln)
-    assert r < TOL_BF16, (a, r)
+    check_close(got, ref, ln, TOL_BF16)
 
 
 def test_bf16_config1_shape(nrp, orc):
     """BASELINE config 1 layer: [16,750,1024] bf16, lengths U[375,750]; the
-    oracle checks 3 utterances (the rest run on the GPU in the same batch)."""
+    oracle checks all 16 utterances."""
     rng = np.random.default_rng(1)
     B, T, D, H = 16, 750, 1024, 8
     w = rand_weights(rng, D, H)
@@ -192,10 +208,8 @@ def test_bf16_config1_shape(nrp, orc):
     attn = make_module(nrp, w, D, H, nrp.BF16)
     got, pe = run_forward(nrp, attn, x, T, ln, None, nrp.BF16)
     assert np.isfinite(got).all()
-    sel = [0, 7, 15]
-    ref = orc.mha_forward(x[sel], w, pe, H, lengths=ln[sel], bf16=True)
-    a, r = rel_err(got[sel], ref, ln[sel])
-    assert r < TOL_BF16, (a, r)
+    ref = orc.mha_forward(x, w, pe, H, lengths=ln, bf16=True)
+    check_close(got, ref, ln, TOL_BF16)
 
 
 def test_bf16_quantized_projections(nrp, orc):
@@ -219,8 +233,7 @@ def test_bf16_quantized_projections(nrp, orc):
     ln = np.array([300, 211], np.int32)
     got, pe = run_forward(nrp, attn, x, T, ln, None, nrp.BF16)
     ref = orc.mha_forward(x, deq, pe, H, lengths=ln, bf16=True)
-    a, r = rel_err(got, ref, ln)
-    assert r < TOL_BF16, (a, r)
+    check_close(got, ref, ln, TOL_BF16)
 
 
 # ---------------------------------------------------------- streaming
@@ -274,8 +287,7 @@ def test_streaming_chunks(nrp, orc, dtype_name, D, H, C, T, ctx, drop):
         ref, nxt = orc.stream_layer_step(x, w, pos_h, H, h_ref, filled, valid, l, r,
                                          bool(ctx and ctx[2]), drop, bf16=bf)
         if valid > 0:
-            a, rr = rel_err(got, ref, [valid] * B)
-            assert rr < tol, (step, a, rr)
+            check_close(got, ref, [valid] * B, tol)
         if valid < T:
             # rows that see no key have a zero context, so linear_out leaves
             # exactly its bias there (attention.rs:786-789, 807)
