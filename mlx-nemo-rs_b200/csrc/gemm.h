@@ -146,8 +146,10 @@ cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq
                          cudaStream_t stream);
 
 // ---- fp32 CUDA-core GEMM (fp32 module dtype): y = x . W^T (+ bias) ----
+// num_sms: the device's SM count (the tile height is chosen for two CTAs per SM)
 cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
-                            const float* bias, float* y, int ldy, cudaStream_t stream);
+                            const float* bias, float* y, int ldy, int num_sms,
+                            cudaStream_t stream);
 
 // ---- offline fused rel-pos attention, bf16, tcgen05 ----
 // Where a launch's rows sit in the sequence.  All frame indices are global

@@ -156,11 +156,13 @@ void launch_f32(bool vec, const float* x, int M, int K, const float* w, int N, c
 }  // namespace
 
 cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
-                            const float* bias, float* y, int ldy, cudaStream_t stream) {
+                            const float* bias, float* y, int ldy, int num_sms,
+                            cudaStream_t stream) {
   const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  // 32-row tiles when 64-row ones would give fewer than two CTAs per SM
   const long tiles64 = static_cast<long>((M + 63) / 64) * ((N + kFN - 1) / kFN);
-  if (tiles64 < 2 * 148)
+  if (tiles64 < 2L * (num_sms > 0 ? num_sms : 148))
     launch_f32<32>(vec, x, M, K, w, N, bias, y, ldy, stream);
   else
     launch_f32<64>(vec, x, M, K, w, N, bias, y, ldy, stream);

@@ -46,6 +46,56 @@ def test_rust_binding_declares_every_function():
     assert bound - names == set(), sorted(bound - names)
 
 
+RUST = os.path.join(ROOT, "mlx-nemo-rs_b200", "rust")
+
+
+def test_rust_sys_crate_matches_header():
+    """The -sys crate (mlx-nemo-rs_b200/rust/nemo-relpos-sys, not compiled
+    here: no Rust toolchain) declares every function and constant of the
+    header, and only those, with the header's values."""
+    names = set(_declared_functions())
+    src = open(os.path.join(RUST, "nemo-relpos-sys", "src", "lib.rs")).read()
+    bound = set(re.findall(r"\bpub fn (nrp_[a-z0-9_]+)\(", src))
+    assert bound == names, (sorted(names - bound), sorted(bound - names))
+    hdr = open(os.path.join(ROOT, "include", "nemo_relpos.h")).read()
+    consts = dict(re.findall(r"^#define (NRP_[A-Z0-9_]+) (-?\d+)", hdr, re.M))
+    consts.update(re.findall(r"\b(NRP_[A-Z0-9_]+) = (-?\d+)", hdr))
+    rust = dict(re.findall(r"pub const (NRP_[A-Z0-9_]+): \w+ = (-?\d+);", src))
+    assert rust == consts
+    build = open(os.path.join(RUST, "nemo-relpos-sys", "build.rs")).read()
+    srcs = set(re.findall(r'"([a-z0-9_]+\.(?:cu|cpp))"', build))
+    csrc = {f for f in os.listdir(os.path.join(ROOT, "mlx-nemo-rs_b200", "csrc"))
+            if f.endswith((".cu", ".cpp"))}
+    assert srcs == csrc, (sorted(csrc - srcs), sorted(srcs - csrc))
+
+
+def test_rust_safe_crate_keeps_reference_signatures():
+    """The safe crate calls only functions the -sys crate declares and keeps
+    the reference's method names and argument lists
+    (attention.rs:35-188, 220, 280, 367, 409, 446, 606, 863)."""
+    sys_src = open(os.path.join(RUST, "nemo-relpos-sys", "src", "lib.rs")).read()
+    declared = set(re.findall(r"\bpub fn ([a-zA-Z0-9_]+)\(", sys_src))
+    src = open(os.path.join(RUST, "nemo-relpos", "src", "lib.rs")).read()
+    called = set(re.findall(r"\bsys::(?:cuda::)?([a-zA-Z0-9_]+)\(", src))
+    assert called and called <= declared, sorted(called - declared)
+    for sig in [
+        r"pub fn new\(d_model: i32, max_len: i32, xscaling: bool\) -> Self",
+        r"pub fn get_encoding\(&self, seq_len: i32\) -> Result<Array>",
+        r"pub fn new\(size: \(i32, i32\), style: &str\) -> Option<Self>",
+        r"pub fn key_padding_mask\(lengths: &\[i32\], max_len: i32\) -> Result<Option<Array>>",
+        r"pub fn new\(d_model: i32, n_heads: i32, use_bias: bool\) -> Result<Self>",
+        r"pub fn set_dtype\(&mut self, dtype: Dtype\) -> Result<\(\)>",
+        r"pub fn forward\(&mut self, x: &Array, pos_emb: &Array, context: Option<AttentionContext>,"
+        r"\s+key_mask: Option<&Array>\) -> Result<Array>",
+        r"pub fn forward_with_cache\(&mut self, x: &Array, pos_emb: &Array, cache: Option<&Array>,"
+        r"\s+filled: i32, att_mask: Option<&Array>\)\s+-> Result<\(Array, Option<Array>\)>",
+        r"pub fn load_weights\(&mut self, weights: &Weights, prefix: &str,"
+        r"\s+quant: Option<&QuantizationConfig>\) -> Result<\(\)>",
+        r"pub cache_drop_size: i32", r"pub att_context_size: Option<AttentionContext>",
+    ]:
+        assert re.search(sig, src), sig
+
+
 def test_python_mirror_declares_every_function():
     """The Python mirror gives ctypes argument and return types for every
     function the header declares."""
