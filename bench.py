@@ -481,10 +481,13 @@ def strong_split_encoder(nrp, ctx, world, rank, dev, barrier, args):
                         "nrp_partition_utterances; no collective"}
 
 
-# config 3's block linears (N, K): FF1 1024->4096->1024, pointwise convs,
-# q, k, v, out, pos; 24 layers
-QL_SHAPES = [(ENC_FF, D), (D, ENC_FF), (2 * D, D), (D, D), (ENC_FF, D), (D, ENC_FF),
-             (D, D), (D, D), (D, D), (D, D), (D, D)]
+def ql_shapes():
+    """Config 3's block linears (N, K): FF1 1024->4096->1024, the pointwise
+    convs, FF2, then q, k, v, out, pos."""
+    return [(ENC_FF, D), (D, ENC_FF), (2 * D, D), (D, D), (ENC_FF, D), (D, ENC_FF),
+            (D, D), (D, D), (D, D), (D, D), (D, D)]
+
+
 QL_WORKLOAD = ("config 3's MLX 8-bit linears (group 64, bf16 scales and biases): the 11 linears "
                "of each of 24 layers, one after another on one stream, at M rows (M = 14: one "
                "streaming session's 14-frame chunk; M = 128)")
@@ -508,7 +511,7 @@ def main_qlinear(args):
     g.manual_seed(77)
     layers = []
     for _ in range(ENC_LAYERS):
-        for n, k in QL_SHAPES:
+        for n, k in ql_shapes():
             wq = torch.randint(-2**31, 2**31 - 1, (n, k // 4), dtype=torch.int32, device=dev,
                                generator=g)
             sc = (torch.rand((n, k // 64), device=dev, generator=g) * 4e-4 + 1e-4).bfloat16()
@@ -525,7 +528,7 @@ def main_qlinear(args):
 
     def measure(M, n_steps):
         xs = {k: torch.randn((M, k), device=dev, generator=g).bfloat16()
-              for k in {k for _, k in QL_SHAPES}}
+              for k in {k for _, k in ql_shapes()}}
         ys = [torch.empty((M, n), dtype=torch.bfloat16, device=dev) for *_, n, _ in layers]
 
         def run():

@@ -4,9 +4,13 @@ Tolerances: f32 modules 1e-4, bf16 modules 2e-2, as
 max-abs error relative to the output's scale: rel = max|got - ref| /
 max|ref| over the valid query rows (padded rows are unspecified in the reference,
 src/asr/modules/encoders/conformer.rs:1590-1593), and per element
-|got - ref| <= tol * (rms(ref) + |ref|), so that a wrong small element
+|got - ref| <= tol * (|ref| + 4 * rms(ref)), so that a wrong small element
 cannot hide behind the largest one.  The bf16 oracle rounds to bf16 where the
-reference's bf16 graph does.
+reference's bf16 graph does -- among them the positional scores bd * scale
+before the softmax (attention.rs:530-556), which the device keeps in f32.
+That rounding moves a whole row's probabilities, so its effect on an output
+element scales with the row's magnitude, not the element's: the 4 * rms(ref)
+term (0.08 rms at tol 2e-2).
 """
 import numpy as np
 import pytest
@@ -63,7 +67,7 @@ def check_close(got, ref, lengths, tol):
     a = float(d.max())
     rel = a / max(float(np.abs(r).max()), 1e-12)
     rms = float(np.sqrt(np.mean(r * r)))
-    worst = float((d / (tol * (rms + np.abs(r)) + 1e-30)).max())
+    worst = float((d / (tol * (4.0 * rms + np.abs(r)) + 1e-30)).max())
     assert rel < tol and worst <= 1.0, (a, rel, worst)
     return a, rel, worst
 
