@@ -497,10 +497,13 @@ def main_qlinear(args):
     """North-star kernel (3), LinearLayer::forward's quantised arm
     (quantization.rs:137-160) through nrp_qlinear: one step runs all 264
     linears of config 3's 24 layers on M rows, replayed as a CUDA graph (the
-    launches are microseconds each).  M = 14 takes the GEMV (HBM-bound:
-    codes, scales and biases read once); M = 128 the tcgen05 GEMM that
-    dequantises the codes in its B producer.  Algorithmic bytes per linear:
-    N*K codes + 4*N*K/64 scale/bias + 2*M*K in + 2*M*N out; FLOP 2*M*N*K."""
+    launches are microseconds each).  Both row counts take the small-M
+    8-bit kernel (codes staged in shared memory by bulk copies, dequantised
+    in registers into bf16 MMA fragments); M = 128 runs two 64-row chunks.
+    one_large_launch: a single linear over 64 MB of codes, the kernel's
+    streaming rate with its launch latency amortised.  Algorithmic bytes per
+    linear: N*K codes + 4*N*K/64 scale/bias + 2*M*K in + 2*M*N out; FLOP
+    2*M*N*K."""
     import torch
     from __graft_entry__ import load_package
     world, rank, local = _dist_init(args)
@@ -556,10 +559,39 @@ def main_qlinear(args):
                 "flop_per_step": flop, "gbs": nbytes / t / 1e9, "tflops": flop / t / 1e12,
                 "hbm_frac": nbytes / t / 1e9 / hbm_peak, "tensor_frac": flop / t / 1e12 / burst}
 
+    def one_launch(M, N, K, reps):
+        """One linear over a large weight, eager, CUDA events around each
+        launch (L2 flushed between): the kernel's streaming rate with its
+        launch latency amortised."""
+        wq = torch.randint(-2**31, 2**31 - 1, (N, K // 4), dtype=torch.int32, device=dev,
+                           generator=g)
+        sc = (torch.rand((N, K // 64), device=dev, generator=g) * 4e-4 + 1e-4).bfloat16()
+        zp = (torch.rand((N, K // 64), device=dev, generator=g) * -0.1).bfloat16()
+        x = torch.randn((M, K), device=dev, generator=g).bfloat16()
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            nrp.qlinear(x, wq, sc, zp, None, ctx=ctx, out=y)
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            nrp.qlinear(x, wq, sc, zp, None, ctx=ctx, out=y)
+            b.record()
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b))
+        ctx.check()
+        ms = statistics.median(ts)
+        nbytes = N * K + 4 * N * K // 64 + 2 * M * K + 2 * M * N
+        return {"rows": M, "N": N, "K": K, "ms_per_launch": ms, "bytes_per_launch": nbytes,
+                "gbs": nbytes / (ms / 1e3) / 1e9, "hbm_frac": nbytes / (ms / 1e3) / 1e9 / hbm_peak,
+                "how": f"median of {reps} eager launches, CUDA events, L2 flushed between"}
+
     n_steps = min(args.steps, 500)
     with ClockSampler(local) as clocks:
         small = measure(14, n_steps)
         big = measure(128, n_steps)
+        large = one_launch(14, 16384, 4096, 50)
     # e2e through the public API: the 14 rows in from pinned host memory,
     # the last linear's output back, per step (eager launches)
     x_host = torch.randn((14, D)).bfloat16().pin_memory()
@@ -588,12 +620,15 @@ def main_qlinear(args):
                     "h2d_bytes_per_step": x_host.numel() * 2,
                     "d2h_bytes_per_step": y_host.numel() * 2},
             "gpu_launches": len(layers) * n_steps,
-            "roofline": {"bound": "hbm", "kernel": "qgemv (M = 14)", "achieved": small["gbs"],
+            "roofline": {"bound": "hbm", "kernel": "small-M 8-bit GEMM (M = 14)",
+                         "achieved": small["gbs"],
                          "peak": hbm_peak, "unit": "GB/s", "frac": small["hbm_frac"],
                          "traffic": None, "peak_source": "measured (hbm_gbs, MEASURED_PEAKS.json)",
                          "algorithmic_bytes_per_step": small["bytes_per_step"]},
             "rows_14": small,
-            "rows_128": dict(big, roofline={"bound": "tensor", "kernel": "gemm_q8 (M = 128)",
+            "one_large_launch": large,
+            "rows_128": dict(big, roofline={"bound": "tensor",
+                                            "kernel": "small-M 8-bit GEMM (M = 128)",
                                             "achieved": big["tflops"], "peak": burst,
                                             "unit": "TFLOP/s", "frac": big["tensor_frac"],
                                             "peak_source": peak_src}),

@@ -256,9 +256,15 @@ int sync_params(nrp_attn* a) {
   return ok();
 }
 
-// Rows from which a quantised linear dequantises its weight once per call
-// (HBM: N*K read, 2*N*K written) instead of inside the GEMM's B producer.
-constexpr int kDequantOnceMinRows = 256;
+// Rows from which a quantised linear runs as the bf16 tcgen05 GEMM over its
+// weight's bf16 copy (kept, or dequantised once per call: N*K read, 2*N*K
+// written).  Up to kQSmallMaxM rows the small-M kernel reads the codes
+// directly.  Measured (N = 4096, K = 1024, M = 128): the tcgen05 GEMM that
+// dequantises in its B producer took 53 us, because only N/256 CTAs work and
+// each dequantises its whole slab, and dequantise-once + the bf16 GEMM 19 us
+// (two launches, few tiles at 128 rows); so the former serves only what the
+// small-M kernel cannot (GLU, batched-stride epilogues) below this row count.
+constexpr int kDequantOnceMinRows = nrp::kQSmallMaxM + 1;
 
 // y[M,N] (row stride ldy) = x[M,K] . W^T (+ bias) in the module dtype; W is
 // either a dense [N,K] matrix or 8-bit codes with bf16 scales/zero points.
@@ -283,17 +289,21 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
   }
   if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)
     return fail(NRP_ERR_UNSUPPORTED, "bf16 linear needs K %% 64 == 0 and N %% 32 == 0 (K=%d N=%d)", K, N);
-  // (the GEMV writes flat rows: not for an output with its own batch stride;
-  // it takes K % 512 == 0, other K go to the 8-bit GEMM below)
-  if (quant && M <= 16 && K % 512 == 0 && rt.y_bstride == 0 && rt.x_bstride == 0 &&
-      ep.mode == nrp::kEpiBias) {
+  // Up to 256 rows: the small-M kernel reads the 8-bit codes (1 byte per
+  // weight) even where a bf16 copy exists.  It writes flat rows: not for an
+  // output or input with its own batch stride, nor the GLU epilogue.
+  if (quant && rt.y_bstride == 0 && rt.x_bstride == 0 &&
+      (ep.mode != nrp::kEpiResidual || ep.res_bs == 0 ||
+       (rt.T > 0 && ep.res_bs == static_cast<int64_t>(rt.T) * ep.ldr)) &&
+      nrp::qgemm_small_supported(M, K, x, w, ep)) {
     ProfScope ps(ctx, NRP_KERNEL_QGEMV, st);
-    CUDA_TRY(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
-                               static_cast<const uint8_t*>(w),
-                               static_cast<const __nv_bfloat16*>(qs),
-                               static_cast<const __nv_bfloat16*>(qb),
-                               static_cast<const __nv_bfloat16*>(bias),
-                               static_cast<__nv_bfloat16*>(y), ldy, N, st));
+    CUDA_TRY(nrp::launch_qgemm_small(static_cast<const __nv_bfloat16*>(x), M, K,
+                                     static_cast<const uint8_t*>(w),
+                                     static_cast<const __nv_bfloat16*>(qs),
+                                     static_cast<const __nv_bfloat16*>(qb),
+                                     static_cast<const __nv_bfloat16*>(bias),
+                                     static_cast<__nv_bfloat16*>(y), ldy, N, ctx->num_sms,
+                                     ctx->d_err, st, ep));
     return ok();
   }
   if (quant)

@@ -139,11 +139,22 @@ struct DeqBatch {
 };
 cudaError_t launch_dequant_q8_batch(const DeqJob* jobs, int n, int num_sms, cudaStream_t stream);
 
-// ---- small-M quantised GEMV (HBM-bound regime): y[M,N] for M <= 16 ----
-cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
-                         const __nv_bfloat16* qs, const __nv_bfloat16* qb,
-                         const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
-                         cudaStream_t stream);
+// ---- small-M quantised GEMM (HBM-bound regime): y[M,N] for M <= 256 ----
+// x bf16 [M, K] (row stride K), wq [N, K] bytes, scales/biases bf16
+// [N, K/64]; epilogues bias, SiLU, residual (res row stride ldr) and ReLU
+// (not GLU).  x and wq 16-byte aligned, K % 64 == 0.
+// Each CTA stages its 8..32 code rows in shared memory (K <= kQSmallMaxK).
+// err: the context's device error word (a bulk copy that never lands is
+// reported there, after a bounded wait).
+constexpr int kQSmallMaxM = 256;
+constexpr int kQSmallMaxK = 8192;
+constexpr int kQSmallMaxSmem = 200 * 1024;
+bool qgemm_small_supported(int M, int K, const void* x, const void* wq, const Epilogue& ep);
+cudaError_t launch_qgemm_small(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
+                               const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                               const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
+                               int num_sms, int* err, cudaStream_t stream,
+                               const Epilogue& ep = Epilogue());
 
 // ---- fp32 CUDA-core GEMM (fp32 module dtype): y = x . W^T (+ bias) ----
 // num_sms: the device's SM count (the tile height is chosen for two CTAs per SM)

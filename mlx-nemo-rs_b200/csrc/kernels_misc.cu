@@ -1,8 +1,9 @@
 // kernels_misc.cu -- the small kernels around the hot path:
 //  * fp32 CUDA-core GEMM for modules whose dtype is f32 (LinearLayer's
 //    Standard arm, src/core/quantization.rs:128-135, at f32 parity);
-//  * the small-M MLX-affine 8-bit GEMV (quantized_matmul for streaming-size
-//    M, quantization.rs:137-160), HBM-bound on the packed weights;
+//  * the small-M MLX-affine 8-bit GEMM (quantized_matmul for streaming-size
+//    M, quantization.rs:137-160): weights dequantised in registers into
+//    bf16 MMA fragments, HBM-bound on the packed weights;
 //  * dtype conversions and the ring-buffer row append of the streaming cache;
 //  * TMA descriptor construction (driver entry point via the runtime).
 #include <cudaTypedefs.h>
@@ -169,83 +170,275 @@ cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
   return cudaGetLastError();
 }
 
-// ------------------------------------------------- small-M quantised GEMV
-// One warp per output column n.  Lane l reads 16 packed weights at a time
-// (a 16-byte load; 32 lanes cover 512 contiguous bytes of the row), all in
-// one group of 64, and FMAs them against every input row staged in shared
-// memory as f32.  K is processed in slices of kQK columns.
+// ------------------------------------------- small-M quantised GEMM
+// y[M, N] = x[M, K] . W^T (+ bias, epilogue) for M <= 256 rows and MLX-affine
+// 8-bit W (quantization.rs:137-160; w = scale * q + bias per 64-wide group,
+// computed in f32 and rounded once to bf16, as the other 8-bit paths do).
+// At these row counts the work is streaming the codes (1 byte per weight):
+// the kernel is HBM-bound when every SM keeps enough code bytes in flight.
+//
+// A CTA owns NG groups of 8 output columns and up to 64 rows; its 8 warps split
+// K (whole 64-wide groups) and reduce their partial sums through shared
+// memory.  Each CTA first brings its code rows into shared memory with one
+// bulk asynchronous copy per row (issued before the PDL wait, so they stream
+// while the previous kernel finishes).  Per 64-wide block a lane (g = lane / 4:
+// column g of a group, c = lane % 4) reads 16 code bytes of its column,
+// dequantises them in registers, and feeds four m16n8k16 bf16 MMAs whose k
+// order is permuted identically for both operands: k-step t, fragment
+// columns 2c, 2c+1 / 2c+8, 2c+9 <-> k = 16c + 4t + {0, 1} / {2, 3}.  So the
+// lane's 16 bytes are exactly its B fragments of the four k-steps, and its A
+// fragments are 16 consecutive bf16 of rows g and g + 8 (two 16-byte loads
+// per row, the next block's issued before the current one's MMAs).
 namespace {
-constexpr int kQMaxM = 16;
-constexpr int kQK = 1024;
-constexpr int kQWarps = 8;
+constexpr int kQsWarps = 8;
 
-__global__ void __launch_bounds__(kQWarps * 32)
-    qgemv_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
-                 const uint8_t* __restrict__ wq, const __nv_bfloat16* __restrict__ qs,
-                 const __nv_bfloat16* __restrict__ qb, const __nv_bfloat16* __restrict__ bias,
-                 __nv_bfloat16* __restrict__ y, int ldy, int N) {
-  extern __shared__ float sxq[];  // [M][kQK]
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
+      " {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// bytes (a multiple of 16, both addresses 16-byte aligned) from global to
+// this CTA's shared memory, completing on `bar`
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// the 16 codes of a 16-byte load as floats: each byte placed in the low
+// mantissa bits of 2^23 (one byte permute), then 2^23 subtracted (exact)
+__device__ __forceinline__ void codes16(const uint4 q, float s, float z, float (&w)[16]) {
+  const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[4 * u + e] =
+          fmaf(s, __uint_as_float(__byte_perm(words[u], 0x4B000000u, 0x7540u | e)) - 8388608.f,
+               z);
+}
+
+// Shared memory: the CTA's code rows (row stride K + 64 bytes: the 8 rows a
+// quarter-warp reads fall in distinct banks), the mbarrier, the scale and
+// zero point of every (column, group) as a bf16 pair, then the partial sums
+// [warp][MT * 16 rows][NG * 8 columns].
+__host__ __device__ constexpr int qs_code_stride(int K) { return K + 64; }
+template <int NG>
+__host__ __device__ constexpr int qs_scale_offset(int K) {
+  return NG * 8 * qs_code_stride(K) + 16;
+}
+template <int MT, int NG>
+__host__ __device__ constexpr int qs_red_offset(int K) {
+  return qs_scale_offset<NG>(K) + NG * 8 * (K / 64) * 4;
+}
+template <int MT, int NG>
+__host__ __device__ constexpr int qs_smem_bytes(int K) {
+  return qs_red_offset<MT, NG>(K) + kQsWarps * MT * 16 * NG * 8 * 4;
+}
+
+template <int MT, int NG>
+__global__ void __launch_bounds__(kQsWarps * 32)
+    qgemm_small_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                       const uint8_t* __restrict__ wq, const __nv_bfloat16* __restrict__ qs,
+                       const __nv_bfloat16* __restrict__ qb, const __nv_bfloat16* __restrict__ bias,
+                       __nv_bfloat16* y, int ldy, int N, Epilogue ep, int* err) {
+  extern __shared__ __align__(128) uint8_t qsm[];
+  constexpr int NC = NG * 8, ROWS = MT * 16;
+  // blockIdx.y: which 64-row chunk of x and y this CTA computes
+  {
+    const int row0 = blockIdx.y * 64;
+    x += static_cast<size_t>(row0) * K;
+    y += static_cast<size_t>(row0) * ldy;
+    if (ep.res) ep.res += static_cast<size_t>(row0) * ep.ldr;
+    M = min(64, M - row0);
+  }
+  const int stride = qs_code_stride(K);
+  uint8_t* codes = qsm;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qsm + NC * stride);
+  uint32_t* szs = reinterpret_cast<uint32_t*>(qsm + qs_scale_offset<NG>(K));
+  float* red = reinterpret_cast<float*>(qsm + qs_red_offset<MT, NG>(K));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * kQWarps + warp;
-  const int kg = K / 64;
-  float acc[kQMaxM];
+  const int g = lane >> 2, c = lane & 3;
+  const int n0 = blockIdx.x * NC;
+  const int ncols = min(NC, N - n0);
+  const int kblocks = K >> 6;
+  // the CTA's code rows into shared memory, before waiting on the previous
+  // kernel: the weights never depend on it
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(ncols) * K);
+  }
+  __syncthreads();
+  if (warp == 0 && lane < ncols)
+    bulk_g2s(codes + lane * stride, wq + static_cast<size_t>(n0 + lane) * K,
+             static_cast<uint32_t>(K), bar);
+  // scales and zero points [column][group] as bf16 pairs, also ahead of the
+  // wait: every load in flight at once instead of one round trip per block
+  for (int e = threadIdx.x; e < ncols * kblocks; e += kQsWarps * 32) {
+    const size_t gi = static_cast<size_t>(n0) * kblocks + e;
+    szs[e] = static_cast<uint32_t>(__bfloat16_as_ushort(qs[gi])) |
+             (static_cast<uint32_t>(__bfloat16_as_ushort(qb[gi])) << 16);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  const int per = (kblocks + kQsWarps - 1) / kQsWarps;
+  const int kb0 = min(kblocks, warp * per), kb1 = min(kblocks, kb0 + per);
+  float acc[MT][NG][4];
 #pragma unroll
-  for (int m = 0; m < kQMaxM; ++m) acc[m] = 0.f;
-  for (int k0 = 0; k0 < K; k0 += kQK) {
-    const int kw = min(kQK, K - k0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < M * kw; e += blockDim.x) {
-      const int m = e / kw, c = e % kw;
-      sxq[m * kQK + c] = __bfloat162float(x[static_cast<size_t>(m) * K + k0 + c]);
-    }
-    __syncthreads();
-    if (n < N) {
-      for (int c = lane * 16; c < kw; c += 32 * 16) {
-        const int k = k0 + c;
-        const uint4 q = *reinterpret_cast<const uint4*>(wq + static_cast<size_t>(n) * K + k);
-        const float s = __bfloat162float(qs[static_cast<size_t>(n) * kg + k / 64]);
-        const float bz = __bfloat162float(qb[static_cast<size_t>(n) * kg + k / 64]);
-        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-        float wv[16];
+  for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+    for (int q = 0; q < NG; ++q)
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            wv[4 * u + e] = fmaf(s, static_cast<float>((words[u] >> (8 * e)) & 0xFFu), bz);
+      for (int e = 0; e < 4; ++e) acc[m][q][e] = 0.f;
+  // x: 16 bf16 of rows g and g + 8 of every m tile for one 64-wide block
+  auto load_x = [&](int kb, uint4 (&xa)[MT][2][2]) {
+    const int k = kb * 64 + 16 * c;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = 16 * m + g + 8 * r;
+        xa[m][r][0] = xa[m][r][1] = make_uint4(0u, 0u, 0u, 0u);
+        if (row < M) {
+          const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * K + k);
+          xa[m][r][0] = src[0];
+          xa[m][r][1] = src[1];
         }
+      }
+  };
+  uint4 xa[2][MT][2][2];
+  if (kb0 < kb1) load_x(kb0, xa[0]);
+  __syncthreads();  // the scale pairs
+  const bool landed = __all_sync(0xffffffffu, mbar_wait(bar, 0, err, kDevTimeoutLoad));
+  if (landed) {
+    for (int kb = kb0; kb < kb1; kb += 2) {
 #pragma unroll
-        for (int m = 0; m < kQMaxM; ++m) {
-          if (m < M) {
-            const float4* xr = reinterpret_cast<const float4*>(sxq + m * kQK + c);
-            float a = acc[m];
+      for (int h = 0; h < 2; ++h) {
+        if (kb + h >= kb1) break;
+        if (kb + h + 1 < kb1) load_x(kb + h + 1, xa[h ^ 1]);
+        const int k = (kb + h) * 64 + 16 * c;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const float4 xv = xr[v];
-              a = fmaf(xv.x, wv[4 * v], a);
-              a = fmaf(xv.y, wv[4 * v + 1], a);
-              a = fmaf(xv.z, wv[4 * v + 2], a);
-              a = fmaf(xv.w, wv[4 * v + 3], a);
-            }
-            acc[m] = a;
+        for (int q = 0; q < NG; ++q) {
+          const int nl = q * 8 + g;
+          uint4 code = make_uint4(0u, 0u, 0u, 0u);
+          float sc = 0.f, zp = 0.f;
+          if (nl < ncols) {
+            code = *reinterpret_cast<const uint4*>(codes + nl * stride + k);
+            const uint32_t sz = szs[nl * kblocks + kb + h];
+            sc = __uint_as_float(sz << 16);
+            zp = __uint_as_float(sz & 0xFFFF0000u);
           }
+          float w[16];
+          codes16(code, sc, zp, w);
+          uint32_t b[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) b[t] = pack_bf16x2(w[2 * t], w[2 * t + 1]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              // word 2t / 2t + 1 of a row's 16 bf16: columns 4t, 4t+1 / 4t+2, 4t+3
+              const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&xa[h][m][0][0]);
+              const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&xa[h][m][1][0]);
+              mma_bf16_16816(acc[m][q], r0[2 * t], r1[2 * t], r0[2 * t + 1], r1[2 * t + 1],
+                             b[2 * t], b[2 * t + 1]);
+            }
         }
       }
     }
   }
-  if (n >= N) return;
+  // partial sums of this warp's k range -> shared memory
+  float* mine = red + warp * ROWS * NC;
 #pragma unroll
-  for (int m = 0; m < kQMaxM; ++m) {
-    if (m >= M) break;
-    float a = acc[m];
+  for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-    if (lane == 0) {
-      if (bias) a += __bfloat162float(bias[n]);
-      y[static_cast<size_t>(m) * ldy + n] = __float2bfloat16_rn(a);
+    for (int q = 0; q < NG; ++q) {
+      const int col = q * 8 + 2 * c;
+      *reinterpret_cast<float2*>(mine + (16 * m + g) * NC + col) =
+          make_float2(acc[m][q][0], acc[m][q][1]);
+      *reinterpret_cast<float2*>(mine + (16 * m + g + 8) * NC + col) =
+          make_float2(acc[m][q][2], acc[m][q][3]);
     }
+  if (!__syncthreads_and(landed)) return;  // a copy never landed: error recorded
+  for (int idx = threadIdx.x; idx < M * NC; idx += kQsWarps * 32) {
+    const int row = idx / NC, col = idx - row * NC, n = n0 + col;
+    if (col >= ncols) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kQsWarps; ++w) v += red[(w * ROWS + row) * NC + col];
+    if (ep.mode == kEpiRelu) v = __bfloat162float(__float2bfloat16_rn(v));
+    if (bias) v += __bfloat162float(bias[n]);
+    if (ep.mode == kEpiSilu) {
+      v = v * sigmoid_approx(v);
+    } else if (ep.mode == kEpiRelu) {
+      v = fmaxf(v, 0.f);
+    } else if (ep.mode == kEpiResidual) {
+      v = fmaf(ep.alpha, v, __bfloat162float(ep.res[static_cast<size_t>(row) * ep.ldr + n]));
+    }
+    y[static_cast<size_t>(row) * ldy + n] = __float2bfloat16_rn(v);
   }
 }
+
+template <int MT, int NG>
+cudaError_t launch_qs(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
+                      const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                      const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
+                      const Epilogue& ep, int* err, cudaStream_t stream) {
+  const int smem = qs_smem_bytes<MT, NG>(K);
+  if (smem > kQSmallMaxSmem) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr{0};
+  if (cudaError_t e = smem_attr_once(qgemm_small_kernel<MT, NG>, kQSmallMaxSmem, attr)) return e;
+  const dim3 grid((N + NG * 8 - 1) / (NG * 8), (M + 63) / 64);
+  return launch_pdl(qgemm_small_kernel<MT, NG>, grid, dim3(kQsWarps * 32), smem, stream,
+                    x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err);
+}
+
+template <int MT>
+cudaError_t launch_qs_ng(int ng, const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
+                         const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                         const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
+                         const Epilogue& ep, int* err, cudaStream_t stream) {
+  // (4 m tiles x 4 column groups would not fit the registers)
+  if constexpr (MT < 4) {
+    if (ng == 4) return launch_qs<MT, 4>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+  } else {
+    if (ng == 4) return launch_qs<MT, 2>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+  }
+  if (ng == 2) return launch_qs<MT, 2>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+  return launch_qs<MT, 1>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+}
 }  // namespace
+
+bool qgemm_small_supported(int M, int K, const void* x, const void* wq, const Epilogue& ep) {
+  return M >= 1 && M <= kQSmallMaxM && K % 64 == 0 && K <= kQSmallMaxK && ep.mode != kEpiGlu &&
+         (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(wq) & 15) == 0;
+}
+
+cudaError_t launch_qgemm_small(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
+                               const __nv_bfloat16* qs, const __nv_bfloat16* qb,
+                               const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
+                               int num_sms, int* err, cudaStream_t stream, const Epilogue& ep) {
+  if (!qgemm_small_supported(M, K, x, wq, ep) || N <= 0) return cudaErrorInvalidValue;
+  // the widest column group that still gives every SM a CTA (fewer x
+  // re-reads), within the shared memory of the staged code rows
+  const int sms = num_sms > 0 ? num_sms : 148;
+  int ng = 1;
+  if ((N + 31) / 32 >= sms && qs_smem_bytes<2, 4>(K) <= kQSmallMaxSmem) ng = 4;
+  else if ((N + 15) / 16 >= sms && qs_smem_bytes<4, 2>(K) <= kQSmallMaxSmem) ng = 2;
+  // more than 64 rows: 64-row chunks on the grid's y dimension, each CTA
+  // staging its column slab again (mostly from L2)
+  if (M <= 16) return launch_qs_ng<1>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+  if (M <= 32) return launch_qs_ng<2>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+  return launch_qs_ng<4>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+}
 
 namespace {
 // MLX affine dequantisation of 8-bit weights (quantization.rs:4-8, group
@@ -310,20 +503,6 @@ cudaError_t launch_dequant_q8(const uint8_t* wq, const __nv_bfloat16* qs, const 
                               __nv_bfloat16* w, int N, int K, int num_sms, cudaStream_t stream) {
   const DeqJob j{wq, qs, qb, w, N, K};
   return launch_dequant_q8_batch(&j, 1, num_sms, stream);
-}
-
-cudaError_t launch_qgemv(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
-                         const __nv_bfloat16* qs, const __nv_bfloat16* qb,
-                         const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
-                         cudaStream_t stream) {
-  if (M > kQMaxM || K % 512 != 0) return cudaErrorInvalidValue;
-  const int smem = kQMaxM * kQK * 4;
-  static std::atomic<uint64_t> attr{0};
-  if (cudaError_t e = smem_attr_once(qgemv_kernel, smem, attr))
-    return e;
-  qgemv_kernel<<<(N + kQWarps - 1) / kQWarps, kQWarps * 32, smem, stream>>>(x, M, K, wq, qs, qb,
-                                                                           bias, y, ldy, N);
-  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------ conversions

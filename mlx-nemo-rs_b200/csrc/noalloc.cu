@@ -98,16 +98,17 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
                                   ctx->num_sms, st));
     return NRP_OK;
   }
-  if (quant && M <= 16 && K % 512 == 0) {
-    TRY_CUDA(nrp::launch_qgemv(static_cast<const __nv_bfloat16*>(x), M, K,
-                               static_cast<const uint8_t*>(w),
-                               static_cast<const __nv_bfloat16*>(qs),
-                               static_cast<const __nv_bfloat16*>(qb),
-                               static_cast<const __nv_bfloat16*>(bias),
-                               static_cast<__nv_bfloat16*>(y), ldy, N, st));
+  if (quant && nrp::qgemm_small_supported(M, K, x, w, nrp::Epilogue())) {
+    TRY_CUDA(nrp::launch_qgemm_small(static_cast<const __nv_bfloat16*>(x), M, K,
+                                     static_cast<const uint8_t*>(w),
+                                     static_cast<const __nv_bfloat16*>(qs),
+                                     static_cast<const __nv_bfloat16*>(qb),
+                                     static_cast<const __nv_bfloat16*>(bias),
+                                     static_cast<__nv_bfloat16*>(y), ldy, N, ctx->num_sms,
+                                     ctx->d_err, st));
     return NRP_OK;
   }
-  if (quant && M >= 256) {
+  if (quant && M > nrp::kQSmallMaxM) {
     const auto it = ctx->deq_cache.find(w);
     if (it != ctx->deq_cache.end()) {
       w = it->second->p;

@@ -122,13 +122,14 @@ def test_linear_f32(nrp, orc):
     assert a < TOL_F32
 
 
-@pytest.mark.parametrize("M", [1, 14, 16, 17, 64, 128, 200, 255, 256, 300, 896, 1024, 2500])
+@pytest.mark.parametrize("M", [1, 14, 16, 17, 33, 64, 65, 128, 200, 255, 256, 257, 300, 896, 2500])
 @pytest.mark.parametrize("K,N", [(1024, 1024), (1024, 4096), (4096, 1024)])
 def test_qlinear_mlx_affine_8bit(nrp, orc, M, K, N):
-    """M <= 16: the GEMV; 17 to 255 rows: the tcgen05 GEMM with the
-    dequantising producer (17, 64, 128, 200, 255: one and two row tiles,
-    full and ragged); from 256 rows: the weight dequantised once per call
-    (caller-owned weights are never kept), then the bf16 GEMM."""
+    """Up to 256 rows: the small-M kernel (codes dequantised in registers
+    into bf16 MMA fragments; 1, 14, 16, 17, 64: one 64-row chunk with 1, 2
+    or 4 m tiles, full and ragged; 128, 200, 255, 256: two to four chunks);
+    from 257 rows: the weight dequantised once per call (caller-owned
+    weights are never kept), then the bf16 tcgen05 GEMM."""
     import torch
     rng = np.random.default_rng(M * 7 + N)
     wm = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
