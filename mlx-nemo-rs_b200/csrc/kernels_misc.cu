@@ -7,6 +7,7 @@
 //  * dtype conversions and the ring-buffer row append of the streaming cache;
 //  * TMA descriptor construction (driver entry point via the runtime).
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <math.h>
 
 #include "gemm.h"
@@ -177,11 +178,12 @@ cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
 // At these row counts the work is streaming the codes (1 byte per weight):
 // the kernel is HBM-bound when every SM keeps enough code bytes in flight.
 //
-// A CTA owns NG groups of 8 output columns and up to 64 rows; its 8 warps split
-// K (whole 64-wide groups) and reduce their partial sums through shared
-// memory.  Each CTA first brings its code rows into shared memory with one
-// bulk asynchronous copy per row (issued before the PDL wait, so they stream
-// while the previous kernel finishes).  Per 64-wide block a lane (g = lane / 4:
+// A work unit is NG groups of 8 output columns and up to 64 rows; a CTA's 8
+// warps split K (whole 64-wide groups) and reduce their partial sums through
+// shared memory.  A unit's code rows come into shared memory by one bulk
+// asynchronous copy per row; the CTA is persistent and double-buffers them
+// (the first two units' copies are issued before the PDL wait, so they
+// stream while the previous kernel finishes).  Per 64-wide block a lane (g = lane / 4:
 // column g of a group, c = lane % 4) reads 16 code bytes of its column,
 // dequantises them in registers, and feeds four m16n8k16 bf16 MMAs whose k
 // order is permuted identically for both operands: k-step t, fragment
@@ -225,24 +227,33 @@ __device__ __forceinline__ void codes16(const uint4 q, float s, float z, float (
                z);
 }
 
-// Shared memory: the CTA's code rows (row stride K + 64 bytes: the 8 rows a
-// quarter-warp reads fall in distinct banks), the mbarrier, the scale and
-// zero point of every (column, group) as a bf16 pair, then the partial sums
-// [warp][MT * 16 rows][NG * 8 columns].
+// Shared memory: two stages of code rows (row stride K + 64 bytes: the 8
+// rows a quarter-warp reads fall in distinct banks), their mbarriers, two
+// stages of (scale, zero point) bf16 pairs [column][group], then the partial
+// sums [warp][MT * 16 rows][NG * 8 columns].
+constexpr int kQsStages = 2;
 __host__ __device__ constexpr int qs_code_stride(int K) { return K + 64; }
 template <int NG>
+__host__ __device__ constexpr int qs_bar_offset(int K) {
+  return kQsStages * NG * 8 * qs_code_stride(K);
+}
+template <int NG>
 __host__ __device__ constexpr int qs_scale_offset(int K) {
-  return NG * 8 * qs_code_stride(K) + 16;
+  return qs_bar_offset<NG>(K) + 16;
 }
 template <int MT, int NG>
 __host__ __device__ constexpr int qs_red_offset(int K) {
-  return qs_scale_offset<NG>(K) + NG * 8 * (K / 64) * 4;
+  return qs_scale_offset<NG>(K) + kQsStages * NG * 8 * (K / 64) * 4;
 }
 template <int MT, int NG>
 __host__ __device__ constexpr int qs_smem_bytes(int K) {
   return qs_red_offset<MT, NG>(K) + kQsWarps * MT * 16 * NG * 8 * 4;
 }
 
+// Persistent: CTA b works units b, b + G, b + 2G, ... (G = gridDim.x); unit
+// u = (column slab u / chunks, 64-row chunk u % chunks).  While a unit
+// computes, the unit two ahead has its code rows in flight into the other
+// stage and its scale pairs in registers.
 template <int MT, int NG>
 __global__ void __launch_bounds__(kQsWarps * 32)
     qgemm_small_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
@@ -251,139 +262,186 @@ __global__ void __launch_bounds__(kQsWarps * 32)
                        __nv_bfloat16* y, int ldy, int N, Epilogue ep, int* err) {
   extern __shared__ __align__(128) uint8_t qsm[];
   constexpr int NC = NG * 8, ROWS = MT * 16;
-  // blockIdx.y: which 64-row chunk of x and y this CTA computes
-  {
-    const int row0 = blockIdx.y * 64;
-    x += static_cast<size_t>(row0) * K;
-    y += static_cast<size_t>(row0) * ldy;
-    if (ep.res) ep.res += static_cast<size_t>(row0) * ep.ldr;
-    M = min(64, M - row0);
-  }
+  constexpr int kMaxPairs = NC * (kQSmallMaxK / 64) / (kQsWarps * 32);  // per thread
   const int stride = qs_code_stride(K);
+  const int kblocks = K >> 6;
   uint8_t* codes = qsm;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(qsm + NC * stride);
+  uint64_t* full = reinterpret_cast<uint64_t*>(qsm + qs_bar_offset<NG>(K));
   uint32_t* szs = reinterpret_cast<uint32_t*>(qsm + qs_scale_offset<NG>(K));
   float* red = reinterpret_cast<float*>(qsm + qs_red_offset<MT, NG>(K));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int n0 = blockIdx.x * NC;
-  const int ncols = min(NC, N - n0);
-  const int kblocks = K >> 6;
-  // the CTA's code rows into shared memory, before waiting on the previous
-  // kernel: the weights never depend on it
+  const int slabs = (N + NC - 1) / NC, chunks = (M + 63) / 64, units = slabs * chunks;
+  const int per = (kblocks + kQsWarps - 1) / kQsWarps;
+  const int kb0 = min(kblocks, warp * per), kb1 = min(kblocks, kb0 + per);
+
+  // the code rows of unit u into stage s (warp 0)
+  auto issue_codes = [&](int u, int s) {
+    if (warp != 0) return;
+    const int n0 = (u / chunks) * NC, ncols = min(NC, N - n0);
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ncols) * K);
+    __syncwarp();
+    if (lane < ncols)
+      bulk_g2s(codes + (s * NC + lane) * stride, wq + static_cast<size_t>(n0 + lane) * K,
+               static_cast<uint32_t>(K), &full[s]);
+  };
+  // the scale pairs of unit u: loaded into registers, stored into a stage
+  uint32_t pend[kMaxPairs];
+  auto load_scales = [&](int u) {
+    const int n0 = (u / chunks) * NC, ncols = min(NC, N - n0);
+#pragma unroll
+    for (int p = 0; p < kMaxPairs; ++p) {
+      const int e = threadIdx.x + p * kQsWarps * 32;
+      if (e < ncols * kblocks) {
+        const size_t gi = static_cast<size_t>(n0) * kblocks + e;
+        pend[p] = static_cast<uint32_t>(__bfloat16_as_ushort(qs[gi])) |
+                  (static_cast<uint32_t>(__bfloat16_as_ushort(qb[gi])) << 16);
+      }
+    }
+  };
+  auto store_scales = [&](int u, int s) {
+    const int n0 = (u / chunks) * NC, ncols = min(NC, N - n0);
+#pragma unroll
+    for (int p = 0; p < kMaxPairs; ++p) {
+      const int e = threadIdx.x + p * kQsWarps * 32;
+      if (e < ncols * kblocks) szs[s * NC * kblocks + e] = pend[p];
+    }
+  };
+
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(ncols) * K);
   }
   __syncthreads();
-  if (warp == 0 && lane < ncols)
-    bulk_g2s(codes + lane * stride, wq + static_cast<size_t>(n0 + lane) * K,
-             static_cast<uint32_t>(K), bar);
-  // scales and zero points [column][group] as bf16 pairs, also ahead of the
-  // wait: every load in flight at once instead of one round trip per block
-  for (int e = threadIdx.x; e < ncols * kblocks; e += kQsWarps * 32) {
-    const size_t gi = static_cast<size_t>(n0) * kblocks + e;
-    szs[e] = static_cast<uint32_t>(__bfloat16_as_ushort(qs[gi])) |
-             (static_cast<uint32_t>(__bfloat16_as_ushort(qb[gi])) << 16);
+  // the first two units' weights, before waiting on the previous kernel:
+  // the weights never depend on it
+  for (int s = 0; s < kQsStages; ++s) {
+    const int u = blockIdx.x + s * gridDim.x;
+    if (u < units) {
+      issue_codes(u, s);
+      load_scales(u);
+      store_scales(u, s);
+    }
   }
   pdl_launch_dependents();
   pdl_wait();
-  const int per = (kblocks + kQsWarps - 1) / kQsWarps;
-  const int kb0 = min(kblocks, warp * per), kb1 = min(kblocks, kb0 + per);
-  float acc[MT][NG][4];
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int q = 0; q < NG; ++q)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[m][q][e] = 0.f;
-  // x: 16 bf16 of rows g and g + 8 of every m tile for one 64-wide block
-  auto load_x = [&](int kb, uint4 (&xa)[MT][2][2]) {
-    const int k = kb * 64 + 16 * c;
+  __syncthreads();  // the stored scale pairs
+
+  int i = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+    const int s = i & 1;
+    const int n0 = (u / chunks) * NC, ncols = min(NC, N - n0);
+    const int row0 = (u % chunks) * 64, mrows = min(64, M - row0);
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row0) * K;
+    const int un = u + kQsStages * gridDim.x;
+    if (un < units) load_scales(un);  // in flight under this unit
+    float acc[MT][NG][4];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int row = 16 * m + g + 8 * r;
-        xa[m][r][0] = xa[m][r][1] = make_uint4(0u, 0u, 0u, 0u);
-        if (row < M) {
-          const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * K + k);
-          xa[m][r][0] = src[0];
-          xa[m][r][1] = src[1];
-        }
-      }
-  };
-  uint4 xa[2][MT][2][2];
-  if (kb0 < kb1) load_x(kb0, xa[0]);
-  __syncthreads();  // the scale pairs
-  const bool landed = __all_sync(0xffffffffu, mbar_wait(bar, 0, err, kDevTimeoutLoad));
-  if (landed) {
-    for (int kb = kb0; kb < kb1; kb += 2) {
+      for (int q = 0; q < NG; ++q)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (kb + h >= kb1) break;
-        if (kb + h + 1 < kb1) load_x(kb + h + 1, xa[h ^ 1]);
-        const int k = (kb + h) * 64 + 16 * c;
+        for (int e = 0; e < 4; ++e) acc[m][q][e] = 0.f;
+    // x: 16 bf16 of rows g and g + 8 of every m tile for one 64-wide block
+    auto load_x = [&](int kb, uint4 (&xa)[MT][2][2]) {
+      const int k = kb * 64 + 16 * c;
 #pragma unroll
-        for (int q = 0; q < NG; ++q) {
-          const int nl = q * 8 + g;
-          uint4 code = make_uint4(0u, 0u, 0u, 0u);
-          float sc = 0.f, zp = 0.f;
-          if (nl < ncols) {
-            code = *reinterpret_cast<const uint4*>(codes + nl * stride + k);
-            const uint32_t sz = szs[nl * kblocks + kb + h];
-            sc = __uint_as_float(sz << 16);
-            zp = __uint_as_float(sz & 0xFFFF0000u);
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int row = 16 * m + g + 8 * r;
+          xa[m][r][0] = xa[m][r][1] = make_uint4(0u, 0u, 0u, 0u);
+          if (row < mrows) {
+            const uint4* src =
+                reinterpret_cast<const uint4*>(xr + static_cast<size_t>(row) * K + k);
+            xa[m][r][0] = src[0];
+            xa[m][r][1] = src[1];
           }
-          float w[16];
-          codes16(code, sc, zp, w);
-          uint32_t b[8];
+        }
+    };
+    uint4 xa[2][MT][2][2];
+    if (kb0 < kb1) load_x(kb0, xa[0]);
+    const bool landed =
+        __all_sync(0xffffffffu, mbar_wait(&full[s], (i >> 1) & 1, err, kDevTimeoutLoad));
+    const uint8_t* cs = codes + s * NC * stride;
+    const uint32_t* ss = szs + s * NC * kblocks;
+    // dequantise one block's codes for column group q into B fragments
+    auto b_frags = [&](int kb, int q, uint32_t (&b)[8]) {
+      const int nl = q * 8 + g;
+      uint4 code = make_uint4(0u, 0u, 0u, 0u);
+      float sc = 0.f, zp = 0.f;
+      if (nl < ncols) {
+        code = *reinterpret_cast<const uint4*>(cs + nl * stride + kb * 64 + 16 * c);
+        const uint32_t sz = ss[nl * kblocks + kb];
+        sc = __uint_as_float(sz << 16);
+        zp = __uint_as_float(sz & 0xFFFF0000u);
+      }
+      float w[16];
+      codes16(code, sc, zp, w);
 #pragma unroll
-          for (int t = 0; t < 8; ++t) b[t] = pack_bf16x2(w[2 * t], w[2 * t + 1]);
+      for (int t = 0; t < 8; ++t) b[t] = pack_bf16x2(w[2 * t], w[2 * t + 1]);
+    };
+    if (landed) {
+      for (int kb = kb0; kb < kb1; kb += 2) {
 #pragma unroll
-          for (int t = 0; t < 4; ++t)
+        for (int h = 0; h < 2; ++h) {
+          if (kb + h >= kb1) break;
+          if (kb + h + 1 < kb1) load_x(kb + h + 1, xa[h ^ 1]);
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              // word 2t / 2t + 1 of a row's 16 bf16: columns 4t, 4t+1 / 4t+2, 4t+3
-              const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&xa[h][m][0][0]);
-              const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&xa[h][m][1][0]);
-              mma_bf16_16816(acc[m][q], r0[2 * t], r1[2 * t], r0[2 * t + 1], r1[2 * t + 1],
-                             b[2 * t], b[2 * t + 1]);
-            }
+          for (int q = 0; q < NG; ++q) {
+            uint32_t b[8];
+            b_frags(kb + h, q, b);
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+#pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                // word 2t / 2t + 1 of a row's 16 bf16: columns 4t, 4t+1 / 4t+2, 4t+3
+                const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&xa[h][m][0][0]);
+                const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&xa[h][m][1][0]);
+                mma_bf16_16816(acc[m][q], r0[2 * t], r1[2 * t], r0[2 * t + 1], r1[2 * t + 1],
+                               b[2 * t], b[2 * t + 1]);
+              }
+          }
         }
       }
     }
-  }
-  // partial sums of this warp's k range -> shared memory
-  float* mine = red + warp * ROWS * NC;
+    // partial sums of this warp's k range -> shared memory
+    float* mine = red + warp * ROWS * NC;
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
+    for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int q = 0; q < NG; ++q) {
-      const int col = q * 8 + 2 * c;
-      *reinterpret_cast<float2*>(mine + (16 * m + g) * NC + col) =
-          make_float2(acc[m][q][0], acc[m][q][1]);
-      *reinterpret_cast<float2*>(mine + (16 * m + g + 8) * NC + col) =
-          make_float2(acc[m][q][2], acc[m][q][3]);
+      for (int q = 0; q < NG; ++q) {
+        const int col = q * 8 + 2 * c;
+        *reinterpret_cast<float2*>(mine + (16 * m + g) * NC + col) =
+            make_float2(acc[m][q][0], acc[m][q][1]);
+        *reinterpret_cast<float2*>(mine + (16 * m + g + 8) * NC + col) =
+            make_float2(acc[m][q][2], acc[m][q][3]);
+      }
+    if (!__syncthreads_and(landed)) return;  // a copy never landed: error recorded
+    for (int idx = threadIdx.x; idx < mrows * NC; idx += kQsWarps * 32) {
+      const int row = idx / NC, col = idx - row * NC, n = n0 + col;
+      if (col >= ncols) continue;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kQsWarps; ++w) v += red[(w * ROWS + row) * NC + col];
+      if (ep.mode == kEpiRelu) v = __bfloat162float(__float2bfloat16_rn(v));
+      if (bias) v += __bfloat162float(bias[n]);
+      if (ep.mode == kEpiSilu) {
+        v = v * sigmoid_approx(v);
+      } else if (ep.mode == kEpiRelu) {
+        v = fmaxf(v, 0.f);
+      } else if (ep.mode == kEpiResidual) {
+        v = fmaf(ep.alpha, v,
+                 __bfloat162float(ep.res[static_cast<size_t>(row0 + row) * ep.ldr + n]));
+      }
+      y[static_cast<size_t>(row0 + row) * ldy + n] = __float2bfloat16_rn(v);
     }
-  if (!__syncthreads_and(landed)) return;  // a copy never landed: error recorded
-  for (int idx = threadIdx.x; idx < M * NC; idx += kQsWarps * 32) {
-    const int row = idx / NC, col = idx - row * NC, n = n0 + col;
-    if (col >= ncols) continue;
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < kQsWarps; ++w) v += red[(w * ROWS + row) * NC + col];
-    if (ep.mode == kEpiRelu) v = __bfloat162float(__float2bfloat16_rn(v));
-    if (bias) v += __bfloat162float(bias[n]);
-    if (ep.mode == kEpiSilu) {
-      v = v * sigmoid_approx(v);
-    } else if (ep.mode == kEpiRelu) {
-      v = fmaxf(v, 0.f);
-    } else if (ep.mode == kEpiResidual) {
-      v = fmaf(ep.alpha, v, __bfloat162float(ep.res[static_cast<size_t>(row) * ep.ldr + n]));
+    __syncthreads();  // stage s and the partial sums are free again
+    if (un < units) {
+      issue_codes(un, s);
+      store_scales(un, s);
     }
-    y[static_cast<size_t>(row) * ldy + n] = __float2bfloat16_rn(v);
   }
 }
 
@@ -391,13 +449,29 @@ template <int MT, int NG>
 cudaError_t launch_qs(const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
                       const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                       const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
-                      const Epilogue& ep, int* err, cudaStream_t stream) {
+                      int num_sms, const Epilogue& ep, int* err, cudaStream_t stream) {
   const int smem = qs_smem_bytes<MT, NG>(K);
   if (smem > kQSmallMaxSmem) return cudaErrorInvalidValue;
   static std::atomic<uint64_t> attr{0};
-  if (cudaError_t e = smem_attr_once(qgemm_small_kernel<MT, NG>, kQSmallMaxSmem, attr)) return e;
-  const dim3 grid((N + NG * 8 - 1) / (NG * 8), (M + 63) / 64);
-  return launch_pdl(qgemm_small_kernel<MT, NG>, grid, dim3(kQsWarps * 32), smem, stream,
+  if (cudaError_t e = smem_attr_once(qgemm_small_kernel<MT, NG>, kQSmallMaxSmem, attr))
+    return e;
+  // persistent: as many CTAs per SM as registers and shared memory allow (at
+  // most 4), asked of the runtime once per shared-memory size
+  static std::atomic<uint64_t> occ{0};  // (smem << 8) | CTAs per SM
+  uint64_t o = occ.load(std::memory_order_relaxed);
+  int per_sm = static_cast<int>(o & 0xFF);
+  if ((o >> 8) != static_cast<uint64_t>(smem) || per_sm == 0) {
+    if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, qgemm_small_kernel<MT, NG>, kQsWarps * 32, smem))
+      return e;
+    per_sm = std::max(1, std::min(4, per_sm));
+    occ.store((static_cast<uint64_t>(smem) << 8) | static_cast<uint64_t>(per_sm),
+              std::memory_order_relaxed);
+  }
+  const int units = ((N + NG * 8 - 1) / (NG * 8)) * ((M + 63) / 64);
+  const int grid = std::min(units, per_sm * (num_sms > 0 ? num_sms : 148));
+  return launch_pdl(qgemm_small_kernel<MT, NG>, dim3(grid), dim3(kQsWarps * 32), smem,
+                    stream,
                     x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err);
 }
 
@@ -405,15 +479,11 @@ template <int MT>
 cudaError_t launch_qs_ng(int ng, const __nv_bfloat16* x, int M, int K, const uint8_t* wq,
                          const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                          const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
-                         const Epilogue& ep, int* err, cudaStream_t stream) {
-  // (4 m tiles x 4 column groups would not fit the registers)
-  if constexpr (MT < 4) {
-    if (ng == 4) return launch_qs<MT, 4>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
-  } else {
-    if (ng == 4) return launch_qs<MT, 2>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
-  }
-  if (ng == 2) return launch_qs<MT, 2>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
-  return launch_qs<MT, 1>(x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+                         int num_sms, const Epilogue& ep, int* err, cudaStream_t stream) {
+  if (ng == 2)
+    return launch_qs<MT, 2>(x, M, K, wq, qs, qb, bias, y, ldy, N, num_sms, ep, err,
+                                   stream);
+  return launch_qs<MT, 1>(x, M, K, wq, qs, qb, bias, y, ldy, N, num_sms, ep, err, stream);
 }
 }  // namespace
 
@@ -427,17 +497,19 @@ cudaError_t launch_qgemm_small(const __nv_bfloat16* x, int M, int K, const uint8
                                const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int N,
                                int num_sms, int* err, cudaStream_t stream, const Epilogue& ep) {
   if (!qgemm_small_supported(M, K, x, wq, ep) || N <= 0) return cudaErrorInvalidValue;
-  // the widest column group that still gives every SM a CTA (fewer x
-  // re-reads), within the shared memory of the staged code rows
-  const int sms = num_sms > 0 ? num_sms : 148;
-  int ng = 1;
-  if ((N + 31) / 32 >= sms && qs_smem_bytes<2, 4>(K) <= kQSmallMaxSmem) ng = 4;
-  else if ((N + 15) / 16 >= sms && qs_smem_bytes<4, 2>(K) <= kQSmallMaxSmem) ng = 2;
-  // more than 64 rows: 64-row chunks on the grid's y dimension, each CTA
-  // staging its column slab again (mostly from L2)
-  if (M <= 16) return launch_qs_ng<1>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
-  if (M <= 32) return launch_qs_ng<2>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
-  return launch_qs_ng<4>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, ep, err, stream);
+  // 16-column slabs (x read once for twice the columns) where two CTAs of
+  // them still fit an SM; 8-column slabs otherwise
+  const int mr = std::min(M, 64);
+  const int ng = (mr <= 16 ? qs_smem_bytes<1, 2>(K)
+                           : mr <= 32 ? qs_smem_bytes<2, 2>(K) : qs_smem_bytes<4, 2>(K)) <=
+                         113 * 1024
+                     ? 2
+                     : 1;
+  if (mr <= 16)
+    return launch_qs_ng<1>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, num_sms, ep, err, stream);
+  if (mr <= 32)
+    return launch_qs_ng<2>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, num_sms, ep, err, stream);
+  return launch_qs_ng<4>(ng, x, M, K, wq, qs, qb, bias, y, ldy, N, num_sms, ep, err, stream);
 }
 
 namespace {
