@@ -40,8 +40,8 @@ L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each
 # of the forward's four launches, from one ncu capture of this workload's
 # bench command; None = not captured.
-TRAFFIC_BYTES = {"linear_pos": None, "qkv_gemm": 26.103e6 + 19.167e6,
-                 "attention": 62.479e6 + 4.606e6, "linear_out": None}
+TRAFFIC_BYTES = {"linear_pos": 5.23e6, "qkv_gemm": 26.14e6 + 13.66e6,
+                 "attention": 62.49e6 + 1.28e6, "linear_out": 21.94e6}
 # config 4's attention launch on one GPU: DRAM read + write of one ncu capture
 LONG_ATTN_TRAFFIC = 309.311e6 + 82.413e6
 # The forward's launches in the order the host issues them (linear_pos on
@@ -587,6 +587,11 @@ def main_qlinear(args):
                 "gbs": nbytes / (ms / 1e3) / 1e9, "hbm_frac": nbytes / (ms / 1e3) / 1e9 / hbm_peak,
                 "how": f"median of {reps} eager launches, CUDA events, L2 flushed between"}
 
+    if args.qlinear_large_only:  # the large launch alone (an ncu capture's driver)
+        large = one_launch(14, 16384, 4096, 5)
+        if rank == 0:
+            print(json.dumps({"one_large_launch": large}), flush=True)
+        return 0
     n_steps = min(args.steps, 500)
     with ClockSampler(local) as clocks:
         small = measure(14, n_steps)
@@ -648,6 +653,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--qlinear-large-only", action="store_true",
+                    help="qlinear workload: only the one large launch (5 launches, for ncu)")
     ap.add_argument("--no-extras", action="store_true",
                     help="config 1 only: skip the strong-scaling and sequence-split keys")
     ap.add_argument("--workload", default="offline",
