@@ -771,26 +771,33 @@ def main():
                   for j, (name, _) in enumerate(FORWARD_LAUNCHES)}
 
     # ---- end to end through the public API with host buffers: each step
-    # copies its utterances' valid frames and the lengths in from pinned
-    # host memory and reads the valid output frames back (copy_frames;
-    # padded rows are unspecified, conformer.rs:1590-1593); run_pipelined
-    # overlaps the copies with the neighbouring steps' compute
-    x_host = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
+    # moves its utterances' valid frames (packed back to back in pinned host
+    # memory) in with one copy and reads the valid output frames back with
+    # one copy (padded rows are unspecified, conformer.rs:1590-1593).  On the
+    # device, unpack_frames scatters the packed rows (and the lengths) into
+    # the [B, T, D] input and pack_frames gathers the output rows; both run
+    # on the compute stream, so each copy stream carries nothing but its
+    # copies.  run_pipelined overlaps the copies with the neighbouring steps'
+    # compute.
+    x_host = torch.cat([torch.from_numpy(x[b, :n]) for b, n in enumerate(lengths)]).to(
+        torch.bfloat16).pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    len_host = torch.from_numpy(lengths.copy()).pin_memory()
     xs = [torch.empty_like(xd) for _ in range(2)]
     outs = [torch.empty_like(xd) for _ in range(2)]
     masks = [nrp.key_padding_mask(lengths, T) for _ in range(2)]
+    packed_in = [torch.empty_like(x_host, device=dev) for _ in range(2)]
+    packed_out = [torch.empty_like(x_host, device=dev) for _ in range(2)]
 
     def h2d_fn(slot):
-        nrp.copy_frames(xs[slot], x_host, lengths)
-        masks[slot].lengths.copy_(len_host, non_blocking=True)
+        packed_in[slot].copy_(x_host, non_blocking=True)
 
     def compute_fn(slot):
+        nrp.unpack_frames(xs[slot], packed_in[slot], lengths, dev_lengths=masks[slot].lengths)
         attn.forward(xs[slot], pos, None, masks[slot], out=outs[slot])
+        nrp.pack_frames(packed_out[slot], outs[slot], lengths)
 
     def d2h_fn(slot):
-        nrp.copy_frames(out_host, outs[slot], lengths)
+        out_host.copy_(packed_out[slot], non_blocking=True)
 
     run_pipelined(4, h2d_fn, compute_fn, d2h_fn)  # warm-up
     barrier()
@@ -801,7 +808,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
     e2e_value = world * frames * args.steps / (e2e_ms / 1e3)
-    h2d = frames * D * 2 + len_host.numel() * 4
+    h2d = frames * D * 2 + lengths.size * 4  # the lengths go in the scatter's parameters
     d2h = frames * D * 2
     link = host_link(world, dev, h2d, d2h, barrier)
     floor_ms = max(link["bidir_ms_per_step"], total_ms / args.steps)

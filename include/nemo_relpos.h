@@ -276,6 +276,28 @@ typedef struct nrp_halo nrp_halo;
 int nrp_copy_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
                     int64_t row_bytes, void* stream, int64_t* bytes);
 
+/* Packed frames: a batch's valid frames back to back, utterance b's
+ * lengths[b] rows from packed row lengths[0] + ... + lengths[b-1] on (the
+ * buffer a serving loop fills per step).  nrp_unpack_frames writes them into
+ * rows [0, lengths[b]) of the [B, T, row_bytes] device tensor dst, and
+ * nrp_pack_frames reads those rows of src into packed dst.  With `staging`
+ * (device memory of at least sum(lengths) * row_bytes bytes) the packed side
+ * may be pinned host memory: one cudaMemcpyAsync crosses the link (into or
+ * out of staging) and a kernel scatters or gathers the rows on the device;
+ * staging NULL means the packed side is device memory.  One copy per
+ * direction instead of nrp_copy_frames' one per utterance: with 16
+ * utterances moving both ways at once, per-utterance copies ran at 36 GB/s
+ * each way on B200 over PCIe, one copy each way at 49 GB/s.  dev_lengths
+ * (may be NULL): the kernel also writes lengths[b] there (the device lengths
+ * of a key-padding mask), so a step needs no second upload.  lengths is a
+ * host array, each in [0, T].  Padded rows are left as they are.  Stream
+ * ordered; *bytes (may be NULL): the packed bytes. */
+int nrp_unpack_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
+                      int64_t row_bytes, void* staging, int32_t* dev_lengths, void* stream,
+                      int64_t* bytes);
+int nrp_pack_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
+                    int64_t row_bytes, void* staging, void* stream, int64_t* bytes);
+
 /* Segment of `rank`: [start, start + len) of seq_len frames cut into nranks
  * pieces of ceil(seq_len / nranks) (the last one ragged; len may be 0). */
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len);

@@ -116,6 +116,8 @@ def lib():
             "nrp_seq_shard": ([i, i, i, vp, vp], i),
             "nrp_partition_utterances": ([vp, i, i, i, vp, vp], i),
             "nrp_copy_frames": ([vp, vp, vp, i, i, C.c_int64, vp, vp], i),
+            "nrp_unpack_frames": ([vp, vp, vp, i, i, C.c_int64, vp, vp, vp, vp], i),
+            "nrp_pack_frames": ([vp, vp, vp, i, i, C.c_int64, vp, vp, vp], i),
             "nrp_seq_shard_plan": ([i, i, i, vp, vp], i),
             "nrp_halo_unique_id": ([vp], i),
             "nrp_halo_comm_create": ([vp, vp, i, i, i, vp], i),
@@ -1117,6 +1119,79 @@ def copy_frames(dst, src, lengths, non_blocking: bool = True) -> int:
         import torch
         torch.cuda.current_stream().synchronize()
     return int(nbytes.value)
+
+
+def _frames_args(name, padded, packed, lengths, staging):
+    """Checks shared by unpack_frames / pack_frames; returns (lengths as
+    int32, row bytes, packed bytes)."""
+    if padded.dim() < 2 or packed.dim() != padded.dim() - 1:
+        raise ValueError(f"{name}: padded [B, T, ...] and packed [rows, ...] tensors")
+    if padded.dtype != packed.dtype or padded.shape[2:] != packed.shape[1:]:
+        raise ValueError(f"{name}: padded and packed rows differ in shape or dtype")
+    if not (padded.is_contiguous() and packed.is_contiguous()):
+        raise ValueError(f"{name}: contiguous tensors only")
+    if not padded.is_cuda:
+        raise ValueError(f"{name}: the padded tensor lives on the device")
+    B, T = padded.shape[0], padded.shape[1]
+    ln = np.ascontiguousarray(
+        lengths.detach().cpu().numpy() if hasattr(lengths, "detach") else lengths, np.int32)
+    if ln.shape != (B,) or (ln < 0).any() or (ln > T).any():
+        raise ValueError(f"{name}: one length in [0, T] per utterance")
+    if packed.shape[0] < int(ln.sum()):
+        raise ValueError(f"{name}: the packed tensor has fewer rows than sum(lengths)")
+    row = padded[0, 0].numel() * padded.element_size() if T else 0
+    nbytes = int(ln.sum()) * row
+    if packed.is_cuda:
+        if staging is not None:
+            raise ValueError(f"{name}: staging is for a packed tensor in host memory")
+    else:
+        if staging is None or not staging.is_cuda or not staging.is_contiguous() or \
+                staging.numel() * staging.element_size() < nbytes:
+            raise ValueError(f"{name}: a host packed tensor needs a device staging buffer of "
+                             f"{nbytes} bytes")
+        if not packed.is_pinned():
+            raise ValueError(f"{name}: the host packed tensor must be pinned")
+    return ln, row, nbytes
+
+
+def unpack_frames(dst, src, lengths, staging=None, dev_lengths=None) -> int:
+    """dst[b, :lengths[b]] = the packed rows of utterance b in src
+    ([sum(lengths), ...], utterances back to back) -- nrp_unpack_frames.
+    A pinned host src crosses the link in one copy into `staging` (a device
+    buffer of at least the packed bytes), then a kernel scatters the rows;
+    a device src is scattered directly.  dev_lengths (an int32 device
+    tensor of B, may be None, e.g. a KeyPaddingMask's lengths) also
+    receives the lengths.  Stream ordered; returns the packed bytes."""
+    ln, row, nbytes = _frames_args("unpack_frames", dst, src, lengths, staging)
+    B, T = dst.shape[0], dst.shape[1]
+    if dev_lengths is not None and (not dev_lengths.is_cuda or dev_lengths.dtype.itemsize != 4
+                                    or dev_lengths.numel() < B):
+        raise ValueError("unpack_frames: dev_lengths is an int32 device tensor of B")
+    if B == 0 or T == 0:
+        return 0
+    out = C.c_int64(0)
+    _check(lib().nrp_unpack_frames(dst.data_ptr(), src.data_ptr(), ln.ctypes.data, B, T, row,
+                                   staging.data_ptr() if staging is not None else None,
+                                   dev_lengths.data_ptr() if dev_lengths is not None else None,
+                                   _stream(), C.byref(out)))
+    return int(out.value)
+
+
+def pack_frames(dst, src, lengths, staging=None) -> int:
+    """The rows src[b, :lengths[b]] of every utterance, back to back into
+    dst ([sum(lengths), ...]) -- nrp_pack_frames.  For a pinned host dst a
+    kernel gathers the rows into `staging` (device, at least the packed
+    bytes) and one copy crosses the link; a device dst is gathered into
+    directly.  Stream ordered; returns the packed bytes."""
+    ln, row, nbytes = _frames_args("pack_frames", src, dst, lengths, staging)
+    B, T = src.shape[0], src.shape[1]
+    if B == 0 or T == 0:
+        return 0
+    out = C.c_int64(0)
+    _check(lib().nrp_pack_frames(dst.data_ptr(), src.data_ptr(), ln.ctypes.data, B, T, row,
+                                 staging.data_ptr() if staging is not None else None,
+                                 _stream(), C.byref(out)))
+    return int(out.value)
 
 
 def partition_utterances(lengths, nranks: int, d_model: int = 1024):

@@ -887,6 +887,90 @@ int nrp_copy_frames(void* dst, const void* src, const int32_t* lengths, int B, i
   return ok();
 }
 
+namespace {
+// Shared by nrp_unpack_frames / nrp_pack_frames: validates the arguments and
+// returns the packed byte count of the batch.
+int frames_args(const void* a, const void* b, const int32_t* lengths, int B, int T,
+                int64_t row_bytes, int64_t* packed_bytes) {
+  if (!a || !b || !lengths || B < 0 || T < 0 || row_bytes <= 0)
+    return fail(NRP_ERR_INVALID, "invalid frames arguments");
+  int64_t rows = 0;
+  for (int i = 0; i < B; ++i) {
+    if (lengths[i] < 0 || lengths[i] > T)
+      return fail(NRP_ERR_INVALID, "lengths[%d] = %d outside [0, %d]", i, lengths[i], T);
+    rows += lengths[i];
+  }
+  *packed_bytes = rows * row_bytes;
+  return ok();
+}
+
+// The scatter (to_padded) or gather of the whole batch between the padded
+// tensor and packed device rows, kMaxFrameUtts utterances per launch.
+int frames_launch(void* padded, void* packed, const int32_t* lengths, int B, int T,
+                  int64_t row_bytes, bool to_padded, int32_t* dev_lengths, cudaStream_t st) {
+  nrp::FramesPlan plan;
+  plan.row_bytes = row_bytes;
+  plan.bstride = static_cast<int64_t>(T) * row_bytes;
+  int64_t off = 0;
+  for (int b0 = 0; b0 < B; b0 += nrp::kMaxFrameUtts) {
+    const int n = std::min(nrp::kMaxFrameUtts, B - b0);
+    plan.b0 = b0;
+    for (int u = 0; u < n; ++u) {
+      plan.off[u] = off;
+      plan.len[u] = lengths[b0 + u];
+      off += lengths[b0 + u];
+    }
+    if (cudaError_t e = nrp::launch_frames(padded, packed, plan, n, to_padded, dev_lengths, st))
+      return fail(NRP_ERR_CUDA, "frames kernel: %s", cudaGetErrorString(e));
+  }
+  return ok();
+}
+}  // namespace
+
+int nrp_unpack_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
+                      int64_t row_bytes, void* staging, int32_t* dev_lengths, void* stream,
+                      int64_t* bytes) {
+  int64_t nb = 0;
+  if (int rc = frames_args(dst, src, lengths, B, T, row_bytes, &nb)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const void* packed = src;
+  if (staging && nb > 0) {  // the one copy over the link
+    const cudaError_t e = cudaMemcpyAsync(staging, src, static_cast<size_t>(nb),
+                                          cudaMemcpyDefault, st);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(NRP_ERR_CUDA, cudaGetErrorString(e));
+    }
+    packed = staging;
+  }
+  if (int rc = frames_launch(dst, const_cast<void*>(packed), lengths, B, T, row_bytes, true,
+                             dev_lengths, st))
+    return rc;
+  if (bytes) *bytes = nb;
+  return ok();
+}
+
+int nrp_pack_frames(void* dst, const void* src, const int32_t* lengths, int B, int T,
+                    int64_t row_bytes, void* staging, void* stream, int64_t* bytes) {
+  int64_t nb = 0;
+  if (int rc = frames_args(dst, src, lengths, B, T, row_bytes, &nb)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* packed = staging ? staging : dst;
+  if (int rc = frames_launch(const_cast<void*>(src), packed, lengths, B, T, row_bytes, false,
+                             nullptr, st))
+    return rc;
+  if (staging && nb > 0) {
+    const cudaError_t e = cudaMemcpyAsync(dst, staging, static_cast<size_t>(nb),
+                                          cudaMemcpyDefault, st);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(NRP_ERR_CUDA, cudaGetErrorString(e));
+    }
+  }
+  if (bytes) *bytes = nb;
+  return ok();
+}
+
 int nrp_seq_shard(int seq_len, int nranks, int rank, int* start, int* len) {
   if (!start || !len) return fail(NRP_ERR_INVALID, "null output");
   if (seq_len <= 0 || nranks < 1 || rank < 0 || rank >= nranks)

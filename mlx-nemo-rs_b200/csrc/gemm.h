@@ -311,6 +311,21 @@ cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,
                                cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n,
                                cudaStream_t stream);
+// Packed <-> padded frames.  One launch covers up to kMaxFrameUtts
+// utterances: utterance u (padded batch index b0 + u) has len[u] rows, at
+// packed rows [off[u], off[u] + len[u]) and padded rows [0, len[u]) of batch
+// row b0 + u (bstride bytes apart).  to_padded: packed -> padded, else the
+// reverse.  dev_lengths (may be null): len[u] is also written to
+// dev_lengths[b0 + u].
+constexpr int kMaxFrameUtts = 128;
+struct FramesPlan {
+  int64_t row_bytes, bstride, b0;
+  int64_t off[kMaxFrameUtts];
+  int32_t len[kMaxFrameUtts];
+};
+cudaError_t launch_frames(void* padded, void* packed, const FramesPlan& plan, int n_utts,
+                          bool to_padded, int32_t* dev_lengths, cudaStream_t stream);
+
 // Ring append of rows: dst[b, (head + i) % C, :] = src[b, src_off + i, :] for
 // i in [0, n), row length `cols` elements of `elem_bytes`.
 cudaError_t launch_ring_append(const void* src, int64_t src_bstride, int64_t src_rstride,

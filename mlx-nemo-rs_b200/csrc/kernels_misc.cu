@@ -4,7 +4,8 @@
 //  * the small-M MLX-affine 8-bit GEMM (quantized_matmul for streaming-size
 //    M, quantization.rs:137-160): weights dequantised in registers into
 //    bf16 MMA fragments, HBM-bound on the packed weights;
-//  * dtype conversions and the ring-buffer row append of the streaming cache;
+//  * dtype conversions, the ring-buffer row append of the streaming cache,
+//    and the packed <-> padded frame moves around a host upload/download;
 //  * TMA descriptor construction (driver entry point via the runtime).
 #include <cudaTypedefs.h>
 #include <algorithm>
@@ -612,6 +613,28 @@ __global__ void ring_append_kernel(const uint8_t* __restrict__ src, int64_t sb, 
     for (int e = threadIdx.x; e < row_bytes; e += blockDim.x) d[e] = s[e];
   }
 }
+
+// Packed <-> padded frames of up to kMaxFrameUtts utterances: utterance u's
+// rows are packed rows [off[u], off[u] + len[u]) and padded rows b0 + u,
+// [0, len[u]).  Each block copies 16-byte vectors (V = uint4) or bytes
+// (V = uint8_t) of one utterance (blockIdx.y), strided over blockIdx.x.
+template <typename V>
+__global__ void frames_kernel(uint8_t* __restrict__ padded, uint8_t* __restrict__ packed,
+                              FramesPlan plan, bool to_padded, int32_t* __restrict__ dev_len) {
+  const int u = blockIdx.y;
+  const int64_t nv = plan.row_bytes / static_cast<int64_t>(sizeof(V));
+  const int64_t n = static_cast<int64_t>(plan.len[u]) * nv;
+  V* pd = reinterpret_cast<V*>(padded + (plan.b0 + u) * plan.bstride);
+  V* pk = reinterpret_cast<V*>(packed + plan.off[u] * plan.row_bytes);
+  if (dev_len && blockIdx.x == 0 && threadIdx.x == 0) dev_len[plan.b0 + u] = plan.len[u];
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (to_padded)
+      pd[e] = pk[e];
+    else
+      pk[e] = pd[e];
+  }
+}
 }  // namespace
 
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,
@@ -625,6 +648,30 @@ cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n,
                                cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   bf16_to_f32_kernel<<<grid_for(n), 256, 0, stream>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_frames(void* padded, void* packed, const FramesPlan& plan, int n_utts,
+                          bool to_padded, int32_t* dev_lengths, cudaStream_t stream) {
+  if (n_utts <= 0) return cudaSuccess;
+  if (n_utts > kMaxFrameUtts || plan.row_bytes <= 0) return cudaErrorInvalidValue;
+  int max_len = 0;
+  for (int u = 0; u < n_utts; ++u) max_len = std::max(max_len, plan.len[u]);
+  const bool vec = (plan.row_bytes & 15) == 0 && (plan.bstride & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(padded) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(packed) & 15) == 0;
+  const int64_t per_utt = static_cast<int64_t>(max_len) * (vec ? plan.row_bytes / 16
+                                                                 : plan.row_bytes);
+  // about four elements per thread; every utterance gets at least one block
+  // (dev_lengths is written by block 0 of each)
+  const int64_t gx = std::min<int64_t>(std::max<int64_t>((per_utt + 1023) / 1024, 1), 4096);
+  dim3 grid(static_cast<unsigned>(gx), n_utts);
+  uint8_t* pd = static_cast<uint8_t*>(padded);
+  uint8_t* pk = static_cast<uint8_t*>(packed);
+  if (vec)
+    frames_kernel<uint4><<<grid, 256, 0, stream>>>(pd, pk, plan, to_padded, dev_lengths);
+  else
+    frames_kernel<uint8_t><<<grid, 256, 0, stream>>>(pd, pk, plan, to_padded, dev_lengths);
   return cudaGetLastError();
 }
 

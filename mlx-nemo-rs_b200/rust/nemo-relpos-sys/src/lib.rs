@@ -222,6 +222,13 @@ extern "C" {
     pub fn nrp_copy_frames(dst: *mut c_void, src: *const c_void, lengths: *const i32,
                            batch: c_int, frames: c_int, row_bytes: i64, stream: *mut c_void,
                            bytes: *mut i64) -> c_int;
+    pub fn nrp_unpack_frames(dst: *mut c_void, src: *const c_void, lengths: *const i32,
+                             batch: c_int, frames: c_int, row_bytes: i64, staging: *mut c_void,
+                             dev_lengths: *mut i32, stream: *mut c_void, bytes: *mut i64)
+                             -> c_int;
+    pub fn nrp_pack_frames(dst: *mut c_void, src: *const c_void, lengths: *const i32,
+                           batch: c_int, frames: c_int, row_bytes: i64, staging: *mut c_void,
+                           stream: *mut c_void, bytes: *mut i64) -> c_int;
     pub fn nrp_subsampling_create(ctx: *mut nrp_context, feat_in: c_int, d_model: c_int,
                                   factor: c_int, conv_channels: c_int, causal_downsampling: c_int,
                                   out: *mut *mut nrp_subsampling) -> c_int;
