@@ -1313,7 +1313,7 @@ int nrp::attn_forward_with_cache(nrp_attn* a, cudaStream_t st, const void* x, in
           q, c->kc.as<__nv_bfloat16>(), c->vc.as<__nv_bfloat16>(), c->hc.as<__nv_bfloat16>(),
           static_cast<const __nv_bfloat16*>(x), C, c->head, fuse ? n_app : 0, src0,
           a->spos.as<__nv_bfloat16>(), a->u_dev.as<float>(), a->v_dev.as<float>(), sm,
-          a->cbuf.as<__nv_bfloat16>(), B, T, D, a->H, st));
+          a->cbuf.as<__nv_bfloat16>(), B, T, D, a->H, ctx->d_err, st));
       appended = fuse;
     } else if (a->dtype == NRP_DTYPE_BF16) {
       const auto* q = a->qkv.as<__nv_bfloat16>();

@@ -298,13 +298,15 @@ cudaError_t launch_subsample_dw(const __nv_bfloat16* x, int B, int Ti, int Fi, i
 // slot `head`), p [2(C+T)-1, D], out [B, T, D].  With n_app > 0 (only when
 // T <= 16) the kernel also writes new frames src0 .. src0+n_app-1 (K, V
 // and the attention input x) into ring slots head .. head+n_app-1 (mod C).
+// err: the context's device error word (a bulk copy that never lands).
 bool stream_attn_supported(int C, int T, int D, int H);
 cudaError_t launch_relpos_attn_stream_mma(const __nv_bfloat16* qkv, const __nv_bfloat16* kc,
                                           const __nv_bfloat16* vc, __nv_bfloat16* hc,
                                           const __nv_bfloat16* x, int C, int head, int n_app,
                                           int src0, const __nv_bfloat16* p, const float* u,
                                           const float* v, StreamMaskDev sm, __nv_bfloat16* out,
-                                          int B, int T, int D, int H, cudaStream_t stream);
+                                          int B, int T, int D, int H, int* err,
+                                          cudaStream_t stream);
 
 // ---- small elementwise helpers ----
 cudaError_t launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n,

@@ -205,16 +205,6 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// bytes (a multiple of 16, both addresses 16-byte aligned) from global to
-// this CTA's shared memory, completing on `bar`
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // the 16 codes of a 16-byte load as floats: each byte placed in the low
 // mantissa bits of 2^23 (one byte permute), then 2^23 subtracted (exact)
 __device__ __forceinline__ void codes16(const uint4 q, float s, float z, float (&w)[16]) {
