@@ -20,7 +20,7 @@ NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]
-SOURCES = ["gemm_sm100.cu", "attn_sm100.cu", "attn_simt.cu", "attn_stream.cu", "kernels_misc.cu",
+SOURCES = ["gemm_sm100.cu", "gemm_tf32.cu", "attn_sm100.cu", "attn_simt.cu", "attn_stream.cu", "kernels_misc.cu",
            "noalloc.cu", "block_kernels.cu", "subsampling_kernels.cu", "api.cpp", "halo.cpp",
            "block.cpp", "subsampling.cpp"]
 

@@ -284,7 +284,7 @@ int run_linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int 
     ProfScope ps(ctx, NRP_KERNEL_GEMM_F32, st);
     CUDA_TRY(nrp::launch_gemm_f32(static_cast<const float*>(x), M, K, static_cast<const float*>(w),
                                   N, static_cast<const float*>(bias), static_cast<float*>(y), ldy,
-                                  ctx->num_sms, st));
+                                  ctx->num_sms, ctx->d_err, st));
     return ok();
   }
   if (K % 64 != 0 || N % 32 != 0 || ldy % 8 != 0)

@@ -3,7 +3,9 @@
 // Serves modules whose dtype is f32 (the reference's default f32 graph,
 // attention.rs:458-573 offline and 606-816 streaming; 1e-4 parity needs
 // FFMA, not TF32 tensor cores) and any head_dim <= 128, plus the streaming
-// form for bf16 storage.  One warp per query row: lanes score 32 keys at a
+// form for bf16 storage.  Offline with head_dim 128, the block-staged kernel
+// below (relpos_attn_f32_blocked_kernel) runs.  Otherwise one warp per query
+// row: lanes score 32 keys at a
 // time ((q+u).k_j + (q+v).p_r with r = Tq-1-i+j, the rel_shift identity of
 // attention.rs:1248-1282), keep an online softmax, and accumulate P.V with
 // each lane owning dims lane, lane+32, lane+64, lane+96.
@@ -155,6 +157,176 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+
+// ---- offline f32 attention, head_dim 128 ----------------------------------
+// A CTA takes 4 consecutive query rows of one (utterance, head), one per
+// warp, and walks the keys in blocks of 32 that all 128 threads stage in
+// shared memory with cp.async (double-buffered: block n+1 lands while block n
+// computes): the block's K and V rows and the 35 positional rows its four
+// query rows reach (P row T-1-i+j is window row 3 - w + l for warp w's row
+// and key jb + l).  Lane l owns head dims 4l .. 4l+3: per key a lane forms
+// its share of (q+u).k_j + (q+v).p_r, and a transposed butterfly over the
+// warp (31 shuffles for 32 keys) leaves lane l with key jb + l's score, so
+// the online softmax and P.V (lane-owned dims, float4 rows) need no
+// per-key global loads.  Rows past the data load as zeros (cp.async with a
+// zero source size), so masked keys meet finite V rows.
+constexpr int kFRows = 4;                     // query rows per CTA
+constexpr int kFKeys = 32;                    // keys per block
+constexpr int kFPRows = kFKeys + kFRows - 1;  // positional rows per block
+constexpr int kFBuf = (2 * kFKeys + kFPRows) * 128;  // floats per staged block
+
+__device__ __forceinline__ void cp_async16z(float* dst, const float* src, bool in) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(in ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kFRows * 32)
+    relpos_attn_f32_blocked_kernel(const float* __restrict__ q, int ldq,
+                                   const float* __restrict__ k, int ldk,
+                                   const float* __restrict__ v, int ldv,
+                                   const float* __restrict__ p, int p_rows,
+                                   const float* __restrict__ pu, const float* __restrict__ pv,
+                                   const int32_t* __restrict__ key_len, AttnContextDev ctx,
+                                   float* __restrict__ out, int T, int D) {
+  extern __shared__ __align__(16) float fsm[];  // [2][kFBuf]
+  __shared__ int s_lo[kFRows], s_hi[kFRows];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int i0 = blockIdx.x * kFRows, i = i0 + warp;
+  const int col = h * 128 + 4 * lane;  // this lane's head dims
+  int kend = T;
+  if (key_len) kend = min(T, max(key_len[b], 1));
+  int lo = 0, hi = 0;
+  const StreamMaskDev none{};
+  const bool any = i < T && key_interval(ctx, none, i, kend, lo, hi);
+  if (lane == 0) {
+    s_lo[warp] = any ? lo : INT32_MAX;
+    s_hi[warp] = any ? hi : 0;
+  }
+  float4 qu = make_float4(0.f, 0.f, 0.f, 0.f), qv = qu;
+  if (i < T) {
+    const float4 x = *reinterpret_cast<const float4*>(q + (static_cast<int64_t>(b) * T + i) * ldq + col);
+    const float4 u4 = *reinterpret_cast<const float4*>(pu + col);
+    const float4 v4 = *reinterpret_cast<const float4*>(pv + col);
+    qu = make_float4(x.x + u4.x, x.y + u4.y, x.z + u4.z, x.w + u4.w);
+    qv = make_float4(x.x + v4.x, x.y + v4.y, x.z + v4.z, x.w + v4.w);
+  }
+  __syncthreads();
+  int jlo = INT32_MAX, jhi = 0;  // the keys any of the CTA's rows sees
+#pragma unroll
+  for (int w = 0; w < kFRows; ++w) {
+    jlo = min(jlo, s_lo[w]);
+    jhi = max(jhi, s_hi[w]);
+  }
+  // block jb -> buffer s: K rows jb.., V rows jb.., positional rows from
+  // T-1-(i0+3)+jb; 16 bytes per thread and step
+  auto stage = [&](int jb, int s) {
+    float* base = fsm + s * kFBuf;
+    const int rbase = T - 1 - (i0 + kFRows - 1) + jb;
+    for (int e = threadIdx.x; e < (2 * kFKeys + kFPRows) * 32; e += kFRows * 32) {
+      const int row = e >> 5, c4 = (e & 31) * 4;
+      const float* src;
+      bool in;
+      if (row < 2 * kFKeys) {
+        const int j = jb + (row & (kFKeys - 1));
+        in = j < T;
+        src = row < kFKeys ? k + (static_cast<int64_t>(b) * T + j) * ldk
+                           : v + (static_cast<int64_t>(b) * T + j) * ldv;
+      } else {
+        const int r = rbase + row - 2 * kFKeys;
+        in = r >= 0 && r < p_rows;
+        src = p + static_cast<int64_t>(r) * D;
+      }
+      cp_async16z(base + row * 128 + c4, in ? src + h * 128 + c4 : p, in);
+    }
+    cp_async_commit();
+  };
+  const float scale = rsqrtf(128.f);
+  float m = -INFINITY, l = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (jlo < jhi) stage(jlo, 0);
+  for (int jb = jlo, n = 0; jb < jhi; jb += kFKeys, ++n) {
+    if (jb + kFKeys < jhi) {
+      stage(jb + kFKeys, (n + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // block n is in shared memory for every thread
+    if (any) {
+      const float* sK = fsm + (n & 1) * kFBuf;
+      const float* sV = sK + kFKeys * 128;
+      const float* sP = sV + kFKeys * 128 + (kFRows - 1 - warp) * 128;
+      float part[kFKeys];
+#pragma unroll
+      for (int kk = 0; kk < kFKeys; ++kk) {
+        const float4 kv = *reinterpret_cast<const float4*>(sK + kk * 128 + 4 * lane);
+        const float4 pr = *reinterpret_cast<const float4*>(sP + kk * 128 + 4 * lane);
+        float a = qu.x * kv.x;
+        a = fmaf(qu.y, kv.y, a);
+        a = fmaf(qu.z, kv.z, a);
+        a = fmaf(qu.w, kv.w, a);
+        a = fmaf(qv.x, pr.x, a);
+        a = fmaf(qv.y, pr.y, a);
+        a = fmaf(qv.z, pr.z, a);
+        part[kk] = fmaf(qv.w, pr.w, a);
+      }
+      // transposed butterfly: after the step of width `off`, a lane keeps
+      // the keys whose bit matches its own lane bit
+#pragma unroll
+      for (int off = 16, nk = kFKeys; off >= 1; off >>= 1, nk >>= 1) {
+        const bool upper = lane & off;
+#pragma unroll
+        for (int kk = 0; kk < nk / 2; ++kk) {
+          const float send = upper ? part[kk] : part[kk + nk / 2];
+          const float keep = upper ? part[kk + nk / 2] : part[kk];
+          part[kk] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      const int j = jb + lane;
+      const float sc = (j >= lo && j < hi) ? part[0] * scale : -INFINITY;
+      float cm = sc;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+      const float mn = fmaxf(m, cm);
+      const float alpha = (m == -INFINITY) ? 0.f : expf(m - mn);
+      const float pj = (sc == -INFINITY) ? 0.f : expf(sc - mn);
+      float ps = pj;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l = l * alpha + ps;
+      o.x *= alpha;
+      o.y *= alpha;
+      o.z *= alpha;
+      o.w *= alpha;
+#pragma unroll
+      for (int kk = 0; kk < kFKeys; ++kk) {
+        const float w = __shfl_sync(0xffffffffu, pj, kk);
+        const float4 vv = *reinterpret_cast<const float4*>(sV + kk * 128 + 4 * lane);
+        o.x = fmaf(w, vv.x, o.x);
+        o.y = fmaf(w, vv.y, o.y);
+        o.z = fmaf(w, vv.z, o.z);
+        o.w = fmaf(w, vv.w, o.w);
+      }
+      m = mn;
+    }
+    __syncthreads();  // buffer n & 1 is restaged for block n + 2
+  }
+  if (i < T) {
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    *reinterpret_cast<float4*>(out + (static_cast<int64_t>(b) * T + i) * D + col) =
+        make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_relpos_attn_f32(const float* q, int ldq, const float* k, int ldk,
@@ -162,6 +334,22 @@ cudaError_t launch_relpos_attn_f32(const float* q, int ldq, const float* k, int 
                                    const float* vb, const int32_t* key_len, AttnContextDev ctx,
                                    StreamMaskDev sm, float* out, int B, int Tq, int Tk, int D,
                                    int H, cudaStream_t stream) {
+  // head_dim 128 with 16-byte aligned rows: the block-staged kernel
+  if (D == H * 128 && Tq == Tk && (ldq & 3) == 0 && (ldk & 3) == 0 && (ldv & 3) == 0 &&
+      (D & 3) == 0 &&
+      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(p) |
+        reinterpret_cast<uintptr_t>(u) | reinterpret_cast<uintptr_t>(vb) |
+        reinterpret_cast<uintptr_t>(out)) & 15) == 0 &&
+      !sm.has) {
+    constexpr int smem = 2 * kFBuf * 4;
+    static std::atomic<uint64_t> attr{0};
+    if (cudaError_t e = smem_attr_once(relpos_attn_f32_blocked_kernel, smem, attr)) return e;
+    dim3 grid((Tq + kFRows - 1) / kFRows, H, B);
+    relpos_attn_f32_blocked_kernel<<<grid, kFRows * 32, smem, stream>>>(
+        q, ldq, k, ldk, v, ldv, p, 2 * Tq - 1, u, vb, key_len, ctx, out, Tq, D);
+    return cudaGetLastError();
+  }
   dim3 grid((Tq + kWarps - 1) / kWarps, H, B);
   relpos_attn_simt_kernel<float><<<grid, kWarps * 32, 0, stream>>>(
       q, ldq, k, ldk, v, ldv, nullptr, nullptr, 0, 0, p, u, vb, key_len, ctx, sm, out, Tq, Tk, D,

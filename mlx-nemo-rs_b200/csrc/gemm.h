@@ -156,11 +156,17 @@ cudaError_t launch_qgemm_small(const __nv_bfloat16* x, int M, int K, const uint8
                                int num_sms, int* err, cudaStream_t stream,
                                const Epilogue& ep = Epilogue());
 
-// ---- fp32 CUDA-core GEMM (fp32 module dtype): y = x . W^T (+ bias) ----
-// num_sms: the device's SM count (the tile height is chosen for two CTAs per SM)
+// ---- fp32 GEMM (fp32 module dtype): y = x . W^T (+ bias) ----
+// The 3xTF32 tcgen05 kernel (gemm_tf32.cu) where gemm_tf32_supported (K a
+// multiple of 32, x and w 16-byte aligned), else CUDA-core FFMA tiles.
+// num_sms: the device's SM count; err: the context's device error word.
 cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
-                            const float* bias, float* y, int ldy, int num_sms,
+                            const float* bias, float* y, int ldy, int num_sms, int* err,
                             cudaStream_t stream);
+bool gemm_tf32_supported(int M, int K, int N, const void* x, const void* w);
+cudaError_t launch_gemm_tf32x3(const float* x, int M, int K, const float* w, int N,
+                               const float* bias, float* y, int ldy, int num_sms, int* err,
+                               cudaStream_t stream);
 
 // ---- offline fused rel-pos attention, bf16, tcgen05 ----
 // Where a launch's rows sit in the sequence.  All frame indices are global

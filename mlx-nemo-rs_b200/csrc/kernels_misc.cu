@@ -159,8 +159,10 @@ void launch_f32(bool vec, const float* x, int M, int K, const float* w, int N, c
 }  // namespace
 
 cudaError_t launch_gemm_f32(const float* x, int M, int K, const float* w, int N,
-                            const float* bias, float* y, int ldy, int num_sms,
+                            const float* bias, float* y, int ldy, int num_sms, int* err,
                             cudaStream_t stream) {
+  if (gemm_tf32_supported(M, K, N, x, w) && ldy >= N)
+    return launch_gemm_tf32x3(x, M, K, w, N, bias, y, ldy, num_sms, err, stream);
   const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(w) & 15) == 0;
   // 32-row tiles when 64-row ones would give fewer than two CTAs per SM

@@ -95,7 +95,7 @@ int linear(nrp_context* ctx, cudaStream_t st, int dtype, const void* x, int M, i
   if (dtype == NRP_DTYPE_F32) {
     TRY_CUDA(nrp::launch_gemm_f32(static_cast<const float*>(x), M, K, static_cast<const float*>(w),
                                   N, static_cast<const float*>(bias), static_cast<float*>(y), ldy,
-                                  ctx->num_sms, st));
+                                  ctx->num_sms, ctx->d_err, st));
     return NRP_OK;
   }
   if (quant && nrp::qgemm_small_supported(M, K, x, w, nrp::Epilogue())) {

@@ -288,6 +288,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 //  MN-major: 128 B rows run along M/N (64 elements), successive rows are
 //           successive K; LBO = byte stride between 64-wide M/N blocks,
 //           SBO = byte stride between 8-row K groups (1024).
+// The same MMA with TF32 operands (32-bit elements in shared memory, 8 per
+// 32-byte K step), f32 accumulation.
+__device__ __forceinline__ void umma_tf32_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
@@ -298,6 +309,12 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
+// kind::tf32 instruction descriptor: f32 accumulator, A and B both TF32
+// (format 2), both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
 // Instruction descriptor, kind::f16 with bf16 A/B and f32 accumulator:
 // c_format F32 (1) at bit 4, a_format BF16 (1) at 7, b_format BF16 (1) at
 // 10, a_major at 15, b_major at 16 (0 = K-major, 1 = MN-major), N>>3 at 17,

@@ -7,7 +7,8 @@ use std::env;
 use std::path::PathBuf;
 
 const CUDA_SOURCES: &[&str] = &[
-    "gemm_sm100.cu", "attn_sm100.cu", "attn_simt.cu", "attn_stream.cu", "kernels_misc.cu",
+    "gemm_sm100.cu", "gemm_tf32.cu", "attn_sm100.cu", "attn_simt.cu", "attn_stream.cu",
+    "kernels_misc.cu",
     "noalloc.cu", "block_kernels.cu", "subsampling_kernels.cu",
 ];
 const CPP_SOURCES: &[&str] = &["api.cpp", "halo.cpp", "block.cpp", "subsampling.cpp"];
