@@ -1016,9 +1016,11 @@ def _harness(args, world, rank, local, ctx, step, frames, flops, kinds_bound, wo
             rk[name] = {"achieved": g, "frac": g / hbm_peak, "unit": "GB/s",
                         "algorithmic_bytes_per_launch": hbm_bytes[name] * args.steps / n}
     if dtype == "f32":
-        # f32 kernels run on the FFMA pipes, not the tensor cores: also give
-        # their fraction of the nominal FFMA peak (SMs x 128 FMA/clock x 2
-        # FLOP x the maximum SM clock seen)
+        # f32 modules: the GEMM runs as three TF32 tensor-core products per
+        # f32 product (frac above is against the bf16 peak), the attention on
+        # the FFMA pipes; both also get their fraction of the nominal FFMA
+        # peak (SMs x 128 FMA/clock x 2 FLOP x the maximum SM clock seen),
+        # the rate of an f32 path without tensor cores
         import torch
         n_sm = torch.cuda.get_device_properties(local).multi_processor_count
         mhz = clocks.summary().get("sm_max_mhz") or 1965.0
