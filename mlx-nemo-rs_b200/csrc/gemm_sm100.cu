@@ -6,7 +6,8 @@
 // where producer warps dequantise u8 weights straight into the swizzled
 // shared-memory B tile, so the dequantised matrix never exists in HBM.
 //
-// Tiling: 128 x 256 output tile per CTA step (128 x 128 or 128 x 192 when
+// Tiling: 128 x 256 output tile per CTA step (128 x 128, 128 x 192 or, for
+// problems whose 128-wide tiles fill at most half the SMs, 128 x 64 when
 // that fills the persistent grid's one wave better), K in 64-element stages
 // (one 128-byte swizzle atom per row; also exactly one quantisation group), a
 // 4-deep TMA/mbarrier pipeline, and two 256-column TMEM accumulators so the
@@ -31,12 +32,12 @@ constexpr int kBM = 128;
 // with few tiles: twice the CTAs, and 6 pipeline stages in the same budget)
 // or 192 (bf16 W: when 128-wide tiles overflow one wave and 192-wide fit it).
 constexpr int kBK = 64;
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 7;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 template <int kBN>
 struct TileCfg {
-  static constexpr int kStages = kBN == 128 ? 6 : 4;
-  static constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 / 16 KB
+  static constexpr int kStages = kBN == 64 ? 7 : kBN == 128 ? 6 : 4;
+  static constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 / 24 / 16 / 8 KB
 };
 constexpr int kEpiWarp0 = 2;
 constexpr int kDeqWarp0 = 6;
@@ -59,7 +60,7 @@ constexpr size_t smem_bytes() {
          kEpiBytes + 256 + 4 * (kMaxBatch + 1);
 }
 static_assert(smem_bytes<256>() <= 232448 && smem_bytes<192>() <= 232448 &&
-                  smem_bytes<128>() <= 232448,
+                  smem_bytes<128>() <= 232448 && smem_bytes<64>() <= 232448,
               "shared memory budget");
 
 // v[e] += bias[n + e] for e < 32 (zero past N); 16-byte loads when `vec`.
@@ -571,6 +572,12 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
       tm * (N / 192) <= num_sms)
     return launch_tn<false, 192>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
                                  num_sms, err, stream, rt, ep, w_early);
+  // 64-wide tiles when 128-wide ones fill at most half the SMs (the N = 1024
+  // projections of a streaming chunk step, M = 896: 56 tiles -> 112): each
+  // CTA streams a quarter less, and twice the SMs pull their operands
+  if (bn == 128 && ep.mode != kEpiGlu && N % 64 == 0 && 2 * tm * ((N + 127) / 128) <= num_sms)
+    return launch_tn<false, 64>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
+                                num_sms, err, stream, rt, ep, w_early);
   if (bn == 128)
     return launch_tn<false, 128>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
                                  num_sms, err, stream, rt, ep, w_early);
