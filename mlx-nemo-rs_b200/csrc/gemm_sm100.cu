@@ -54,13 +54,23 @@ struct GemmSmem {
 constexpr uint32_t kSlabBytes = 32 * 128;  // 32 rows x 64 bf16, 128B-swizzled
 constexpr uint32_t kEpiBytes = 4 * 2 * kSlabBytes;  // 4 warps x 2 buffers
 constexpr int kMaxBatch = 256;  // batched tiling: utterances per GEMM
-template <int kBN>
+// A CTA pair (kPair) shares 256-row x 256-column tiles: each CTA holds its
+// own 128 rows of X and half of the tile's W rows (16 KB per stage), so six
+// stages fit where one CTA's 128 x 256 tile fits four.
+template <int kBN, bool kPair>
+struct StageCfg {
+  static constexpr int kStages = kPair ? 6 : TileCfg<kBN>::kStages;
+  static constexpr uint32_t kBBytes = kPair ? kBN / 2 * kBK * 2 : TileCfg<kBN>::kBBytes;
+};
+template <int kBN, bool kPair = false>
 constexpr size_t smem_bytes() {
-  return 1024 /*align slack*/ + TileCfg<kBN>::kStages * (kABytes + TileCfg<kBN>::kBBytes) +
-         kEpiBytes + 256 + 4 * (kMaxBatch + 1);
+  return 1024 /*align slack*/ +
+         StageCfg<kBN, kPair>::kStages * (kABytes + StageCfg<kBN, kPair>::kBBytes) + kEpiBytes +
+         256 + 4 * (kMaxBatch + 1);
 }
 static_assert(smem_bytes<256>() <= 232448 && smem_bytes<192>() <= 232448 &&
-                  smem_bytes<128>() <= 232448 && smem_bytes<64>() <= 232448,
+                  smem_bytes<128>() <= 232448 && smem_bytes<64>() <= 232448 &&
+                  smem_bytes<256, true>() <= 232448,
               "shared memory budget");
 
 // v[e] += bias[n + e] for e < 32 (zero past N); 16-byte loads when `vec`.
@@ -89,7 +99,7 @@ __device__ __forceinline__ void add_bias64(float* v, const __nv_bfloat16* bias, 
   add_bias32(v + 32, bias, n + 32, N, vec);
 }
 
-template <bool kQuant, int kBN>
+template <bool kQuant, int kBN, bool kPair>
 __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ CUtensorMap map_w,
@@ -99,8 +109,9 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                    const __nv_bfloat16* __restrict__ qb,   // [N, K/64]
                    const __nv_bfloat16* __restrict__ bias, // [N] or null
                    int M, int N, int K, RowTiling rt, Epilogue ep, int w_early, int* err) {
-  constexpr int kStages = TileCfg<kBN>::kStages;
-  constexpr uint32_t kBBytes = TileCfg<kBN>::kBBytes;
+  static_assert(!kPair || (!kQuant && kBN == 256), "pair tiles: bf16 W, 256 columns");
+  constexpr int kStages = StageCfg<kBN, kPair>::kStages;
+  constexpr uint32_t kBBytes = StageCfg<kBN, kPair>::kBBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -122,6 +133,18 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   const int tiles_n = (N + kBN - 1) / kBN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = K / kBK;
+  // Work items: single tiles, or (kPair) pairs of row tiles 2i, 2i + 1 that
+  // share a column tile, CTA rank r of the pair taking row tile 2i + r.
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const int num_work = kPair ? ((tiles_m + 1) / 2) * tiles_n : num_tiles;
+  const int work0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int work_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  // tile of CTA rank r in work item w; -1 past the last row tile
+  auto tile_of = [&](int w, int r) -> int {
+    if (!kPair) return w;
+    const int tm = 2 * (w / tiles_n) + r;
+    return tm < tiles_m ? tm * tiles_n + w % tiles_n : -1;
+  };
   int* live_pre = reinterpret_cast<int*>(sE + kEpiBytes + sizeof(GemmSmem));  // [B+1]
   int live_m = tiles_m;  // (set from the lengths after pdl_wait below)
   // list index -> (first row of the tile, its utterance); true = zero-fill tile
@@ -154,6 +177,26 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     r0 = (live_pre[b + 1] - live_pre[b] + k) * kBM;
     return true;
   };
+  // This CTA's rows of work item w (m0, bb), whether they are dead (zeros
+  // written) or absent (no row tile: loads fall outside X and read zeros,
+  // nothing is written); returns whether the item runs MMAs (a pair runs
+  // unless neither of its tiles is live).
+  auto work_rows = [&](int w, int& m0, int& bb, bool& dead, bool& absent) -> bool {
+    const int t = tile_of(w, static_cast<int>(rank));
+    absent = t < 0;
+    if (absent) {
+      m0 = batched ? tpb * kBM : tiles_m * kBM;
+      bb = 0;
+      dead = true;
+    } else {
+      dead = tile_rows(t, m0, bb);
+    }
+    if (!kPair) return !dead;
+    const int to = tile_of(w, static_cast<int>(rank ^ 1u));
+    int m1 = 0, b1 = 0;
+    const bool other_dead = to < 0 || tile_rows(to, m1, b1);
+    return !(dead && other_dead);
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&ss->full[s], kQuant ? 1 + 4 : 1);  // TMA + one arrival per dequant warp
@@ -161,21 +204,29 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ss->tfull[b], 1);
-      mbar_init(&ss->tempty[b], 4);
+      mbar_init(&ss->tempty[b], kPair ? 8 : 4);  // the epilogue warps of the pair
     }
     ss->abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ss->tmem_base, 512);
-    tmem_relinquish();
+    if (kPair) {
+      tmem_alloc_pair(&ss->tmem_base, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&ss->tmem_base, 512);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&map_x);
     if (!kQuant) prefetch_tensormap(&map_w);
   }
   tc_fence_before();
-  __syncthreads();
+  if (kPair)
+    cluster_sync();  // both CTAs' barriers are initialised before either signals them
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ss->tmem_base;
   volatile int* abort_flag = &ss->abort;
@@ -184,7 +235,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   // kernel, so their HBM latency hides under its tail.  Only when the tile
   // list does not depend on device lengths (the first tile is live).
   int pre = 0;
-  if (!kQuant && w_early && !(batched && rt.len) && warp == 0 && lane == 0 &&
+  if (!kQuant && !kPair && w_early && !(batched && rt.len) && warp == 0 && lane == 0 &&
       static_cast<int>(blockIdx.x) < num_tiles) {
     const int n0 = (static_cast<int>(blockIdx.x) % tiles_n) * kBN;
     pre = num_kb < kStages ? num_kb : kStages;
@@ -215,10 +266,11 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int w = work0; w < num_work && !*abort_flag; w += work_step) {
         int m0, bb;
-        if (tile_rows(tile, m0, bb)) continue;
-        const int n0 = (tile % tiles_n) * kBN;
+        bool dead, absent;
+        if (!work_rows(w, m0, bb, dead, absent)) continue;
+        const int n0 = (w % tiles_n) * kBN;
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t round = it / kStages;
@@ -233,6 +285,19 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
             *abort_flag = 1;
             break;
           }
+          if (kPair) {
+            // both CTAs' stage bytes complete on the leader's barrier, whose
+            // single arrival (with the pair's byte count) comes from here
+            if (rank == 0) mbar_arrive_expect_tx(&ss->full[s], 2 * (kABytes + kBBytes));
+            const uint32_t lb = leader_smem(smem_u32(&ss->full[s]));
+            if (batched)
+              tma_load_3d_pair(sA + s * kABytes, &map_x, lb, kb * kBK, m0, bb);
+            else
+              tma_load_2d_pair(sA + s * kABytes, &map_x, lb, kb * kBK, m0);
+            tma_load_2d_pair(sB + s * kBBytes, &map_w, lb, kb * kBK,
+                             n0 + static_cast<int>(rank) * (kBN / 2));
+            continue;
+          }
           mbar_arrive_expect_tx(&ss->full[s], kQuant ? kABytes : kABytes + kBBytes);
           if (batched)
             tma_load_3d(sA + s * kABytes, &map_x, &ss->full[s], kb * kBK, m0, bb);
@@ -244,13 +309,15 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kBM, kBN, 0, 0);
+    // (a pair's MMAs come from its leader CTA alone)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kPair ? 2 * kBM : kBM, kBN, 0, 0);
       uint32_t it = 0;
       int tc = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int w = work0; w < num_work && !*abort_flag; w += work_step) {
         int m0, bb;
-        if (tile_rows(tile, m0, bb)) continue;
+        bool dead, absent;
+        if (!work_rows(w, m0, bb, dead, absent)) continue;
         const int buf = tc & 1;
         const uint32_t use = tc >> 1;
         ++tc;
@@ -276,12 +343,21 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
-            umma_ss(dcol, ad, bd, idesc, (kb | k) != 0);
+            if (kPair)
+              umma_ss_pair(dcol, ad, bd, idesc, (kb | k) != 0);
+            else
+              umma_ss(dcol, ad, bd, idesc, (kb | k) != 0);
           }
-          umma_commit(&ss->empty[s]);
+          if (kPair)
+            umma_commit_pair_mc(&ss->empty[s], 0x3);  // both CTAs' stages are free
+          else
+            umma_commit(&ss->empty[s]);
         }
         if (!ok) break;
-        umma_commit(&ss->tfull[buf]);
+        if (kPair)
+          umma_commit_pair_mc(&ss->tfull[buf], 0x3);  // both CTAs' accumulators
+        else
+          umma_commit(&ss->tfull[buf]);
       }
     }
   } else if (warp < kEpiWarp0 + 4) {
@@ -291,10 +367,11 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
     if (lane == 0) prefetch_tensormap(&map_y);
     int tc = 0;
     uint32_t nslab = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+    for (int w = work0; w < num_work && !*abort_flag; w += work_step) {
       int m0, bb;
-      const bool skip = tile_rows(tile, m0, bb);
-      const int n0 = (tile % tiles_n) * kBN;
+      bool skip, absent;  // skip: zeros (dead rows); absent: nothing to write
+      const bool runs = work_rows(w, m0, bb, skip, absent);
+      const int n0 = (w % tiles_n) * kBN;
       const int buf = tc & 1;
       const uint32_t use = tc >> 1;
       const bool glu = ep.mode == kEpiGlu;
@@ -324,7 +401,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
                          : make_uint4(0u, 0u, 0u, 0u);
       };
       load_res(0);
-      if (!skip) {
+      if (runs) {
         ++tc;
         if (!mbar_wait(&ss->tfull[buf], use & 1, err, kDevTimeoutMma)) {
           *abort_flag = 1;
@@ -396,7 +473,7 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
           for (int e = 0; e < 64; ++e) v[e] = 0.f;
         }
         if (resid && c + 64 < ncols) load_res(c + 64);  // the next slab's residual
-        if (on0 + c >= n_out) continue;  // whole slab past N (warp-uniform)
+        if (absent || on0 + c >= n_out) continue;  // whole slab past N (warp-uniform)
         uint8_t* sb = slab + (nslab & 1) * kSlabBytes;
         // the store issued two slabs ago must have finished reading sb
         if (lane == 0) bulk_wait_read<1>();
@@ -420,10 +497,15 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
         }
         ++nslab;
       }
-      if (!skip) {
+      if (runs) {  // the accumulator may take the next work item (the pair's leader counts 8)
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ss->tempty[buf]);
+        if (lane == 0) {
+          if (kPair && rank != 0)
+            mbar_arrive_cluster(&ss->tempty[buf], 0);
+          else
+            mbar_arrive(&ss->tempty[buf]);
+        }
       }
     }
     if (lane == 0) bulk_wait_all();  // stores read shared memory until done
@@ -485,10 +567,20 @@ __global__ void __launch_bounds__(kQuant ? 320 : 192, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
+  if (kPair) {
+    // neither CTA leaves (or frees the pair's TMEM) while the other may still
+    // signal its barriers or feed the leader's MMAs from its shared memory
+    cluster_sync();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, 512);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, 512);
+    }
   }
 }
 
@@ -524,6 +616,14 @@ int tiles_m_of(int M, const RowTiling& rt) {
 // the 256-wide tile is faster per FLOP (it reads 1.5x less shared memory per
 // MMA), which outweighs the better wave fill (config 1's linear_out: 312
 // tiles ran 7% slower as 624).  GLU needs the 256-wide layout.
+// The CTA-pair GEMM is on unless NRP_PAIR_GEMM=0 (read once).
+bool pair_gemm_enabled() {
+  static const int on = [] {
+    const char* e = getenv("NRP_PAIR_GEMM");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
 int pick_bn(int M, int N, const RowTiling& rt, const Epilogue& ep, int num_sms) {
   if (ep.mode == kEpiGlu) return 256;
   const int tiles256 = tiles_m_of(M, rt) * ((N + 255) / 256);
@@ -534,26 +634,51 @@ int grid_size(int M, int N, int bn, const RowTiling& rt, int num_sms) {
   return tiles < num_sms ? tiles : num_sms;
 }
 
-template <bool kQuant, int kBN>
+template <bool kQuant, int kBN, bool kPair = false>
 cudaError_t launch_tn(const CUtensorMap& map_x, const void* w, const uint8_t* wq,
                       const __nv_bfloat16* qs, const __nv_bfloat16* qb,
                       const __nv_bfloat16* bias, __nv_bfloat16* y, int ldy, int M, int N, int K,
                       int num_sms, int* err, cudaStream_t stream, const RowTiling& rt,
                       const Epilogue& ep, bool w_early) {
   static std::atomic<uint64_t> attr{0};
-  constexpr int kSmem = static_cast<int>(smem_bytes<kBN>());
-  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<kQuant, kBN>, kSmem, attr)) return e;
+  constexpr int kSmem = static_cast<int>(smem_bytes<kBN, kPair>());
+  if (cudaError_t e = smem_attr_once(gemm_tn_kernel<kQuant, kBN, kPair>, kSmem, attr)) return e;
   CUtensorMap map_w = map_x;  // unused by the quantised kernel
+  // a pair's CTA loads half of the tile's W rows
   if (!kQuant && !make_tmap_2d(&map_w, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N,
-                               static_cast<uint64_t>(K) * 2, 64, kBN, true))
+                               static_cast<uint64_t>(K) * 2, 64, kPair ? kBN / 2 : kBN, true))
     return cudaErrorInvalidValue;
   CUtensorMap map_y;
   if (!make_y_map(&map_y, y, ldy, M, ep.mode == kEpiGlu ? N / 2 : N, rt))
     return cudaErrorInvalidValue;
-  const int grid = grid_size(M, N, kBN, rt, num_sms);
-  return launch_pdl(gemm_tn_kernel<kQuant, kBN>, dim3(grid), dim3(kQuant ? 320 : 192),
-                    static_cast<size_t>(kSmem), stream, map_x, map_w, map_y, wq, qs, qb, bias, M,
-                    N, K, rt, ep, w_early ? 1 : 0, err);
+  if constexpr (!kPair) {
+    const int grid = grid_size(M, N, kBN, rt, num_sms);
+    return launch_pdl(gemm_tn_kernel<kQuant, kBN, false>, dim3(grid), dim3(kQuant ? 320 : 192),
+                      static_cast<size_t>(kSmem), stream, map_x, map_w, map_y, wq, qs, qb, bias,
+                      M, N, K, rt, ep, w_early ? 1 : 0, err);
+  } else {
+  // clusters of two CTAs, one per work item (a pair of row tiles), at most
+  // one per two SMs
+  const int tiles_m = tiles_m_of(M, rt), tiles_n = (N + kBN - 1) / kBN;
+  const int work = ((tiles_m + 1) / 2) * tiles_n;
+  const int pairs = std::min(work, std::max(1, (num_sms > 0 ? num_sms : 148) / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = static_cast<size_t>(kSmem);
+  cfg.stream = stream;
+  cudaLaunchAttribute la[2];
+  la[0].id = cudaLaunchAttributeClusterDimension;
+  la[0].val.clusterDim.x = 2;
+  la[0].val.clusterDim.y = 1;
+  la[0].val.clusterDim.z = 1;
+  la[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  la[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = la;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gemm_tn_kernel<kQuant, kBN, true>, map_x, map_w, map_y, wq,
+                            qs, qb, bias, M, N, K, rt, ep, 0, err);
+  }
 }
 }  // namespace
 
@@ -581,6 +706,14 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& map_x, const void* w,
   if (bn == 128)
     return launch_tn<false, 128>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
                                  num_sms, err, stream, rt, ep, w_early);
+  // CTA pairs (256 x 256 tiles shared by two SMs) for tall problems: from
+  // 128 row tiles on (same-box A/B: config 3's encoder, 128 row tiles, 21.2 ->
+  // 20.3 ms; config 4's windowed layer, 391, 0.595 -> 0.571 ms; config 1's
+  // 96 per-utterance row tiles ran 2% slower as pairs)
+  if (pair_gemm_enabled() && N % 256 == 0 && tm >= 128 &&
+      ((tm + 1) / 2) * (N / 256) >= (num_sms > 0 ? num_sms : 148) / 2)
+    return launch_tn<false, 256, true>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N,
+                                       K, num_sms, err, stream, rt, ep, w_early);
   return launch_tn<false, 256>(map_x, w, nullptr, nullptr, nullptr, bias, y, ldy, M, N, K,
                                num_sms, err, stream, rt, ep, w_early);
 }
