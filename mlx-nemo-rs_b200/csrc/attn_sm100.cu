@@ -86,7 +86,7 @@ constexpr uint32_t kOffX = kOffPr + kTileBytes;      // [2 parity][2 halves][128
 constexpr uint32_t kOffBar = kOffX + 2048;
 
 struct Bars {
-  uint64_t q, prep, p0, kp, v[2], s, sfree, p, o, x, ob, ofree, dfull[2], dempty[2];
+  uint64_t q, prep, p0, kp, v[2], s, sfree, p, o, x[4], ob, ofree, dfull[2], dempty[2];
   uint32_t tmem_base;
   int abort;
   int desc[2][8];  // item descriptors, helper -> issuer and softmax (nt < 0: done)
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->sfree, kSoftmaxWarps);
     mbar_init(&bars->p, kSoftmaxWarps);
     mbar_init(&bars->o, 1);
-    mbar_init(&bars->x, kSoftmaxWarps);
+    for (int k = 0; k < 4; ++k) mbar_init(&bars->x[k], 2);  // the two warps of a quadrant
     mbar_init(&bars->ob, kSoftmaxWarps);
     mbar_init(&bars->ofree, 1);
     mbar_init(&bars->dfull[0], 1);
@@ -581,8 +581,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         tc_fence_after();
         xbuf[xphase * 256 + kh * 128 + il] = pl;
-        warp_arrive(&bars->x);
-        ok = warp_wait(&bars->x, xphase, err, kDevTimeoutEpi);
+        warp_arrive(&bars->x[quad]);
+        ok = warp_wait(&bars->x[quad], xphase, err, kDevTimeoutEpi);
         if (ok) {
           const float lt = pl + xbuf[xphase * 256 + (kh ^ 1) * 128 + il];
           inv = lt > 0.f ? 1.f / lt : 0.f;
@@ -730,8 +730,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // buffers let one sync per tile suffice (a thread cannot write the
         // buffer of parity p again before its partner passed this sync)
         xbuf[xphase * 256 + kh * 128 + il] = mx;
-        warp_arrive(&bars->x);
-        if (!warp_wait(&bars->x, xphase, err, kDevTimeoutEpi)) { ok = false; break; }
+        warp_arrive(&bars->x[quad]);
+        if (!warp_wait(&bars->x[quad], xphase, err, kDevTimeoutEpi)) { ok = false; break; }
         mx = fmaxf(mx, xbuf[xphase * 256 + (kh ^ 1) * 128 + il]);
         xphase ^= 1;
         float alpha = 1.f;
