@@ -211,3 +211,13 @@ def _shard_forward(rank, world, T, B, D, H, context, lengths, seed):
 def test_two_ranks_with_halo_match_single_device_forward(T, context, lengths):
     err = _spawn(_shard_forward, 2, T, 2, 64, 2, context, np.array(lengths, np.int32), 7)[0]
     assert err < 1e-4, err
+
+
+# Middle ranks exchange halos with both neighbours (world > 2).
+@pytest.mark.parametrize("world,T,context,lengths", [
+    (3, 120, (4, 1, True), [120, 33]),
+    (4, 600, (128, 128, False), [600, 421]),
+])
+def test_middle_ranks_with_halo_match_single_device_forward(world, T, context, lengths):
+    err = _spawn(_shard_forward, world, T, 2, 64, 2, context, np.array(lengths, np.int32), 11)[0]
+    assert err < 1e-4, err
