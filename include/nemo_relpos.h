@@ -555,6 +555,14 @@ int nrp_subsampling_load_out_quantized(nrp_subsampling* sub, int bits, int group
  * [batch, T', d_model] bf16, T' = nrp_subsampling_output_length(frames). */
 int nrp_subsampling_forward(nrp_subsampling* sub, void* stream, const float* features, int layout,
                             int batch, int frames, const int32_t* lengths, void* out);
+/* Subsampling::forward_frames_chunked (1334-1377): with frames > 0, inputs
+ * longer than `frames` mel frames (rounded down to a multiple of the factor)
+ * run the conv stack in time chunks, each with twice the receptive field of
+ * real neighbouring frames on either side, the frames that saw a chunk's edge
+ * padding cropped.  This bounds the activation memory to one chunk's; the
+ * output equals the single pass bit for bit.  0 (the default): the whole
+ * input at once.  The reference uses 4096 (SUBSAMPLING_CHUNK_FRAMES, 1060). */
+int nrp_subsampling_set_chunk_frames(nrp_subsampling* sub, int frames);
 
 /* --------------------------------------------------- linear primitives */
 /* LinearLayer::forward, Standard arm (quantization.rs:128-135) on device

@@ -159,6 +159,7 @@ def lib():
             "nrp_subsampling_load_out": ([vp, vp, vp], i),
             "nrp_subsampling_load_out_quantized": ([vp, i, i, vp, vp, vp, vp], i),
             "nrp_subsampling_forward": ([vp, vp, vp, i, i, i, vp, vp], i),
+            "nrp_subsampling_set_chunk_frames": ([vp, i], i),
             "nrp_context_set_weight_cache": ([vp, i], i),
             "nrp_profile_enable": ([vp, i], i),
             "nrp_profile_reset": ([vp], i),
@@ -761,6 +762,13 @@ class Subsampling:
 
     def set_dtype(self, dtype: int):
         _check(lib().nrp_subsampling_set_dtype(self.handle, dtype))
+
+    def set_chunk_frames(self, frames: int):
+        """forward_frames_chunked (conformer.rs:1334-1377): inputs longer than
+        `frames` mel frames run in time chunks (same output, bounded memory);
+        0, the default, runs the whole input at once.  The reference uses
+        4096."""
+        _check(lib().nrp_subsampling_set_chunk_frames(self.handle, int(frames)))
 
     def output_length(self, frames: int) -> int:
         """Subsampling::output_length (conformer.rs:1315-1327)."""

@@ -275,6 +275,7 @@ struct SubConvArgs {
   const float* mel = nullptr;
   int64_t mel_bs = 0, mel_ts = 0, mel_fs = 0;
   const int32_t* len = nullptr;
+  int len_off = 0;  // subtracted from len[b]: the first frame of a time chunk
   int T = 0, F = 0, T1 = 0, F1 = 0, T2 = 0, F2 = 0, C = 0, pad = 1;
   const uint32_t *f0 = nullptr, *f1 = nullptr;  // conv.0 and depthwise fragments
   __nv_bfloat16* out = nullptr;

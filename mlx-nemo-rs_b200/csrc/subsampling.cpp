@@ -12,10 +12,13 @@
 // [B, T', F', C] and the columns of `out`'s weight are permuted once at load
 // to the same order, so no transpose runs.  A quantised `out` is dequantised
 // on the host at load (a 5 MB weight: its bf16 copy is what the 8-bit GEMM
-// path would make each call).  The whole input is processed at once: the
-// reference's 4096-frame chunking (1345-1377) only bounds its memory and is
-// exact, and the largest buffer here (the first pointwise conv's output) is
-// 2 * T/4 * F/4 * C bytes per utterance.
+// path would make each call).  By default the whole input is processed at
+// once (the largest buffer, the first pointwise conv's output, is
+// 2 * T/4 * F/4 * C bytes per utterance); nrp_subsampling_set_chunk_frames
+// selects the reference's time chunking (forward_frames_chunked,
+// 1334-1377), which bounds that memory and gives the same frames: each
+// output frame is computed from the same input frames by the same
+// arithmetic.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -75,6 +78,8 @@ struct nrp_subsampling {
   nrp::DevBuf d_out_w, d_out_b;  // bf16 [D][F' * C] (columns f' * C + c), [D]
   bool has_out_b = false;
   nrp::DevBuf act[2];  // ping-pong NHWC activations
+  int chunk_frames = 0;   // mel frames per time chunk (0: the whole input at once)
+  nrp::DevBuf chunk_out;  // one chunk's output frames, before the crop
 };
 
 namespace {
@@ -182,15 +187,13 @@ int subsampling_output_frames(const nrp_subsampling* s, int frames) {
 
 int subsampling_feat_in(const nrp_subsampling* s) { return s->F; }
 
-int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64_t bs, int64_t ts,
-                    int64_t fs, int B, int T, const int32_t* lengths, void* out) {
-  if (s->dtype != NRP_DTYPE_BF16)
-    return failf(NRP_ERR_UNSUPPORTED, "the subsampling runs in bf16 (nrp_subsampling_set_dtype)");
-  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
-  if (!s->ctx) return failf(NRP_ERR_INVALID, "the subsampling was created without a context");
-  if (select_device(s->ctx)) return NRP_ERR_CUDA;
-  int rc = sync_sub(s);
-  if (rc) return rc;
+namespace {
+
+// The conv stack and `out` over mel frames [0, T) of mel (lengths counted
+// from frame len_off of the full input).
+int run_frames(nrp_subsampling* s, cudaStream_t st, const float* mel, int64_t bs, int64_t ts,
+               int64_t fs, int B, int T, const int32_t* lengths, int len_off, void* out) {
+  int rc = NRP_OK;
   const int C = s->C, pad = s->causal ? 2 : 1;
   int Ti[kMaxStrides + 1], Fi[kMaxStrides + 1];
   Ti[0] = T;
@@ -215,6 +218,7 @@ int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64
     a.mel_ts = ts;
     a.mel_fs = fs;
     a.len = lengths;
+    a.len_off = len_off;
     a.T = T;
     a.F = s->F;
     a.T1 = Ti[1];
@@ -251,6 +255,59 @@ int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64
   return linear(s->ctx, st, NRP_DTYPE_BF16, buf[cur], B * Tp, K, s->d_out_w.p, false, nullptr,
                 nullptr, s->D, s->has_out_b ? s->d_out_b.p : nullptr, out, s->D, RowTiling(),
                 Epilogue());
+}
+
+}  // namespace
+
+int subsampling_run(nrp_subsampling* s, cudaStream_t st, const float* mel, int64_t bs, int64_t ts,
+                    int64_t fs, int B, int T, const int32_t* lengths, void* out) {
+  if (s->dtype != NRP_DTYPE_BF16)
+    return failf(NRP_ERR_UNSUPPORTED, "the subsampling runs in bf16 (nrp_subsampling_set_dtype)");
+  if (B <= 0 || T <= 0) return failf(NRP_ERR_INVALID, "empty input [%d, %d]", B, T);
+  if (!s->ctx) return failf(NRP_ERR_INVALID, "the subsampling was created without a context");
+  if (select_device(s->ctx)) return NRP_ERR_CUDA;
+  int rc = sync_sub(s);
+  if (rc) return rc;
+  // forward_frames_chunked (conformer.rs:1344-1377): chunks of a multiple of
+  // the factor, each run with `context` real neighbouring frames on either
+  // side (twice the receptive field of the stacked stride-2 convs, rounded
+  // up to the factor), its first left/factor output frames cropped; the
+  // last chunk keeps every frame after the crop.
+  const int factor = 1 << s->S;
+  const int chunk = s->chunk_frames > 0 ? std::max(s->chunk_frames, factor) / factor * factor : 0;
+  if (chunk == 0 || T <= chunk)
+    return run_frames(s, st, mel, bs, ts, fs, B, T, lengths, 0, out);
+  const int receptive = 1 + (3 - 1) * (factor - 1);
+  const int context = (2 * receptive + factor - 1) / factor * factor;
+  const int Tp_all = subsampling_output_frames(s, T);
+  const size_t row = static_cast<size_t>(s->D) * 2;  // bytes per output frame
+  const int piece_max = chunk + 2 * context;
+  TRY_CUDA(s->chunk_out.ensure(static_cast<size_t>(B) * subsampling_output_frames(s, piece_max) *
+                               row));
+  int done = 0;  // output frames written per utterance
+  for (int start = 0; start < T;) {
+    const int end = std::min(start + chunk, T);
+    const int left = std::min(context, start), right = std::min(context, T - end);
+    const int p0 = start - left, n = end + right - p0;
+    const int Tp = subsampling_output_frames(s, n);
+    rc = run_frames(s, st, mel + p0 * ts, bs, ts, fs, B, n, lengths, p0, s->chunk_out.p);
+    if (rc) return rc;
+    const int first = left / factor;
+    const int keep = end == T ? Tp - first : (end - start) / factor;
+    if (keep < 0 || done + keep > Tp_all)
+      return failf(NRP_ERR_UNSUPPORTED, "chunk plan: %d + %d frames of %d", done, keep, Tp_all);
+    if (keep > 0) {
+      ProfScope ps(s->ctx, NRP_KERNEL_ELEMENTWISE, st);
+      TRY_CUDA(cudaMemcpy2DAsync(static_cast<uint8_t*>(out) + done * row, Tp_all * row,
+                                 s->chunk_out.as<uint8_t>() + first * row, Tp * row, keep * row,
+                                 B, cudaMemcpyDeviceToDevice, st));
+    }
+    done += keep;
+    start = end;
+  }
+  if (done != Tp_all)
+    return failf(NRP_ERR_UNSUPPORTED, "chunk plan wrote %d of %d frames", done, Tp_all);
+  return NRP_OK;
 }
 
 }  // namespace nrp
@@ -371,6 +428,13 @@ int nrp_subsampling_load_out_quantized(nrp_subsampling* s, int bits, int group_s
   }
   if (bias) L.bias.assign(bias, bias + s->D);
   s->dirty = true;
+  return NRP_OK;
+}
+
+int nrp_subsampling_set_chunk_frames(nrp_subsampling* s, int frames) {
+  if (!s) return failf(NRP_ERR_INVALID, "null subsampling");
+  if (frames < 0) return failf(NRP_ERR_INVALID, "chunk frames %d < 0", frames);
+  s->chunk_frames = frames;
   return NRP_OK;
 }
 

@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(kSubThreads, 2) conv0_dw_kernel(const SubConvA
   uint8_t* zero = ctile + R1 * tr.slots * kPosStride;
   const int g = lane >> 2, t = lane & 3;
   pdl_wait();
-  const int lenb = a.len ? a.len[b] : a.T;
+  const int lenb = a.len ? a.len[b] - a.len_off : a.T;
 
   // 1. mel rows (zero outside the input and past the length), copied
   // asynchronously; lanes walk the layout's contiguous axis.  (The bf16

@@ -247,6 +247,7 @@ extern "C" {
     pub fn nrp_subsampling_forward(s: *mut nrp_subsampling, stream: *mut c_void,
                                    features: *const c_float, layout: c_int, batch: c_int,
                                    frames: c_int, lengths: *const i32, out: *mut c_void) -> c_int;
+    pub fn nrp_subsampling_set_chunk_frames(s: *mut nrp_subsampling, frames: c_int) -> c_int;
     pub fn nrp_qlinear(ctx: *mut nrp_context, stream: *mut c_void, x: *const c_void, m: c_int, k: c_int,
                        wq: *const u32, scales: *const c_void, biases: *const c_void, n: c_int,
                        group: c_int, bits: c_int, bias: *const c_void, y: *mut c_void) -> c_int;

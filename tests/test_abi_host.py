@@ -221,3 +221,15 @@ def test_subsampling_sizes_match_oracle(nrp, orc):
         s.set_conv(1, np.zeros((64, 3, 3, 1), np.float32))  # conv.1 is the ReLU
     with pytest.raises(nrp.NrpError):
         nrp.Subsampling(80, 64, 8, 96, False, host_only=True)  # channels not a power of two
+
+
+def test_subsampling_chunk_frames_argument(nrp):
+    """nrp_subsampling_set_chunk_frames takes 0 (the whole input at once) or a
+    chunk size, and rejects a negative one (forward_frames_chunked,
+    conformer.rs:1334-1377)."""
+    s = nrp.Subsampling(80, 64, 8, 64, False, host_only=True)
+    s.set_chunk_frames(4096)
+    s.set_chunk_frames(0)
+    with pytest.raises(nrp.NrpError) as e:
+        s.set_chunk_frames(-1)
+    assert e.value.code == nrp.NRP_ERR_INVALID

@@ -152,3 +152,42 @@ def test_encoder_forward_from_mel(nrp, orc):
         h = orc.block_forward(h, bw, pe, H, ff, K, lengths=out_len, bf16=True)
     err = max(rel(got[b, :n], h[b, :n]) for b, n in enumerate(out_len))
     assert err < TOL_BF16, err
+
+
+@pytest.mark.parametrize("B,T,factor,causal,layout,lengths,chunk", [
+    # lengths ending inside a chunk, on a chunk edge, and inside the context
+    (3, 1300, 8, False, "btf", [1300, 700, 1030], 512),
+    (2, 1300, 8, True, "bft", [1300, 517], 512),
+    (2, 901, 4, False, "bft", None, 256),
+    (2, 901, 4, True, "btf", [901, 260], 256),
+    (1, 330, 2, False, "btf", [300], 64),
+    (2, 4100, 8, False, "bft", [4100, 4096], 4096),  # the reference's chunk size
+])
+def test_chunked_subsampling_equals_single_pass(nrp, orc, B, T, factor, causal, layout, lengths,
+                                                 chunk):
+    """forward_frames_chunked (conformer.rs:1334-1377) on the device gives the
+    single pass's output bit for bit: every output frame is computed from the
+    same input frames by the same arithmetic."""
+    import torch
+    F, C, D = 80, 256 if factor == 8 else 128, 512
+    rng = np.random.default_rng(T + factor + 7 * causal)
+    sw, wd = sub_weights(orc, rng, C, F, D, factor, causal, False)
+    sub = nrp.Subsampling(F, D, factor, C, causal)
+    sub.load_weights(wd)
+    sub.set_dtype(nrp.BF16)
+    x = rng.standard_normal((B, T, F)).astype(np.float32)
+    if layout == "btf":
+        xd, lay = torch.from_numpy(x).cuda(), nrp.FEATURES_BTF
+    else:
+        xd = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 1))).cuda()
+        lay = nrp.FEATURES_BFT
+    whole, _ = sub.forward(xd, lengths, layout=lay)
+    sub.set_chunk_frames(chunk)
+    chunked, _ = sub.forward(xd, lengths, layout=lay)
+    sub.set_chunk_frames(0)
+    sub.ctx.check()
+    assert chunked.shape == whole.shape == (B, sub.output_length(T), D)
+    assert torch.equal(chunked.view(torch.int16), whole.view(torch.int16))
+    if T <= 1300:  # and the single pass against the oracle
+        ref = orc.subsampling_forward(masked(x, lengths), sw, D, factor, causal, bf16=True)
+        assert rel(whole.float().cpu().numpy(), ref) < TOL_BF16
