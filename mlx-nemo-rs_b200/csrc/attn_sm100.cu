@@ -195,8 +195,9 @@ __device__ __forceinline__ void release_sched(int* sched) {
 }
 
 // Persistent: one CTA per SM, four roles.
-//   helpers (warps 9-11) warp 9 takes items from a counter shared by the
-//           grid (sched[0]; the last CTA to finish resets sched[0..1]), in
+//   helpers (warps 9-11) warp 9 takes a CTA's first item by its block
+//           index and the rest from a counter shared by the grid (sched[0]:
+//           items from gridDim.x on; the last CTA to finish resets sched[0..1]), in
 //           order of decreasing utterance length, writes padding tiles as
 //           zeros and hands each item with keys to the other roles through a
 //           two-slot descriptor ring; the three build the item's q+u/q+v
@@ -481,14 +482,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t pc = 0, ic = 0, dc = 0;
     bool ok = true;
     const int per_b = X * H;
+    bool first = true;  // a CTA's first item is its block index; then the counter
     while (true) {
       if (warp == 9) {
         // the next item with keys; padding tiles are written as zeros here
         Item it;
         while (true) {
-          int qn = 0;
-          if (lane == 0) qn = atomicAdd(sched, 1);
-          qn = __shfl_sync(0xffffffffu, qn, 0);
+          int qn = static_cast<int>(blockIdx.x);
+          if (!first) {
+            if (lane == 0) qn = atomicAdd(sched, 1) + static_cast<int>(gridDim.x);
+            qn = __shfl_sync(0xffffffffu, qn, 0);
+          }
+          first = false;
           if (qn >= n_items || !ok) {
             it.nt = -1;
             break;
