@@ -233,3 +233,30 @@ def test_subsampling_chunk_frames_argument(nrp):
     with pytest.raises(nrp.NrpError) as e:
         s.set_chunk_frames(-1)
     assert e.value.code == nrp.NRP_ERR_INVALID
+
+
+def test_chunk_plan_frames_match_output_length(nrp):
+    """The reference's time-chunk plan (forward_frames_chunked,
+    conformer.rs:1344-1377: chunks of a multiple of the factor, context of
+    twice the receptive field rounded up to the factor, the first left/factor
+    frames of each piece cropped, the last piece kept whole) yields exactly
+    Subsampling::output_length(T) frames, so the chunked device path writes
+    the same frames as the single pass."""
+    for factor in (2, 4, 8):
+        for causal in (False, True):
+            s = nrp.Subsampling(80, 64, factor, 64, causal, host_only=True)
+            for chunk in (64, 512, 4096):
+                for T in list(range(1, 700, 7)) + [4095, 4096, 4097, 8200, 12001]:
+                    c = max(chunk, factor) // factor * factor
+                    if T <= c:
+                        continue
+                    rf = 1 + (3 - 1) * (factor - 1)
+                    ctx = -(-2 * rf // factor) * factor
+                    total, start = 0, 0
+                    while start < T:
+                        end = min(start + c, T)
+                        left, right = min(ctx, start), min(ctx, T - end)
+                        n = s.output_length(end + right - (start - left))
+                        total += n - left // factor if end == T else (end - start) // factor
+                        start = end
+                    assert total == s.output_length(T), (factor, causal, chunk, T)
