@@ -136,6 +136,12 @@ int nrp_context_destroy(nrp_context* ctx);
 /* Synchronises `stream`, then reads and clears the device error word:
  * NRP_ERR_DEVICE if a kernel gave up on a bounded wait since the last check. */
 int nrp_context_check(nrp_context* ctx, void* stream);
+/* Failure-path self-test: queues on `stream` a kernel that waits on a
+ * barrier nothing ever arrives on for budget_us microseconds (1 .. 10^6) and
+ * then gives up, the way every kernel's bounded wait does.  The next
+ * nrp_context_check returns NRP_ERR_DEVICE and clears the error; the context
+ * stays usable.  No GPU fault is involved. */
+int nrp_context_selftest_wait_expiry(nrp_context* ctx, void* stream, int budget_us);
 /* Quantised linears with 256 or more rows run as bf16 GEMMs over their
  * weight's dequantised copy.  With the weight cache on (the default), each
  * weight's copy is made on its first such use and kept until its module

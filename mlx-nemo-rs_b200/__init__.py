@@ -93,6 +93,7 @@ def lib():
             "nrp_context_create": ([i, vp], i),
             "nrp_context_destroy": ([vp], i),
             "nrp_context_check": ([vp, vp], i),
+            "nrp_context_selftest_wait_expiry": ([vp, vp, i], i),
             "nrp_pe_encoding": ([vp, i, i, i, i, vp, vp], i),
             "nrp_attn_create": ([vp, i, i, i, vp], i),
             "nrp_attn_destroy": ([vp], i),
@@ -227,6 +228,13 @@ class Context:
         """Synchronise and raise NrpError(NRP_ERR_DEVICE) if a kernel gave up
         on a bounded wait."""
         _check(lib().nrp_context_check(self.handle, stream if stream is not None else _stream()))
+
+    def selftest_wait_expiry(self, budget_us: int = 20000, stream=None):
+        """Queues a kernel whose bounded wait (on a barrier nothing arrives
+        on) gives up after budget_us; the next check() raises NRP_ERR_DEVICE
+        and the context stays usable."""
+        _check(lib().nrp_context_selftest_wait_expiry(
+            self.handle, stream if stream is not None else _stream(), int(budget_us)))
 
     KERNELS = ("gemm_bf16", "gemm_q8", "qgemv", "gemm_f32", "attn_sm100", "attn_simt",
                "attn_stream", "ring_append", "layernorm", "dwconv", "elementwise", "dequant",

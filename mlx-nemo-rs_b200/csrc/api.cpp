@@ -609,6 +609,16 @@ int nrp_context_check(nrp_context* ctx, void* stream) {
   return ok();
 }
 
+int nrp_context_selftest_wait_expiry(nrp_context* ctx, void* stream, int budget_us) {
+  if (!ctx) return fail(NRP_ERR_INVALID, "null context");
+  if (budget_us < 1 || budget_us > 1000000)
+    return fail(NRP_ERR_INVALID, "budget %d us outside [1, 1000000]", budget_us);
+  if (check_device(ctx)) return NRP_ERR_CUDA;
+  CUDA_TRY(nrp::launch_wait_expiry(ctx->d_err, static_cast<uint64_t>(budget_us) * 1000,
+                                   static_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
 int nrp_pe_encoding(nrp_context* ctx, int d_model, int max_len, int seq_len, int dtype,
                     void* dev_out, void* stream) {
   if (!ctx || !dev_out) return fail(NRP_ERR_INVALID, "null argument");

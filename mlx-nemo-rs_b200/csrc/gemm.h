@@ -332,6 +332,10 @@ struct FramesPlan {
   int64_t off[kMaxFrameUtts];
   int32_t len[kMaxFrameUtts];
 };
+// A one-warp kernel that waits on an mbarrier nothing arrives on until
+// budget_ns have passed, then records kDevTimeoutSelftest in *err and exits:
+// the bounded-wait failure path, exercised without a fault.
+cudaError_t launch_wait_expiry(int* err, uint64_t budget_ns, cudaStream_t stream);
 cudaError_t launch_frames(void* padded, void* packed, const FramesPlan& plan, int n_utts,
                           bool to_padded, int32_t* dev_lengths, cudaStream_t stream);
 

@@ -643,6 +643,34 @@ cudaError_t launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n,
   return cudaGetLastError();
 }
 
+namespace {
+
+__global__ void wait_expiry_kernel(int* err, uint64_t budget_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x != 0) return;
+  // nothing arrives on `bar`: the wait ends by its deadline
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(&bar, 0)) {
+    if (globaltimer_ns() - t0 > budget_ns) {
+      atomicCAS(err, 0, kDevTimeoutSelftest);
+      return;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_wait_expiry(int* err, uint64_t budget_ns, cudaStream_t stream) {
+  if (!err || budget_ns == 0 || budget_ns > kWaitBudgetNs) return cudaErrorInvalidValue;
+  wait_expiry_kernel<<<1, 32, 0, stream>>>(err, budget_ns);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_frames(void* padded, void* packed, const FramesPlan& plan, int n_utts,
                           bool to_padded, int32_t* dev_lengths, cudaStream_t stream) {
   if (n_utts <= 0) return cudaSuccess;

@@ -22,6 +22,7 @@ enum DeviceError : int {
   kDevTimeoutMma = 2,     // an MMA-completion wait expired
   kDevTimeoutEpi = 3,     // an accumulator hand-off wait expired
   kDevBadArgs = 4,        // a kernel saw arguments it cannot handle
+  kDevTimeoutSelftest = 5,  // the self-test wait (nothing ever arrives) expired
 };
 
 // Wall-clock budget of one mbarrier wait (ns).  Correct code waits for

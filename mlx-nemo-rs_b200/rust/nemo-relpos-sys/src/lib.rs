@@ -118,6 +118,8 @@ extern "C" {
     pub fn nrp_context_create(device: c_int, out: *mut *mut nrp_context) -> c_int;
     pub fn nrp_context_destroy(ctx: *mut nrp_context) -> c_int;
     pub fn nrp_context_check(ctx: *mut nrp_context, stream: *mut c_void) -> c_int;
+    pub fn nrp_context_selftest_wait_expiry(ctx: *mut nrp_context, stream: *mut c_void,
+                                            budget_us: c_int) -> c_int;
     pub fn nrp_pe_encoding(ctx: *mut nrp_context, d_model: c_int, max_len: c_int, seq_len: c_int,
                            dtype: c_int, dev_out: *mut c_void, stream: *mut c_void) -> c_int;
     pub fn nrp_attn_create(ctx: *mut nrp_context, d_model: c_int, n_heads: c_int, use_bias: c_int,
